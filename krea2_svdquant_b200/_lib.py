@@ -1,0 +1,83 @@
+"""ctypes binding of ``libsvdq_b200.so`` (the C ABI in ``include/svdq_b200.h``).
+
+The library is loaded from this package directory.  There is no fallback:
+if it is missing or fails to load, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libsvdq_b200.so")
+
+_lock = threading.Lock()
+_lib = None
+
+c_void_p = ctypes.c_void_p
+c_int = ctypes.c_int
+c_int64 = ctypes.c_int64
+
+# name -> (argtypes, restype) for every entry point of include/svdq_b200.h
+SIGNATURES = {
+    "svdq_last_error": ([], ctypes.c_char_p),
+    "svdq_version": ([], ctypes.c_char_p),
+    "svdq_device_error": ([ctypes.POINTER(c_int), c_int], c_int),
+    "svdq_act_quant": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                        c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                        c_void_p, c_int, c_void_p], c_int),
+    "svdq_repack_weight": ([c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                            c_void_p], c_int),
+    "svdq_build_up_hl": ([c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p], c_int),
+    "svdq_w4a4_gemm": ([c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                        c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_void_p], c_int),
+}
+
+SVDQ_BF16, SVDQ_FP16, SVDQ_FP32 = 0, 1, 2
+STATUS_NAMES = {0: "SVDQ_OK", 1: "SVDQ_ERR_INVALID_ARGUMENT", 2: "SVDQ_ERR_UNSUPPORTED",
+                3: "SVDQ_ERR_CUDA", 4: "SVDQ_ERR_TIMEOUT", 5: "SVDQ_ERR_DEVICE_WAIT"}
+
+
+class SVDQError(RuntimeError):
+    """A C-ABI entry point returned a non-zero status."""
+
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {msg}")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the library; raises if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with `python -m krea2_svdquant_b200.build` "
+                    "(there is no non-CUDA fallback)")
+            handle = ctypes.CDLL(LIB_PATH)
+            for name, (argtypes, restype) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.argtypes = argtypes
+                fn.restype = restype
+            _lib = handle
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != 0:
+        raise SVDQError(status, lib().svdq_last_error().decode(errors="replace"))
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args))
+
+
+def device_error(clear: bool = True) -> int:
+    """Synchronize and return (and clear) the library's device-side wait error word."""
+    code = c_int(0)
+    check(lib().svdq_device_error(ctypes.byref(code), 1 if clear else 0))
+    return code.value

@@ -1,0 +1,107 @@
+// Host runtime pieces shared by all entry points: error strings, the device
+// error word, tensor-map encoding through the driver entry point, SM count.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <string>
+
+#include "svdq_common.cuh"
+
+namespace svdq {
+
+static __device__ int g_device_error = 0;
+
+int* device_error_word() {
+  static int* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!cache[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
+
+static thread_local std::string t_last_error;
+
+int set_error(int status, const std::string& msg) {
+  t_last_error = msg;
+  return status;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return SVDQ_OK;
+  return set_error(SVDQ_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int check_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+int make_tma_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                CUtensorMapSwizzle swizzle) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) return set_error(SVDQ_ERR_CUDA, "cuTensorMapEncodeTiled entry point not found");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return set_error(SVDQ_ERR_INVALID_ARGUMENT, "TMA base address is not 16-byte aligned");
+  if (row_stride_bytes % 16 != 0)
+    return set_error(SVDQ_ERR_INVALID_ARGUMENT, "TMA row stride is not a multiple of 16 bytes");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(SVDQ_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return SVDQ_OK;
+}
+
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+}  // namespace svdq
+
+extern "C" {
+
+const char* svdq_last_error(void) { return svdq::t_last_error.c_str(); }
+
+const char* svdq_version(void) { return "svdq_b200 0.1"; }
+
+int svdq_device_error(int* code, int clear) {
+  if (!code) return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "code is NULL");
+  int st = svdq::check_cuda(cudaDeviceSynchronize(), "svdq_device_error: synchronize");
+  if (st) return st;
+  st = svdq::check_cuda(cudaMemcpyFromSymbol(code, svdq::g_device_error, sizeof(int)),
+                        "svdq_device_error: read");
+  if (st) return st;
+  if (clear) {
+    int zero = 0;
+    st = svdq::check_cuda(cudaMemcpyToSymbol(svdq::g_device_error, &zero, sizeof(int)),
+                          "svdq_device_error: clear");
+  }
+  return st;
+}
+
+}  // extern "C"

@@ -1,0 +1,254 @@
+"""``SVDQuantLinear``: drop-in module for src/krea2_svdquant/runtime/linear.py:62-161.
+
+Same constructor, buffers (``smooth_scale, qweight, weight_scales, l1, l2[,
+bias]``), attributes, ``add_lora_adapter``, ``state`` property and
+``_forward_base`` / ``forward`` split.  The forward runs on the B200 CUDA
+library only:
+
+* ``b200`` (W4A4, the default): one activation pass (smoothing, INT4 codes,
+  low-rank + LoRA down-projection) and one fused tcgen05 GEMM (INT4 x INT4
+  residual with per-group rescale, low-rank/LoRA up-projection, bias, cast).
+* ``b200_w4a16``: bf16 activations against the INT4 weight.
+
+Errors raise; nothing falls back to another implementation (the reference
+swallows kernel errors and reruns its simulation, linear.py:133-154).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from . import ops
+from .config import BackendKind, resolve_backend
+from .quant import SVDQuantLinearState
+
+
+class SVDQuantLoRAAdapter(nn.Module):
+    """Inference-only LoRA branch (linear.py:11-45): ``(x @ down^T) @ up^T * multiplier``
+    with ``multiplier = scale * network_alpha / rank``.  Inside
+    :class:`SVDQuantLinear` the branch is fused into the CUDA kernels; this
+    module's own ``forward`` exists for API parity."""
+
+    def __init__(self, down_weight: torch.Tensor, up_weight: torch.Tensor, *, scale: float = 1.0,
+                 network_alpha: float | None = None) -> None:
+        super().__init__()
+        if down_weight.ndim != 2 or up_weight.ndim != 2:
+            raise ValueError("LoRA down/up weights must be rank-2 tensors")
+        rank = int(down_weight.shape[0])
+        if rank <= 0:
+            raise ValueError("LoRA rank must be positive")
+        if int(up_weight.shape[1]) != rank:
+            raise ValueError(f"LoRA shape mismatch: down={tuple(down_weight.shape)} up={tuple(up_weight.shape)}")
+        self.rank = rank
+        self.scale = float(scale)
+        self.network_alpha = float(network_alpha) if network_alpha is not None else float(rank)
+        self.register_buffer("down_weight", down_weight.contiguous(), persistent=True)
+        self.register_buffer("up_weight", up_weight.contiguous(), persistent=True)
+
+    @property
+    def multiplier(self) -> float:
+        return self.scale * (self.network_alpha / self.rank)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        down = self.down_weight.to(dtype=x.dtype)
+        up = self.up_weight.to(dtype=x.dtype)
+        return F.linear(F.linear(x, down), up) * self.multiplier
+
+
+@dataclass
+class PreparedOperands:
+    """Device-resident operands derived once from the checkpoint buffers."""
+
+    device: torch.device
+    key: tuple
+    k_in: int        # activation width the kernels read (original in_features rounded up to 8)
+    k_pad: int       # padded K of the checkpoint
+    n: int
+    smooth: torch.Tensor           # [k_in] bf16 (padded with ones)
+    l2: torch.Tensor | None        # [r8, k_in] bf16
+    lora_down: torch.Tensor | None  # [rl8, k_in] bf16, stacked adapters
+    lora_col_scale: torch.Tensor | None  # [rl8] fp32 multiplier per stacked row
+    up_hl: torch.Tensor | None     # [n, R2] bf16, [l1 | lora_up] hi/lo operand
+    up_hl_base: torch.Tensor | None  # same without the LoRA columns (for _forward_base)
+    w_codes: torch.Tensor          # [n, k_pad] e4m3 codes
+    w_scales_t: torch.Tensor       # [k_pad/64, n] fp32
+    bias: torch.Tensor | None      # [n] bf16
+
+
+def _pad_rows(t: torch.Tensor, rows: int) -> torch.Tensor:
+    return t if t.shape[0] == rows else F.pad(t, (0, 0, 0, rows - t.shape[0]))
+
+
+def _pad_cols(t: torch.Tensor, cols: int, value: float = 0.0) -> torch.Tensor:
+    return t if t.shape[-1] == cols else F.pad(t, (0, cols - t.shape[-1]), value=value)
+
+
+class SVDQuantLinear(nn.Module):
+    """Runtime SVDQuant linear on the B200 kernels (see module docstring)."""
+
+    def __init__(self, state: SVDQuantLinearState, backend: BackendKind | str = BackendKind.AUTO,
+                 *, act_group_size: int = 64):
+        super().__init__()
+        self.backend = resolve_backend(backend)
+        self.group_size = int(state.group_size)
+        self.original_shape = tuple(int(v) for v in state.original_shape)
+        self.qweight_packed = bool(state.qweight_packed)
+        self.padded_in_features = state.padded_in_features
+        self.act_group_size = int(act_group_size)
+        self.output_fp32 = False  # fp32-output mode (parity checks); default output dtype follows x
+        self.register_buffer("smooth_scale", state.smooth_scale.contiguous(), persistent=True)
+        self.register_buffer("qweight", state.qweight.contiguous(), persistent=True)
+        self.register_buffer("weight_scales", state.weight_scales.contiguous(), persistent=True)
+        self.register_buffer("l1", state.l1.contiguous(), persistent=True)
+        self.register_buffer("l2", state.l2.contiguous(), persistent=True)
+        if state.bias is None:
+            self.bias = None
+        else:
+            self.register_buffer("bias", state.bias.contiguous(), persistent=True)
+        self.lora_adapters = nn.ModuleList()
+        self._prepared: PreparedOperands | None = None
+
+    # ------------------------------------------------------------------ reference API
+    def add_lora_adapter(self, down_weight: torch.Tensor, up_weight: torch.Tensor, *, scale: float = 1.0,
+                         network_alpha: float | None = None) -> None:
+        """Attach an inference LoRA adapter (linear.py:88-111)."""
+        expected_out, expected_in = self.original_shape
+        if tuple(down_weight.shape[1:]) != (expected_in,):
+            raise ValueError(f"LoRA down input mismatch for SVDQuantLinear: expected {expected_in}, "
+                             f"got {tuple(down_weight.shape)}")
+        if int(up_weight.shape[0]) != expected_out:
+            raise ValueError(f"LoRA up output mismatch for SVDQuantLinear: expected {expected_out}, "
+                             f"got {tuple(up_weight.shape)}")
+        self.lora_adapters.append(SVDQuantLoRAAdapter(down_weight, up_weight, scale=scale,
+                                                      network_alpha=network_alpha))
+        self._prepared = None
+
+    @property
+    def state(self) -> SVDQuantLinearState:
+        return SVDQuantLinearState(smooth_scale=self.smooth_scale, qweight=self.qweight,
+                                   weight_scales=self.weight_scales, l1=self.l1, l2=self.l2, bias=self.bias,
+                                   group_size=self.group_size, original_shape=self.original_shape,
+                                   qweight_packed=self.qweight_packed,
+                                   padded_in_features=self.padded_in_features)
+
+    @property
+    def k_pad(self) -> int:
+        if self.padded_in_features:
+            return int(self.padded_in_features)
+        return int(self.qweight.shape[-1]) * (2 if self.qweight_packed else 1)
+
+    # ------------------------------------------------------------------ operand preparation
+    def _operand_key(self, device: torch.device) -> tuple:
+        bufs = [self.smooth_scale, self.qweight, self.weight_scales, self.l1, self.l2, self.bias]
+        for a in self.lora_adapters:
+            bufs += [a.down_weight, a.up_weight]
+        return (device,) + tuple((None if b is None else (b.data_ptr(), b.device)) for b in bufs) + tuple(
+            a.multiplier for a in self.lora_adapters)
+
+    def prepare(self, device: torch.device | str | None = None) -> PreparedOperands:
+        """Derive (once per device and buffer set) the kernel operands: e4m3
+        weight codes, transposed fp32 scales, ``[l1|lora_up]`` hi/lo operand,
+        padded smoothing / down-projection weights."""
+        device = torch.device(device) if device is not None else self.qweight.device
+        if device.type != "cuda":
+            raise ValueError("SVDQuantLinear.prepare needs a CUDA device (no CPU path in this runtime)")
+        key = self._operand_key(device)
+        if self._prepared is not None and self._prepared.key == key:
+            return self._prepared
+        if not self.qweight_packed:
+            raise ValueError("SVDQuantLinear on b200 expects a packed uint8 qweight (checkpoint format)")
+        n, k_orig = self.original_shape
+        k_pad = self.k_pad
+        k_in = ops.round_up(k_orig, 8)
+        if k_in > k_pad:
+            raise ValueError(f"padded K {k_pad} is smaller than in_features rounded to 8 ({k_in})")
+        if k_pad % 64:
+            raise ValueError(f"padded K {k_pad} must be a multiple of 64")
+        if self.group_size % 64:
+            raise ValueError(f"weight group size {self.group_size} must be a multiple of 64")
+        bf = torch.bfloat16
+        with torch.no_grad():
+            smooth = _pad_cols(self.smooth_scale.to(device=device, dtype=bf), k_in, 1.0).contiguous()
+            rank = int(self.l1.shape[1])
+            r8 = ops.round_up(rank, 8)
+            l2 = None
+            l1p = None
+            if rank > 0:
+                l2 = _pad_rows(_pad_cols(self.l2.to(device=device, dtype=bf), k_in), r8).contiguous()
+                l1p = _pad_cols(self.l1.to(device=device, dtype=bf), r8).contiguous()
+            downs, ups, cscale = [], [], []
+            for a in self.lora_adapters:
+                rl8 = ops.round_up(a.rank, 8)
+                downs.append(_pad_rows(_pad_cols(a.down_weight.to(device=device, dtype=bf), k_in), rl8))
+                ups.append(_pad_cols(a.up_weight.to(device=device, dtype=bf), rl8))
+                cscale.append(torch.full((rl8,), a.multiplier, dtype=torch.float32, device=device))
+            lora_down = torch.cat(downs).contiguous() if downs else None
+            lora_up = torch.cat(ups, dim=1).contiguous() if ups else None
+            col_scale = torch.cat(cscale).contiguous() if cscale else None
+            r_tot = (r8 if rank > 0 else 0) + (0 if lora_down is None else lora_down.shape[0])
+            r2 = ops.lowrank_width(r_tot)
+            l1_in = l1p if l1p is not None else torch.zeros((n, 0), dtype=bf, device=device)
+            up_hl = ops.build_up_hl(l1_in, lora_up, r2) if r2 else None
+            up_hl_base = up_hl
+            if lora_up is not None:
+                r2b = ops.lowrank_width(r8 if rank > 0 else 0)
+                up_hl_base = ops.build_up_hl(l1_in, None, r2b) if r2b else None
+            qw = self.qweight.to(device=device).contiguous()
+            ws = self.weight_scales.to(device=device).contiguous()
+            w_codes, w_scales_t = ops.repack_weight(qw, ws, self.group_size)
+            bias = None if self.bias is None else self.bias.to(device=device, dtype=bf).contiguous()
+        self._prepared = PreparedOperands(device=device, key=key, k_in=k_in, k_pad=k_pad, n=n, smooth=smooth,
+                                          l2=l2, lora_down=lora_down, lora_col_scale=col_scale, up_hl=up_hl,
+                                          up_hl_base=up_hl_base,
+                                          w_codes=w_codes, w_scales_t=w_scales_t, bias=bias)
+        return self._prepared
+
+    # ------------------------------------------------------------------ forward
+    def _run(self, x: torch.Tensor, include_lora: bool) -> torch.Tensor:
+        if not x.is_cuda:
+            raise ValueError("SVDQuantLinear (b200) needs CUDA activations; this runtime has no CPU path")
+        if x.dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError(f"SVDQuantLinear (b200) takes bf16 or fp32 activations, got {x.dtype}")
+        n, k_orig = self.original_shape
+        if x.shape[-1] != k_orig:
+            raise ValueError(f"expected [..., {k_orig}] activations, got {tuple(x.shape)}")
+        p = self.prepare(x.device)
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, k_orig)
+        if x2.dtype != torch.bfloat16:
+            x2 = x2.to(torch.bfloat16)
+        if p.k_in != k_orig or x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+            x2 = _pad_cols(x2, p.k_in).contiguous()
+        out_fp32 = self.output_fp32 or x.dtype == torch.float32
+        if self.backend is BackendKind.B200_W4A16:
+            raise NotImplementedError("b200_w4a16 backend is not built yet")
+        lora_down = p.lora_down if include_lora else None
+        col_scale = p.lora_col_scale if include_lora else None
+        up_hl = p.up_hl if include_lora else p.up_hl_base
+        codes, scales_t, mid, _, _ = ops.act_quant(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
+                                                   self.act_group_size, True, False)
+        y = ops.w4a4_gemm(codes, scales_t, p.w_codes, p.w_scales_t, mid if mid.numel() else None,
+                          up_hl if mid.numel() else None, p.bias, out_fp32)
+        return y.reshape(*lead, n)
+
+    def _forward_base(self, x: torch.Tensor) -> torch.Tensor:
+        """SVDQuant base term (residual + low-rank + bias), without LoRA branches."""
+        return self._run(x, include_lora=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if "_forward_base" in self.__dict__:
+            # an instance-level override of the base (as the reference's LoRA test does,
+            # test_lora_loading.py:60): keep the reference's composition base + adapters
+            y = self._forward_base(x)
+            for adapter in self.lora_adapters:
+                y = y + adapter(x)
+            return y
+        return self._run(x, include_lora=True)
+
+    def extra_repr(self) -> str:
+        n, k = self.original_shape
+        return (f"in_features={k}, out_features={n}, rank={self.l1.shape[1]}, group_size={self.group_size}, "
+                f"backend={self.backend.value}, loras={len(self.lora_adapters)}")

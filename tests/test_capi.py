@@ -1,0 +1,61 @@
+"""The C-ABI library loads and exports every entry point include/svdq_b200.h declares
+(no compute calls: runs without a GPU)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "svdq_b200.h")
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(svdq_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from krea2_svdquant_b200 import build
+    build.build()
+    return ctypes.CDLL(build.LIB_PATH)
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for must in ("svdq_act_quant", "svdq_w4a4_gemm", "svdq_repack_weight", "svdq_build_up_hl",
+                 "svdq_last_error", "svdq_device_error"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_python_binding_covers_header():
+    from krea2_svdquant_b200 import _lib
+    assert set(declared_functions()) <= set(_lib.SIGNATURES)
+
+
+def test_version_and_error_string(lib):
+    from krea2_svdquant_b200 import _lib
+    L = _lib.lib()
+    assert L.svdq_version().decode().startswith("svdq_b200")
+    assert isinstance(L.svdq_last_error(), bytes)
+
+
+def test_invalid_arguments_rejected_without_gpu():
+    """Host-side validation runs before any CUDA call: a bad group size is an error status."""
+    from krea2_svdquant_b200 import _lib
+    L = _lib.lib()
+    st = L.svdq_act_quant(ctypes.c_void_p(16), 8, ctypes.c_void_p(16), None, 0, None, None, 0,
+                          4, 8, 64, 96, None, None, None, None, 4, None, 0, None)
+    assert st == 1
+    assert "a_group" in L.svdq_last_error().decode()
+    st = L.svdq_w4a4_gemm(None, None, 4, None, None, None, None, 0, None, None, 0, 8, 4, 8, 64, None)
+    assert st == 1
