@@ -1,0 +1,309 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 SVDQuant linear hot path (BASELINE.json metric).
+
+Default workload: one W4A4 ``SVDQuantLinear`` forward at
+M=4096 tokens, K=6144, N=16384, rank 32, group 64, bf16 bias; a step is the
+whole forward (activation-quant kernel + fused tcgen05 GEMM) over one batch
+already resident in HBM.  Metric: dense-equivalent TOPS = 2*M*N*K / step time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one process per GPU; each rank runs its own batch
+(the image batch is sharded, no collective on the data path), so the reported
+value is the whole-job aggregate (weak scaling).  Timing: per-step CUDA events
+on the launching stream with an L2 flush (256 MiB memset) between steps,
+barrier + synchronize around the timed region, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+M, K, N, RANK, GROUP = 4096, 6144, 16384, 32, 64
+OPS = 2 * M * N * K  # dense-equivalent ops per step (svd.py:158 residual GEMM)
+METRIC = "SVDQuantLinear TOPS @M4096 K6144 N16384"
+WORKLOAD = ("BASELINE config 2: W4A4 SVDQuantLinear forward (act-quant + fused tcgen05 GEMM with "
+            "low-rank r32 + bias), M4096 K6144 N16384, group 64, bf16 in/out")
+
+
+def _peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+def _ncu_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch of ``kernel`` from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    try:
+        for line in open(path):
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == kernel:
+                return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int):
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+                mask = self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.05)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        busy = [s for s in self.samples if self.max_mhz is None or s > 0.3 * self.max_mhz] or self.samples
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def cpu_reference_tops(calls: int, warmup: int, x_cpu, st_cpu) -> tuple[float, int, str]:
+    """Time the reference's CPU path (torch-on-CPU restatement of svdquant_linear_sim, bf16,
+    all host threads) on full config-2 calls."""
+    import torch
+
+    from oracle.svdq_oracle import svdquant_linear_sim_torch
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    args = (st_cpu.smooth_scale, st_cpu.qweight, st_cpu.weight_scales, st_cpu.l1, st_cpu.l2, st_cpu.bias)
+    kw = dict(group=GROUP, k_in=K, k_pad=K)
+    with torch.no_grad():
+        for _ in range(warmup):
+            svdquant_linear_sim_torch(x_cpu, *args, **kw)
+        t0 = time.perf_counter()
+        for _ in range(calls):
+            svdquant_linear_sim_torch(x_cpu, *args, **kw)
+        dt = (time.perf_counter() - t0) / calls
+    sample = (f"{calls} full config-2 calls (M=4096) after {warmup} warm-up, bf16, torch CPU "
+              f"restatement of svdquant_linear_sim (svd.py:119-163), {cores} threads")
+    return OPS / dt / 1e12, cores, sample
+
+
+def run_reference(args) -> None:
+    """--impl reference: the reference's own CPU implementation of the path on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    from krea2_svdquant_b200.quant import make_synthetic_state
+
+    x, st = make_synthetic_state(M, K, N, RANK, GROUP, seed=0, device="cpu")
+    tops, cores, _ = cpu_reference_tops(args.steps, args.warmup, x, st)
+    ms = OPS / (tops * 1e12) * 1e3
+    sample = (f"each step one full config-2 call (M=4096), {args.warmup} warm-up steps, bf16, torch CPU "
+              f"restatement of svdquant_linear_sim (svd.py:119-163), {cores} threads")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(tops, 4), "unit": "TOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (BASELINE recipe, seeded)", "config": {"workload": WORKLOAD},
+        "cpu_baseline": {"value": round(tops, 4), "unit": "TOPS", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(tops, 4), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from krea2_svdquant_b200 import _lib, ops
+    from krea2_svdquant_b200.linear import SVDQuantLinear
+    from krea2_svdquant_b200.quant import make_synthetic_state
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+
+    x, st = make_synthetic_state(M, K, N, RANK, GROUP, seed=rank, device=dev)
+    mod = SVDQuantLinear(st, backend="b200")
+    p = mod.prepare(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def step(ev=None):
+        # the module forward, with an event between its two kernels
+        codes, sat, mid, _, _ = ops.act_quant(x, p.smooth, p.l2, None, None, p.k_pad, 64, True, False)
+        if ev is not None:
+            ev.record()
+        return ops.w4a4_gemm(codes, sat, p.w_codes, p.w_scales_t, mid, p.up_hl, p.bias, False)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            step(mids[i])
+            ends[i].record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    aq_ms = [s.elapsed_time(m) for s, m in zip(starts, mids)]
+    gemm_ms = [m.elapsed_time(e) for m, e in zip(mids, ends)]
+    total = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    total_ms = float(total.item())
+    dev_err = _lib.device_error()
+    if dev_err:
+        raise RuntimeError(f"device-side wait error 0x{dev_err:x}")
+
+    # end-to-end through the public API with host buffers (pinned), copies inside the timed region
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+    for _ in range(max(1, args.warmup)):
+        x_dev.copy_(x_host, non_blocking=True)
+        y_host.copy_(mod(x_dev), non_blocking=True)
+    torch.cuda.synchronize()
+    e_steps = max(3, min(args.steps, 20))
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    es.record()
+    for _ in range(e_steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        y_host.copy_(mod(x_dev), non_blocking=True)
+    ee.record()
+    torch.cuda.synchronize()
+    e2e = torch.tensor([es.elapsed_time(ee) / e_steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+        dist.barrier()
+
+    cpu_base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from krea2_svdquant_b200.quant import SVDQuantLinearState
+        c = lambda t: None if t is None else t.cpu()
+        stc = SVDQuantLinearState(c(st.smooth_scale), c(st.qweight), c(st.weight_scales), c(st.l1), c(st.l2),
+                                  c(st.bias), st.group_size, st.original_shape, True, st.padded_in_features)
+        tops, cores, sample = cpu_reference_tops(args.cpu_calls, 1, x.cpu(), stc)
+        cpu_base = {"value": round(tops, 4), "unit": "TOPS", "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        ms = total_ms / args.steps
+        value = world * OPS / (ms * 1e-3) / 1e12
+        gemm_avg = statistics.mean(gemm_ms)
+        achieved = OPS / (gemm_avg * 1e-3) / 1e12
+        peaks = _peaks()
+        if peaks.get("bf16_tflops"):
+            peak = 2.0 * float(peaks["bf16_tflops"])
+            peak_src = ("of measured: 2 x MEASURED_PEAKS.bf16_tflops (burst cuBLAS bf16); the B200 dense "
+                        "e4m3/int8 tensor rate is twice its dense bf16 rate")
+        else:
+            peak = 2.0 * 1590.0
+            peak_src = "of fallback: 2 x 1.59 PFLOP/s bf16 (profiling recipe)"
+        e2e_ms = float(e2e.item())
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int4 (e4m3 MMA operands, fp32 accumulate)",
+            "data": "synthetic (BASELINE recipe, seeded per rank), random-init weights",
+            "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N, "rank": RANK, "group": GROUP,
+                       "l2": "flushed between timed steps (256 MiB memset outside the step events)",
+                       "parallelism": f"batch-sharded replicas x{world} (no collective on the data path)"},
+            "roofline": {"bound": "tensor", "kernel": "w4a4_gemm_kernel", "achieved": round(achieved, 2),
+                         "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "traffic": _ncu_traffic("w4a4_gemm_kernel"), "peak_source": peak_src,
+                         "gemm_us": round(gemm_avg * 1e3, 2),
+                         "act_quant_us": round(statistics.mean(aq_ms) * 1e3, 2)},
+            "cpu_baseline": cpu_base,
+            "e2e": {"value": round(world * OPS / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
+                    "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
+                    "ms_per_step": round(e2e_ms, 3),
+                    "api": "SVDQuantLinear.forward with pinned host x -> device, y -> pinned host"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-calls", type=int, default=3)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,6 +1,6 @@
 // Activation quantization pass of the W4A4 SVDQuant linear (sm_100a).
 //
-// One pass over x [M, K_in] bf16 produces, per 16-row band:
+// One pass over x [M, K_in] bf16 produces, per 32-row band and 128-column chunk:
 //   x_hat = bf16(x / smooth)                             (svd.py:122)
 //   q     = clamp(rint(x_hat / scale), -8, 7) per group  (pack.py:6-23)
 //   scale = bf16(max(amax, bf16(1e-8)) / 7)              (pack.py:20)
@@ -8,7 +8,16 @@
 //   e4m3 codes (exact integers) + fp32 scales^T for the GEMM
 //   mid = [x_hat @ l2^T | (x @ lora_down^T) * col_scale] (svd.py:159, linear.py:45)
 //         written as a bf16 hi/lo pair so the GEMM's bf16 MMA keeps ~16 mantissa bits.
-// The down-projection runs on mma.sync tensor cores from shared memory.
+// The down-projection runs on mma.sync tensor cores from shared memory; loads
+// are a cp.async ring of 128-column chunks.
+//
+// Divisions must round exactly like float32 IEEE division followed by the
+// reference's rounding (bf16 for x_hat, rint for q).  Each quotient is first
+// formed as a product with the correctly rounded reciprocal; that product is
+// within 2 ulp of the correctly rounded quotient, so the final rounding can
+// only differ when the product lies within a few ulp of a rounding boundary
+// (a bf16 midpoint, or a half-integer).  Those rare elements are recomputed
+// with the IEEE division intrinsic __fdiv_rn.
 #include <cuda_fp8.h>
 
 #include "svdq_common.cuh"
@@ -16,10 +25,11 @@
 namespace svdq {
 namespace {
 
-constexpr int kBM = 16;        // rows per CTA
-constexpr int kThreads = 128;  // 4 warps
-constexpr int kStages = 3;
-constexpr int kMaxTilesPerWarp = 8;  // r_tot <= 4 warps * 8 tiles * 8 cols = 256
+constexpr int kBM = 32;         // rows per CTA
+constexpr int kThreads = 512;   // 16 warps
+constexpr int kChunk = 128;     // columns per pipeline stage
+constexpr int kLD = kChunk + 8; // padded smem row (bf16) so ldmatrix rows hit distinct banks
+constexpr int kTilesPerWarp = 4;  // 8 column-tile sets x 4 tiles x 8 columns: r_tot <= 256
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
@@ -31,10 +41,9 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                            uint32_t& r3) {
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
 __device__ __forceinline__ void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
@@ -49,6 +58,19 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a
       "{%8, %9}, {%0, %1, %2, %3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Near-boundary tests for the reciprocal-product quotients (see file comment).
+// bf16 rounding of a float32 depends on its low 16 bits against 0x8000; a
+// product within 2.5 ulp of the exact quotient can only round differently when
+// its low bits are within 8 of 0x8000.
+__device__ __forceinline__ bool near_bf16_midpoint(float t) {
+  return ((__float_as_uint(t) & 0xFFFFu) - 0x7FF8u) < 0x10u;
+}
+// rint of a value below 8 in magnitude: the product is within 2.5 * 2^-21 of the
+// exact quotient, so rint can only differ when it lies within 2^-19 of a half-integer.
+__device__ __forceinline__ bool near_half_integer(float t, float r) {
+  return 0.5f - fabsf(t - r) < 1.9073486e-06f;
 }
 
 struct ActQuantParams {
@@ -69,58 +91,35 @@ struct ActQuantParams {
   int R2;
 };
 
-// Shared-memory rows are padded by 8 bf16 so ldmatrix row addresses hit distinct banks.
-template <int G>
-struct Smem {
-  static constexpr int LD = G + 8;
-};
-
-template <int G>
+template <int G, int STAGES>
 __global__ void __launch_bounds__(kThreads) act_quant_kernel(const ActQuantParams p) {
-  constexpr int LD = Smem<G>::LD;
-  constexpr int EPT = G / 8;  // elements per thread in the quant step (8 threads per row)
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int r_tot = p.rank + p.lora_rank;
-  // layout: xs[kStages][kBM][LD], ws[kStages][r_tot][LD], sm[kStages][G], xh[kBM][LD]
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);
-  __nv_bfloat16* ws = xs + kStages * kBM * LD;
-  __nv_bfloat16* sm = ws + kStages * r_tot * LD;
-  __nv_bfloat16* xh = sm + kStages * G;
+  const int n_chunks = (p.K_pad + kChunk - 1) / kChunk;
+  // layout: rsm[n_chunks * kChunk] fp32 (1/smooth), xs[STAGES][kBM][kLD], ws[STAGES][r_tot][kLD], xh[kBM][kLD]
+  float* rsm = reinterpret_cast<float*>(smem_raw);
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rsm + n_chunks * kChunk);
+  __nv_bfloat16* ws = xs + STAGES * kBM * kLD;
+  __nv_bfloat16* xh = ws + STAGES * r_tot * kLD;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int m0 = blockIdx.x * kBM;
-  const int n_chunks = p.K_pad / G;
 
-  // ---- async loads of one K chunk (x band, smooth slice, weight rows) ----
   auto load_chunk = [&](int c) {
-    const int st = c % kStages;
-    const int k0 = c * G;
-    constexpr int SEG = G / 8;  // 16-byte segments per row
-    // x band: kBM rows x SEG segments
+    const int st = c % STAGES;
+    const int k0 = c * kChunk;
+    constexpr int SEG = kChunk / 8;  // 16-byte segments per row
     for (int i = tid; i < kBM * SEG; i += kThreads) {
       const int r = i / SEG, s = i % SEG;
-      const int col = k0 + s * 8;
-      const int row = m0 + r;
+      const int col = k0 + s * 8, row = m0 + r;
       int bytes = 0;
       const __nv_bfloat16* src = p.x;
       if (row < p.M && col < p.K_in) {
         bytes = min(16, (p.K_in - col) * 2);
         src = p.x + (int64_t)row * p.ldx + col;
       }
-      cp_async16(smem_u32(xs + (st * kBM + r) * LD + s * 8), src, bytes);
+      cp_async16(smem_u32(xs + (st * kBM + r) * kLD + s * 8), src, bytes);
     }
-    // smooth slice (G values); padded columns read as 1 through bytes == 0 -> handled below
-    for (int s = tid; s < SEG; s += kThreads) {
-      const int col = k0 + s * 8;
-      int bytes = 0;
-      const __nv_bfloat16* src = p.smooth;
-      if (col < p.K_in) {
-        bytes = min(16, (p.K_in - col) * 2);
-        src = p.smooth + col;
-      }
-      cp_async16(smem_u32(sm + st * G + s * 8), src, bytes);
-    }
-    // weight rows: l2 rows then lora rows
     for (int i = tid; i < r_tot * SEG; i += kThreads) {
       const int r = i / SEG, s = i % SEG;
       const int col = k0 + s * 8;
@@ -132,94 +131,128 @@ __global__ void __launch_bounds__(kThreads) act_quant_kernel(const ActQuantParam
         bytes = min(16, (p.K_in - col) * 2);
         src = base + col;
       }
-      cp_async16(smem_u32(ws + (st * r_tot + r) * LD + s * 8), src, bytes);
+      cp_async16(smem_u32(ws + (st * r_tot + r) * kLD + s * 8), src, bytes);
     }
   };
 
-  float acc[kMaxTilesPerWarp][4];
-#pragma unroll
-  for (int j = 0; j < kMaxTilesPerWarp; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  const int n_tiles = r_tot / 8;
-
-  const float eps = __bfloat162float(__float2bfloat16_rn(1e-8f));
-  const int qrow = tid / 8;               // quant step: row of the band
-  const int qcol = (tid % 8) * EPT;       // first column of this thread within the chunk
-  const int grow = m0 + qrow;
-
 #pragma unroll 1
-  for (int c = 0; c < kStages - 1; ++c) {
+  for (int c = 0; c < STAGES - 1; ++c) {
     if (c < n_chunks) load_chunk(c);
     cp_async_commit();
   }
+  // correctly rounded reciprocals of the smoothing scale, once per CTA
+  for (int k = tid; k < n_chunks * kChunk; k += kThreads)
+    rsm[k] = k < p.K_in ? __frcp_rn(__bfloat162float(p.smooth[k])) : 0.f;
+
+  // MMA work split: warp -> m-tile (warp & 1) and column tiles (warp >> 1) + 8 j
+  const int mt = warp & 1;
+  const int tset = warp >> 1;
+  const int n_tiles = r_tot / 8;
+  float acc[kTilesPerWarp][4];
+#pragma unroll
+  for (int j = 0; j < kTilesPerWarp; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+
+  const float eps = __bfloat162float(__float2bfloat16_rn(1e-8f));
+  const int qrow = tid / 16;        // quant step: 16 threads per row, 8 columns each
+  const int cc = (tid % 16) * 8;    // column within the chunk
+  const int grow = m0 + qrow;
 
 #pragma unroll 1
   for (int c = 0; c < n_chunks; ++c) {
-    const int st = c % kStages;
-    cp_async_wait<kStages - 2>();
+    const int st = c % STAGES;
+    cp_async_wait<STAGES - 2>();
     __syncthreads();  // chunk c landed; everyone finished chunk c-1
-    if (c + kStages - 1 < n_chunks) load_chunk(c + kStages - 1);
+    if (c + STAGES - 1 < n_chunks) load_chunk(c + STAGES - 1);
     cp_async_commit();
 
-    const int k0 = c * G;
+    const int col0 = c * kChunk + cc;
     // ---- smoothing + group quantization (bit-exact with the reference) ----
     {
-      const __nv_bfloat16* xr = xs + (st * kBM + qrow) * LD + qcol;
-      const __nv_bfloat16* sr = sm + st * G + qcol;
-      float xhv[EPT];
+      const uint4 xv = *reinterpret_cast<const uint4*>(xs + (st * kBM + qrow) * kLD + cc);
+      const float4 r0 = *reinterpret_cast<const float4*>(rsm + col0);
+      const float4 r1 = *reinterpret_cast<const float4*>(rsm + col0 + 4);
+      const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+      const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
+      float xf[8], t[8];
+      bool slow = false;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(x2[i]);
+        xf[2 * i] = f.x;
+        xf[2 * i + 1] = f.y;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        t[i] = xf[i] * rv[i];
+        slow |= near_bf16_midpoint(t[i]);
+      }
+      if (slow) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (near_bf16_midpoint(t[i]) && col0 + i < p.K_in)
+            t[i] = __fdiv_rn(xf[i], __bfloat162float(p.smooth[col0 + i]));
+      }
+      uint32_t hw[4];
+      float xhv[8];
       float amax = 0.f;
 #pragma unroll
-      for (int i = 0; i < EPT; ++i) {
-        const int col = k0 + qcol + i;
-        float v = 0.f;
-        if (col < p.K_in) v = __bfloat162float(__float2bfloat16_rn(
-                              __fdiv_rn(__bfloat162float(xr[i]), __bfloat162float(sr[i]))));
-        xhv[i] = v;
-        amax = fmaxf(amax, fabsf(v));
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 pr = __floats2bfloat162_rn(t[2 * i], t[2 * i + 1]);
+        hw[i] = *reinterpret_cast<uint32_t*>(&pr);
+        const float2 f = __bfloat1622float2(pr);
+        xhv[2 * i] = f.x;
+        xhv[2 * i + 1] = f.y;
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
       }
+      *reinterpret_cast<uint4*>(xh + qrow * kLD + cc) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
 #pragma unroll
-      for (int i = 0; i < EPT; i += 2) {
-        __nv_bfloat162 pr;
-        pr.x = __float2bfloat16_rn(xhv[i]);
-        pr.y = __float2bfloat16_rn(xhv[i + 1]);
-        *reinterpret_cast<__nv_bfloat162*>(xh + qrow * LD + qcol + i) = pr;
-      }
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+      for (int o = 1; o < G / 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float scale = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(fmaxf(amax, eps), 7.0f)));
-      uint32_t nib[EPT / 8];
-      uint32_t e4[EPT / 4];
+      const float rs = __frcp_rn(scale);
+      // rint and the offset-binary code in one add: for |t| < 2^22, t + 1.5*2^23 + 8
+      // rounds t to the nearest integer (ties to even) and its low mantissa bits
+      // hold rint(t) + 8.  |x_hat / scale| <= 7 * (1 + 2^-8), so rint(t) is in
+      // [-7, 7] and the reference's clamp to [-8, 7] never binds.
+      constexpr float kMagic = 12582920.0f;  // 1.5 * 2^23 + 8
+      float tq[8], qv[8];
+      uint32_t u[8];
+      slow = false;
 #pragma unroll
-      for (int i = 0; i < EPT / 8; ++i) nib[i] = 0;
-#pragma unroll
-      for (int i = 0; i < EPT; i += 2) {
-        float q0 = fminf(fmaxf(rintf(__fdiv_rn(xhv[i], scale)), -8.f), 7.f);
-        float q1 = fminf(fmaxf(rintf(__fdiv_rn(xhv[i + 1], scale)), -8.f), 7.f);
-        const uint32_t u0 = (uint32_t)((int)q0 + 8), u1 = (uint32_t)((int)q1 + 8);
-        nib[i / 8] |= (u0 | (u1 << 4)) << ((i % 8) * 4);
-        const __nv_fp8x2_storage_t f8 =
-            __nv_cvt_float2_to_fp8x2(make_float2(q0, q1), __NV_SATFINITE, __NV_E4M3);
-        if ((i % 4) == 0) e4[i / 4] = (uint32_t)f8;
-        else e4[i / 4] |= (uint32_t)f8 << 16;
+      for (int i = 0; i < 8; ++i) {
+        tq[i] = xhv[i] * rs;
+        const float m = tq[i] + kMagic;
+        qv[i] = m - kMagic;  // rint(tq), exact
+        u[i] = __float_as_uint(m);
+        slow |= near_half_integer(tq[i], qv[i]);
       }
-      if (grow < p.M) {
-        const int kc = k0 + qcol;
-        if (p.packed) {
-          uint8_t* dst = p.packed + (int64_t)grow * (p.K_pad / 2) + kc / 2;
-          if constexpr (EPT == 8) *reinterpret_cast<uint32_t*>(dst) = nib[0];
-          else *reinterpret_cast<uint2*>(dst) = make_uint2(nib[0], nib[1]);
+      if (slow) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (near_half_integer(tq[i], qv[i])) {
+            const float m = __fdiv_rn(xhv[i], scale) + kMagic;
+            qv[i] = m - kMagic;
+            u[i] = __float_as_uint(m);
+          }
         }
-        if (p.codes) {
-          uint8_t* dst = p.codes + (int64_t)grow * p.K_pad + kc;
-          if constexpr (EPT == 8) *reinterpret_cast<uint2*>(dst) = make_uint2(e4[0], e4[1]);
-          else *reinterpret_cast<uint4*>(dst) = make_uint4(e4[0], e4[1], e4[2], e4[3]);
-        }
-        if ((tid % 8) == 0) {
-          if (p.scales) p.scales[(int64_t)grow * (p.K_pad / G) + c] = __float2bfloat16_rn(scale);
+      }
+      uint32_t nib = 0, e4[2];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        nib |= ((u[i] & 0xFu) | ((u[i + 1] & 0xFu) << 4)) << (i * 4);
+        const uint32_t f8 =
+            (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(qv[i], qv[i + 1]), __NV_SATFINITE, __NV_E4M3);
+        if ((i % 4) == 0) e4[i / 4] = f8;
+        else e4[i / 4] |= f8 << 16;
+      }
+      if (col0 < p.K_pad && grow < p.M) {
+        if (p.packed) *reinterpret_cast<uint32_t*>(p.packed + (int64_t)grow * (p.K_pad / 2) + col0 / 2) = nib;
+        if (p.codes) *reinterpret_cast<uint2*>(p.codes + (int64_t)grow * p.K_pad + col0) = make_uint2(e4[0], e4[1]);
+        if ((tid % (G / 8)) == 0) {
+          if (p.scales) p.scales[(int64_t)grow * (p.K_pad / G) + col0 / G] = __float2bfloat16_rn(scale);
           if (p.scales_t) {
 #pragma unroll
             for (int h = 0; h < G / 64; ++h)
-              p.scales_t[(int64_t)(k0 / 64 + h) * p.ld_ast + grow] = scale;
+              p.scales_t[(int64_t)(col0 / 64 + h) * p.ld_ast + grow] = scale;
           }
         }
       }
@@ -227,24 +260,23 @@ __global__ void __launch_bounds__(kThreads) act_quant_kernel(const ActQuantParam
     __syncthreads();  // x_hat tile complete
 
     // ---- low-rank down-projection on tensor cores ----
-    if (n_tiles > 0) {
-      const __nv_bfloat16* wst = ws + st * r_tot * LD;
-      const __nv_bfloat16* xst = xs + st * kBM * LD;
-#pragma unroll
-      for (int kk = 0; kk < G / 16; ++kk) {
-        // A fragments: rows (lane % 16), column block (lane / 16) * 8
+    if (tset < n_tiles) {
+      const __nv_bfloat16* wst = ws + st * r_tot * kLD;
+      const __nv_bfloat16* xst = xs + (st * kBM + mt * 16) * kLD;
+      const __nv_bfloat16* xht = xh + (mt * 16) * kLD;
+#pragma unroll 2
+      for (int kk = 0; kk < kChunk / 16; ++kk) {
         const int ar = lane % 16, ac = kk * 16 + (lane / 16) * 8;
         uint32_t a_hat[4], a_raw[4];
-        ldmatrix_x4(smem_u32(xh + ar * LD + ac), a_hat[0], a_hat[1], a_hat[2], a_hat[3]);
-        if (p.lora_rank > 0)
-          ldmatrix_x4(smem_u32(xst + ar * LD + ac), a_raw[0], a_raw[1], a_raw[2], a_raw[3]);
+        ldmatrix_x4(smem_u32(xht + ar * kLD + ac), a_hat);
+        if (p.lora_rank > 0) ldmatrix_x4(smem_u32(xst + ar * kLD + ac), a_raw);
 #pragma unroll
-        for (int j = 0; j < kMaxTilesPerWarp; ++j) {
-          const int t = warp + 4 * j;
+        for (int j = 0; j < kTilesPerWarp; ++j) {
+          const int t = tset + 8 * j;
           if (t < n_tiles) {
             const int br = t * 8 + (lane % 8), bc = kk * 16 + ((lane / 8) % 2) * 8;
             uint32_t b0, b1;
-            ldmatrix_x2(smem_u32(wst + br * LD + bc), b0, b1);
+            ldmatrix_x2(smem_u32(wst + br * kLD + bc), b0, b1);
             if (t * 8 < p.rank) mma_bf16_16816(acc[j], a_hat, b0, b1);
             else mma_bf16_16816(acc[j], a_raw, b0, b1);
           }
@@ -258,13 +290,13 @@ __global__ void __launch_bounds__(kThreads) act_quant_kernel(const ActQuantParam
   if (p.mid_hl) {
     const int g = lane / 4, t4 = lane % 4;
 #pragma unroll
-    for (int j = 0; j < kMaxTilesPerWarp; ++j) {
-      const int t = warp + 4 * j;
+    for (int j = 0; j < kTilesPerWarp; ++j) {
+      const int t = tset + 8 * j;
       if (t < n_tiles) {
         const int col = t * 8 + 2 * t4;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int row = m0 + g + 8 * h;
+          const int row = m0 + mt * 16 + g + 8 * h;
           float v0 = acc[j][2 * h], v1 = acc[j][2 * h + 1];
           if (col >= p.rank) {
             v0 *= p.lora_col_scale[col - p.rank];
@@ -283,13 +315,40 @@ __global__ void __launch_bounds__(kThreads) act_quant_kernel(const ActQuantParam
         }
       }
     }
-    // zero the padding columns [2 r_tot, R2)
     const int pad = p.R2 - 2 * r_tot;
     for (int i = tid; i < kBM * pad; i += kThreads) {
       const int r = i / pad, cidx = 2 * r_tot + i % pad;
       if (m0 + r < p.M) p.mid_hl[(int64_t)(m0 + r) * p.R2 + cidx] = __float2bfloat16_rn(0.f);
     }
   }
+}
+
+constexpr size_t kSmemBudget = 220 * 1024;
+
+size_t smem_bytes(int stages, int r_tot, int k_pad) {
+  const size_t n_chunks = (size_t)((k_pad + kChunk - 1) / kChunk);
+  return sizeof(float) * n_chunks * kChunk +
+         sizeof(__nv_bfloat16) * (size_t)(stages * kBM * kLD + stages * r_tot * kLD + kBM * kLD);
+}
+
+template <int G, int STAGES>
+int launch(const ActQuantParams& prm, int r_tot, cudaStream_t stream) {
+  const size_t smem = smem_bytes(STAGES, r_tot, prm.K_pad);
+  auto kern = act_quant_kernel<G, STAGES>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return check_cuda(e, "svdq_act_quant: shared memory attribute");
+  const int grid = (prm.M + kBM - 1) / kBM;
+  kern<<<grid, kThreads, smem, stream>>>(prm);
+  return check_launch("svdq_act_quant launch");
+}
+
+template <int G>
+int launch_g(const ActQuantParams& prm, int r_tot, cudaStream_t stream) {
+  // deepest ring that fits in the shared-memory budget
+  if (smem_bytes(4, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 4>(prm, r_tot, stream);
+  if (smem_bytes(3, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 3>(prm, r_tot, stream);
+  if (smem_bytes(2, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 2>(prm, r_tot, stream);
+  return set_error(SVDQ_ERR_UNSUPPORTED, "svdq_act_quant: K_pad / rank too large for shared memory");
 }
 
 }  // namespace
@@ -324,8 +383,8 @@ extern "C" int svdq_act_quant(const void* x, int64_t ldx, const void* smooth, co
                    (!l2 || (reinterpret_cast<uintptr_t>(l2) & 15u) == 0) &&
                    (!lora_down || (reinterpret_cast<uintptr_t>(lora_down) & 15u) == 0),
                "svdq_act_quant: x, smooth, l2, lora_down must be 16-byte aligned");
-  SVDQ_REQUIRE((!out_codes || (reinterpret_cast<uintptr_t>(out_codes) & 15u) == 0) &&
-                   (!out_packed || (reinterpret_cast<uintptr_t>(out_packed) & 7u) == 0),
+  SVDQ_REQUIRE((!out_codes || (reinterpret_cast<uintptr_t>(out_codes) & 7u) == 0) &&
+                   (!out_packed || (reinterpret_cast<uintptr_t>(out_packed) & 3u) == 0),
                "svdq_act_quant: output code buffers are misaligned");
   if (M == 0) return SVDQ_OK;
 
@@ -348,20 +407,5 @@ extern "C" int svdq_act_quant(const void* x, int64_t ldx, const void* smooth, co
   p.ld_ast = ld_ast;
   p.mid_hl = r_tot > 0 ? static_cast<__nv_bfloat16*>(out_mid_hl) : nullptr;
   p.R2 = R2;
-
-  const int grid = (M + kBM - 1) / kBM;
-  if (a_group == 64) {
-    constexpr int LD = Smem<64>::LD;
-    const size_t smem = sizeof(__nv_bfloat16) *
-                        (size_t)(kStages * kBM * LD + kStages * r_tot * LD + kStages * 64 + kBM * LD);
-    cudaFuncSetAttribute(act_quant_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    act_quant_kernel<64><<<grid, kThreads, smem, stream>>>(p);
-  } else {
-    constexpr int LD = Smem<128>::LD;
-    const size_t smem = sizeof(__nv_bfloat16) *
-                        (size_t)(kStages * kBM * LD + kStages * r_tot * LD + kStages * 128 + kBM * LD);
-    cudaFuncSetAttribute(act_quant_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    act_quant_kernel<128><<<grid, kThreads, smem, stream>>>(p);
-  }
-  return check_launch("svdq_act_quant launch");
+  return a_group == 64 ? launch_g<64>(p, r_tot, stream) : launch_g<128>(p, r_tot, stream);
 }

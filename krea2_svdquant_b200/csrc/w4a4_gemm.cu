@@ -14,8 +14,9 @@
 //               mid_hl x up_hl into a buffer of its own.
 //   warps 4-11  rescale + epilogue: two warpgroups, each owning 128 of the
 //               256 columns of the 128 TMEM lanes.  They drain a buffer with
-//               tcgen05.ld, free it for the next group, and fold it into fp32
-//               register accumulators: acc += P_g * (sa * sw).  After the last
+//               tcgen05.ld (16x256b shape, double-buffered), free it for the
+//               next group, and fold it into fp32 register accumulators with
+//               packed f32x2 math: acc += P_g * (sa * sw).  After the last
 //               group: + bias, cast, store.
 // Every wait is bounded; a wait that runs out sets a CTA abort flag and the
 // library's device error word, and all roles leave their loops.
@@ -36,6 +37,14 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SA_BYTES + SW_BYTES;  // 51 KiB,
 constexpr int NUM_THREADS = 384;
 constexpr int TMEM_COLS = 512;  // two 256-column fp32 accumulators
 constexpr int EPI_COLS = 128;   // columns per rescale warpgroup
+// Register split: 384 threads launch with 168 registers each (64512); the
+// producer/MMA warpgroup drops to 40 and the two rescale warpgroups rise to 232
+// (128*40 + 256*232 = 64512).  The host refuses to launch if the compiled
+// kernel's register count differs, since the split would then not balance.
+constexpr int LAUNCH_REGS = 168;
+constexpr int REGS_CTRL = 40;
+constexpr int REGS_EPI = 232;
+static_assert(128 * REGS_CTRL + 256 * REGS_EPI == NUM_THREADS * LAUNCH_REGS, "register split");
 
 static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1 KiB alignment for 128B swizzle");
 
@@ -76,23 +85,6 @@ __device__ __forceinline__ void advance(int& stage, uint32_t& phase, int n) {
   if (++stage == n) {
     stage = 0;
     phase ^= 1u;
-  }
-}
-
-template <bool OUT_F32>
-__device__ __forceinline__ void store8(void* out, int64_t off, const float* v) {
-  if constexpr (OUT_F32) {
-    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + off);
-    o[0] = make_float4(v[0], v[1], v[2], v[3]);
-    o[1] = make_float4(v[4], v[5], v[6], v[7]);
-  } else {
-    uint32_t w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-      w[i] = *reinterpret_cast<uint32_t*>(&h);
-    }
-    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + off) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -152,115 +144,123 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t filled_mask = 0, fill_parity = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
-        const int m0 = (t % args.num_m_blocks) * BM;
-        const int n0 = (t / args.num_m_blocks) * BN;
-        for (int j = 0; ok && j < args.n_lr; ++j) {
-          if (!(ok = mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.err, kWaitProdEmpty))) break;
-          mbar_arrive_expect_tx(full_bar(stage), A_BYTES + B_BYTES);
-          tma_load_2d(stage_a(stage), &tm_mid, full_bar(stage), j * 64, m0);
-          tma_load_2d(stage_b(stage), &tm_up, full_bar(stage), j * 64, n0);
-          filled_mask |= 1u << stage;
-          fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
-          advance(stage, phase, STAGES);
-        }
-        for (int s = 0; ok && s < n_ks; ++s) {
-          if (!(ok = mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.err, kWaitProdEmpty))) break;
-          mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES);
-          tma_load_2d(stage_a(stage), &tm_a, full_bar(stage), s * KB, m0);
-          tma_load_2d(stage_b(stage), &tm_b, full_bar(stage), s * KB, n0);
-          tma_load_2d(stage_b(stage) + B_BYTES, &tm_sa, full_bar(stage), m0, 2 * s);
-          tma_load_2d(stage_b(stage) + B_BYTES + SA_BYTES, &tm_sw, full_bar(stage), n0, 2 * s);
-          filled_mask |= 1u << stage;
-          fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
-          advance(stage, phase, STAGES);
-        }
-      }
-      if (!ok) {
-        // let copies already in flight land before the CTA exits
-        for (int s = 0; s < STAGES; ++s)
-          if (filled_mask & (1u << s)) mbar_wait_drain(full_bar(s), (fill_parity >> s) & 1u, 100000000ull);
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc_bf16 = make_idesc(kFmtBF16, kFmtBF16, BM, BN);
-      const uint32_t idesc_e4m3 = make_idesc(kFmtE4M3, kFmtE4M3, BM, BN);
-      int stage = 0;
-      uint32_t phase = 0;
-      int tb = 0;
-      uint32_t tphase = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
-        if (args.n_lr > 0) {
-          if (!(ok = mbar_wait(smem_u32(&bars->tmem_empty[tb]), tphase ^ 1u, abort_flag, args.err,
-                               kWaitMmaTmemEmpty)))
-            break;
-          tc_fence_after();
-          const uint32_t d = tmem_base + (uint32_t)(tb * BN);
+  if (warp < 4) {
+    setmaxnreg_dec<REGS_CTRL>();
+    if (warp == 0) {
+      // ------------------------------------------------------------ producer
+      if (lane == 0) {
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t filled_mask = 0, fill_parity = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+          const int m0 = (t % args.num_m_blocks) * BM;
+          const int n0 = (t / args.num_m_blocks) * BN;
           for (int j = 0; ok && j < args.n_lr; ++j) {
-            if (!(ok = mbar_wait(full_bar(stage), phase, abort_flag, args.err, kWaitMmaFull))) break;
-            tc_fence_after();
-            const uint64_t da = desc_k_sw128(stage_a(stage));
-            const uint64_t db = desc_k_sw128(stage_b(stage));
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)  // 4 x K=16 bf16 = 128 bytes
-              umma_f16(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc_bf16,
-                       (j > 0 || kk > 0) ? 1u : 0u);
-            umma_commit(empty_bar(stage));
+            if (!(ok = mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.err, kWaitProdEmpty))) break;
+            mbar_arrive_expect_tx(full_bar(stage), A_BYTES + B_BYTES);
+            tma_load_2d(stage_a(stage), &tm_mid, full_bar(stage), j * 64, m0);
+            tma_load_2d(stage_b(stage), &tm_up, full_bar(stage), j * 64, n0);
+            filled_mask |= 1u << stage;
+            fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
             advance(stage, phase, STAGES);
           }
-          if (!ok) break;
-          umma_commit(smem_u32(&bars->tmem_full[tb]));
-          advance(tb, tphase, 2);
+          for (int s = 0; ok && s < n_ks; ++s) {
+            if (!(ok = mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, args.err, kWaitProdEmpty))) break;
+            mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES);
+            tma_load_2d(stage_a(stage), &tm_a, full_bar(stage), s * KB, m0);
+            tma_load_2d(stage_b(stage), &tm_b, full_bar(stage), s * KB, n0);
+            tma_load_2d(stage_b(stage) + B_BYTES, &tm_sa, full_bar(stage), m0, 2 * s);
+            tma_load_2d(stage_b(stage) + B_BYTES + SA_BYTES, &tm_sw, full_bar(stage), n0, 2 * s);
+            filled_mask |= 1u << stage;
+            fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
+            advance(stage, phase, STAGES);
+          }
         }
-        for (int s = 0; ok && s < n_ks; ++s) {
-          if (!(ok = mbar_wait(full_bar(stage), phase, abort_flag, args.err, kWaitMmaFull))) break;
-          tc_fence_after();
-          const uint64_t da = desc_k_sw128(stage_a(stage));
-          const uint64_t db = desc_k_sw128(stage_b(stage));
-          const int ngs = min(2, args.n_groups - 2 * s);
-          for (int h = 0; h < ngs; ++h) {
+        if (!ok) {
+          // let copies already in flight land before the CTA exits
+          for (int s = 0; s < STAGES; ++s)
+            if (filled_mask & (1u << s)) mbar_wait_drain(full_bar(s), (fill_parity >> s) & 1u, 100000000ull);
+        }
+      }
+    } else if (warp == 1) {
+      // ------------------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        const uint32_t idesc_bf16 = make_idesc(kFmtBF16, kFmtBF16, BM, BN);
+        const uint32_t idesc_e4m3 = make_idesc(kFmtE4M3, kFmtE4M3, BM, BN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int tb = 0;
+        uint32_t tphase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+          if (args.n_lr > 0) {
             if (!(ok = mbar_wait(smem_u32(&bars->tmem_empty[tb]), tphase ^ 1u, abort_flag, args.err,
                                  kWaitMmaTmemEmpty)))
               break;
             tc_fence_after();
             const uint32_t d = tmem_base + (uint32_t)(tb * BN);
-#pragma unroll
-            for (int kk = 0; kk < 2; ++kk) {  // 2 x K=32 e4m3 = one 64-group
-              const uint64_t off = (uint64_t)((h * 64 + kk * 32) >> 4);
-              umma_f8f6f4(d, da + off, db + off, idesc_e4m3, kk > 0 ? 1u : 0u);
+            for (int j = 0; ok && j < args.n_lr; ++j) {
+              if (!(ok = mbar_wait(full_bar(stage), phase, abort_flag, args.err, kWaitMmaFull))) break;
+              tc_fence_after();
+              const uint64_t da = desc_k_sw128(stage_a(stage));
+              const uint64_t db = desc_k_sw128(stage_b(stage));
+  #pragma unroll
+              for (int kk = 0; kk < 4; ++kk)  // 4 x K=16 bf16 = 128 bytes
+                umma_f16(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc_bf16,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+              umma_commit(empty_bar(stage));
+              advance(stage, phase, STAGES);
             }
+            if (!ok) break;
             umma_commit(smem_u32(&bars->tmem_full[tb]));
             advance(tb, tphase, 2);
           }
-          if (!ok) break;
-          umma_commit(empty_bar(stage));
-          advance(stage, phase, STAGES);
+          for (int s = 0; ok && s < n_ks; ++s) {
+            if (!(ok = mbar_wait(full_bar(stage), phase, abort_flag, args.err, kWaitMmaFull))) break;
+            tc_fence_after();
+            const uint64_t da = desc_k_sw128(stage_a(stage));
+            const uint64_t db = desc_k_sw128(stage_b(stage));
+            const int ngs = min(2, args.n_groups - 2 * s);
+            for (int h = 0; h < ngs; ++h) {
+              if (!(ok = mbar_wait(smem_u32(&bars->tmem_empty[tb]), tphase ^ 1u, abort_flag, args.err,
+                                   kWaitMmaTmemEmpty)))
+                break;
+              tc_fence_after();
+              const uint32_t d = tmem_base + (uint32_t)(tb * BN);
+  #pragma unroll
+              for (int kk = 0; kk < 2; ++kk) {  // 2 x K=32 e4m3 = one 64-group
+                const uint64_t off = (uint64_t)((h * 64 + kk * 32) >> 4);
+                umma_f8f6f4(d, da + off, db + off, idesc_e4m3, kk > 0 ? 1u : 0u);
+              }
+              umma_commit(smem_u32(&bars->tmem_full[tb]));
+              advance(tb, tphase, 2);
+            }
+            if (!ok) break;
+            umma_commit(empty_bar(stage));
+            advance(stage, phase, STAGES);
+          }
+        }
+        // all issued MMAs must finish before TMEM is released
+        umma_commit(smem_u32(&bars->mma_done));
+        if (!mbar_wait_drain(smem_u32(&bars->mma_done), 0, 1000000000ull)) {
+          *abort_flag = 1;
+          atomicCAS(args.err, 0, kWaitMmaDone);
         }
       }
-      // all issued MMAs must finish before TMEM is released
-      umma_commit(smem_u32(&bars->mma_done));
-      if (!mbar_wait_drain(smem_u32(&bars->mma_done), 0, 1000000000ull)) {
-        *abort_flag = 1;
-        atomicCAS(args.err, 0, kWaitMmaDone);
-      }
     }
-  } else if (warp >= 4) {
+  } else {
+    setmaxnreg_inc<REGS_EPI>();
     // ------------------------------------------------------------ rescale + epilogue
+    // TMEM is drained with the 16x256b shape: thread i of a warp owns rows
+    // {r0, r0+8, r0+16, r0+24} (r0 = 32q + i/4) and column pairs
+    // {8j + 2(i%4), +1 : j = 0..15} of its warpgroup's 128 columns, so per group
+    // it needs 4 activation scales and 16 weight-scale pairs.
     const int ew = warp - 4;
-    const int q = warp & 3;               // TMEM lane quarter this warp may access
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int col0 = (ew >> 2) * EPI_COLS;  // warpgroup's column half
-    const int row = q * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const int r0 = q * 32 + (lane >> 2);
+    const int cpair = 2 * (lane & 3);
     int stage = 0;
     uint32_t phase = 0;
     int tb = 0;
@@ -269,19 +269,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
       const int m0 = (t % args.num_m_blocks) * BM;
       const int n0 = (t / args.num_m_blocks) * BN;
-      float acc[EPI_COLS];
+      uint64_t acc[4][16];  // [row r0 + 8*k][column pair j]
       if (args.n_lr > 0) {
         if (!(ok = mbar_wait(smem_u32(&bars->tmem_full[tb]), tphase, abort_flag, args.err, kWaitEpiTmemFull)))
           break;
         tc_fence_after();
-        const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + col0);
 #pragma unroll
-        for (int c = 0; c < EPI_COLS / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld16(taddr + (uint32_t)(c * 16), r);
-          tmem_ld_wait();
+        for (int lh = 0; lh < 2; ++lh) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[c * 16 + i] = __uint_as_float(r[i]);
+          for (int cb = 0; cb < 2; ++cb) {
+            uint32_t r[32];
+            tmem_ld_16x256b_x8(tmem_base + ((uint32_t)(q * 32 + lh * 16) << 16) + (uint32_t)(tb * BN + col0 + cb * 64), r);
+            tmem_ld_wait_regs(r);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              acc[2 * lh][cb * 8 + j] = ((uint64_t)r[4 * j + 1] << 32) | r[4 * j];
+              acc[2 * lh + 1][cb * 8 + j] = ((uint64_t)r[4 * j + 3] << 32) | r[4 * j + 2];
+            }
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -293,7 +298,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < EPI_COLS; ++i) acc[i] = 0.f;
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[k][j] = 0ull;
       }
       for (int s = 0; ok && s < n_ks; ++s) {
         if (!(ok = mbar_wait(full_bar(stage), phase, abort_flag, args.err, kWaitEpiFull))) break;
@@ -304,26 +311,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!(ok = mbar_wait(smem_u32(&bars->tmem_full[tb]), tphase, abort_flag, args.err, kWaitEpiTmemFull)))
             break;
           tc_fence_after();
-          const float sa = sa_s[h * BM + row];
-          const float* swr = sw_s + h * BN + col0;
-          const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + col0);
+          const float* sar = sa_s + h * BM + r0;
+          uint64_t sa2[4];
 #pragma unroll
-          for (int c = 0; c < EPI_COLS / 16; ++c) {
-            uint32_t r[16];
-            tmem_ld16(taddr + (uint32_t)(c * 16), r);
-            tmem_ld_wait();
-            if (c == EPI_COLS / 16 - 1) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(smem_u32(&bars->tmem_empty[tb]));
+          for (int k = 0; k < 4; ++k) {
+            const float v = sar[8 * k];
+            sa2[k] = f2_pack(v, v);
+          }
+          const float* swr = sw_s + h * BN + col0 + cpair;
+          const uint32_t tcol = tmem_base + (uint32_t)(tb * BN + col0);
+          // chunks: (cb, lh) = (0,0) (0,1) (1,0) (1,1); each 16 lanes x 64 columns.
+          uint32_t pa[32], pb[32];
+          tmem_ld_16x256b_x8(tcol + ((uint32_t)(q * 32) << 16), pa);
+          tmem_ld_wait_regs(pa);
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            const int cb = ch >> 1, lh = ch & 1;
+            uint32_t (&cur)[32] = (ch & 1) ? pb : pa;
+            uint32_t (&nxt)[32] = (ch & 1) ? pa : pb;
+            if (ch + 1 < 4) {
+              const int ncb = (ch + 1) >> 1, nlh = (ch + 1) & 1;
+              tmem_ld_16x256b_x8(tcol + ((uint32_t)(q * 32 + nlh * 16) << 16) + (uint32_t)(ncb * 64), nxt);
             }
 #pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-              const float4 w = *reinterpret_cast<const float4*>(swr + c * 16 + i);
-              acc[c * 16 + i + 0] = fmaf(__uint_as_float(r[i + 0]), sa * w.x, acc[c * 16 + i + 0]);
-              acc[c * 16 + i + 1] = fmaf(__uint_as_float(r[i + 1]), sa * w.y, acc[c * 16 + i + 1]);
-              acc[c * 16 + i + 2] = fmaf(__uint_as_float(r[i + 2]), sa * w.z, acc[c * 16 + i + 2]);
-              acc[c * 16 + i + 3] = fmaf(__uint_as_float(r[i + 3]), sa * w.w, acc[c * 16 + i + 3]);
+            for (int j = 0; j < 8; ++j) {
+              const uint64_t w2 = *reinterpret_cast<const uint64_t*>(swr + (cb * 8 + j) * 8);
+              const uint64_t s_lo = f2_mul(w2, sa2[2 * lh]);
+              const uint64_t s_hi = f2_mul(w2, sa2[2 * lh + 1]);
+              const uint64_t p_lo = ((uint64_t)cur[4 * j + 1] << 32) | cur[4 * j];
+              const uint64_t p_hi = ((uint64_t)cur[4 * j + 3] << 32) | cur[4 * j + 2];
+              acc[2 * lh][cb * 8 + j] = f2_fma(p_lo, s_lo, acc[2 * lh][cb * 8 + j]);
+              acc[2 * lh + 1][cb * 8 + j] = f2_fma(p_hi, s_hi, acc[2 * lh + 1][cb * 8 + j]);
+            }
+            if (ch + 1 < 4) {
+              tmem_ld_wait_regs(nxt);
+              if (ch + 2 == 4) {
+                // last chunk is in registers: release the TMEM buffer to the MMA warp
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&bars->tmem_empty[tb]));
+              }
             }
           }
           advance(tb, tphase, 2);
@@ -334,28 +361,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         advance(stage, phase, STAGES);
       }
       if (!ok) break;
-      // epilogue: + bias, cast, store
-      const int grow = m0 + row;
-      if (grow < args.M) {
-        const int64_t rbase = (int64_t)grow * args.ldo;
+      // epilogue: + bias, cast, store (4 rows x 16 column pairs per thread)
+      float2 bias2[16];
 #pragma unroll
-        for (int j = 0; j < EPI_COLS; j += 8) {
-          const int n = n0 + col0 + j;
-          if (n < args.N) {
-            float v[8];
+      for (int j = 0; j < 16; ++j) {
+        const int n = n0 + col0 + 8 * j + cpair;
+        bias2[j] = (args.bias && n < args.N)
+                       ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(args.bias + n))
+                       : make_float2(0.f, 0.f);
+      }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = acc[j + i];
-            if (args.bias) {
-              const uint4 braw = *reinterpret_cast<const uint4*>(args.bias + n);
-              const __nv_bfloat162* bb = reinterpret_cast<const __nv_bfloat162*>(&braw);
+      for (int k = 0; k < 4; ++k) {
+        const int grow = m0 + r0 + 8 * k;
+        if (grow < args.M) {
+          const int64_t rbase = (int64_t)grow * args.ldo;
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float2 f = __bfloat1622float2(bb[i]);
-                v[2 * i] += f.x;
-                v[2 * i + 1] += f.y;
+          for (int j = 0; j < 16; ++j) {
+            const int n = n0 + col0 + 8 * j + cpair;
+            if (n < args.N) {
+              const float v0 = f2_lo(acc[k][j]) + bias2[j].x;
+              const float v1 = f2_hi(acc[k][j]) + bias2[j].y;
+              if constexpr (OUT_F32) {
+                *reinterpret_cast<float2*>(static_cast<float*>(args.out) + rbase + n) = make_float2(v0, v1);
+              } else {
+                *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(args.out) + rbase + n) =
+                    __floats2bfloat162_rn(v0, v1);
               }
             }
-            store8<OUT_F32>(args.out, rbase + n, v);
           }
         }
       }
@@ -431,6 +463,16 @@ extern "C" int svdq_w4a4_gemm(const void* act_codes, const float* act_scales_t, 
   a.num_m_blocks = (M + BM - 1) / BM;
   a.num_n_blocks = (N + BN - 1) / BN;
   a.err = err;
+  {
+    cudaFuncAttributes fa;
+    cudaError_t e = out_dtype == SVDQ_FP32 ? cudaFuncGetAttributes(&fa, w4a4_gemm_kernel<true>)
+                                           : cudaFuncGetAttributes(&fa, w4a4_gemm_kernel<false>);
+    if (e != cudaSuccess) return check_cuda(e, "svdq_w4a4_gemm: kernel attributes");
+    if (fa.numRegs != LAUNCH_REGS)
+      return set_error(SVDQ_ERR_UNSUPPORTED, "svdq_w4a4_gemm: kernel compiled with " + std::to_string(fa.numRegs) +
+                                                 " registers/thread; the warp-group register split needs " +
+                                                 std::to_string(LAUNCH_REGS));
+  }
   const int tiles = a.num_m_blocks * a.num_n_blocks;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   if (out_dtype == SVDQ_FP32) {
