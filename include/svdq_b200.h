@@ -5,26 +5,31 @@
  * point is asynchronous on the given stream unless stated otherwise and
  * returns an int status (SVDQ_OK on success).  Device pointers are borrowed
  * for the duration of the call only.  A failing call never falls back to
- * another implementation: it returns an error status, and
- * svdq_last_error() gives a one-line reason for the calling host thread.
+ * another implementation: it returns an error status, and svdq_last_error()
+ * gives a one-line reason for the calling host thread.
  *
- * Data layouts (row-major unless stated; "K_pad" is the checkpoint's padded
- * input width, 2 * qweight.shape[1]; "G64" = K_pad / 64):
- *   x            [M, K_in]    bf16, row stride ldx elements
- *   smooth       [K_in]       bf16
- *   l2           [rank, K_in] bf16
+ * The linear forward is two launches:
+ *   activation pass  svdq_act_quant (W4A4) or svdq_w4a16_prep (W4A16)
+ *   GEMM             svdq_linear_gemm
+ * on operands prepared once per layer by svdq_repack_weight and
+ * svdq_build_up_hl.
+ *
+ * Data layouts (row-major unless stated; K_pad is the checkpoint's padded input
+ * width, 2 * qweight.shape[1]):
+ *   x            [M, K_in]        bf16, row stride ldx elements
+ *   smooth       [K_in]           bf16
+ *   l2           [rank, K_in]     bf16
  *   lora_down    [lora_rank, K_in] bf16 (all adapters stacked)
- *   lora_col_scale [lora_rank] fp32 (adapter multiplier per stacked row)
- *   act packed   [M, K_pad/2] u8, nibble = q + 8, even k in the low nibble
+ *   lora_col_scale [lora_rank]    fp32 (adapter multiplier per stacked row)
+ *   act packed   [M, K_pad/2]     u8, nibble = q + 8, even k in the low nibble
  *   act scales   [M, K_pad/a_group] bf16
- *   act codes    [M, K_pad]   fp8 e4m3 holding the integer codes q exactly
- *   act scales^T [G64, ld_ast] fp32 (scale of the 64-group containing k)
- *   mid_hl       [M, R2]      bf16: [hi(r_tot) | lo(r_tot) | 0], r_tot = rank + lora_rank,
- *                             hi = bf16(mid), lo = bf16(mid - hi), R2 = round_up(2 r_tot, 64)
- *   up_hl        [N, R2]      bf16: [up(r_tot) | up(r_tot) | 0], up = [l1 | lora_up]
- *   w codes      [N, K_pad]   fp8 e4m3 holding the integer weight codes exactly
- *   w scales^T   [G64, N]     fp32
- *   out          [M, N]       bf16 or fp32, row stride ldo elements
+ *   a16          [M, K_pad]       fp16 GEMM operand: q * scale (W4A4, exact) or
+ *                                 x / smooth (W4A16)
+ *   mid_hl       [M, R2]          bf16: [hi(r_tot) | lo(r_tot) | 0], r_tot = rank + lora_rank,
+ *                                 hi = bf16(mid), lo = bf16(mid - hi), R2 = round_up(2 r_tot, 64)
+ *   up_hl        [N, R2]          bf16: [up(r_tot) | up(r_tot) | 0], up = [l1 | lora_up]
+ *   w16          [N, K_pad]       fp16 GEMM operand: q_w * weight scale
+ *   out          [M, N]           bf16 or fp32, row stride ldo elements
  */
 #ifndef SVDQ_B200_H
 #define SVDQ_B200_H
@@ -61,41 +66,47 @@ const char* svdq_version(void);
 int svdq_device_error(int* code, int clear);
 
 /*
- * Activation quantization pass of the W4A4 linear.
- * Replaces, on the device, the reference's
+ * Activation pass of the W4A4 linear.  Replaces, on the device, the reference's
  *   x_hat = x / smooth                                  (src/krea2_svdquant/quant/svd.py:122)
  *   quantize_symmetric_int4(x_hat, a_group) + pack_int4 (src/krea2_svdquant/quant/pack.py:6-56)
  *   F.linear(x_hat, l2)                                 (svd.py:159, low-rank down)
  *   F.linear(x, lora_down) * multiplier                 (src/krea2_svdquant/runtime/linear.py:38-45)
  * in one pass over x.  Codes, packing and scales are bit-exact with the
  * reference.  Optional outputs may be NULL: out_packed / out_scales (the
- * reference-format codes), out_codes / out_scales_t (the GEMM operands),
- * out_mid_hl (needs r_tot > 0).
- *   a_group in {64, 128}; K_in <= K_pad; K_pad % a_group == 0;
- *   rank % 8 == 0, lora_rank % 8 == 0, rank + lora_rank <= 256; ldx % 8 == 0;
- *   ld_ast % 4 == 0 and ld_ast >= M.
+ * reference-format codes), out_a16 (the GEMM operand), out_mid_hl (needs
+ * rank + lora_rank > 0).
+ *   a_group in {64, 128}; K_in <= K_pad; K_pad % a_group == 0; K_in % 8 == 0;
+ *   rank % 8 == 0, lora_rank % 8 == 0, rank + lora_rank <= 256; ldx % 8 == 0.
  */
 int svdq_act_quant(const void* x, int64_t ldx, const void* smooth,
                    const void* l2, int rank,
                    const void* lora_down, const float* lora_col_scale, int lora_rank,
                    int M, int K_in, int K_pad, int a_group,
-                   void* out_packed, void* out_scales,
-                   void* out_codes, float* out_scales_t, int ld_ast,
-                   void* out_mid_hl, int R2,
-                   cudaStream_t stream);
+                   void* out_packed, void* out_scales, void* out_a16,
+                   void* out_mid_hl, int R2, cudaStream_t stream);
 
 /*
- * Load-time weight preparation for the W4A4 GEMM: packed INT4 qweight
- * [N, K_pad/2] + group scales [N, K_pad/w_group] (bf16, fp16 or fp32 as the
- * checkpoint stores them) -> e4m3 codes [N, K_pad] + fp32 scales^T [G64, N].
- * Replaces the per-call unpack + dequantize of the reference
- * (src/krea2_svdquant/quant/svd.py:128-135, quant/pack.py:26-70); the
- * checkpoint layout it reads is the one load_svdquant_transformer reads
- * (src/krea2_svdquant/runtime/load.py:104-124).  w_group % 64 == 0.
+ * Activation pass of the W4A16 linear: a16 = fp16(fp32(x) / fp32(smooth)) and
+ * the low-rank/LoRA down-projection.  Replaces x / smooth and F.linear(x_hat, l2)
+ * of the reference's float run (svd.py:122, 159) and the smoothing done by
+ * kernels/triton/generic_int4.py:169-191.  Same constraints as svdq_act_quant.
+ */
+int svdq_w4a16_prep(const void* x, int64_t ldx, const void* smooth,
+                    const void* l2, int rank,
+                    const void* lora_down, const float* lora_col_scale, int lora_rank,
+                    int M, int K_in, int K_pad,
+                    void* out_a16, void* out_mid_hl, int R2, cudaStream_t stream);
+
+/*
+ * Load-time weight preparation: packed INT4 qweight [N, K_pad/2] + group scales
+ * [N, K_pad/w_group] (bf16, fp16 or fp32 as the checkpoint stores them) ->
+ * w16 [N, K_pad] fp16 = q * scale (exact for bf16 scales).  Replaces the
+ * per-call unpack + dequantize of the reference (src/krea2_svdquant/quant/svd.py:128-135,
+ * quant/pack.py:26-70); reads the layout load_svdquant_transformer reads
+ * (src/krea2_svdquant/runtime/load.py:104-124).
  */
 int svdq_repack_weight(const void* qweight, const void* scales, int scale_dtype,
-                       int N, int K_pad, int w_group,
-                       void* out_codes, float* out_scales_t, cudaStream_t stream);
+                       int N, int K_pad, int w_group, void* out_w16, cudaStream_t stream);
 
 /*
  * Build up_hl [N, R2] = [up | up | 0] from up = [l1 | lora_up] (bf16 inputs).
@@ -106,24 +117,22 @@ int svdq_build_up_hl(const void* l1, int rank, const void* lora_up, int lora_ran
                      int N, void* out_up_hl, int R2, cudaStream_t stream);
 
 /*
- * Fused W4A4 GEMM + low-rank/LoRA up-projection + bias:
- *   out[m, n] = sum_g sa[m,g] * sw[n,g] * sum_{k in g} qa[m,k] * qw[n,k]
- *             + sum_j mid_hl[m,j] * up_hl[n,j] + bias[n]
- * tcgen05 MMAs (e4m3 codes, exact fp32 per 64-group partials in TMEM), fp32
- * per-group rescale, bf16 low-rank MMA, bias and output cast in the epilogue.
- * Replaces F.linear(x_hat, w_res) + F.linear(mid, l1) + bias of
- * src/krea2_svdquant/quant/svd.py:158-162 in the W4A4 form of README.md:64
- * (the slot of kernels/gluon/blackwell_fused_svdquant.py:29-38).
+ * SVDQuant linear GEMM with the fused low-rank/LoRA up-projection and bias:
+ *   out[m, n] = sum_k a16[m,k] w16[n,k] + sum_j mid_hl[m,j] up_hl[n,j] + bias[n]
+ * tcgen05 MMAs on CTA pairs, fp32 accumulation in TMEM, bias and output cast
+ * in the epilogue.  Replaces F.linear(x_hat, w_res) + F.linear(mid, l1) + bias
+ * of src/krea2_svdquant/quant/svd.py:158-162 (W4A4 form: README.md:64; the
+ * slot of kernels/gluon/blackwell_fused_svdquant.py:29-38 and of the Triton
+ * kernels in kernels/triton/generic_int4.py:19-133).
  *   K_pad % 64 == 0, N % 8 == 0, ldo % 8 == 0, R2 % 64 == 0 (R2 may be 0),
- *   ld_ast % 4 == 0, out_dtype in {SVDQ_BF16, SVDQ_FP32}; bias may be NULL.
+ *   out_dtype in {SVDQ_BF16, SVDQ_FP32}; bias may be NULL (16-byte aligned).
  */
-int svdq_w4a4_gemm(const void* act_codes, const float* act_scales_t, int ld_ast,
-                   const void* w_codes, const float* w_scales_t,
-                   const void* mid_hl, const void* up_hl, int R2,
-                   const void* bias,
-                   void* out, int out_dtype, int64_t ldo,
-                   int M, int N, int K_pad,
-                   cudaStream_t stream);
+int svdq_linear_gemm(const void* a16, const void* w16,
+                     const void* mid_hl, const void* up_hl, int R2,
+                     const void* bias,
+                     void* out, int out_dtype, int64_t ldo,
+                     int M, int N, int K_pad,
+                     cudaStream_t stream);
 
 #ifdef __cplusplus
 }

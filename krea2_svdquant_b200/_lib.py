@@ -26,12 +26,13 @@ SIGNATURES = {
     "svdq_device_error": ([ctypes.POINTER(c_int), c_int], c_int),
     "svdq_act_quant": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
                         c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
-                        c_void_p, c_int, c_void_p], c_int),
-    "svdq_repack_weight": ([c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
-                            c_void_p], c_int),
+                        c_void_p], c_int),
+    "svdq_w4a16_prep": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                         c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p], c_int),
+    "svdq_repack_weight": ([c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p], c_int),
     "svdq_build_up_hl": ([c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p], c_int),
-    "svdq_w4a4_gemm": ([c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
-                        c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_void_p], c_int),
+    "svdq_linear_gemm": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                          c_int64, c_int, c_int, c_int, c_void_p], c_int),
 }
 
 SVDQ_BF16, SVDQ_FP16, SVDQ_FP32 = 0, 1, 2

@@ -1,17 +1,21 @@
-// Activation quantization pass of the W4A4 SVDQuant linear (sm_100a).
+// Activation pass of the SVDQuant linear (sm_100a).
 //
-// One pass over x [M, K_in] bf16 produces, per 32-row band and 128-column chunk:
+// W4A4 mode: one pass over x [M, K_in] bf16 produces, per 32-row band and
+// 128-column chunk:
 //   x_hat = bf16(x / smooth)                             (svd.py:122)
 //   q     = clamp(rint(x_hat / scale), -8, 7) per group  (pack.py:6-23)
 //   scale = bf16(max(amax, bf16(1e-8)) / 7)              (pack.py:20)
 //   packed nibbles (q + 8, even k low)                   (pack.py:47-56)
-//   e4m3 codes (exact integers) + fp32 scales^T for the GEMM
-//   mid = [x_hat @ l2^T | (x @ lora_down^T) * col_scale] (svd.py:159, linear.py:45)
-//         written as a bf16 hi/lo pair so the GEMM's bf16 MMA keeps ~16 mantissa bits.
+//   a16   = fp16(q * scale): the dequantized activation, exact in fp16
+//   mid   = [x_hat @ l2^T | (x @ lora_down^T) * col_scale] (svd.py:159, linear.py:45)
+//           written as a bf16 hi/lo pair so the GEMM's bf16 MMA keeps ~16 mantissa bits.
+// W4A16 mode: a16 = fp16(fp32(x) / fp32(smooth)) (the reference run in fp32,
+// svd.py:122 on float inputs) and mid from the fp16 x_hat against l2 converted
+// to fp16 (exact for bf16 values in fp16 range).
 // The down-projection runs on mma.sync tensor cores from shared memory; loads
 // are a cp.async ring of 128-column chunks.
 //
-// Divisions must round exactly like float32 IEEE division followed by the
+// W4A4 divisions must round exactly like float32 IEEE division followed by the
 // reference's rounding (bf16 for x_hat, rint for q).  Each quotient is first
 // formed as a product with the correctly rounded reciprocal; that product is
 // within 2 ulp of the correctly rounded quotient, so the final rounding can
@@ -60,6 +64,14 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 // Near-boundary tests for the reciprocal-product quotients (see file comment).
 // bf16 rounding of a float32 depends on its low 16 bits against 0x8000; a
 // product within 2.5 ulp of the exact quotient can only round differently when
@@ -84,14 +96,12 @@ struct ActQuantParams {
   int M, K_in, K_pad;
   uint8_t* packed;             // [M, K_pad/2]
   __nv_bfloat16* scales;       // [M, K_pad/G]
-  uint8_t* codes;              // [M, K_pad] e4m3
-  float* scales_t;             // [K_pad/64, ld_ast]
-  int ld_ast;
+  __half* a16;                 // [M, K_pad] fp16 GEMM operand
   __nv_bfloat16* mid_hl;       // [M, R2]
   int R2;
 };
 
-template <int G, int STAGES>
+template <int G, int STAGES, bool W4A16>
 __global__ void __launch_bounds__(kThreads) act_quant_kernel(const ActQuantParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int r_tot = p.rank + p.lora_rank;
@@ -166,94 +176,122 @@ __global__ void __launch_bounds__(kThreads) act_quant_kernel(const ActQuantParam
     cp_async_commit();
 
     const int col0 = c * kChunk + cc;
-    // ---- smoothing + group quantization (bit-exact with the reference) ----
-    {
+    if constexpr (W4A16) {
+      // ---- x_hat = fp16(fp32 division), and l2 rows of this chunk to fp16 ----
       const uint4 xv = *reinterpret_cast<const uint4*>(xs + (st * kBM + qrow) * kLD + cc);
-      const float4 r0 = *reinterpret_cast<const float4*>(rsm + col0);
-      const float4 r1 = *reinterpret_cast<const float4*>(rsm + col0 + 4);
-      const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
       const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
-      float xf[8], t[8];
-      bool slow = false;
+      uint32_t hw[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 f = __bfloat1622float2(x2[i]);
-        xf[2 * i] = f.x;
-        xf[2 * i + 1] = f.y;
+        const int col = col0 + 2 * i;
+        const float v0 = col < p.K_in ? __fdiv_rn(f.x, __bfloat162float(p.smooth[col])) : 0.f;
+        const float v1 = col + 1 < p.K_in ? __fdiv_rn(f.y, __bfloat162float(p.smooth[col + 1])) : 0.f;
+        __half2 h = __floats2half2_rn(v0, v1);
+        hw[i] = *reinterpret_cast<uint32_t*>(&h);
       }
+      const uint4 hv = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(xh + qrow * kLD + cc) = hv;
+      if (col0 < p.K_pad && grow < p.M && p.a16)
+        *reinterpret_cast<uint4*>(p.a16 + (int64_t)grow * p.K_pad + col0) = hv;
+      // the l2 rows are consumed by an fp16 MMA in this mode
+      for (int i = tid; i < p.rank * (kChunk / 8); i += kThreads) {
+        const int r = i / (kChunk / 8), sg = i % (kChunk / 8);
+        uint4* ptr = reinterpret_cast<uint4*>(ws + (st * r_tot + r) * kLD + sg * 8);
+        uint4 v = *ptr;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        t[i] = xf[i] * rv[i];
-        slow |= near_bf16_midpoint(t[i]);
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[e]));
+          __half2 h = __floats2half2_rn(f.x, f.y);
+          w[e] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        *ptr = v;
       }
-      if (slow) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (near_bf16_midpoint(t[i]) && col0 + i < p.K_in)
-            t[i] = __fdiv_rn(xf[i], __bfloat162float(p.smooth[col0 + i]));
-      }
-      uint32_t hw[4];
-      float xhv[8];
-      float amax = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        __nv_bfloat162 pr = __floats2bfloat162_rn(t[2 * i], t[2 * i + 1]);
-        hw[i] = *reinterpret_cast<uint32_t*>(&pr);
-        const float2 f = __bfloat1622float2(pr);
-        xhv[2 * i] = f.x;
-        xhv[2 * i + 1] = f.y;
-        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
-      }
-      *reinterpret_cast<uint4*>(xh + qrow * kLD + cc) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-#pragma unroll
-      for (int o = 1; o < G / 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float scale = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(fmaxf(amax, eps), 7.0f)));
-      const float rs = __frcp_rn(scale);
-      // rint and the offset-binary code in one add: for |t| < 2^22, t + 1.5*2^23 + 8
-      // rounds t to the nearest integer (ties to even) and its low mantissa bits
-      // hold rint(t) + 8.  |x_hat / scale| <= 7 * (1 + 2^-8), so rint(t) is in
-      // [-7, 7] and the reference's clamp to [-8, 7] never binds.
-      constexpr float kMagic = 12582920.0f;  // 1.5 * 2^23 + 8
-      float tq[8], qv[8];
-      uint32_t u[8];
-      slow = false;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        tq[i] = xhv[i] * rs;
-        const float m = tq[i] + kMagic;
-        qv[i] = m - kMagic;  // rint(tq), exact
-        u[i] = __float_as_uint(m);
-        slow |= near_half_integer(tq[i], qv[i]);
-      }
-      if (slow) {
-#pragma unroll
+    } else {
+    // ---- smoothing + group quantization (bit-exact with the reference) ----
+      {
+        const uint4 xv = *reinterpret_cast<const uint4*>(xs + (st * kBM + qrow) * kLD + cc);
+        const float4 r0 = *reinterpret_cast<const float4*>(rsm + col0);
+        const float4 r1 = *reinterpret_cast<const float4*>(rsm + col0 + 4);
+        const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
+        float xf[8], t[8];
+        bool slow = false;
+  #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(x2[i]);
+          xf[2 * i] = f.x;
+          xf[2 * i + 1] = f.y;
+        }
+  #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          if (near_half_integer(tq[i], qv[i])) {
-            const float m = __fdiv_rn(xhv[i], scale) + kMagic;
-            qv[i] = m - kMagic;
-            u[i] = __float_as_uint(m);
+          t[i] = xf[i] * rv[i];
+          slow |= near_bf16_midpoint(t[i]);
+        }
+        if (slow) {
+  #pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (near_bf16_midpoint(t[i]) && col0 + i < p.K_in)
+              t[i] = __fdiv_rn(xf[i], __bfloat162float(p.smooth[col0 + i]));
+        }
+        uint32_t hw[4];
+        float xhv[8];
+        float amax = 0.f;
+  #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          __nv_bfloat162 pr = __floats2bfloat162_rn(t[2 * i], t[2 * i + 1]);
+          hw[i] = *reinterpret_cast<uint32_t*>(&pr);
+          const float2 f = __bfloat1622float2(pr);
+          xhv[2 * i] = f.x;
+          xhv[2 * i + 1] = f.y;
+          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+        *reinterpret_cast<uint4*>(xh + qrow * kLD + cc) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  #pragma unroll
+        for (int o = 1; o < G / 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float scale = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(fmaxf(amax, eps), 7.0f)));
+        const float rs = __frcp_rn(scale);
+        // rint and the offset-binary code in one add: for |t| < 2^22, t + 1.5*2^23 + 8
+        // rounds t to the nearest integer (ties to even) and its low mantissa bits
+        // hold rint(t) + 8.  |x_hat / scale| <= 7 * (1 + 2^-8), so rint(t) is in
+        // [-7, 7] and the reference's clamp to [-8, 7] never binds.
+        constexpr float kMagic = 12582920.0f;  // 1.5 * 2^23 + 8
+        float tq[8], qv[8];
+        uint32_t u[8];
+        slow = false;
+  #pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          tq[i] = xhv[i] * rs;
+          const float m = tq[i] + kMagic;
+          qv[i] = m - kMagic;  // rint(tq), exact
+          u[i] = __float_as_uint(m);
+          slow |= near_half_integer(tq[i], qv[i]);
+        }
+        if (slow) {
+  #pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (near_half_integer(tq[i], qv[i])) {
+              const float m = __fdiv_rn(xhv[i], scale) + kMagic;
+              qv[i] = m - kMagic;
+              u[i] = __float_as_uint(m);
+            }
           }
         }
-      }
-      uint32_t nib = 0, e4[2];
+        uint32_t nib = 0, aw[4];
 #pragma unroll
-      for (int i = 0; i < 8; i += 2) {
-        nib |= ((u[i] & 0xFu) | ((u[i + 1] & 0xFu) << 4)) << (i * 4);
-        const uint32_t f8 =
-            (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(qv[i], qv[i + 1]), __NV_SATFINITE, __NV_E4M3);
-        if ((i % 4) == 0) e4[i / 4] = f8;
-        else e4[i / 4] |= f8 << 16;
-      }
-      if (col0 < p.K_pad && grow < p.M) {
-        if (p.packed) *reinterpret_cast<uint32_t*>(p.packed + (int64_t)grow * (p.K_pad / 2) + col0 / 2) = nib;
-        if (p.codes) *reinterpret_cast<uint2*>(p.codes + (int64_t)grow * p.K_pad + col0) = make_uint2(e4[0], e4[1]);
-        if ((tid % (G / 8)) == 0) {
-          if (p.scales) p.scales[(int64_t)grow * (p.K_pad / G) + col0 / G] = __float2bfloat16_rn(scale);
-          if (p.scales_t) {
-#pragma unroll
-            for (int h = 0; h < G / 64; ++h)
-              p.scales_t[(int64_t)(col0 / 64 + h) * p.ld_ast + grow] = scale;
-          }
+        for (int i = 0; i < 8; i += 2) {
+          nib |= ((u[i] & 0xFu) | ((u[i + 1] & 0xFu) << 4)) << (i * 4);
+          // q * scale is exact in fp32 and in fp16 (at most 11 significant bits)
+          __half2 h = __floats2half2_rn(qv[i] * scale, qv[i + 1] * scale);
+          aw[i / 2] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        if (col0 < p.K_pad && grow < p.M) {
+          if (p.packed) *reinterpret_cast<uint32_t*>(p.packed + (int64_t)grow * (p.K_pad / 2) + col0 / 2) = nib;
+          if (p.a16)
+            *reinterpret_cast<uint4*>(p.a16 + (int64_t)grow * p.K_pad + col0) = make_uint4(aw[0], aw[1], aw[2], aw[3]);
+          if ((tid % (G / 8)) == 0 && p.scales)
+            p.scales[(int64_t)grow * (p.K_pad / G) + col0 / G] = __float2bfloat16_rn(scale);
         }
       }
     }
@@ -277,8 +315,12 @@ __global__ void __launch_bounds__(kThreads) act_quant_kernel(const ActQuantParam
             const int br = t * 8 + (lane % 8), bc = kk * 16 + ((lane / 8) % 2) * 8;
             uint32_t b0, b1;
             ldmatrix_x2(smem_u32(wst + br * kLD + bc), b0, b1);
-            if (t * 8 < p.rank) mma_bf16_16816(acc[j], a_hat, b0, b1);
-            else mma_bf16_16816(acc[j], a_raw, b0, b1);
+            if (t * 8 < p.rank) {
+              if constexpr (W4A16) mma_f16_16816(acc[j], a_hat, b0, b1);
+              else mma_bf16_16816(acc[j], a_hat, b0, b1);
+            } else {
+              mma_bf16_16816(acc[j], a_raw, b0, b1);
+            }
           }
         }
       }
@@ -331,10 +373,10 @@ size_t smem_bytes(int stages, int r_tot, int k_pad) {
          sizeof(__nv_bfloat16) * (size_t)(stages * kBM * kLD + stages * r_tot * kLD + kBM * kLD);
 }
 
-template <int G, int STAGES>
+template <int G, int STAGES, bool W4A16>
 int launch(const ActQuantParams& prm, int r_tot, cudaStream_t stream) {
   const size_t smem = smem_bytes(STAGES, r_tot, prm.K_pad);
-  auto kern = act_quant_kernel<G, STAGES>;
+  auto kern = act_quant_kernel<G, STAGES, W4A16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "svdq_act_quant: shared memory attribute");
   const int grid = (prm.M + kBM - 1) / kBM;
@@ -342,52 +384,48 @@ int launch(const ActQuantParams& prm, int r_tot, cudaStream_t stream) {
   return check_launch("svdq_act_quant launch");
 }
 
-template <int G>
+template <int G, bool W4A16>
 int launch_g(const ActQuantParams& prm, int r_tot, cudaStream_t stream) {
   // deepest ring that fits in the shared-memory budget
-  if (smem_bytes(4, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 4>(prm, r_tot, stream);
-  if (smem_bytes(3, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 3>(prm, r_tot, stream);
-  if (smem_bytes(2, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 2>(prm, r_tot, stream);
+  if (smem_bytes(4, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 4, W4A16>(prm, r_tot, stream);
+  if (smem_bytes(3, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 3, W4A16>(prm, r_tot, stream);
+  if (smem_bytes(2, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 2, W4A16>(prm, r_tot, stream);
   return set_error(SVDQ_ERR_UNSUPPORTED, "svdq_act_quant: K_pad / rank too large for shared memory");
 }
 
 }  // namespace
 }  // namespace svdq
 
-extern "C" int svdq_act_quant(const void* x, int64_t ldx, const void* smooth, const void* l2,
-                              int rank, const void* lora_down, const float* lora_col_scale,
-                              int lora_rank, int M, int K_in, int K_pad, int a_group,
-                              void* out_packed, void* out_scales, void* out_codes,
-                              float* out_scales_t, int ld_ast, void* out_mid_hl, int R2,
-                              cudaStream_t stream) {
-  using namespace svdq;
-  SVDQ_REQUIRE(x && smooth, "svdq_act_quant: x and smooth are required");
-  SVDQ_REQUIRE(M >= 0 && K_in > 0 && K_pad >= K_in, "svdq_act_quant: need 0 < K_in <= K_pad");
-  SVDQ_REQUIRE(a_group == 64 || a_group == 128, "svdq_act_quant: a_group must be 64 or 128");
-  SVDQ_REQUIRE(K_pad % a_group == 0, "svdq_act_quant: K_pad must be a multiple of a_group");
-  SVDQ_REQUIRE(K_in % 8 == 0, "svdq_act_quant: K_in must be a multiple of 8 (pad smooth/l2 at load)");
-  SVDQ_REQUIRE(ldx >= K_in && ldx % 8 == 0, "svdq_act_quant: ldx must be >= K_in and a multiple of 8");
-  SVDQ_REQUIRE(rank >= 0 && lora_rank >= 0 && rank % 8 == 0 && lora_rank % 8 == 0,
-               "svdq_act_quant: rank and lora_rank must be non-negative multiples of 8");
-  SVDQ_REQUIRE(rank + lora_rank <= 256, "svdq_act_quant: rank + lora_rank must be <= 256");
-  SVDQ_REQUIRE(rank == 0 || l2, "svdq_act_quant: l2 is NULL");
-  SVDQ_REQUIRE(lora_rank == 0 || (lora_down && lora_col_scale),
-               "svdq_act_quant: lora_down / lora_col_scale are NULL");
-  const int r_tot = rank + lora_rank;
-  SVDQ_REQUIRE(!out_mid_hl || (R2 >= 2 * r_tot && R2 % 8 == 0),
-               "svdq_act_quant: R2 must be >= 2*(rank+lora_rank) and a multiple of 8");
-  SVDQ_REQUIRE(!out_scales_t || (ld_ast >= M && ld_ast % 4 == 0),
-               "svdq_act_quant: ld_ast must be >= M and a multiple of 4");
-  SVDQ_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
-                   (reinterpret_cast<uintptr_t>(smooth) & 15u) == 0 &&
-                   (!l2 || (reinterpret_cast<uintptr_t>(l2) & 15u) == 0) &&
-                   (!lora_down || (reinterpret_cast<uintptr_t>(lora_down) & 15u) == 0),
-               "svdq_act_quant: x, smooth, l2, lora_down must be 16-byte aligned");
-  SVDQ_REQUIRE((!out_codes || (reinterpret_cast<uintptr_t>(out_codes) & 7u) == 0) &&
-                   (!out_packed || (reinterpret_cast<uintptr_t>(out_packed) & 3u) == 0),
-               "svdq_act_quant: output code buffers are misaligned");
-  if (M == 0) return SVDQ_OK;
+namespace svdq {
+namespace {
 
+int validate_common(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank, const void* lora_down,
+                    const float* lora_col_scale, int lora_rank, int M, int K_in, int K_pad, void* out_a16,
+                    void* out_mid_hl, int R2, const char* who) {
+  const std::string w(who);
+  auto bad = [&](const char* msg) { return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": " + msg); };
+  if (!(x && smooth)) return bad("x and smooth are required");
+  if (!(M >= 0 && K_in > 0 && K_pad >= K_in)) return bad("need 0 < K_in <= K_pad");
+  if (K_in % 8 != 0) return bad("K_in must be a multiple of 8 (pad smooth/l2 at load)");
+  if (!(ldx >= K_in && ldx % 8 == 0)) return bad("ldx must be >= K_in and a multiple of 8");
+  if (!(rank >= 0 && lora_rank >= 0 && rank % 8 == 0 && lora_rank % 8 == 0))
+    return bad("rank and lora_rank must be non-negative multiples of 8");
+  if (rank + lora_rank > 256) return bad("rank + lora_rank must be <= 256");
+  if (rank > 0 && !l2) return bad("l2 is NULL");
+  if (lora_rank > 0 && !(lora_down && lora_col_scale)) return bad("lora_down / lora_col_scale are NULL");
+  const int r_tot = rank + lora_rank;
+  if (out_mid_hl && !(R2 >= 2 * r_tot && R2 % 8 == 0)) return bad("R2 must be >= 2*(rank+lora_rank) and a multiple of 8");
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(smooth) & 15u) ||
+      (l2 && (reinterpret_cast<uintptr_t>(l2) & 15u)) || (lora_down && (reinterpret_cast<uintptr_t>(lora_down) & 15u)))
+    return bad("x, smooth, l2, lora_down must be 16-byte aligned");
+  if (out_a16 && ((reinterpret_cast<uintptr_t>(out_a16) & 15u) || K_pad % 8 != 0))
+    return bad("a16 must be 16-byte aligned with K_pad a multiple of 8");
+  return SVDQ_OK;
+}
+
+ActQuantParams make_params(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank,
+                           const void* lora_down, const float* lora_col_scale, int lora_rank, int M, int K_in,
+                           int K_pad, void* out_packed, void* out_scales, void* out_a16, void* out_mid_hl, int R2) {
   ActQuantParams p;
   p.x = static_cast<const __nv_bfloat16*>(x);
   p.ldx = ldx;
@@ -402,10 +440,45 @@ extern "C" int svdq_act_quant(const void* x, int64_t ldx, const void* smooth, co
   p.K_pad = K_pad;
   p.packed = static_cast<uint8_t*>(out_packed);
   p.scales = static_cast<__nv_bfloat16*>(out_scales);
-  p.codes = static_cast<uint8_t*>(out_codes);
-  p.scales_t = out_scales_t;
-  p.ld_ast = ld_ast;
-  p.mid_hl = r_tot > 0 ? static_cast<__nv_bfloat16*>(out_mid_hl) : nullptr;
+  p.a16 = static_cast<__half*>(out_a16);
+  p.mid_hl = (rank + lora_rank) > 0 ? static_cast<__nv_bfloat16*>(out_mid_hl) : nullptr;
   p.R2 = R2;
-  return a_group == 64 ? launch_g<64>(p, r_tot, stream) : launch_g<128>(p, r_tot, stream);
+  return p;
+}
+
+}  // namespace
+}  // namespace svdq
+
+extern "C" int svdq_act_quant(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank,
+                              const void* lora_down, const float* lora_col_scale, int lora_rank, int M, int K_in,
+                              int K_pad, int a_group, void* out_packed, void* out_scales, void* out_a16,
+                              void* out_mid_hl, int R2, cudaStream_t stream) {
+  using namespace svdq;
+  int st = validate_common(x, ldx, smooth, l2, rank, lora_down, lora_col_scale, lora_rank, M, K_in, K_pad, out_a16,
+                           out_mid_hl, R2, "svdq_act_quant");
+  if (st) return st;
+  SVDQ_REQUIRE(a_group == 64 || a_group == 128, "svdq_act_quant: a_group must be 64 or 128");
+  SVDQ_REQUIRE(K_pad % a_group == 0, "svdq_act_quant: K_pad must be a multiple of a_group");
+  SVDQ_REQUIRE(!out_packed || (reinterpret_cast<uintptr_t>(out_packed) & 3u) == 0,
+               "svdq_act_quant: packed output must be 4-byte aligned");
+  if (M == 0) return SVDQ_OK;
+  const ActQuantParams p = make_params(x, ldx, smooth, l2, rank, lora_down, lora_col_scale, lora_rank, M, K_in,
+                                       K_pad, out_packed, out_scales, out_a16, out_mid_hl, R2);
+  const int r_tot = rank + lora_rank;
+  return a_group == 64 ? launch_g<64, false>(p, r_tot, stream) : launch_g<128, false>(p, r_tot, stream);
+}
+
+extern "C" int svdq_w4a16_prep(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank,
+                               const void* lora_down, const float* lora_col_scale, int lora_rank, int M, int K_in,
+                               int K_pad, void* out_a16, void* out_mid_hl, int R2, cudaStream_t stream) {
+  using namespace svdq;
+  int st = validate_common(x, ldx, smooth, l2, rank, lora_down, lora_col_scale, lora_rank, M, K_in, K_pad, out_a16,
+                           out_mid_hl, R2, "svdq_w4a16_prep");
+  if (st) return st;
+  SVDQ_REQUIRE(out_a16, "svdq_w4a16_prep: out_a16 is required");
+  SVDQ_REQUIRE(K_pad % 64 == 0, "svdq_w4a16_prep: K_pad must be a multiple of 64");
+  if (M == 0) return SVDQ_OK;
+  const ActQuantParams p = make_params(x, ldx, smooth, l2, rank, lora_down, lora_col_scale, lora_rank, M, K_in,
+                                       K_pad, nullptr, nullptr, out_a16, out_mid_hl, R2);
+  return launch_g<64, true>(p, rank + lora_rank, stream);
 }

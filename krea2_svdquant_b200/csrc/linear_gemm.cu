@@ -1,0 +1,391 @@
+// SVDQuant linear GEMM for sm_100a (tcgen05 + TMA + TMEM, CTA pairs).
+//
+//   out[m, n] = sum_k A[m,k] W[n,k] + sum_j mid_hl[m,j] up_hl[n,j] + bias[n]
+//
+// A and W are fp16 operands that hold the dequantized INT4 values exactly:
+// A = fp16(q_a * s_a) from the activation pass (W4A4) or fp16(x / smooth)
+// (W4A16), W = fp16(q_w * s_w) from the load-time weight preparation.  The
+// product of a code in [-8, 7] (at most 3 significant bits) and a bf16 scale
+// (8 significant bits) has at most 11 significant bits, so it is exact in
+// fp16 whenever it lies in fp16's range; the MMA then sums exact products in
+// fp32, which is the staged W4A4 result of the reference's README formula.
+// Accumulating the whole K in TMEM keeps the tensor core's accumulator private:
+// nothing reads TMEM between K steps (reading per-group partials out of TMEM
+// while MMAs run is limited to a small fraction of TMEM bandwidth on B200).
+//
+// Persistent kernel launched as clusters of two CTAs.  A pair owns one 256x256
+// output tile at a time; the even CTA issues cta_group::2 MMAs (M=256, N=256)
+// whose A rows (128 per CTA) and W rows (128 per CTA) are split between the two
+// CTAs' shared memory, so each operand byte crosses L2 once per pair.  Each
+// CTA's TMEM receives its 128 rows x 256 columns; two accumulators let the
+// epilogue of one tile overlap the MMAs of the next.  12 warps per CTA:
+//   warp 0      TMA producer (both CTAs): per stage one 128-byte K slice (64
+//               fp16) of the CTA's A rows and W half, counted on the even CTA's
+//               barrier; then the low-rank stages (mid_hl x up_hl, bf16).
+//   warp 1      TMEM allocator (both CTAs) and, in the even CTA, MMA issuer
+//               (kind::f16: fp16 for the residual, bf16 for the low-rank term).
+//   warps 4-11  epilogue (both CTAs): two warpgroups, 128 columns each; TMEM ->
+//               registers -> + bias -> bf16/fp32 -> global.
+// Every mbarrier wait is bounded; a wait that runs out sets a CTA abort flag and
+// the library's device error word, and all roles leave their loops, so both
+// CTAs always reach the closing cluster barrier.
+#include "svdq_common.cuh"
+
+namespace svdq {
+namespace {
+
+constexpr int BM = 128;          // rows per CTA (the pair tile is 2*BM)
+constexpr int BN = 256;          // columns per tile
+constexpr int BN_HALF = BN / 2;  // W rows staged per CTA
+constexpr int KB = 128;          // bytes of K per operand stage row (64 fp16/bf16)
+constexpr int STAGES = 6;
+constexpr int A_BYTES = BM * KB;       // 16 KiB
+constexpr int B_BYTES = BN_HALF * KB;  // 16 KiB
+constexpr int AB_BYTES = A_BYTES + B_BYTES;
+constexpr int NUM_THREADS = 384;
+constexpr int NUM_ACC = 2;             // TMEM accumulators (tile double buffering)
+constexpr int TMEM_COLS = NUM_ACC * BN;
+constexpr int EPI_COLS = BN / 2;       // columns per epilogue warpgroup
+static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "operand tiles keep 1 KiB alignment for 128B swizzle");
+static_assert(TMEM_COLS == 512, "TMEM allocation");
+
+struct Barriers {
+  uint64_t full[STAGES];       // used in the even CTA (both CTAs' loads count here)
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[NUM_ACC];
+  uint64_t tmem_empty[NUM_ACC];  // used in the even CTA (16 arrivals: 8 warps per CTA)
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+constexpr size_t SMEM_BYTES = (size_t)STAGES * AB_BYTES + sizeof(Barriers) + 1024;
+
+struct GemmArgs {
+  const __nv_bfloat16* bias;
+  void* out;
+  int64_t ldo;
+  int M, N;
+  int n_k;   // K_pad / 64 residual stages
+  int n_lr;  // R2 / 64 low-rank stages
+  int num_m_blocks, num_n_blocks;  // pair tiles: 256 rows x 256 columns
+  int* err;
+};
+
+// Wait sites recorded in the device error word.
+enum : int {
+  kWaitProdEmpty = 0x101,
+  kWaitMmaFull = 0x201,
+  kWaitMmaTmemEmpty = 0x202,
+  kWaitMmaDone = 0x203,
+  kWaitEpiTmemFull = 0x301,
+};
+
+constexpr uint32_t kFmtF16 = 0;  // kind::f16 format code for fp16
+
+__device__ __forceinline__ void advance(int& idx, uint32_t& phase, int n) {
+  if (++idx == n) {
+    idx = 0;
+    phase ^= 1u;
+  }
+}
+
+template <bool OUT_F32>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    linear_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
+                       const __grid_constant__ CUtensorMap tm_mid, const __grid_constant__ CUtensorMap tm_up,
+                       const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  const uint32_t smem_base = raw_addr + pad;
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + (size_t)STAGES * AB_BYTES);
+  volatile int* abort_flag = &bars->abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = even CTA (MMA issuer), 1 = its pair
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_tiles = args.num_m_blocks * args.num_n_blocks;
+
+  auto full_bar = [&](int s) { return smem_u32(&bars->full[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars->empty[s]); };
+  auto tm_full = [&](int b) { return smem_u32(&bars->tmem_full[b]); };
+  auto tm_empty = [&](int b) { return smem_u32(&bars->tmem_empty[b]); };
+  auto stage_a = [&](int s) { return smem_base + (uint32_t)(s * AB_BYTES); };
+  auto stage_b = [&](int s) { return smem_base + (uint32_t)(s * AB_BYTES + A_BYTES); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);   // the even CTA's producer arrives (with both CTAs' bytes)
+      mbar_init(empty_bar(s), 1);  // MMA commit
+    }
+    for (int b = 0; b < NUM_ACC; ++b) {
+      mbar_init(tm_full(b), 1);
+      mbar_init(tm_empty(b), 16);  // epilogue warps of both CTAs
+    }
+    mbar_init(smem_u32(&bars->mma_done), 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tma_desc(&tm_a);
+    prefetch_tma_desc(&tm_w);
+    if (args.n_lr > 0) {
+      prefetch_tma_desc(&tm_mid);
+      prefetch_tma_desc(&tm_up);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&bars->tmem_base), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t filled = 0, par = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < num_tiles; t += num_pairs) {
+        const int m0 = (t % args.num_m_blocks) * (2 * BM) + (int)rank * BM;
+        const int n0 = (t / args.num_m_blocks) * BN + (int)rank * BN_HALF;
+        const int total = args.n_k + args.n_lr;
+        for (int s = 0; ok && s < total; ++s) {
+          if (!(ok = mbar_wait<true>(empty_bar(stage), phase ^ 1u, abort_flag, args.err, kWaitProdEmpty))) break;
+          const uint32_t full_c = mapa_shared(full_bar(stage), 0);
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * AB_BYTES);
+          if (s < args.n_k) {
+            tma_load_2d_pair(stage_a(stage), &tm_a, full_c, s * 64, m0);
+            tma_load_2d_pair(stage_b(stage), &tm_w, full_c, s * 64, n0);
+          } else {
+            tma_load_2d_pair(stage_a(stage), &tm_mid, full_c, (s - args.n_k) * 64, m0);
+            tma_load_2d_pair(stage_b(stage), &tm_up, full_c, (s - args.n_k) * 64, n0);
+          }
+          filled |= 1u << stage;
+          par = (par & ~(1u << stage)) | (phase << stage);
+          advance(stage, phase, STAGES);
+        }
+      }
+      if (!ok && leader) {
+        // let copies already in flight land before the CTA exits
+        for (int s = 0; s < STAGES; ++s)
+          if (filled & (1u << s)) mbar_wait_drain(full_bar(s), (par >> s) & 1u, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer (even CTA)
+      const uint32_t idesc_f16 = make_idesc(kFmtF16, kFmtF16, 2 * BM, BN);
+      const uint32_t idesc_bf16 = make_idesc(kFmtBF16, kFmtBF16, 2 * BM, BN);
+      int stage = 0, tb = 0;
+      uint32_t phase = 0, tb_ph = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < num_tiles; t += num_pairs) {
+        if (!(ok = mbar_wait<true>(tm_empty(tb), tb_ph ^ 1u, abort_flag, args.err, kWaitMmaTmemEmpty))) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(tb * BN);
+        const int total = args.n_k + args.n_lr;
+        for (int s = 0; ok && s < total; ++s) {
+          if (!(ok = mbar_wait<true>(full_bar(stage), phase, abort_flag, args.err, kWaitMmaFull))) break;
+          tc_fence_after();
+          const uint64_t da = desc_k_sw128(stage_a(stage));
+          const uint64_t db = desc_k_sw128(stage_b(stage));
+          const uint32_t idesc = s < args.n_k ? idesc_f16 : idesc_bf16;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)  // 4 x K=16 = 128 bytes
+            umma_f16_pair(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (s > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_pair(empty_bar(stage));
+          advance(stage, phase, STAGES);
+        }
+        if (!ok) break;
+        umma_commit_pair(tm_full(tb));
+        advance(tb, tb_ph, NUM_ACC);
+      }
+      // all issued MMAs must finish before either CTA releases TMEM or exits
+      umma_commit_pair_local(smem_u32(&bars->mma_done));
+      if (!mbar_wait_drain(smem_u32(&bars->mma_done), 0, 1000000000ull)) {
+        *abort_flag = 1;
+        atomicCAS(args.err, 0, kWaitMmaDone);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int ew = warp - 4;
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int col0 = (ew >> 2) * EPI_COLS;  // warpgroup's column half
+    const int row = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    int tb = 0;
+    uint32_t tb_ph = 0;
+    bool ok = true;
+    for (int t = pair; ok && t < num_tiles; t += num_pairs) {
+      const int m0 = (t % args.num_m_blocks) * (2 * BM) + (int)rank * BM;
+      const int n0 = (t / args.num_m_blocks) * BN;
+      if (!(ok = mbar_wait<true>(tm_full(tb), tb_ph, abort_flag, args.err, kWaitEpiTmemFull))) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + col0);
+      const int grow = m0 + row;
+      const int64_t rbase = (int64_t)grow * args.ldo;
+      uint32_t va[32], vb[32];
+      tmem_ld32(taddr, va);
+#pragma unroll
+      for (int c = 0; c < EPI_COLS / 32; ++c) {
+        uint32_t (&cur)[32] = (c & 1) ? vb : va;
+        uint32_t (&nxt)[32] = (c & 1) ? va : vb;
+        tmem_ld_wait_regs(cur);
+        if (c + 1 < EPI_COLS / 32) {
+          tmem_ld32(taddr + (uint32_t)((c + 1) * 32), nxt);
+        } else {
+          // the whole accumulator slice is in registers: hand TMEM back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(tm_empty(tb), 0));
+        }
+        const int nc = n0 + col0 + c * 32;
+        if (grow < args.M) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            const int n = nc + i;
+            if (n < args.N) {
+              float v[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(cur[i + e]);
+              if (args.bias) {
+                const uint4 braw = *reinterpret_cast<const uint4*>(args.bias + n);
+                const __nv_bfloat162* bb = reinterpret_cast<const __nv_bfloat162*>(&braw);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = __bfloat1622float2(bb[e]);
+                  v[2 * e] += f.x;
+                  v[2 * e + 1] += f.y;
+                }
+              }
+              if constexpr (OUT_F32) {
+                float4* o = reinterpret_cast<float4*>(static_cast<float*>(args.out) + rbase + n);
+                o[0] = make_float4(v[0], v[1], v[2], v[3]);
+                o[1] = make_float4(v[4], v[5], v[6], v[7]);
+              } else {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+                  w[e] = *reinterpret_cast<uint32_t*>(&h);
+                }
+                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(args.out) + rbase + n) =
+                    make_uint4(w[0], w[1], w[2], w[3]);
+              }
+            }
+          }
+        }
+      }
+      advance(tb, tb_ph, NUM_ACC);
+    }
+  }
+
+  // Neither CTA may exit or release TMEM while the pair's MMAs can still touch
+  // its shared memory or TMEM; every role above has left its loop (all waits
+  // are bounded) and the even CTA's MMA warp has drained its MMAs.
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, const void* up_hl, int R2,
+                       const void* bias, void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
+                       cudaStream_t stream, const char* who) {
+  const std::string w(who);
+  if (!(a16 && w16 && out)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": null operand pointer");
+  if (!(M >= 0 && N > 0 && K_pad > 0)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": bad M/N/K_pad");
+  if (K_pad % 64 != 0) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": K_pad must be a multiple of 64");
+  if (!(N % 8 == 0 && ldo >= N && ldo % 8 == 0))
+    return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": N and ldo must be multiples of 8, ldo >= N");
+  if (!(R2 >= 0 && R2 % 64 == 0)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": R2 must be a multiple of 64");
+  if (R2 > 0 && !(mid_hl && up_hl)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": mid_hl/up_hl are NULL");
+  if (!(out_dtype == SVDQ_BF16 || out_dtype == SVDQ_FP32))
+    return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": out_dtype must be bf16 or fp32");
+  if (bias && (reinterpret_cast<uintptr_t>(bias) & 15u))
+    return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": bias must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(out) & 15u)
+    return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": out must be 16-byte aligned");
+  if (M == 0) return SVDQ_OK;
+  int* err = device_error_word();
+  if (!err) return set_error(SVDQ_ERR_CUDA, w + ": device error word unavailable");
+
+  CUtensorMap tm_a, tm_w, tm_mid, tm_up;
+  int st;
+  if ((st = make_tma_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a16, K_pad, M, (uint64_t)K_pad * 2, 64, BM,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if ((st = make_tma_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w16, K_pad, N, (uint64_t)K_pad * 2, 64, BN_HALF,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if (R2 > 0) {
+    if ((st = make_tma_2d(&tm_mid, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, mid_hl, R2, M, (uint64_t)R2 * 2, 64, BM,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+    if ((st = make_tma_2d(&tm_up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, up_hl, R2, N, (uint64_t)R2 * 2, 64, BN_HALF,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+  } else {
+    tm_mid = tm_a;
+    tm_up = tm_w;
+  }
+
+  GemmArgs a;
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.out = out;
+  a.ldo = ldo;
+  a.M = M;
+  a.N = N;
+  a.n_k = K_pad / 64;
+  a.n_lr = R2 / 64;
+  a.num_m_blocks = (M + 2 * BM - 1) / (2 * BM);
+  a.num_n_blocks = (N + BN - 1) / BN;
+  a.err = err;
+  auto kern = out_dtype == SVDQ_FP32 ? linear_gemm_kernel<true> : linear_gemm_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+  if (e != cudaSuccess) return check_cuda(e, (w + ": shared memory attribute").c_str());
+  const int tiles = a.num_m_blocks * a.num_n_blocks;
+  const int max_pairs = num_sms() / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, tm_a, tm_w, tm_mid, tm_up, a);
+  if (e != cudaSuccess) return check_cuda(e, (w + " launch").c_str());
+  return check_launch((w + " launch").c_str());
+}
+
+}  // namespace svdq
+
+extern "C" int svdq_linear_gemm(const void* a16, const void* w16, const void* mid_hl, const void* up_hl, int R2,
+                                const void* bias, void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
+                                cudaStream_t stream) {
+  return svdq::launch_linear_gemm(a16, w16, mid_hl, up_hl, R2, bias, out, out_dtype, ldo, M, N, K_pad, stream,
+                                  "svdq_linear_gemm");
+}

@@ -1,49 +1,14 @@
-// Load-time operand preparation for the W4A4 GEMM.
+// Load-time operand preparation for the linear GEMM.
 //
 // The checkpoint stores the residual weight as packed INT4 (q + 8 per nibble,
 // even k in the low nibble; pack.py:47-56) with one scale per (row, group)
-// (convert_simulated.py:201-204).  The GEMM consumes the same integers as e4m3
-// bytes (every integer in [-8, 7] is exact in e4m3) and the scales transposed
-// to [K_pad/64, N] fp32, one row per 64-wide K group, so a 128x256 output tile
-// reads its scales as contiguous TMA boxes.
-#include <cuda_fp8.h>
-
+// (convert_simulated.py:201-204).  The GEMM consumes w16 = fp16(q * scale):
+// q has at most 3 significant bits and a bf16 scale 8, so the product is exact
+// in fp16 for bf16 scales (fp16 / fp32 scales round once, to nearest).
 #include "svdq_common.cuh"
 
 namespace svdq {
 namespace {
-
-// e4m3 bytes of q = u - 8 for every nibble value u (offset-binary code).
-__device__ __forceinline__ uint32_t nib_to_e4m3_pair(uint32_t byte) {
-  const float q0 = (float)((int)(byte & 0xF) - 8);
-  const float q1 = (float)((int)(byte >> 4) - 8);
-  return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(q0, q1), __NV_SATFINITE, __NV_E4M3);
-}
-
-// Each thread expands 8 packed bytes (16 codes).
-__global__ void repack_codes_kernel(const uint8_t* __restrict__ qw, uint8_t* __restrict__ out,
-                                    int64_t n_bytes) {
-  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
-  if (i >= n_bytes) return;
-  if (i + 8 <= n_bytes) {
-    const uint2 v = *reinterpret_cast<const uint2*>(qw + i);
-    uint32_t w[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t word = j < 2 ? v.x : v.y;
-      const uint32_t b0 = (word >> ((j % 2) * 16)) & 0xFF;
-      const uint32_t b1 = (word >> ((j % 2) * 16 + 8)) & 0xFF;
-      w[j] = nib_to_e4m3_pair(b0) | (nib_to_e4m3_pair(b1) << 16);
-    }
-    *reinterpret_cast<uint4*>(out + 2 * i) = make_uint4(w[0], w[1], w[2], w[3]);
-  } else {
-    for (int64_t k = i; k < n_bytes; ++k) {
-      const uint32_t pr = nib_to_e4m3_pair(qw[k]);
-      out[2 * k] = (uint8_t)(pr & 0xFF);
-      out[2 * k + 1] = (uint8_t)(pr >> 8);
-    }
-  }
-}
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
@@ -54,14 +19,28 @@ __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(
 template <>
 __device__ __forceinline__ float to_f32<float>(float v) { return v; }
 
-// out[g64][n] = scales[n][g64 * 64 / w_group]
+// Each thread expands 8 packed bytes (16 codes) of one row into 16 fp16 values.
 template <typename T>
-__global__ void repack_scales_kernel(const T* __restrict__ sc, float* __restrict__ out, int N,
-                                     int n_g64, int n_gw, int ratio) {
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  const int g = blockIdx.y;
-  if (n >= N || g >= n_g64) return;
-  out[(int64_t)g * N + n] = to_f32<T>(sc[(int64_t)n * n_gw + g / ratio]);
+__global__ void repack_w16_kernel(const uint8_t* __restrict__ qw, const T* __restrict__ sc,
+                                  __half* __restrict__ out, int N, int K_pad, int w_group) {
+  const int64_t per_row = K_pad / 16;  // 16-code units per row
+  const int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= (int64_t)N * per_row) return;
+  const int n = (int)(u / per_row);
+  const int k0 = (int)(u % per_row) * 16;
+  const float s = to_f32<T>(sc[(int64_t)n * (K_pad / w_group) + k0 / w_group]);  // w_group % 16 == 0
+  const uint2 v = *reinterpret_cast<const uint2*>(qw + (int64_t)n * (K_pad / 2) + k0 / 2);
+  uint32_t w[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t byte = ((j < 4 ? v.x : v.y) >> ((j % 4) * 8)) & 0xFF;
+    const float q0 = (float)((int)(byte & 0xF) - 8), q1 = (float)((int)(byte >> 4) - 8);
+    __half2 h = __floats2half2_rn(q0 * s, q1 * s);
+    w[j] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  uint4* o = reinterpret_cast<uint4*>(out + (int64_t)n * K_pad + k0);
+  o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  o[1] = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
 // up_hl[n] = [l1[n] | lora_up[n] | l1[n] | lora_up[n] | 0 ...]
@@ -84,43 +63,34 @@ __global__ void build_up_hl_kernel(const __nv_bfloat16* __restrict__ l1, int ran
 }  // namespace svdq
 
 extern "C" int svdq_repack_weight(const void* qweight, const void* scales, int scale_dtype, int N,
-                                  int K_pad, int w_group, void* out_codes, float* out_scales_t,
-                                  cudaStream_t stream) {
+                                  int K_pad, int w_group, void* out_w16, cudaStream_t stream) {
   using namespace svdq;
-  SVDQ_REQUIRE(qweight && scales && out_codes && out_scales_t, "svdq_repack_weight: null pointer");
+  SVDQ_REQUIRE(qweight && scales && out_w16, "svdq_repack_weight: null pointer");
   SVDQ_REQUIRE(N > 0 && K_pad > 0 && K_pad % 64 == 0, "svdq_repack_weight: K_pad must be a positive multiple of 64");
-  SVDQ_REQUIRE(w_group > 0 && w_group % 64 == 0 && K_pad % w_group == 0,
-               "svdq_repack_weight: w_group must be a multiple of 64 dividing K_pad");
+  SVDQ_REQUIRE(w_group > 0 && w_group % 16 == 0 && K_pad % w_group == 0,
+               "svdq_repack_weight: w_group must be a multiple of 16 dividing K_pad");
   SVDQ_REQUIRE((reinterpret_cast<uintptr_t>(qweight) & 7u) == 0 &&
-                   (reinterpret_cast<uintptr_t>(out_codes) & 15u) == 0,
-               "svdq_repack_weight: qweight must be 8-byte and out_codes 16-byte aligned");
-  SVDQ_REQUIRE(N <= 65535, "svdq_repack_weight: N must be <= 65535");
-  const int64_t n_bytes = (int64_t)N * (K_pad / 2);
+                   (reinterpret_cast<uintptr_t>(out_w16) & 15u) == 0,
+               "svdq_repack_weight: qweight must be 8-byte and out_w16 16-byte aligned");
+  const int64_t units = (int64_t)N * (K_pad / 16);
   const int threads = 256;
-  const int64_t blocks = ((n_bytes + 7) / 8 + threads - 1) / threads;
-  repack_codes_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
-      static_cast<const uint8_t*>(qweight), static_cast<uint8_t*>(out_codes), n_bytes);
-  int st = check_launch("svdq_repack_weight codes");
-  if (st) return st;
-  const int n_g64 = K_pad / 64, n_gw = K_pad / w_group, ratio = w_group / 64;
-  dim3 grid((N + 255) / 256, n_g64);
+  const unsigned blocks = (unsigned)((units + threads - 1) / threads);
+  __half* out = static_cast<__half*>(out_w16);
+  const uint8_t* qw = static_cast<const uint8_t*>(qweight);
   switch (scale_dtype) {
     case SVDQ_BF16:
-      repack_scales_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(scales),
-                                                     out_scales_t, N, n_g64, n_gw, ratio);
+      repack_w16_kernel<<<blocks, threads, 0, stream>>>(qw, static_cast<const __nv_bfloat16*>(scales), out, N, K_pad, w_group);
       break;
     case SVDQ_FP16:
-      repack_scales_kernel<<<grid, 256, 0, stream>>>(static_cast<const __half*>(scales),
-                                                     out_scales_t, N, n_g64, n_gw, ratio);
+      repack_w16_kernel<<<blocks, threads, 0, stream>>>(qw, static_cast<const __half*>(scales), out, N, K_pad, w_group);
       break;
     case SVDQ_FP32:
-      repack_scales_kernel<<<grid, 256, 0, stream>>>(static_cast<const float*>(scales),
-                                                     out_scales_t, N, n_g64, n_gw, ratio);
+      repack_w16_kernel<<<blocks, threads, 0, stream>>>(qw, static_cast<const float*>(scales), out, N, K_pad, w_group);
       break;
     default:
       return set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_repack_weight: scale_dtype must be bf16, fp16 or fp32");
   }
-  return check_launch("svdq_repack_weight scales");
+  return check_launch("svdq_repack_weight");
 }
 
 extern "C" int svdq_build_up_hl(const void* l1, int rank, const void* lora_up, int lora_rank, int N,

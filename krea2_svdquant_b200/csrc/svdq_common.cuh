@@ -85,35 +85,105 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Up to 64 polls of the phase in one tight PTX loop; each poll may suspend the
+// thread for up to `hint_ns` while the phase is incomplete.  Returns true once
+// the phase with the given parity has completed.
+template <bool CLUSTER>
+__device__ __forceinline__ bool mbar_poll64(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  constexpr uint32_t hint_ns = 20000;
+  if (CLUSTER) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .u32 i;\n\t"
+        "mov.u32 i, 0;\n"
+        "MBAR_POLL:\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "@p bra.uni MBAR_DONE;\n\t"
+        "add.u32 i, i, 1;\n\t"
+        "setp.lt.u32 p, i, 64;\n\t"
+        "@p bra.uni MBAR_POLL;\n\t"
+        "mov.u32 %0, 0;\n\t"
+        "bra.uni MBAR_END;\n"
+        "MBAR_DONE:\n\t"
+        "mov.u32 %0, 1;\n"
+        "MBAR_END:\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .u32 i;\n\t"
+        "mov.u32 i, 0;\n"
+        "MBAR_POLL:\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "@p bra.uni MBAR_DONE;\n\t"
+        "add.u32 i, i, 1;\n\t"
+        "setp.lt.u32 p, i, 64;\n\t"
+        "@p bra.uni MBAR_POLL;\n\t"
+        "mov.u32 %0, 0;\n\t"
+        "bra.uni MBAR_END;\n"
+        "MBAR_DONE:\n\t"
+        "mov.u32 %0, 1;\n"
+        "MBAR_END:\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+  }
+  return ok != 0;
+}
+
 // Bounded wait on the phase with the given parity.  Returns false (and raises
 // the CTA-wide abort flag plus the device error word) if the wait ran out, or
-// if another role of the CTA already aborted.
+// if another role of the CTA already aborted.  CLUSTER selects cluster-scope
+// acquire, for barriers that also receive arrivals from the other CTA of a pair.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
                                           volatile int* abort_flag, int* err, int where) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_poll64<CLUSTER>(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        atomicCAS(err, 0, where);
-        return false;
-      }
+  while (true) {
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      atomicCAS(err, 0, where);
+      return false;
     }
+    if (mbar_poll64<CLUSTER>(bar, parity)) return true;
   }
 }
 
 // Bounded wait that ignores the abort flag: used while draining in-flight
-// copies after an abort.  Returns false if the limit ran out.
+// copies or MMAs after an abort.  Returns false if the limit ran out.
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity,
                                                 unsigned long long limit_ns) {
+  if (mbar_poll64<false>(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_poll64<false>(bar, parity)) {
     if (globaltimer() - t0 > limit_ns) return false;
   }
   return true;
+}
+
+// ---------------------------------------------------------------------------
+// clusters (CTA pairs for cta_group::2 MMAs)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory location in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// arrive on an mbarrier given by a shared::cluster address (own CTA or the peer)
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -125,6 +195,18 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Pair load for cta_group::2 MMAs: the data lands in this CTA's shared memory and
+// the transaction bytes are counted on the mbarrier at `bar_cluster`, which may be
+// the even (leader) CTA's barrier.  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                                 int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
       : "memory");
 }
 
@@ -174,6 +256,50 @@ __device__ __forceinline__ void umma_f8f6f4(uint32_t d_tmem, uint64_t a_desc, ui
       "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// ---- CTA-pair (cta_group::2) forms ----
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f8f6f4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the mbarrier at the same offset in both CTAs of the pair once all
+// previously issued tcgen05 ops of this thread complete (commit, not a load).
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)3)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair_local(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
 }
 
 // Arrive on an mbarrier once all previously issued tcgen05 ops of this thread complete.

@@ -73,8 +73,7 @@ class PreparedOperands:
     lora_col_scale: torch.Tensor | None  # [rl8] fp32 multiplier per stacked row
     up_hl: torch.Tensor | None     # [n, R2] bf16, [l1 | lora_up] hi/lo operand
     up_hl_base: torch.Tensor | None  # same without the LoRA columns (for _forward_base)
-    w_codes: torch.Tensor          # [n, k_pad] e4m3 codes
-    w_scales_t: torch.Tensor       # [k_pad/64, n] fp32
+    w16: torch.Tensor              # [n, k_pad] fp16 = q * weight scale
     bias: torch.Tensor | None      # [n] bf16
 
 
@@ -167,8 +166,8 @@ class SVDQuantLinear(nn.Module):
             raise ValueError(f"padded K {k_pad} is smaller than in_features rounded to 8 ({k_in})")
         if k_pad % 64:
             raise ValueError(f"padded K {k_pad} must be a multiple of 64")
-        if self.group_size % 64:
-            raise ValueError(f"weight group size {self.group_size} must be a multiple of 64")
+        if self.group_size % 16 or k_pad % self.group_size:
+            raise ValueError(f"weight group size {self.group_size} must be a multiple of 16 dividing K_pad")
         bf = torch.bfloat16
         with torch.no_grad():
             smooth = _pad_cols(self.smooth_scale.to(device=device, dtype=bf), k_in, 1.0).contiguous()
@@ -198,12 +197,12 @@ class SVDQuantLinear(nn.Module):
                 up_hl_base = ops.build_up_hl(l1_in, None, r2b) if r2b else None
             qw = self.qweight.to(device=device).contiguous()
             ws = self.weight_scales.to(device=device).contiguous()
-            w_codes, w_scales_t = ops.repack_weight(qw, ws, self.group_size)
+            w16 = ops.repack_weight(qw, ws, self.group_size)
             bias = None if self.bias is None else self.bias.to(device=device, dtype=bf).contiguous()
         self._prepared = PreparedOperands(device=device, key=key, k_in=k_in, k_pad=k_pad, n=n, smooth=smooth,
                                           l2=l2, lora_down=lora_down, lora_col_scale=col_scale, up_hl=up_hl,
                                           up_hl_base=up_hl_base,
-                                          w_codes=w_codes, w_scales_t=w_scales_t, bias=bias)
+                                          w16=w16, bias=bias)
         return self._prepared
 
     # ------------------------------------------------------------------ forward
@@ -223,15 +222,16 @@ class SVDQuantLinear(nn.Module):
         if p.k_in != k_orig or x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
             x2 = _pad_cols(x2, p.k_in).contiguous()
         out_fp32 = self.output_fp32 or x.dtype == torch.float32
-        if self.backend is BackendKind.B200_W4A16:
-            raise NotImplementedError("b200_w4a16 backend is not built yet")
         lora_down = p.lora_down if include_lora else None
         col_scale = p.lora_col_scale if include_lora else None
         up_hl = p.up_hl if include_lora else p.up_hl_base
-        codes, scales_t, mid, _, _ = ops.act_quant(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
-                                                   self.act_group_size, True, False)
-        y = ops.w4a4_gemm(codes, scales_t, p.w_codes, p.w_scales_t, mid if mid.numel() else None,
-                          up_hl if mid.numel() else None, p.bias, out_fp32)
+        if self.backend is BackendKind.B200_W4A16:
+            a16, mid = ops.w4a16_prep(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad)
+        else:
+            a16, mid, _, _ = ops.act_quant(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
+                                           self.act_group_size, True, False)
+        y = ops.linear_gemm(a16, p.w16, mid if mid.numel() else None, up_hl if mid.numel() else None,
+                            p.bias, out_fp32)
         return y.reshape(*lead, n)
 
     def _forward_base(self, x: torch.Tensor) -> torch.Tensor:

@@ -49,73 +49,94 @@ def lowrank_width(r_tot: int) -> int:
 _DT = {torch.bfloat16: _lib.SVDQ_BF16, torch.float16: _lib.SVDQ_FP16, torch.float32: _lib.SVDQ_FP32}
 
 
-# --------------------------------------------------------------------------- act_quant
+# --------------------------------------------------------------------------- activation passes
+def _lowrank_args(l2, lora_down):
+    rank = 0 if l2 is None else l2.shape[0]
+    lrank = 0 if lora_down is None else lora_down.shape[0]
+    return rank, lrank, lowrank_width(rank + lrank)
+
+
 @torch.library.custom_op("svdq_b200::act_quant", mutates_args=())
 def act_quant(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Optional[Tensor],
-              lora_col_scale: Optional[Tensor], k_pad: int, a_group: int, emit_gemm: bool,
-              emit_packed: bool) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
-    """Smoothing + dynamic INT4 activation quantization + low-rank down-projection.
+              lora_col_scale: Optional[Tensor], k_pad: int, a_group: int, emit_a16: bool,
+              emit_packed: bool) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """W4A4 activation pass: smoothing, dynamic INT4 quantization, low-rank down-projection.
 
-    Returns ``(codes_e4m3 [M,K_pad] u8, scales_t [K_pad/64, ld] f32, mid_hl [M,R2] bf16,
-    packed [M,K_pad/2] u8, scales [M,K_pad/a_group] bf16)``; outputs that were not
-    requested are empty.  ``packed``/``scales`` are bit-exact with
-    ``pack_int4(quantize_symmetric_int4(x / smooth, a_group))`` of the reference.
+    Returns ``(a16 [M,K_pad] fp16, mid_hl [M,R2] bf16, packed [M,K_pad/2] u8,
+    scales [M,K_pad/a_group] bf16)``; outputs that were not requested are empty.
+    ``packed``/``scales`` are bit-exact with ``pack_int4(quantize_symmetric_int4(x / smooth,
+    a_group))`` of the reference; ``a16`` holds ``q * scale`` exactly.
     """
     _need_cuda("act_quant", x, smooth, l2, lora_down, lora_col_scale)
     _need(x.dim() == 2 and x.dtype == torch.bfloat16, "act_quant: x must be a 2-D bf16 tensor")
     _need(x.stride(1) == 1, "act_quant: x must have unit column stride")
     m, k_in = x.shape
-    rank = 0 if l2 is None else l2.shape[0]
-    lrank = 0 if lora_down is None else lora_down.shape[0]
-    r_tot = rank + lrank
-    r2 = lowrank_width(r_tot)
+    rank, lrank, r2 = _lowrank_args(l2, lora_down)
     dev = x.device
-    codes = torch.empty((m, k_pad) if emit_gemm else (0,), dtype=torch.uint8, device=dev)
-    ld_ast = round_up(max(m, 1), 4)
-    scales_t = torch.empty((k_pad // 64, ld_ast) if emit_gemm else (0,), dtype=torch.float32, device=dev)
-    mid = torch.empty((m, r2) if (emit_gemm and r2) else (0,), dtype=torch.bfloat16, device=dev)
+    a16 = torch.empty((m, k_pad) if emit_a16 else (0,), dtype=torch.float16, device=dev)
+    mid = torch.empty((m, r2) if (emit_a16 and r2) else (0,), dtype=torch.bfloat16, device=dev)
     packed = torch.empty((m, k_pad // 2) if emit_packed else (0,), dtype=torch.uint8, device=dev)
     scales = torch.empty((m, k_pad // a_group) if emit_packed else (0,), dtype=torch.bfloat16, device=dev)
     _lib.call("svdq_act_quant", _p(x), x.stride(0), _p(smooth), _p(l2), rank, _p(lora_down),
-              _p(lora_col_scale), lrank, m, k_in, k_pad, a_group, _p(packed), _p(scales), _p(codes),
-              _p(scales_t), ld_ast, _p(mid), r2, _stream(dev))
-    return codes, scales_t, mid, packed, scales
+              _p(lora_col_scale), lrank, m, k_in, k_pad, a_group, _p(packed), _p(scales), _p(a16),
+              _p(mid), r2, _stream(dev))
+    return a16, mid, packed, scales
 
 
 @act_quant.register_fake
-def _(x, smooth, l2, lora_down, lora_col_scale, k_pad, a_group, emit_gemm, emit_packed):
+def _(x, smooth, l2, lora_down, lora_col_scale, k_pad, a_group, emit_a16, emit_packed):
     m = x.shape[0]
-    r_tot = (0 if l2 is None else l2.shape[0]) + (0 if lora_down is None else lora_down.shape[0])
-    r2 = lowrank_width(r_tot)
+    _, _, r2 = _lowrank_args(l2, lora_down)
     e = x.new_empty
-    return (e((m, k_pad) if emit_gemm else (0,), dtype=torch.uint8),
-            e((k_pad // 64, round_up(max(m, 1), 4)) if emit_gemm else (0,), dtype=torch.float32),
-            e((m, r2) if (emit_gemm and r2) else (0,), dtype=torch.bfloat16),
+    return (e((m, k_pad) if emit_a16 else (0,), dtype=torch.float16),
+            e((m, r2) if (emit_a16 and r2) else (0,), dtype=torch.bfloat16),
             e((m, k_pad // 2) if emit_packed else (0,), dtype=torch.uint8),
             e((m, k_pad // a_group) if emit_packed else (0,), dtype=torch.bfloat16))
 
 
-# --------------------------------------------------------------------------- repack
+@torch.library.custom_op("svdq_b200::w4a16_prep", mutates_args=())
+def w4a16_prep(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Optional[Tensor],
+               lora_col_scale: Optional[Tensor], k_pad: int) -> tuple[Tensor, Tensor]:
+    """W4A16 activation pass: ``a16 = fp16(x / smooth)`` (fp32 division) and the low-rank
+    down-projection.  Returns ``(a16 [M,K_pad] fp16, mid_hl [M,R2] bf16)``."""
+    _need_cuda("w4a16_prep", x, smooth, l2, lora_down, lora_col_scale)
+    _need(x.dim() == 2 and x.dtype == torch.bfloat16, "w4a16_prep: x must be a 2-D bf16 tensor")
+    _need(x.stride(1) == 1, "w4a16_prep: x must have unit column stride")
+    m, k_in = x.shape
+    rank, lrank, r2 = _lowrank_args(l2, lora_down)
+    a16 = torch.empty((m, k_pad), dtype=torch.float16, device=x.device)
+    mid = torch.empty((m, r2) if r2 else (0,), dtype=torch.bfloat16, device=x.device)
+    _lib.call("svdq_w4a16_prep", _p(x), x.stride(0), _p(smooth), _p(l2), rank, _p(lora_down),
+              _p(lora_col_scale), lrank, m, k_in, k_pad, _p(a16), _p(mid), r2, _stream(x.device))
+    return a16, mid
+
+
+@w4a16_prep.register_fake
+def _(x, smooth, l2, lora_down, lora_col_scale, k_pad):
+    m = x.shape[0]
+    _, _, r2 = _lowrank_args(l2, lora_down)
+    return (x.new_empty((m, k_pad), dtype=torch.float16),
+            x.new_empty((m, r2) if r2 else (0,), dtype=torch.bfloat16))
+
+
+# --------------------------------------------------------------------------- load-time operands
 @torch.library.custom_op("svdq_b200::repack_weight", mutates_args=())
-def repack_weight(qweight: Tensor, scales: Tensor, w_group: int) -> tuple[Tensor, Tensor]:
-    """Checkpoint INT4 weight -> (e4m3 codes [N, K_pad] u8, fp32 scales^T [K_pad/64, N])."""
+def repack_weight(qweight: Tensor, scales: Tensor, w_group: int) -> Tensor:
+    """Checkpoint INT4 weight -> ``w16 [N, K_pad]`` fp16 = q * scale."""
     _need_cuda("repack_weight", qweight, scales)
     _need(qweight.dtype == torch.uint8 and qweight.dim() == 2 and qweight.is_contiguous(),
           "repack_weight: qweight must be contiguous uint8 [N, K_pad/2]")
     _need(scales.dtype in _DT and scales.is_contiguous(), "repack_weight: scales must be contiguous bf16/fp16/fp32")
     n, k_pad = qweight.shape[0], qweight.shape[1] * 2
-    codes = torch.empty((n, k_pad), dtype=torch.uint8, device=qweight.device)
-    sw_t = torch.empty((k_pad // 64, n), dtype=torch.float32, device=qweight.device)
-    _lib.call("svdq_repack_weight", _p(qweight), _p(scales), _DT[scales.dtype], n, k_pad, w_group,
-              _p(codes), _p(sw_t), _stream(qweight.device))
-    return codes, sw_t
+    w16 = torch.empty((n, k_pad), dtype=torch.float16, device=qweight.device)
+    _lib.call("svdq_repack_weight", _p(qweight), _p(scales), _DT[scales.dtype], n, k_pad, w_group, _p(w16),
+              _stream(qweight.device))
+    return w16
 
 
 @repack_weight.register_fake
 def _(qweight, scales, w_group):
-    n, k_pad = qweight.shape[0], qweight.shape[1] * 2
-    return (qweight.new_empty((n, k_pad), dtype=torch.uint8),
-            qweight.new_empty((k_pad // 64, n), dtype=torch.float32))
+    return qweight.new_empty((qweight.shape[0], qweight.shape[1] * 2), dtype=torch.float16)
 
 
 @torch.library.custom_op("svdq_b200::build_up_hl", mutates_args=())
@@ -134,27 +155,25 @@ def _(l1, lora_up, r2):
     return l1.new_empty((l1.shape[0], r2), dtype=torch.bfloat16)
 
 
-# --------------------------------------------------------------------------- W4A4 GEMM
-@torch.library.custom_op("svdq_b200::w4a4_gemm", mutates_args=())
-def w4a4_gemm(codes: Tensor, scales_t: Tensor, w_codes: Tensor, w_scales_t: Tensor,
-              mid_hl: Optional[Tensor], up_hl: Optional[Tensor], bias: Optional[Tensor],
-              out_fp32: bool) -> Tensor:
-    """Fused W4A4 residual GEMM + low-rank/LoRA up-projection + bias (tcgen05)."""
-    _need_cuda("w4a4_gemm", codes, scales_t, w_codes, w_scales_t, mid_hl, up_hl, bias)
-    m, k_pad = codes.shape
-    n = w_codes.shape[0]
-    _need(w_codes.shape[1] == k_pad, "w4a4_gemm: activation / weight K mismatch")
+# --------------------------------------------------------------------------- GEMM
+@torch.library.custom_op("svdq_b200::linear_gemm", mutates_args=())
+def linear_gemm(a16: Tensor, w16: Tensor, mid_hl: Optional[Tensor], up_hl: Optional[Tensor],
+                bias: Optional[Tensor], out_fp32: bool) -> Tensor:
+    """``a16 @ w16^T + mid_hl @ up_hl^T + bias`` on tcgen05 CTA pairs (fp32 accumulation)."""
+    _need_cuda("linear_gemm", a16, w16, mid_hl, up_hl, bias)
+    _need(a16.dtype == torch.float16 and w16.dtype == torch.float16, "linear_gemm: a16/w16 must be fp16")
+    m, k_pad = a16.shape
+    n = w16.shape[0]
+    _need(w16.shape[1] == k_pad, "linear_gemm: activation / weight K mismatch")
     r2 = 0 if mid_hl is None or mid_hl.numel() == 0 else mid_hl.shape[1]
-    _need(r2 == 0 or (up_hl is not None and up_hl.shape == (n, r2)), "w4a4_gemm: up_hl shape mismatch")
-    out = torch.empty((m, n), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=codes.device)
-    _lib.call("svdq_w4a4_gemm", _p(codes), _p(scales_t), scales_t.shape[1], _p(w_codes), _p(w_scales_t),
-              _p(mid_hl) if r2 else None, _p(up_hl) if r2 else None, r2, _p(bias), _p(out),
-              _lib.SVDQ_FP32 if out_fp32 else _lib.SVDQ_BF16, out.stride(0), m, n, k_pad,
-              _stream(codes.device))
+    _need(r2 == 0 or (up_hl is not None and tuple(up_hl.shape) == (n, r2)), "linear_gemm: up_hl shape mismatch")
+    out = torch.empty((m, n), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=a16.device)
+    _lib.call("svdq_linear_gemm", _p(a16), _p(w16), _p(mid_hl) if r2 else None, _p(up_hl) if r2 else None, r2,
+              _p(bias), _p(out), _lib.SVDQ_FP32 if out_fp32 else _lib.SVDQ_BF16, out.stride(0), m, n, k_pad,
+              _stream(a16.device))
     return out
 
 
-@w4a4_gemm.register_fake
-def _(codes, scales_t, w_codes, w_scales_t, mid_hl, up_hl, bias, out_fp32):
-    return codes.new_empty((codes.shape[0], w_codes.shape[0]),
-                           dtype=torch.float32 if out_fp32 else torch.bfloat16)
+@linear_gemm.register_fake
+def _(a16, w16, mid_hl, up_hl, bias, out_fp32):
+    return a16.new_empty((a16.shape[0], w16.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)

@@ -27,8 +27,8 @@ def lib():
 
 def test_header_declares_entry_points():
     names = declared_functions()
-    for must in ("svdq_act_quant", "svdq_w4a4_gemm", "svdq_repack_weight", "svdq_build_up_hl",
-                 "svdq_last_error", "svdq_device_error"):
+    for must in ("svdq_act_quant", "svdq_w4a16_prep", "svdq_linear_gemm", "svdq_repack_weight",
+                 "svdq_build_up_hl", "svdq_last_error", "svdq_device_error"):
         assert must in names
 
 
@@ -54,8 +54,11 @@ def test_invalid_arguments_rejected_without_gpu():
     from krea2_svdquant_b200 import _lib
     L = _lib.lib()
     st = L.svdq_act_quant(ctypes.c_void_p(16), 8, ctypes.c_void_p(16), None, 0, None, None, 0,
-                          4, 8, 64, 96, None, None, None, None, 4, None, 0, None)
+                          4, 8, 64, 96, None, None, None, None, 0, None)
     assert st == 1
     assert "a_group" in L.svdq_last_error().decode()
-    st = L.svdq_w4a4_gemm(None, None, 4, None, None, None, None, 0, None, None, 0, 8, 4, 8, 64, None)
+    st = L.svdq_linear_gemm(None, None, None, None, 0, None, None, 0, 8, 4, 8, 64, None)
     assert st == 1
+    st = L.svdq_linear_gemm(ctypes.c_void_p(256), ctypes.c_void_p(256), None, None, 0, None, ctypes.c_void_p(256),
+                            0, 8, 4, 8, 96, None)
+    assert st == 1 and "K_pad" in L.svdq_last_error().decode()

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from oracle import svdq_oracle as O
-from tests._helpers import (bf16_tensor, e4m3_decode, golden_state, staged_oracle, state_numpy)
+from tests._helpers import bf16_tensor, golden_state, staged_oracle, state_numpy
 
 pytestmark = pytest.mark.gpu
 
@@ -33,6 +33,10 @@ def _act(x, smooth, l2=None, lora_down=None, col_scale=None, k_pad=None, a_group
     return ops.act_quant(x, smooth, l2, lora_down, col_scale, k_pad, a_group, True, packed)
 
 
+def _dequant_np(q, scales, group):
+    return (q.astype(np.float32).reshape(q.shape[0], -1, group) * scales[:, :, None]).reshape(q.shape)
+
+
 def _pad8(x: torch.Tensor, value: float = 0.0) -> torch.Tensor:
     k = x.shape[-1]
     k8 = (k + 7) // 8 * 8
@@ -48,17 +52,13 @@ def test_act_quant_bit_exact_vs_reference(golden, case, ag):
     x = _pad8(bf16_tensor(g["x"]))
     s = _pad8(bf16_tensor(g["smooth"]), 1.0)
     l2 = _pad8(bf16_tensor(g["l2"]))
-    codes, sat, mid, packed, scales = _act(x, s, l2, k_pad=k_pad, a_group=ag)
+    a16, mid, packed, scales = _act(x, s, l2, k_pad=k_pad, a_group=ag)
     torch.cuda.synchronize()
-    m = x.shape[0]
     assert np.array_equal(packed.cpu().numpy(), g[f"act_packed_g{ag}"])
     assert np.array_equal(scales.view(torch.int16).cpu().numpy().view(np.uint16), g[f"act_scale_g{ag}__bits"])
-    # e4m3 GEMM codes hold the same integers; scales^T hold the same scale per 64-group
-    q = e4m3_decode(codes.cpu().numpy())
-    assert np.array_equal(q.astype(np.int8), g[f"act_q_g{ag}"])
-    sat_np = sat.cpu().numpy()[:, :m]
-    sc = g[f"act_scale_g{ag}"]
-    assert np.array_equal(sat_np, np.repeat(sc, ag // 64, axis=1).T)
+    # the fp16 GEMM operand holds q * scale exactly
+    deq = _dequant_np(g[f"act_q_g{ag}"], g[f"act_scale_g{ag}"], ag)
+    assert np.array_equal(a16.float().cpu().numpy(), deq)
     # hi/lo mid against float64 x_hat @ l2^T
     r = g["l2"].shape[0]
     mid_np = mid.float().cpu().numpy()
@@ -72,7 +72,7 @@ def test_act_quant_edges_bit_exact(golden):
     g = golden("quant_edges")
     x = bf16_tensor(g["x"])
     ones = torch.ones(x.shape[1], dtype=torch.bfloat16, device="cuda")
-    codes, sat, mid, packed, scales = _act(x, ones, k_pad=64)
+    a16, mid, packed, scales = _act(x, ones, k_pad=64)
     torch.cuda.synchronize()
     assert np.array_equal(packed.cpu().numpy(), g["packed"])
     assert np.array_equal(scales.view(torch.int16).cpu().numpy().view(np.uint16), g["scales__bits"])
@@ -86,11 +86,11 @@ def test_act_quant_ragged_rows_and_lora():
     l2 = (torch.randn(r, k) * 0.05).bfloat16().cuda()
     a = (torch.randn(rl, k) * 0.05).bfloat16().cuda()
     cs = torch.full((rl,), 0.7, device="cuda")
-    codes, sat, mid, packed, scales = _act(x, s, l2, a, cs, k_pad=320)
+    a16, mid, packed, scales = _act(x, s, l2, a, cs, k_pad=320)
     torch.cuda.synchronize()
     xh, q, pk, sa = O.act_quant(x.float().cpu().numpy(), s.float().cpu().numpy(), 64)
     assert np.array_equal(packed.cpu().numpy(), pk)
-    assert np.array_equal(e4m3_decode(codes.cpu().numpy()).astype(np.int8), q)
+    assert np.array_equal(a16.float().cpu().numpy()[:37], _dequant_np(q, sa, 64))
     mid_np = mid.float().cpu().numpy()
     rt = r + rl
     got = mid_np[:, :rt] + mid_np[:, rt:2 * rt]
@@ -104,12 +104,14 @@ def test_repack_weight(golden, case):
     from krea2_svdquant_b200 import ops
     g = golden(case)
     st = golden_state(g)
-    codes, sw_t = ops.repack_weight(st.qweight, st.weight_scales, st.group_size)
+    w16 = ops.repack_weight(st.qweight, st.weight_scales, st.group_size)
     torch.cuda.synchronize()
     q = O.unpack_int4(g["qweight"], int(g["k_pad"]))
-    assert np.array_equal(e4m3_decode(codes.cpu().numpy()).astype(np.int8), q)
-    ratio = int(g["group"]) // 64
-    assert np.array_equal(sw_t.cpu().numpy(), np.repeat(g["weight_scales"], ratio, axis=1).T)
+    exact = _dequant_np(q, g["weight_scales"], int(g["group"]))
+    # fp16(q * scale): exact for bf16 scales, one round-to-nearest for fp16 scales
+    assert np.array_equal(w16.float().cpu().numpy(), exact.astype(np.float16).astype(np.float32))
+    if "weight_scales__fp16raw" not in g:
+        assert np.array_equal(w16.float().cpu().numpy(), exact)
 
 
 def _linear_vs_oracle(st, x, loras=(), a_group=64):
@@ -204,7 +206,7 @@ def test_w4a4_full_size_config2_vs_torch_fp32():
     mod.output_fp32 = True
     y = mod(x)
     p = mod.prepare()
-    codes, sat, mid, packed, scales = ops.act_quant(x, p.smooth, p.l2, None, None, p.k_pad, 64, True, True)
+    a16, mid, packed, scales = ops.act_quant(x, p.smooth, p.l2, None, None, p.k_pad, 64, True, True)
     torch.backends.cuda.matmul.allow_tf32 = False
     # dequantized operands in fp32 (exact)
     lo = (packed & 0xF).to(torch.int16) - 8
