@@ -62,8 +62,18 @@ const char* svdq_version(void);
  * In-kernel bounded waits record the place they gave up in a device-side
  * word instead of hanging.  Reads (and optionally clears) that word on the
  * current device; synchronizes the device.  *code == 0 means no failure.
+ * Codes: 0x101-0x301 GEMM waits, 0x41xx activation-pass waits, 0x4200 an
+ * activation group scale above 65504/7 (the fp16 GEMM operand a16 overflowed);
+ * the first failure since the last clear is kept.
  */
 int svdq_device_error(int* code, int clear);
+
+/*
+ * Device workspace (bytes) the activation passes need for the low-rank
+ * down-projection: fp32 partial sums of K slices, combined in a fixed order
+ * by a second launch.  0 when rank + lora_rank == 0 or mid is not requested.
+ */
+size_t svdq_act_quant_workspace_bytes(int M, int K_pad, int rank, int lora_rank);
 
 /*
  * Activation pass of the W4A4 linear.  Replaces, on the device, the reference's
@@ -72,30 +82,38 @@ int svdq_device_error(int* code, int clear);
  *   F.linear(x_hat, l2)                                 (svd.py:159, low-rank down)
  *   F.linear(x, lora_down) * multiplier                 (src/krea2_svdquant/runtime/linear.py:38-45)
  * in one pass over x.  Codes, packing and scales are bit-exact with the
- * reference.  Optional outputs may be NULL: out_packed / out_scales (the
+ * reference.  a16 = q * scale is exact while every group scale lies in
+ * [2^-17, 65504/7] (group max |x_hat| up to ~65000); larger scales overflow
+ * fp16 and are reported through svdq_device_error (code 0x4200).  Optional outputs may be NULL: out_packed / out_scales (the
  * reference-format codes), out_a16 (the GEMM operand), out_mid_hl (needs
- * rank + lora_rank > 0).
- *   a_group in {64, 128}; K_in <= K_pad; K_pad % a_group == 0; K_in % 8 == 0;
- *   rank % 8 == 0, lora_rank % 8 == 0, rank + lora_rank <= 256; ldx % 8 == 0.
+ * rank + lora_rank > 0 and a workspace of svdq_act_quant_workspace_bytes()).
+ * out_packed and out_scales are written together (both NULL or both set).
+ *   a_group in {64, 128}; K_in <= K_pad; K_pad % 64 == 0; K_pad % a_group == 0;
+ *   K_in % 8 == 0; rank % 8 == 0, lora_rank % 8 == 0, rank + lora_rank <= 256;
+ *   ldx % 8 == 0; all pointers 16-byte aligned.
  */
 int svdq_act_quant(const void* x, int64_t ldx, const void* smooth,
                    const void* l2, int rank,
                    const void* lora_down, const float* lora_col_scale, int lora_rank,
                    int M, int K_in, int K_pad, int a_group,
                    void* out_packed, void* out_scales, void* out_a16,
-                   void* out_mid_hl, int R2, cudaStream_t stream);
+                   void* out_mid_hl, int R2,
+                   void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
  * Activation pass of the W4A16 linear: a16 = fp16(fp32(x) / fp32(smooth)) and
  * the low-rank/LoRA down-projection.  Replaces x / smooth and F.linear(x_hat, l2)
  * of the reference's float run (svd.py:122, 159) and the smoothing done by
- * kernels/triton/generic_int4.py:169-191.  Same constraints as svdq_act_quant.
+ * kernels/triton/generic_int4.py:169-191.  l2_f16 is l2 [rank, K_in] in fp16
+ * (converted once at load; the product x_hat @ l2^T runs on fp16 MMAs).
+ * Same constraints as svdq_act_quant.
  */
 int svdq_w4a16_prep(const void* x, int64_t ldx, const void* smooth,
-                    const void* l2, int rank,
+                    const void* l2_f16, int rank,
                     const void* lora_down, const float* lora_col_scale, int lora_rank,
                     int M, int K_in, int K_pad,
-                    void* out_a16, void* out_mid_hl, int R2, cudaStream_t stream);
+                    void* out_a16, void* out_mid_hl, int R2,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
  * Load-time weight preparation: packed INT4 qweight [N, K_pad/2] + group scales

@@ -24,11 +24,13 @@ SIGNATURES = {
     "svdq_last_error": ([], ctypes.c_char_p),
     "svdq_version": ([], ctypes.c_char_p),
     "svdq_device_error": ([ctypes.POINTER(c_int), c_int], c_int),
+    "svdq_act_quant_workspace_bytes": ([c_int, c_int, c_int, c_int], ctypes.c_size_t),
     "svdq_act_quant": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
                         c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
-                        c_void_p], c_int),
+                        c_void_p, ctypes.c_size_t, c_void_p], c_int),
     "svdq_w4a16_prep": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
-                         c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p], c_int),
+                         c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p, ctypes.c_size_t,
+                         c_void_p], c_int),
     "svdq_repack_weight": ([c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p], c_int),
     "svdq_build_up_hl": ([c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p], c_int),
     "svdq_linear_gemm": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,

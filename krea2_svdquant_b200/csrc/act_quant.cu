@@ -1,407 +1,512 @@
 // Activation pass of the SVDQuant linear (sm_100a).
 //
-// W4A4 mode: one pass over x [M, K_in] bf16 produces, per 32-row band and
-// 128-column chunk:
+// W4A4 mode, per element of x [M, K_in] bf16:
 //   x_hat = bf16(x / smooth)                             (svd.py:122)
-//   q     = clamp(rint(x_hat / scale), -8, 7) per group  (pack.py:6-23)
-//   scale = bf16(max(amax, bf16(1e-8)) / 7)              (pack.py:20)
-//   packed nibbles (q + 8, even k low)                   (pack.py:47-56)
-//   a16   = fp16(q * scale): the dequantized activation, exact in fp16
+//   scale = bf16(max(amax_group(x_hat), bf16(1e-8)) / 7) (pack.py:20)
+//   q     = clamp(rint(x_hat / scale), -8, 7)            (pack.py:6-23)
+//   packed nibble q + 8, even k in the low nibble        (pack.py:47-56)   [optional output]
+//   a16   = fp16(q * scale): the dequantized activation, exact in fp16 (GEMM operand)
 //   mid   = [x_hat @ l2^T | (x @ lora_down^T) * col_scale] (svd.py:159, linear.py:45)
-//           written as a bf16 hi/lo pair so the GEMM's bf16 MMA keeps ~16 mantissa bits.
-// W4A16 mode: a16 = fp16(fp32(x) / fp32(smooth)) (the reference run in fp32,
-// svd.py:122 on float inputs) and mid from the fp16 x_hat against l2 converted
-// to fp16 (exact for bf16 values in fp16 range).
-// The down-projection runs on mma.sync tensor cores from shared memory; loads
-// are a cp.async ring of 128-column chunks.
+// W4A16 mode: a16 = fp16(fp32(x) / fp32(smooth)) (the reference's fp32 run of
+// svd.py:122) and mid from that fp16 x_hat against l2 given in fp16.
 //
-// W4A4 divisions must round exactly like float32 IEEE division followed by the
-// reference's rounding (bf16 for x_hat, rint for q).  Each quotient is first
-// formed as a product with the correctly rounded reciprocal; that product is
-// within 2 ulp of the correctly rounded quotient, so the final rounding can
-// only differ when the product lies within a few ulp of a rounding boundary
-// (a bf16 midpoint, or a half-integer).  Those rare elements are recomputed
-// with the IEEE division intrinsic __fdiv_rn.
-#include <cuda_fp8.h>
+// Work decomposition.  A CTA owns 64 rows x one K slice (a whole number of
+// 64-column stages) x up to 64 low-rank columns; each of its 4 warps owns 16
+// rows.  TMA brings each stage's x tile (64 x 64) and low-rank rows (8-row
+// boxes) into a ring of shared-memory stages with 128-byte swizzle.  A warp
+// loads its 16 x 64 x tile straight into mma.sync A-fragment registers with
+// ldmatrix and does all per-element work on those registers: the LoRA
+// down-projection MMAs on raw x, the division and group quantization, the
+// l2 MMAs on x_hat.  a16 leaves through stmatrix into a per-warp swizzled
+// staging tile and a TMA store.  Whichever warp releases a stage last refills
+// it, so no warp waits on another except through the data itself.
+// Low-rank sums of a K slice go to an fp32 workspace; a second launch adds the
+// slices in a fixed order (deterministic) and writes the bf16 hi/lo mid.
+//
+// Exact division without a data-dependent slow path: with y = RN(1/b)
+// (__frcp_rn), q0 = RN(a*y), r = fma(-q0, b, a) (exact), q1 = RN(q0 + r*y)
+// (Markstein's correction, P. Markstein, IBM J. R&D 34(1), 1990) is the
+// correctly rounded quotient RN(a/b).  For bf16 operands this was checked
+// exhaustively against IEEE division on sm_100a: the bf16-rounded x_hat agrees
+// for every finite x with |x| >= 2^-118 or x == 0 and every normal smooth
+// whose quotient stays below 2^126; rint(x_hat / scale) and the /7 of the scale
+// agree for all bf16 inputs with a normal scale (the scale is >= 1.4e-9).
+#include <algorithm>
 
 #include "svdq_common.cuh"
 
 namespace svdq {
 namespace {
 
-constexpr int kBM = 32;         // rows per CTA
-constexpr int kThreads = 512;   // 16 warps
-constexpr int kChunk = 128;     // columns per pipeline stage
-constexpr int kLD = kChunk + 8; // padded smem row (bf16) so ldmatrix rows hit distinct banks
-constexpr int kTilesPerWarp = 4;  // 8 column-tile sets x 4 tiles x 8 columns: r_tot <= 256
+constexpr int kWarps = 4;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kBM = 64;              // rows per CTA (16 per warp)
+constexpr int kBK = 64;              // columns per stage: one 128-byte swizzle row of bf16
+constexpr int kMaxSliceStages = 16;  // stages per CTA slice (bounds the reciprocal table)
+constexpr int kMinSliceStages = 2;
+constexpr int kTargetCtasPerSm = 4;
+constexpr uint32_t kXTileBytes = kBM * kBK * 2;   // 8 KB
+constexpr uint32_t kLrTileBytes = 8 * kBK * 2;    // 1 KB: 8 low-rank rows
+constexpr uint32_t kOutTileBytes = 16 * kBK * 2;  // 2 KB: one warp's a16 tile
+// a16 = q * scale is exact in fp16 while the group scale lies in [2^-17, 65504 / 7]:
+// above it a16 overflows (recorded as kErrA16Range in the device error word),
+// below it the smallest codes round in fp16's subnormal range (absolute error < 2^-25).
+constexpr float kA16ScaleMax = 65504.0f / 7.0f;
+constexpr int kErrA16Range = 0x4200;
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
-               : "memory");
+// ---- fragment-level helpers ----
+__device__ __forceinline__ uint32_t swz128(int row, int chunk) {
+  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
-__device__ __forceinline__ void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
-               : "=r"(r0), "=r"(r1)
-               : "r"(addr));
+__device__ __forceinline__ void stmatrix_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r0), "r"(r1),
+               "r"(r2), "r"(r3)
+               : "memory");
 }
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
-                                               uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-      "{%8, %9}, {%0, %1, %2, %3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+template <bool F16>
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (F16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+// bf16x2 register (low half = lower column) -> {lo, hi} fp32 pair
+__device__ __forceinline__ uint64_t bf2_to_f2(uint32_t v) {
+  return f2_pack(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+}
+__device__ __forceinline__ uint32_t f2_to_bf2(uint64_t v) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(f2_hi(v)), "f"(f2_lo(v)));
+  return d;
+}
+__device__ __forceinline__ uint32_t f2_to_h2(uint64_t v) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(f2_hi(v)), "f"(f2_lo(v)));
+  return d;
+}
+// Correctly rounded a / b for a pair, given y = RN(1/b) and nb = -b (Markstein).
+__device__ __forceinline__ uint64_t div_f2(uint64_t a, uint64_t y, uint64_t nb) {
+  const uint64_t q0 = f2_mul(a, y);
+  const uint64_t r = f2_fma(q0, nb, a);
+  return f2_fma(r, y, q0);
+}
+// running max of |.| over bf16x2 lanes (the sign bit of the result is meaningless)
+__device__ __forceinline__ uint32_t bf2_maxabs(uint32_t m, uint32_t v) {
+  uint32_t d;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(m), "r"(v));
+  return d;
+}
+__device__ __forceinline__ float bf2_absmax_f(uint32_t m) {
+  return fmaxf(fabsf(__uint_as_float(m << 16)), fabsf(__uint_as_float(m & 0xFFFF0000u)));
 }
 
-__device__ __forceinline__ void mma_f16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-      "{%8, %9}, {%0, %1, %2, %3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Near-boundary tests for the reciprocal-product quotients (see file comment).
-// bf16 rounding of a float32 depends on its low 16 bits against 0x8000; a
-// product within 2.5 ulp of the exact quotient can only round differently when
-// its low bits are within 8 of 0x8000.
-__device__ __forceinline__ bool near_bf16_midpoint(float t) {
-  return ((__float_as_uint(t) & 0xFFFFu) - 0x7FF8u) < 0x10u;
-}
-// rint of a value below 8 in magnitude: the product is within 2.5 * 2^-21 of the
-// exact quotient, so rint can only differ when it lies within 2^-19 of a half-integer.
-__device__ __forceinline__ bool near_half_integer(float t, float r) {
-  return 0.5f - fabsf(t - r) < 1.9073486e-06f;
-}
-
-struct ActQuantParams {
-  const __nv_bfloat16* x;
-  int64_t ldx;
-  const __nv_bfloat16* smooth;
-  const __nv_bfloat16* l2;     // [rank, K_in]
-  const __nv_bfloat16* lora;   // [lora_rank, K_in]
-  const float* lora_col_scale; // [lora_rank]
-  int rank, lora_rank;
+struct AqArgs {
   int M, K_in, K_pad;
-  uint8_t* packed;             // [M, K_pad/2]
-  __nv_bfloat16* scales;       // [M, K_pad/G]
-  __half* a16;                 // [M, K_pad] fp16 GEMM operand
-  __nv_bfloat16* mid_hl;       // [M, R2]
-  int R2;
+  int rank, lora_rank, r_tot;
+  int n_stages;      // K_pad / 64
+  int slice_stages;  // stages per CTA along K (the last slice may be shorter)
+  int G;             // quantization group (W4A4)
+  int write_a16;
+  const __nv_bfloat16* smooth;
+  uint8_t* packed;        // [M, K_pad/2] or null
+  __nv_bfloat16* scales;  // [M, K_pad/G] or null
+  float* partial;         // [ksplit, M, r_tot] or null
+  int* err;
 };
 
-template <int G, int STAGES, bool W4A16>
-__global__ void __launch_bounds__(kThreads) act_quant_kernel(const ActQuantParams p) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  const int r_tot = p.rank + p.lora_rank;
-  const int n_chunks = (p.K_pad + kChunk - 1) / kChunk;
-  // layout: rsm[n_chunks * kChunk] fp32 (1/smooth), xs[STAGES][kBM][kLD], ws[STAGES][r_tot][kLD], xh[kBM][kLD]
-  float* rsm = reinterpret_cast<float*>(smem_raw);
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rsm + n_chunks * kChunk);
-  __nv_bfloat16* ws = xs + STAGES * kBM * kLD;
-  __nv_bfloat16* xh = ws + STAGES * r_tot * kLD;
+struct AqSmem {
+  uint32_t xs, ws, ost, rst, bars;  // shared addresses
+};
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+template <int STAGES, int NT>
+__host__ __device__ constexpr uint32_t aq_smem_layout_bytes() {
+  return 1024 /*align slack*/ + STAGES * kXTileBytes + STAGES * NT * kLrTileBytes + kWarps * kOutTileBytes +
+         kMaxSliceStages * 32 * 16 /*reciprocal table*/ + 256 /*barriers, counters*/;
+}
+
+// GS: stages per quantization group (1: G=64, 2: G=128).  NT: 8-column
+// low-rank tiles per CTA (0: no mid).  PACKED: also write reference-format
+// codes and scales.
+template <int GS, int STAGES, int NT, bool W4A16, bool PACKED>
+__global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
+    act_quant_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_l2,
+                     const __grid_constant__ CUtensorMap tm_lora, const __grid_constant__ CUtensorMap tm_a16,
+                     const AqArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t xs = base;
+  const uint32_t ws = xs + STAGES * kXTileBytes;
+  const uint32_t ost = ws + STAGES * NT * kLrTileBytes;
+  const uint32_t rst = ost + kWarps * kOutTileBytes;
+  const uint32_t bars = rst + kMaxSliceStages * 32 * 16;
+  uint8_t* gbase = smem_raw + (base - smem_u32(smem_raw));
+  const float4* rst_p = reinterpret_cast<const float4*>(gbase + (rst - base));
+  int* cnt = reinterpret_cast<int*>(gbase + (bars - base) + 8 * STAGES);        // releases per stage
+  int* issued = cnt + STAGES;                                                    // loads issued per stage
+  volatile int* abort_flag = issued + STAGES;
+  auto full_bar = [&](int s) { return bars + 8u * (uint32_t)s; };
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
   const int m0 = blockIdx.x * kBM;
+  const int st0 = blockIdx.y * a.slice_stages;
+  const int n_loc = min(a.slice_stages, a.n_stages - st0);
+  const int r0 = blockIdx.z * 8 * NT;
+  const int ntl = NT > 0 ? min(NT, (a.r_tot - r0) / 8) : 0;  // live low-rank tiles of this CTA
+  const bool emit = blockIdx.z == 0 && (a.write_a16 || PACKED);
 
-  auto load_chunk = [&](int c) {
-    const int st = c % STAGES;
-    const int k0 = c * kChunk;
-    constexpr int SEG = kChunk / 8;  // 16-byte segments per row
-    for (int i = tid; i < kBM * SEG; i += kThreads) {
-      const int r = i / SEG, s = i % SEG;
-      const int col = k0 + s * 8, row = m0 + r;
-      int bytes = 0;
-      const __nv_bfloat16* src = p.x;
-      if (row < p.M && col < p.K_in) {
-        bytes = min(16, (p.K_in - col) * 2);
-        src = p.x + (int64_t)row * p.ldx + col;
-      }
-      cp_async16(smem_u32(xs + (st * kBM + r) * kLD + s * 8), src, bytes);
+  auto issue = [&](int s, int c) {
+    const uint32_t bar = full_bar(s);
+    issued[s] += 1;
+    mbar_arrive_expect_tx(bar, kXTileBytes + (uint32_t)ntl * kLrTileBytes);
+    const int kx = (st0 + c) * kBK;
+    tma_load_2d(xs + s * kXTileBytes, &tm_x, bar, kx, m0);
+    for (int t = 0; t < ntl; ++t) {
+      const int r = r0 + 8 * t;
+      const uint32_t dst = ws + (s * NT + t) * kLrTileBytes;
+      if (r < a.rank) tma_load_2d(dst, &tm_l2, bar, kx, r);
+      else tma_load_2d(dst, &tm_lora, bar, kx, r - a.rank);
     }
-    for (int i = tid; i < r_tot * SEG; i += kThreads) {
-      const int r = i / SEG, s = i % SEG;
-      const int col = k0 + s * 8;
-      const __nv_bfloat16* base = r < p.rank ? p.l2 + (int64_t)r * p.K_in
-                                             : p.lora + (int64_t)(r - p.rank) * p.K_in;
-      int bytes = 0;
-      const __nv_bfloat16* src = base;
-      if (col < p.K_in) {
-        bytes = min(16, (p.K_in - col) * 2);
-        src = base + col;
+  };
+
+  if (tid == 0) {
+    prefetch_tma_desc(&tm_x);
+    if (ntl > 0) { prefetch_tma_desc(&tm_l2); prefetch_tma_desc(&tm_lora); }
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      cnt[s] = 0;
+      issued[s] = 0;
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    for (int s = 0; s < STAGES && s < n_loc; ++s) issue(s, s);
+  }
+  // reciprocal table of the slice: {RN(1/s_c), RN(1/s_c+1), -s_c, -s_c+1} per column pair
+  {
+    float4* tbl = reinterpret_cast<float4*>(gbase + (rst - base));
+    for (int i = tid; i < n_loc * (kBK / 2); i += kThreads) {
+      const int col = st0 * kBK + 2 * i;
+      const float s0 = col < a.K_in ? __bfloat162float(a.smooth[col]) : 1.f;
+      const float s1 = col + 1 < a.K_in ? __bfloat162float(a.smooth[col + 1]) : 1.f;
+      tbl[i] = make_float4(__frcp_rn(s0), __frcp_rn(s1), -s0, -s1);
+    }
+  }
+  __syncthreads();
+
+  float acc[NT > 0 ? NT : 1][4];
+#pragma unroll
+  for (int t = 0; t < (NT > 0 ? NT : 1); ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+
+  const float eps = __bfloat162float(__float2bfloat16_rn(1e-8f));
+  const float y7 = __frcp_rn(7.0f);
+  constexpr float kMagic = 12582920.0f;  // 1.5 * 2^23 + 8: rint and the offset-binary code in one add
+  const uint64_t mag2 = f2_pack(kMagic, kMagic), nmag2 = f2_pack(-kMagic, -kMagic);
+  const int wrow = warp * 16;              // first row of this warp within the CTA tile
+  const int row_g = m0 + wrow + g;         // global rows held by this lane
+  const int row_g8 = row_g + 8;
+  const uint32_t my_ost = ost + warp * kOutTileBytes;
+  bool ok = true;
+  bool a16_range = false;  // some group scale of this lane exceeded kA16ScaleMax
+
+  // A-fragment address of k16 block kk for this lane within a 64 x 64 swizzled tile
+  const int a_row = wrow + (lane & 15);
+  const int a_chk = lane >> 4;
+  // B-fragment (two 8-row tiles) address offsets
+  const int b_row = (lane & 7) + ((lane >> 4) << 3);
+  const int b_chk = (lane >> 3) & 1;
+
+  auto lowrank_mma = [&](const uint32_t (&fr)[4][4], int s, bool lora_pass) {
+    if constexpr (NT > 0) {
+#pragma unroll
+      for (int t = 0; t < NT; t += 2) {
+        const bool l0 = t < ntl && ((r0 + 8 * t >= a.rank) == lora_pass);
+        const bool l1 = t + 1 < ntl && ((r0 + 8 * (t + 1) >= a.rank) == lora_pass);
+        if (!(l0 || l1)) continue;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          uint32_t b[4];
+          ldmatrix_x4(ws + (s * NT + t) * kLrTileBytes + swz128(b_row, 2 * kk + b_chk), b);
+          constexpr bool kF16 = W4A16;
+          if (l0) {
+            if (lora_pass) mma_16816<false>(acc[t], fr[kk], b[0], b[1]);
+            else mma_16816<kF16>(acc[t], fr[kk], b[0], b[1]);
+          }
+          if (NT > 1 && l1) {
+            if (lora_pass) mma_16816<false>(acc[t + 1], fr[kk], b[2], b[3]);
+            else mma_16816<kF16>(acc[t + 1], fr[kk], b[2], b[3]);
+          }
+        }
       }
-      cp_async16(smem_u32(ws + (st * r_tot + r) * kLD + s * 8), src, bytes);
     }
   };
 
 #pragma unroll 1
-  for (int c = 0; c < STAGES - 1; ++c) {
-    if (c < n_chunks) load_chunk(c);
-    cp_async_commit();
-  }
-  // correctly rounded reciprocals of the smoothing scale, once per CTA
-  for (int k = tid; k < n_chunks * kChunk; k += kThreads)
-    rsm[k] = k < p.K_in ? __frcp_rn(__bfloat162float(p.smooth[k])) : 0.f;
-
-  // MMA work split: warp -> m-tile (warp & 1) and column tiles (warp >> 1) + 8 j
-  const int mt = warp & 1;
-  const int tset = warp >> 1;
-  const int n_tiles = r_tot / 8;
-  float acc[kTilesPerWarp][4];
+  for (int c0 = 0; c0 < n_loc && ok; c0 += GS) {
+    uint32_t fr[GS][4][4];  // x fragments, then x_hat fragments (bf16x2, or f16x2 in W4A16 mode)
+    uint32_t mx_g = 0, mx_g8 = 0;
 #pragma unroll
-  for (int j = 0; j < kTilesPerWarp; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-
-  const float eps = __bfloat162float(__float2bfloat16_rn(1e-8f));
-  const int qrow = tid / 16;        // quant step: 16 threads per row, 8 columns each
-  const int cc = (tid % 16) * 8;    // column within the chunk
-  const int grow = m0 + qrow;
-
-#pragma unroll 1
-  for (int c = 0; c < n_chunks; ++c) {
-    const int st = c % STAGES;
-    cp_async_wait<STAGES - 2>();
-    __syncthreads();  // chunk c landed; everyone finished chunk c-1
-    if (c + STAGES - 1 < n_chunks) load_chunk(c + STAGES - 1);
-    cp_async_commit();
-
-    const int col0 = c * kChunk + cc;
-    if constexpr (W4A16) {
-      // ---- x_hat = fp16(fp32 division), and l2 rows of this chunk to fp16 ----
-      const uint4 xv = *reinterpret_cast<const uint4*>(xs + (st * kBM + qrow) * kLD + cc);
-      const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
-      uint32_t hw[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(x2[i]);
-        const int col = col0 + 2 * i;
-        const float v0 = col < p.K_in ? __fdiv_rn(f.x, __bfloat162float(p.smooth[col])) : 0.f;
-        const float v1 = col + 1 < p.K_in ? __fdiv_rn(f.y, __bfloat162float(p.smooth[col + 1])) : 0.f;
-        __half2 h = __floats2half2_rn(v0, v1);
-        hw[i] = *reinterpret_cast<uint32_t*>(&h);
+    for (int j = 0; j < GS; ++j) {
+      const int c = c0 + j, s = c % STAGES;
+      if (!mbar_wait(full_bar(s), (uint32_t)((c / STAGES) & 1), abort_flag, a.err, 0x4100 + s)) {
+        ok = false;
+        break;
       }
-      const uint4 hv = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(xh + qrow * kLD + cc) = hv;
-      if (col0 < p.K_pad && grow < p.M && p.a16)
-        *reinterpret_cast<uint4*>(p.a16 + (int64_t)grow * p.K_pad + col0) = hv;
-      // the l2 rows are consumed by an fp16 MMA in this mode
-      for (int i = tid; i < p.rank * (kChunk / 8); i += kThreads) {
-        const int r = i / (kChunk / 8), sg = i % (kChunk / 8);
-        uint4* ptr = reinterpret_cast<uint4*>(ws + (st * r_tot + r) * kLD + sg * 8);
-        uint4 v = *ptr;
-        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[e]));
-          __half2 h = __floats2half2_rn(f.x, f.y);
-          w[e] = *reinterpret_cast<uint32_t*>(&h);
-        }
-        *ptr = v;
-      }
-    } else {
-    // ---- smoothing + group quantization (bit-exact with the reference) ----
-      {
-        const uint4 xv = *reinterpret_cast<const uint4*>(xs + (st * kBM + qrow) * kLD + cc);
-        const float4 r0 = *reinterpret_cast<const float4*>(rsm + col0);
-        const float4 r1 = *reinterpret_cast<const float4*>(rsm + col0 + 4);
-        const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
-        float xf[8], t[8];
-        bool slow = false;
-  #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __bfloat1622float2(x2[i]);
-          xf[2 * i] = f.x;
-          xf[2 * i + 1] = f.y;
-        }
-  #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          t[i] = xf[i] * rv[i];
-          slow |= near_bf16_midpoint(t[i]);
-        }
-        if (slow) {
-  #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            if (near_bf16_midpoint(t[i]) && col0 + i < p.K_in)
-              t[i] = __fdiv_rn(xf[i], __bfloat162float(p.smooth[col0 + i]));
-        }
-        uint32_t hw[4];
-        float xhv[8];
-        float amax = 0.f;
-  #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          __nv_bfloat162 pr = __floats2bfloat162_rn(t[2 * i], t[2 * i + 1]);
-          hw[i] = *reinterpret_cast<uint32_t*>(&pr);
-          const float2 f = __bfloat1622float2(pr);
-          xhv[2 * i] = f.x;
-          xhv[2 * i + 1] = f.y;
-          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
-        }
-        *reinterpret_cast<uint4*>(xh + qrow * kLD + cc) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-  #pragma unroll
-        for (int o = 1; o < G / 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const float scale = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(fmaxf(amax, eps), 7.0f)));
-        const float rs = __frcp_rn(scale);
-        // rint and the offset-binary code in one add: for |t| < 2^22, t + 1.5*2^23 + 8
-        // rounds t to the nearest integer (ties to even) and its low mantissa bits
-        // hold rint(t) + 8.  |x_hat / scale| <= 7 * (1 + 2^-8), so rint(t) is in
-        // [-7, 7] and the reference's clamp to [-8, 7] never binds.
-        constexpr float kMagic = 12582920.0f;  // 1.5 * 2^23 + 8
-        float tq[8], qv[8];
-        uint32_t u[8];
-        slow = false;
-  #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          tq[i] = xhv[i] * rs;
-          const float m = tq[i] + kMagic;
-          qv[i] = m - kMagic;  // rint(tq), exact
-          u[i] = __float_as_uint(m);
-          slow |= near_half_integer(tq[i], qv[i]);
-        }
-        if (slow) {
-  #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            if (near_half_integer(tq[i], qv[i])) {
-              const float m = __fdiv_rn(xhv[i], scale) + kMagic;
-              qv[i] = m - kMagic;
-              u[i] = __float_as_uint(m);
-            }
-          }
-        }
-        uint32_t nib = 0, aw[4];
+      for (int kk = 0; kk < 4; ++kk) ldmatrix_x4(xs + s * kXTileBytes + swz128(a_row, 2 * kk + a_chk), fr[j][kk]);
+      if (a.lora_rank > 0) lowrank_mma(fr[j], s, true);  // LoRA down-projection on raw x
+      const float4* tb = rst_p + c * (kBK / 2) + t4;
 #pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          nib |= ((u[i] & 0xFu) | ((u[i + 1] & 0xFu) << 4)) << (i * 4);
-          // q * scale is exact in fp32 and in fp16 (at most 11 significant bits)
-          __half2 h = __floats2half2_rn(qv[i] * scale, qv[i + 1] * scale);
-          aw[i / 2] = *reinterpret_cast<uint32_t*>(&h);
+      for (int kk = 0; kk < 4; ++kk) {
+        const float4 cA = tb[8 * kk], cB = tb[8 * kk + 4];
+        const uint64_t yA = f2_pack(cA.x, cA.y), nA = f2_pack(cA.z, cA.w);
+        const uint64_t yB = f2_pack(cB.x, cB.y), nB = f2_pack(cB.z, cB.w);
+        // fragment regs: 0 = (row g, cols A), 1 = (row g+8, cols A), 2 = (row g, cols B), 3 = (row g+8, cols B)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint64_t q = div_f2(bf2_to_f2(fr[j][kk][i]), i < 2 ? yA : yB, i < 2 ? nA : nB);
+          fr[j][kk][i] = W4A16 ? f2_to_h2(q) : f2_to_bf2(q);
         }
-        if (col0 < p.K_pad && grow < p.M) {
-          if (p.packed) *reinterpret_cast<uint32_t*>(p.packed + (int64_t)grow * (p.K_pad / 2) + col0 / 2) = nib;
-          if (p.a16)
-            *reinterpret_cast<uint4*>(p.a16 + (int64_t)grow * p.K_pad + col0) = make_uint4(aw[0], aw[1], aw[2], aw[3]);
-          if ((tid % (G / 8)) == 0 && p.scales)
-            p.scales[(int64_t)grow * (p.K_pad / G) + col0 / G] = __float2bfloat16_rn(scale);
+        if constexpr (!W4A16) {
+          mx_g = bf2_maxabs(bf2_maxabs(mx_g, fr[j][kk][0]), fr[j][kk][2]);
+          mx_g8 = bf2_maxabs(bf2_maxabs(mx_g8, fr[j][kk][1]), fr[j][kk][3]);
         }
       }
     }
-    __syncthreads();  // x_hat tile complete
+    if (!ok) break;
 
-    // ---- low-rank down-projection on tensor cores ----
-    if (tset < n_tiles) {
-      const __nv_bfloat16* wst = ws + st * r_tot * kLD;
-      const __nv_bfloat16* xst = xs + (st * kBM + mt * 16) * kLD;
-      const __nv_bfloat16* xht = xh + (mt * 16) * kLD;
-#pragma unroll 2
-      for (int kk = 0; kk < kChunk / 16; ++kk) {
-        const int ar = lane % 16, ac = kk * 16 + (lane / 16) * 8;
-        uint32_t a_hat[4], a_raw[4];
-        ldmatrix_x4(smem_u32(xht + ar * kLD + ac), a_hat);
-        if (p.lora_rank > 0) ldmatrix_x4(smem_u32(xst + ar * kLD + ac), a_raw);
-#pragma unroll
-        for (int j = 0; j < kTilesPerWarp; ++j) {
-          const int t = tset + 8 * j;
-          if (t < n_tiles) {
-            const int br = t * 8 + (lane % 8), bc = kk * 16 + ((lane / 8) % 2) * 8;
-            uint32_t b0, b1;
-            ldmatrix_x2(smem_u32(wst + br * kLD + bc), b0, b1);
-            if (t * 8 < p.rank) {
-              if constexpr (W4A16) mma_f16_16816(acc[j], a_hat, b0, b1);
-              else mma_bf16_16816(acc[j], a_hat, b0, b1);
-            } else {
-              mma_bf16_16816(acc[j], a_raw, b0, b1);
-            }
-          }
-        }
-      }
-    }
-  }
-  cp_async_wait<0>();
-
-  // ---- mid as bf16 hi/lo pair ----
-  if (p.mid_hl) {
-    const int g = lane / 4, t4 = lane % 4;
-#pragma unroll
-    for (int j = 0; j < kTilesPerWarp; ++j) {
-      const int t = tset + 8 * j;
-      if (t < n_tiles) {
-        const int col = t * 8 + 2 * t4;
+    // ---- group scale of rows g and g+8 (W4A4) ----
+    uint64_t sc2[2], ys2[2], ns2[2];
+    if constexpr (!W4A16) {
+      if (emit) {
+        float am[2] = {bf2_absmax_f(mx_g), bf2_absmax_f(mx_g8)};
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int row = m0 + mt * 16 + g + 8 * h;
-          float v0 = acc[j][2 * h], v1 = acc[j][2 * h + 1];
-          if (col >= p.rank) {
-            v0 *= p.lora_col_scale[col - p.rank];
-            v1 *= p.lora_col_scale[col + 1 - p.rank];
-          }
-          const __nv_bfloat16 h0 = __float2bfloat16_rn(v0), h1 = __float2bfloat16_rn(v1);
-          const __nv_bfloat16 l0 = __float2bfloat16_rn(v0 - __bfloat162float(h0));
-          const __nv_bfloat16 l1 = __float2bfloat16_rn(v1 - __bfloat162float(h1));
-          if (row < p.M) {
-            __nv_bfloat16* dst = p.mid_hl + (int64_t)row * p.R2;
-            __nv_bfloat162 hp, lp;
-            hp.x = h0; hp.y = h1; lp.x = l0; lp.y = l1;
-            *reinterpret_cast<__nv_bfloat162*>(dst + col) = hp;
-            *reinterpret_cast<__nv_bfloat162*>(dst + r_tot + col) = lp;
+          am[h] = fmaxf(am[h], __shfl_xor_sync(0xffffffffu, am[h], 1));
+          am[h] = fmaxf(am[h], __shfl_xor_sync(0xffffffffu, am[h], 2));
+          const float v = fmaxf(am[h], eps);
+          const float q0 = v * y7;
+          const float sc = __bfloat162float(__float2bfloat16_rn(fmaf(fmaf(-q0, 7.0f, v), y7, q0)));
+          const float ys = __frcp_rn(sc);
+          a16_range |= sc > kA16ScaleMax;
+          sc2[h] = f2_pack(sc, sc);
+          ys2[h] = f2_pack(ys, ys);
+          ns2[h] = f2_pack(-sc, -sc);
+          if constexpr (PACKED) {
+            const int row = h ? row_g8 : row_g;
+            if (t4 == 0 && row < a.M && a.scales)
+              a.scales[(int64_t)row * (a.K_pad / a.G) + (st0 + c0) * kBK / a.G] = __float2bfloat16_rn(sc);
           }
         }
       }
     }
-    const int pad = p.R2 - 2 * r_tot;
-    for (int i = tid; i < kBM * pad; i += kThreads) {
-      const int r = i / pad, cidx = 2 * r_tot + i % pad;
-      if (m0 + r < p.M) p.mid_hl[(int64_t)(m0 + r) * p.R2 + cidx] = __float2bfloat16_rn(0.f);
+
+#pragma unroll
+    for (int j = 0; j < GS; ++j) {
+      const int c = c0 + j, s = c % STAGES;
+      const int kcol = (st0 + c) * kBK;
+      if (emit) {
+        if (a.write_a16) {
+          if (lane == 0) bulk_wait_read0();  // previous store of this warp's staging tile has read it
+          __syncwarp();
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          uint32_t o[4];
+          if constexpr (W4A16) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[i] = fr[j][kk][i];
+          } else {
+            uint32_t nib[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int h = i & 1;
+              const uint64_t q = div_f2(bf2_to_f2(fr[j][kk][i]), ys2[h], ns2[h]);
+              const uint64_t m = f2_add(q, mag2);        // low mantissa bits = rint(q) + 8
+              o[i] = f2_to_h2(f2_mul(f2_add(m, nmag2), sc2[h]));  // q * scale, exact in fp16
+              nib[i] = ((uint32_t)m & 0xFu) | (((uint32_t)(m >> 32) & 0xFu) << 4);
+            }
+            if constexpr (PACKED) {
+              uint8_t* prow_g = a.packed + (int64_t)row_g * (a.K_pad / 2) + (kcol + 16 * kk + 2 * t4) / 2;
+              uint8_t* prow_g8 = prow_g + (int64_t)8 * (a.K_pad / 2);
+              if (row_g < a.M) { prow_g[0] = (uint8_t)nib[0]; prow_g[4] = (uint8_t)nib[2]; }
+              if (row_g8 < a.M) { prow_g8[0] = (uint8_t)nib[1]; prow_g8[4] = (uint8_t)nib[3]; }
+            }
+          }
+          if (a.write_a16) stmatrix_x4(my_ost + swz128(lane & 15, 2 * kk + (lane >> 4)), o[0], o[1], o[2], o[3]);
+        }
+        if (a.write_a16) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && m0 + wrow < a.M) {
+            tma_store_2d(&tm_a16, my_ost, kcol, m0 + wrow);
+            bulk_commit();
+          }
+        }
+      }
+      if (ntl > 0 && a.rank > 0 && r0 < a.rank) lowrank_mma(fr[j], s, false);  // l2 on x_hat
+
+      // release the stage; the last of the four warps refills it
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        const int old = atomicAdd(&cnt[s], 1);
+        if ((old & (kWarps - 1)) == kWarps - 1) {
+          __threadfence_block();
+          fence_proxy_async_smem();
+          if (c + STAGES < n_loc) issue(s, c + STAGES);
+        }
+      }
+    }
+  }
+
+  // ---- fp32 partial of the low-rank projection over this K slice ----
+  if constexpr (NT > 0) {
+    if (ok && a.partial) {
+      float* part = a.partial + (int64_t)blockIdx.y * a.M * a.r_tot;
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (t < ntl) {
+          const int col = r0 + 8 * t + 2 * t4;
+          if (row_g < a.M)
+            *reinterpret_cast<float2*>(part + (int64_t)row_g * a.r_tot + col) = make_float2(acc[t][0], acc[t][1]);
+          if (row_g8 < a.M)
+            *reinterpret_cast<float2*>(part + (int64_t)row_g8 * a.r_tot + col) = make_float2(acc[t][2], acc[t][3]);
+        }
+      }
+    }
+  }
+  if (__any_sync(0xffffffffu, a16_range) && lane == 0 && a.write_a16) atomicCAS(a.err, 0, kErrA16Range);
+  if (lane == 0) bulk_wait0();
+  __syncthreads();
+  if (tid == 0) {
+    // no load may still be landing when the CTA exits (only possible after an abort)
+    for (int s = 0; s < STAGES; ++s)
+      if (issued[s] > 0 && !mbar_wait_drain(full_bar(s), (uint32_t)((issued[s] - 1) & 1), kWaitLimitNs))
+        atomicCAS(a.err, 0, 0x4180 + s);
+  }
+}
+
+// mid_hl[m] = [hi(v) | lo(v) | 0], v = (sum of the K-slice partials, in slice order) * column scale
+// (LoRA columns), hi = bf16(v), lo = bf16(v - hi).
+__global__ void mid_finalize_kernel(const float* __restrict__ partial, int ksplit, int M, int rank, int r_tot,
+                                    const float* __restrict__ lora_col_scale, __nv_bfloat16* __restrict__ mid_hl,
+                                    int R2) {
+  const int w = R2 - r_tot;  // work items per row: r_tot (hi+lo pairs) + zero padding
+  const int64_t total = (int64_t)M * w;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / w), j = (int)(i % w);
+    __nv_bfloat16* out = mid_hl + (int64_t)row * R2;
+    if (j < r_tot) {
+      float v = 0.f;
+      for (int k = 0; k < ksplit; ++k) v += partial[((int64_t)k * M + row) * r_tot + j];
+      if (j >= rank) v *= lora_col_scale[j - rank];
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      out[j] = hi;
+      out[r_tot + j] = __float2bfloat16_rn(v - __bfloat162float(hi));
+    } else {
+      out[r_tot + j] = __float2bfloat16_rn(0.f);
     }
   }
 }
 
-constexpr size_t kSmemBudget = 220 * 1024;
+// ---- launch geometry (shared by the workspace query and the launch) ----
+struct Geometry {
+  int nt, nz, slice, ksplit;
+};
 
-size_t smem_bytes(int stages, int r_tot, int k_pad) {
-  const size_t n_chunks = (size_t)((k_pad + kChunk - 1) / kChunk);
-  return sizeof(float) * n_chunks * kChunk +
-         sizeof(__nv_bfloat16) * (size_t)(stages * kBM * kLD + stages * r_tot * kLD + kBM * kLD);
+int pick_nt(int r_use) {
+  if (r_use <= 0) return 0;
+  const int tiles = r_use / 8;
+  return tiles <= 1 ? 1 : tiles <= 2 ? 2 : tiles <= 4 ? 4 : 8;
 }
 
-template <int G, int STAGES, bool W4A16>
-int launch(const ActQuantParams& prm, int r_tot, cudaStream_t stream) {
-  const size_t smem = smem_bytes(STAGES, r_tot, prm.K_pad);
-  auto kern = act_quant_kernel<G, STAGES, W4A16>;
+Geometry geometry(int M, int K_pad, int r_use) {
+  Geometry gm;
+  gm.nt = pick_nt(r_use);
+  gm.nz = gm.nt ? (r_use + 8 * gm.nt - 1) / (8 * gm.nt) : 1;
+  const int n_st = K_pad / kBK;
+  const int bands = (M + kBM - 1) / kBM;
+  const int slots = num_sms() * kTargetCtasPerSm;
+  const int want = std::max(1, slots / std::max(1, bands * gm.nz));
+  int slice = (n_st + want - 1) / want;
+  slice = (slice + 1) & ~1;  // even: a 128-column group never straddles two slices
+  slice = std::min(std::max(slice, kMinSliceStages), kMaxSliceStages);
+  gm.slice = slice;
+  gm.ksplit = (n_st + slice - 1) / slice;
+  return gm;
+}
+
+size_t workspace_bytes(int M, int K_pad, int r_tot) {
+  if (r_tot <= 0 || M <= 0 || K_pad <= 0) return 0;
+  const Geometry gm = geometry(M, K_pad, r_tot);
+  return sizeof(float) * (size_t)gm.ksplit * (size_t)M * (size_t)r_tot;
+}
+
+struct LaunchSpec {
+  CUtensorMap tm_x, tm_l2, tm_lora, tm_a16;
+  AqArgs args;
+  Geometry gm;
+  int gs;
+  bool w4a16, packed;
+  const float* lora_col_scale;
+  __nv_bfloat16* mid_hl;
+  int R2;
+};
+
+template <int GS, int NT, bool W4A16, bool PACKED>
+int launch_t(const LaunchSpec& L, cudaStream_t stream) {
+  constexpr int STAGES = GS == 2 ? 4 : 3;
+  constexpr uint32_t smem = aq_smem_layout_bytes<STAGES, NT>();
+  auto kern = act_quant_kernel<GS, STAGES, NT, W4A16, PACKED>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return check_cuda(e, "svdq_act_quant: shared memory attribute");
-  const int grid = (prm.M + kBM - 1) / kBM;
-  kern<<<grid, kThreads, smem, stream>>>(prm);
-  return check_launch("svdq_act_quant launch");
+  if (e != cudaSuccess) return check_cuda(e, "activation pass: shared memory attribute");
+  const dim3 grid((L.args.M + kBM - 1) / kBM, L.gm.ksplit, L.gm.nz);
+  kern<<<grid, kThreads, smem, stream>>>(L.tm_x, L.tm_l2, L.tm_lora, L.tm_a16, L.args);
+  return check_launch("activation pass launch");
 }
 
-template <int G, bool W4A16>
-int launch_g(const ActQuantParams& prm, int r_tot, cudaStream_t stream) {
-  // deepest ring that fits in the shared-memory budget
-  if (smem_bytes(4, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 4, W4A16>(prm, r_tot, stream);
-  if (smem_bytes(3, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 3, W4A16>(prm, r_tot, stream);
-  if (smem_bytes(2, r_tot, prm.K_pad) <= kSmemBudget) return launch<G, 2, W4A16>(prm, r_tot, stream);
-  return set_error(SVDQ_ERR_UNSUPPORTED, "svdq_act_quant: K_pad / rank too large for shared memory");
+template <int GS, bool W4A16, bool PACKED>
+int launch_nt(const LaunchSpec& L, cudaStream_t stream) {
+  switch (L.gm.nt) {
+    case 0: return launch_t<GS, 0, W4A16, PACKED>(L, stream);
+    case 1: return launch_t<GS, 1, W4A16, PACKED>(L, stream);
+    case 2: return launch_t<GS, 2, W4A16, PACKED>(L, stream);
+    case 4: return launch_t<GS, 4, W4A16, PACKED>(L, stream);
+    default: return launch_t<GS, 8, W4A16, PACKED>(L, stream);
+  }
 }
 
-}  // namespace
-}  // namespace svdq
-
-namespace svdq {
-namespace {
+int launch(const LaunchSpec& L, cudaStream_t stream) {
+  int st;
+  if (L.w4a16) st = launch_nt<1, true, false>(L, stream);
+  else if (L.gs == 1) st = L.packed ? launch_nt<1, false, true>(L, stream) : launch_nt<1, false, false>(L, stream);
+  else st = L.packed ? launch_nt<2, false, true>(L, stream) : launch_nt<2, false, false>(L, stream);
+  if (st || !L.args.partial) return st;
+  const int64_t items = (int64_t)L.args.M * (L.R2 - L.args.r_tot);
+  const int blocks = (int)std::min<int64_t>((items + 255) / 256, (int64_t)num_sms() * 8);
+  mid_finalize_kernel<<<blocks, 256, 0, stream>>>(L.args.partial, L.gm.ksplit, L.args.M, L.args.rank, L.args.r_tot,
+                                                  L.lora_col_scale, L.mid_hl, L.R2);
+  return check_launch("activation pass finalize");
+}
 
 int validate_common(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank, const void* lora_down,
                     const float* lora_col_scale, int lora_rank, int M, int K_in, int K_pad, void* out_a16,
-                    void* out_mid_hl, int R2, const char* who) {
+                    void* out_mid_hl, int R2, void* workspace, size_t ws_bytes, const char* who) {
   const std::string w(who);
   auto bad = [&](const char* msg) { return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": " + msg); };
   if (!(x && smooth)) return bad("x and smooth are required");
@@ -418,67 +523,111 @@ int validate_common(const void* x, int64_t ldx, const void* smooth, const void* 
   if ((reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(smooth) & 15u) ||
       (l2 && (reinterpret_cast<uintptr_t>(l2) & 15u)) || (lora_down && (reinterpret_cast<uintptr_t>(lora_down) & 15u)))
     return bad("x, smooth, l2, lora_down must be 16-byte aligned");
-  if (out_a16 && ((reinterpret_cast<uintptr_t>(out_a16) & 15u) || K_pad % 8 != 0))
-    return bad("a16 must be 16-byte aligned with K_pad a multiple of 8");
+  if (K_pad % kBK != 0) return bad("K_pad must be a multiple of 64");
+  if (out_a16 && (reinterpret_cast<uintptr_t>(out_a16) & 15u)) return bad("a16 must be 16-byte aligned");
+  if (out_mid_hl && r_tot > 0 && M > 0) {
+    if (!workspace || ws_bytes < workspace_bytes(M, K_pad, r_tot))
+      return bad("workspace missing or smaller than svdq_act_quant_workspace_bytes()");
+    if (reinterpret_cast<uintptr_t>(workspace) & 15u) return bad("workspace must be 16-byte aligned");
+  }
   return SVDQ_OK;
 }
 
-ActQuantParams make_params(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank,
-                           const void* lora_down, const float* lora_col_scale, int lora_rank, int M, int K_in,
-                           int K_pad, void* out_packed, void* out_scales, void* out_a16, void* out_mid_hl, int R2) {
-  ActQuantParams p;
-  p.x = static_cast<const __nv_bfloat16*>(x);
-  p.ldx = ldx;
-  p.smooth = static_cast<const __nv_bfloat16*>(smooth);
-  p.l2 = static_cast<const __nv_bfloat16*>(l2);
-  p.lora = static_cast<const __nv_bfloat16*>(lora_down);
-  p.lora_col_scale = lora_col_scale;
-  p.rank = rank;
-  p.lora_rank = lora_rank;
+// Tensor maps and arguments of one activation pass.
+int build_spec(LaunchSpec& L, const void* x, int64_t ldx, const void* smooth, const void* l2, bool l2_f16, int rank,
+               const void* lora_down, const float* lora_col_scale, int lora_rank, int M, int K_in, int K_pad, int G,
+               void* out_packed, void* out_scales, void* out_a16, void* out_mid_hl, int R2, void* workspace) {
+  const int r_tot = rank + lora_rank;
+  const bool want_mid = out_mid_hl && r_tot > 0;
+  const int r_use = want_mid ? r_tot : 0;
+  L.gm = geometry(M, K_pad, r_use);
+  int st;
+  if ((st = make_tma_2d(&L.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K_in, M, (uint64_t)ldx * 2, kBK, kBM,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  L.tm_l2 = L.tm_x;
+  L.tm_lora = L.tm_x;
+  L.tm_a16 = L.tm_x;
+  if (want_mid && rank > 0 &&
+      (st = make_tma_2d(&L.tm_l2, l2_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, l2,
+                        K_in, rank, (uint64_t)K_in * 2, kBK, 8, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if (want_mid && lora_rank > 0 &&
+      (st = make_tma_2d(&L.tm_lora, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lora_down, K_in, lora_rank, (uint64_t)K_in * 2,
+                        kBK, 8, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if (out_a16 && (st = make_tma_2d(&L.tm_a16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, out_a16, K_pad, M, (uint64_t)K_pad * 2,
+                                   kBK, 16, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  AqArgs& p = L.args;
   p.M = M;
   p.K_in = K_in;
   p.K_pad = K_pad;
+  p.rank = want_mid ? rank : 0;
+  p.lora_rank = want_mid ? lora_rank : 0;
+  p.r_tot = r_use;
+  p.n_stages = K_pad / kBK;
+  p.slice_stages = L.gm.slice;
+  p.G = G;
+  p.write_a16 = out_a16 != nullptr;
+  p.smooth = static_cast<const __nv_bfloat16*>(smooth);
   p.packed = static_cast<uint8_t*>(out_packed);
   p.scales = static_cast<__nv_bfloat16*>(out_scales);
-  p.a16 = static_cast<__half*>(out_a16);
-  p.mid_hl = (rank + lora_rank) > 0 ? static_cast<__nv_bfloat16*>(out_mid_hl) : nullptr;
-  p.R2 = R2;
-  return p;
+  p.partial = want_mid ? static_cast<float*>(workspace) : nullptr;
+  p.err = device_error_word();
+  if (!p.err) return set_error(SVDQ_ERR_CUDA, "device error word unavailable");
+  L.gs = G / kBK;
+  L.lora_col_scale = lora_col_scale;
+  L.mid_hl = static_cast<__nv_bfloat16*>(out_mid_hl);
+  L.R2 = R2;
+  return SVDQ_OK;
 }
 
 }  // namespace
 }  // namespace svdq
 
+extern "C" size_t svdq_act_quant_workspace_bytes(int M, int K_pad, int rank, int lora_rank) {
+  return svdq::workspace_bytes(M, K_pad, rank + lora_rank);
+}
+
 extern "C" int svdq_act_quant(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank,
                               const void* lora_down, const float* lora_col_scale, int lora_rank, int M, int K_in,
                               int K_pad, int a_group, void* out_packed, void* out_scales, void* out_a16,
-                              void* out_mid_hl, int R2, cudaStream_t stream) {
+                              void* out_mid_hl, int R2, void* workspace, size_t workspace_bytes,
+                              cudaStream_t stream) {
   using namespace svdq;
   int st = validate_common(x, ldx, smooth, l2, rank, lora_down, lora_col_scale, lora_rank, M, K_in, K_pad, out_a16,
-                           out_mid_hl, R2, "svdq_act_quant");
+                           out_mid_hl, R2, workspace, workspace_bytes, "svdq_act_quant");
   if (st) return st;
   SVDQ_REQUIRE(a_group == 64 || a_group == 128, "svdq_act_quant: a_group must be 64 or 128");
   SVDQ_REQUIRE(K_pad % a_group == 0, "svdq_act_quant: K_pad must be a multiple of a_group");
-  SVDQ_REQUIRE(!out_packed || (reinterpret_cast<uintptr_t>(out_packed) & 3u) == 0,
-               "svdq_act_quant: packed output must be 4-byte aligned");
+  SVDQ_REQUIRE((out_packed == nullptr) == (out_scales == nullptr),
+               "svdq_act_quant: packed codes and scales are emitted together");
   if (M == 0) return SVDQ_OK;
-  const ActQuantParams p = make_params(x, ldx, smooth, l2, rank, lora_down, lora_col_scale, lora_rank, M, K_in,
-                                       K_pad, out_packed, out_scales, out_a16, out_mid_hl, R2);
-  const int r_tot = rank + lora_rank;
-  return a_group == 64 ? launch_g<64, false>(p, r_tot, stream) : launch_g<128, false>(p, r_tot, stream);
+  LaunchSpec L;
+  if ((st = build_spec(L, x, ldx, smooth, l2, false, rank, lora_down, lora_col_scale, lora_rank, M, K_in, K_pad,
+                       a_group, out_packed, out_scales, out_a16, out_mid_hl, R2, workspace)))
+    return st;
+  L.w4a16 = false;
+  L.packed = out_packed != nullptr;
+  return launch(L, stream);
 }
 
-extern "C" int svdq_w4a16_prep(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank,
+extern "C" int svdq_w4a16_prep(const void* x, int64_t ldx, const void* smooth, const void* l2_f16, int rank,
                                const void* lora_down, const float* lora_col_scale, int lora_rank, int M, int K_in,
-                               int K_pad, void* out_a16, void* out_mid_hl, int R2, cudaStream_t stream) {
+                               int K_pad, void* out_a16, void* out_mid_hl, int R2, void* workspace,
+                               size_t workspace_bytes, cudaStream_t stream) {
   using namespace svdq;
-  int st = validate_common(x, ldx, smooth, l2, rank, lora_down, lora_col_scale, lora_rank, M, K_in, K_pad, out_a16,
-                           out_mid_hl, R2, "svdq_w4a16_prep");
+  int st = validate_common(x, ldx, smooth, l2_f16, rank, lora_down, lora_col_scale, lora_rank, M, K_in, K_pad,
+                           out_a16, out_mid_hl, R2, workspace, workspace_bytes, "svdq_w4a16_prep");
   if (st) return st;
   SVDQ_REQUIRE(out_a16, "svdq_w4a16_prep: out_a16 is required");
-  SVDQ_REQUIRE(K_pad % 64 == 0, "svdq_w4a16_prep: K_pad must be a multiple of 64");
   if (M == 0) return SVDQ_OK;
-  const ActQuantParams p = make_params(x, ldx, smooth, l2, rank, lora_down, lora_col_scale, lora_rank, M, K_in,
-                                       K_pad, nullptr, nullptr, out_a16, out_mid_hl, R2);
-  return launch_g<64, true>(p, rank + lora_rank, stream);
+  LaunchSpec L;
+  if ((st = build_spec(L, x, ldx, smooth, l2_f16, true, rank, lora_down, lora_col_scale, lora_rank, M, K_in, K_pad,
+                       64, nullptr, nullptr, out_a16, out_mid_hl, R2, workspace)))
+    return st;
+  L.w4a16 = true;
+  L.packed = false;
+  return launch(L, stream);
 }

@@ -69,6 +69,7 @@ class PreparedOperands:
     n: int
     smooth: torch.Tensor           # [k_in] bf16 (padded with ones)
     l2: torch.Tensor | None        # [r8, k_in] bf16
+    l2_f16: torch.Tensor | None    # [r8, k_in] fp16 copy (W4A16 activation pass)
     lora_down: torch.Tensor | None  # [rl8, k_in] bf16, stacked adapters
     lora_col_scale: torch.Tensor | None  # [rl8] fp32 multiplier per stacked row
     up_hl: torch.Tensor | None     # [n, R2] bf16, [l1 | lora_up] hi/lo operand
@@ -200,7 +201,8 @@ class SVDQuantLinear(nn.Module):
             w16 = ops.repack_weight(qw, ws, self.group_size)
             bias = None if self.bias is None else self.bias.to(device=device, dtype=bf).contiguous()
         self._prepared = PreparedOperands(device=device, key=key, k_in=k_in, k_pad=k_pad, n=n, smooth=smooth,
-                                          l2=l2, lora_down=lora_down, lora_col_scale=col_scale, up_hl=up_hl,
+                                          l2=l2, l2_f16=None if l2 is None else l2.to(torch.float16),
+                                          lora_down=lora_down, lora_col_scale=col_scale, up_hl=up_hl,
                                           up_hl_base=up_hl_base,
                                           w16=w16, bias=bias)
         return self._prepared
@@ -226,7 +228,7 @@ class SVDQuantLinear(nn.Module):
         col_scale = p.lora_col_scale if include_lora else None
         up_hl = p.up_hl if include_lora else p.up_hl_base
         if self.backend is BackendKind.B200_W4A16:
-            a16, mid = ops.w4a16_prep(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad)
+            a16, mid = ops.w4a16_prep(x2, p.smooth, p.l2_f16, lora_down, col_scale, p.k_pad)
         else:
             a16, mid, _, _ = ops.act_quant(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
                                            self.act_group_size, True, False)

@@ -56,6 +56,11 @@ def _lowrank_args(l2, lora_down):
     return rank, lrank, lowrank_width(rank + lrank)
 
 
+def _workspace(m: int, k_pad: int, rank: int, lrank: int, dev: torch.device) -> Tensor:
+    n = int(_lib.lib().svdq_act_quant_workspace_bytes(m, k_pad, rank, lrank))
+    return torch.empty((max(n, 0),), dtype=torch.uint8, device=dev)
+
+
 @torch.library.custom_op("svdq_b200::act_quant", mutates_args=())
 def act_quant(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Optional[Tensor],
               lora_col_scale: Optional[Tensor], k_pad: int, a_group: int, emit_a16: bool,
@@ -77,9 +82,10 @@ def act_quant(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Option
     mid = torch.empty((m, r2) if (emit_a16 and r2) else (0,), dtype=torch.bfloat16, device=dev)
     packed = torch.empty((m, k_pad // 2) if emit_packed else (0,), dtype=torch.uint8, device=dev)
     scales = torch.empty((m, k_pad // a_group) if emit_packed else (0,), dtype=torch.bfloat16, device=dev)
+    ws = _workspace(m, k_pad, rank, lrank, dev) if mid.numel() else None
     _lib.call("svdq_act_quant", _p(x), x.stride(0), _p(smooth), _p(l2), rank, _p(lora_down),
               _p(lora_col_scale), lrank, m, k_in, k_pad, a_group, _p(packed), _p(scales), _p(a16),
-              _p(mid), r2, _stream(dev))
+              _p(mid), r2, _p(ws), 0 if ws is None else ws.numel(), _stream(dev))
     return a16, mid, packed, scales
 
 
@@ -98,16 +104,20 @@ def _(x, smooth, l2, lora_down, lora_col_scale, k_pad, a_group, emit_a16, emit_p
 def w4a16_prep(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Optional[Tensor],
                lora_col_scale: Optional[Tensor], k_pad: int) -> tuple[Tensor, Tensor]:
     """W4A16 activation pass: ``a16 = fp16(x / smooth)`` (fp32 division) and the low-rank
-    down-projection.  Returns ``(a16 [M,K_pad] fp16, mid_hl [M,R2] bf16)``."""
+    down-projection.  ``l2`` is the fp16 copy of the checkpoint's l2 (made once at load).
+    Returns ``(a16 [M,K_pad] fp16, mid_hl [M,R2] bf16)``."""
     _need_cuda("w4a16_prep", x, smooth, l2, lora_down, lora_col_scale)
     _need(x.dim() == 2 and x.dtype == torch.bfloat16, "w4a16_prep: x must be a 2-D bf16 tensor")
+    _need(l2 is None or l2.dtype == torch.float16, "w4a16_prep: l2 must be fp16 (convert once at load)")
     _need(x.stride(1) == 1, "w4a16_prep: x must have unit column stride")
     m, k_in = x.shape
     rank, lrank, r2 = _lowrank_args(l2, lora_down)
     a16 = torch.empty((m, k_pad), dtype=torch.float16, device=x.device)
     mid = torch.empty((m, r2) if r2 else (0,), dtype=torch.bfloat16, device=x.device)
+    ws = _workspace(m, k_pad, rank, lrank, x.device) if r2 else None
     _lib.call("svdq_w4a16_prep", _p(x), x.stride(0), _p(smooth), _p(l2), rank, _p(lora_down),
-              _p(lora_col_scale), lrank, m, k_in, k_pad, _p(a16), _p(mid), r2, _stream(x.device))
+              _p(lora_col_scale), lrank, m, k_in, k_pad, _p(a16), _p(mid), r2, _p(ws),
+              0 if ws is None else ws.numel(), _stream(x.device))
     return a16, mid
 
 

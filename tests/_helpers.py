@@ -55,3 +55,17 @@ def staged_oracle(x_np: np.ndarray, s: dict, loras=(), a_group=64, mid=None):
     return O.w4a4_linear_staged(x_np, s["smooth"], s["qweight"], s["weight_scales"], s["l1"], s["l2"],
                                 s["bias"], w_group=s["group"], a_group=a_group, k_in=s["k_in"],
                                 k_pad=s["k_pad"], loras=loras, mid=mid)
+
+
+def bf16_sweep(k: int, lo_exp: int = -100, hi_exp: int = 100) -> np.ndarray:
+    """Every bf16 value with exponent in [lo_exp, hi_exp) (both signs) plus zeros, sorted by
+    magnitude so that each quantization group holds values of similar size, as [rows, k] fp32."""
+    bits = np.arange(0, 1 << 16, dtype=np.uint32)
+    e = ((bits >> 7) & 0xFF).astype(np.int64) - 127
+    keep = ((e >= lo_exp) & (e < hi_exp)) | ((bits & 0x7FFF) == 0)
+    vals = (bits[keep] << 16).view(np.float32)
+    vals = vals[np.argsort(np.abs(vals), kind="stable")]
+    rows = -(-vals.size // k)
+    out = np.zeros(rows * k, np.float32)
+    out[:vals.size] = vals
+    return out.reshape(rows, k)

@@ -54,7 +54,7 @@ def test_invalid_arguments_rejected_without_gpu():
     from krea2_svdquant_b200 import _lib
     L = _lib.lib()
     st = L.svdq_act_quant(ctypes.c_void_p(16), 8, ctypes.c_void_p(16), None, 0, None, None, 0,
-                          4, 8, 64, 96, None, None, None, None, 0, None)
+                          4, 8, 64, 96, None, None, None, None, 0, None, 0, None)
     assert st == 1
     assert "a_group" in L.svdq_last_error().decode()
     st = L.svdq_linear_gemm(None, None, None, None, 0, None, None, 0, 8, 4, 8, 64, None)

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from oracle import svdq_oracle as O
-from tests._helpers import bf16_tensor, golden_state, state_numpy
+from tests._helpers import bf16_sweep, bf16_tensor, golden_state, state_numpy
 
 pytestmark = pytest.mark.gpu
 
@@ -54,6 +54,20 @@ def test_w4a16_prep_smoothing_exact():
     a16, mid = ops.w4a16_prep(x, s, None, None, None, 256)
     torch.cuda.synchronize()
     ref = (x.float().cpu().numpy() / s.float().cpu().numpy()).astype(np.float32).astype(np.float16)
+    assert np.array_equal(a16.cpu().numpy(), ref)
+
+
+def test_w4a16_prep_division_sweep():
+    """a16 = fp16(fp32(x) / fp32(s)) over every bf16 magnitude in [2^-100, 2^100)."""
+    from krea2_svdquant_b200 import ops
+    k = 512
+    xn = bf16_sweep(k)
+    rng = np.random.default_rng(6)
+    sn = torch.tensor(2.0 ** rng.uniform(-6, 6, k)).bfloat16().float().numpy()
+    a16, _ = ops.w4a16_prep(bf16_tensor(xn), bf16_tensor(sn), None, None, None, k)
+    torch.cuda.synchronize()
+    with np.errstate(over="ignore"):
+        ref = (xn / sn[None, :]).astype(np.float32).astype(np.float16)
     assert np.array_equal(a16.cpu().numpy(), ref)
 
 

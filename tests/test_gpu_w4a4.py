@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from oracle import svdq_oracle as O
-from tests._helpers import bf16_tensor, golden_state, staged_oracle, state_numpy
+from tests._helpers import bf16_sweep, bf16_tensor, golden_state, staged_oracle, state_numpy
 
 pytestmark = pytest.mark.gpu
 
@@ -76,6 +76,62 @@ def test_act_quant_edges_bit_exact(golden):
     torch.cuda.synchronize()
     assert np.array_equal(packed.cpu().numpy(), g["packed"])
     assert np.array_equal(scales.view(torch.int16).cpu().numpy().view(np.uint16), g["scales__bits"])
+
+
+@pytest.mark.parametrize("ag", [64, 128])
+def test_act_quant_division_sweep(ag):
+    """Codes, scales and a16 stay bit-exact over every bf16 magnitude in [2^-100, 2^100)
+    divided by smoothing factors spread over [2^-6, 2^6]."""
+    from krea2_svdquant_b200 import _lib
+    k = 512
+    xn = bf16_sweep(k)
+    rng = np.random.default_rng(5)
+    sn = torch.tensor(2.0 ** rng.uniform(-6, 6, k)).bfloat16().float().numpy()
+    x = bf16_tensor(xn)
+    s = bf16_tensor(sn)
+    a16, mid, packed, scales = _act(x, s, k_pad=k, a_group=ag)
+    torch.cuda.synchronize()
+    xh, q, pk, sa = O.act_quant(xn, sn, ag)
+    assert np.array_equal(packed.cpu().numpy(), pk)
+    assert np.array_equal(scales.float().cpu().numpy(), sa)
+    # a16 = q * scale is exact in fp16 for group scales in [2^-17, 65504/7]; larger scales
+    # overflow the fp16 operand and must be reported through the device error word
+    in_range = np.repeat((sa >= 2.0 ** -17) & (sa <= 65504.0 / 7.0), ag, axis=1)
+    got, ref = a16.float().cpu().numpy(), _dequant_np(q, sa, ag)
+    assert np.array_equal(got[in_range], ref[in_range])
+    assert (~in_range).any() and (sa > 65504.0 / 7.0).any()
+    assert _lib.device_error(clear=True) == 0x4200
+
+
+def test_act_quant_no_range_flag_in_domain():
+    from krea2_svdquant_b200 import _lib
+    x = (torch.randn(64, 256) * 1000).bfloat16().cuda()
+    s = torch.ones(256, dtype=torch.bfloat16, device="cuda")
+    _act(x, s, k_pad=256)
+    assert _lib.device_error(clear=True) == 0
+
+
+def test_act_quant_wide_lowrank():
+    """rank + LoRA wider than one CTA's 64 low-rank columns (split across CTAs)."""
+    torch.manual_seed(3)
+    m, k, r, rl = 100, 640, 128, 48
+    x = (torch.randn(m, k) * 2).bfloat16().cuda()
+    s = (torch.rand(k) * 3 + 0.25).bfloat16().cuda()
+    l2 = (torch.randn(r, k) * 0.05).bfloat16().cuda()
+    a = (torch.randn(rl, k) * 0.05).bfloat16().cuda()
+    cs = torch.full((rl,), -1.25, device="cuda")
+    a16, mid, packed, scales = _act(x, s, l2, a, cs, k_pad=k)
+    torch.cuda.synchronize()
+    xh, q, pk, sa = O.act_quant(x.float().cpu().numpy(), s.float().cpu().numpy(), 64)
+    assert np.array_equal(packed.cpu().numpy(), pk)
+    assert np.array_equal(a16.float().cpu().numpy(), _dequant_np(q, sa, 64))
+    mid_np = mid.float().cpu().numpy()
+    rt = r + rl
+    got = mid_np[:, :rt] + mid_np[:, rt:2 * rt]
+    ref = np.concatenate([O.lowrank_down(xh, l2.float().cpu().numpy()),
+                          -1.25 * O.lowrank_down(x.float().cpu().numpy(), a.float().cpu().numpy())], 1)
+    assert O.rel_fro(got, ref) < TOL_MID
+    assert np.all(mid_np[:, 2 * rt:] == 0)
 
 
 def test_act_quant_ragged_rows_and_lora():
