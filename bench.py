@@ -3,15 +3,16 @@
 
 Default workload: one W4A4 ``SVDQuantLinear`` forward at
 M=4096 tokens, K=6144, N=16384, rank 32, group 64, bf16 bias; a step is the
-whole forward (activation-quant kernel + fused tcgen05 GEMM) over one batch
-already resident in HBM.  Metric: dense-equivalent TOPS = 2*M*N*K / step time.
+whole forward (activation pass + its low-rank finalize + fused tcgen05 GEMM)
+over one batch already resident in HBM.  Metric: dense-equivalent TOPS =
+2*M*N*K / step time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N > 1 runs under torchrun, one process per GPU; each rank runs its own batch
 (the image batch is sharded, no collective on the data path), so the reported
 value is the whole-job aggregate (weak scaling).  Timing: per-step CUDA events
-on the launching stream with an L2 flush (256 MiB memset) between steps,
+on the launching stream with an L2 flush (256 MiB write + 256 MiB read) between steps,
 barrier + synchronize around the timed region, max over ranks.
 """
 from __future__ import annotations
@@ -90,7 +91,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            time.sleep(0.05)
+            time.sleep(0.005)
 
     def __enter__(self):
         if self._nv is not None:
@@ -109,9 +110,10 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def cpu_reference_tops(calls: int, warmup: int, x_cpu, st_cpu) -> tuple[float, int, str]:
+def cpu_reference_tops(calls: int, warmup: int, x_cpu, st_cpu, budget_s: float = 0.0) -> tuple[float, int, str]:
     """Time the reference's CPU path (torch-on-CPU restatement of svdquant_linear_sim, bf16,
-    all host threads) on full config-2 calls."""
+    all host threads) on full config-2 calls: at least ``calls`` calls, and more until
+    ``budget_s`` seconds of CPU work have run."""
     import torch
 
     from oracle.svdq_oracle import svdquant_linear_sim_torch
@@ -124,9 +126,12 @@ def cpu_reference_tops(calls: int, warmup: int, x_cpu, st_cpu) -> tuple[float, i
         for _ in range(warmup):
             svdquant_linear_sim_torch(x_cpu, *args, **kw)
         t0 = time.perf_counter()
-        for _ in range(calls):
+        done = 0
+        while done < calls or time.perf_counter() - t0 < budget_s:
             svdquant_linear_sim_torch(x_cpu, *args, **kw)
-        dt = (time.perf_counter() - t0) / calls
+            done += 1
+        dt = (time.perf_counter() - t0) / done
+        calls = done
     sample = (f"{calls} full config-2 calls (M=4096) after {warmup} warm-up, bf16, torch CPU "
               f"restatement of svdquant_linear_sim (svd.py:119-163), {cores} threads")
     return OPS / dt / 1e12, cores, sample
@@ -177,17 +182,26 @@ def run_ours(args) -> None:
     x, st = make_synthetic_state(M, K, N, RANK, GROUP, seed=rank, device=dev)
     mod = SVDQuantLinear(st, backend="b200")
     p = mod.prepare(dev)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    # L2 flush between timed steps (outside the step events): write a 256 MiB buffer, then
+    # read another 256 MiB one so the written lines are evicted (written back) before the
+    # step starts instead of inside it
+    flush_w = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(32 * 1024 * 1024, dtype=torch.int64, device=dev)
+
+    def flush_l2():
+        flush_w.zero_()
+        return flush_r.sum()
 
     def step(ev=None):
-        # the module forward, with an event between its two kernels
+        # the module forward (SVDQuantLinear._run), with an event between the activation
+        # pass (2 launches: quantize + low-rank finalize) and the GEMM
         a16, mid, _, _ = ops.act_quant(x, p.smooth, p.l2, None, None, p.k_pad, 64, True, False)
         if ev is not None:
             ev.record()
         return ops.linear_gemm(a16, p.w16, mid, p.up_hl, p.bias, False)
 
     for _ in range(args.warmup):
-        flush.zero_()
+        flush_l2()
         step()
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -198,7 +212,7 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         for i in range(args.steps):
-            flush.zero_()
+            flush_l2()
             starts[i].record()
             step(mids[i])
             ends[i].record()
@@ -245,7 +259,7 @@ def run_ours(args) -> None:
         c = lambda t: None if t is None else t.cpu()
         stc = SVDQuantLinearState(c(st.smooth_scale), c(st.qweight), c(st.weight_scales), c(st.l1), c(st.l2),
                                   c(st.bias), st.group_size, st.original_shape, True, st.padded_in_features)
-        tops, cores, sample = cpu_reference_tops(args.cpu_calls, 1, x.cpu(), stc)
+        tops, cores, sample = cpu_reference_tops(args.cpu_calls, 1, x.cpu(), stc, budget_s=args.cpu_seconds)
         cpu_base = {"value": round(tops, 4), "unit": "TOPS", "cores": cores, "kind": "port", "sample": sample}
 
     if rank == 0:
@@ -255,32 +269,44 @@ def run_ours(args) -> None:
         achieved = OPS / (gemm_avg * 1e-3) / 1e12
         peaks = _peaks()
         if peaks.get("bf16_tflops"):
-            peak = 2.0 * float(peaks["bf16_tflops"])
-            peak_src = ("of measured: 2 x MEASURED_PEAKS.bf16_tflops (burst cuBLAS bf16); the B200 dense "
-                        "e4m3/int8 tensor rate is twice its dense bf16 rate")
+            peak = float(peaks["bf16_tflops"])
+            peak_src = ("of measured: MEASURED_PEAKS.bf16_tflops (burst cuBLAS bf16 GEMM); the GEMM's "
+                        "operands are fp16, whose dense tensor rate equals bf16's")
         else:
-            peak = 2.0 * 1590.0
-            peak_src = "of fallback: 2 x 1.59 PFLOP/s bf16 (profiling recipe)"
+            peak = 1590.0
+            peak_src = "of fallback: 1.59 PFLOP/s bf16 (profiling recipe)"
+        hbm = float(peaks.get("hbm_gbs") or 6650.0)
+        aq_avg = statistics.mean(aq_ms)
+        r2 = 0 if p.up_hl is None else p.up_hl.shape[1]
+        aq_bytes = 2 * M * K * 2 + M * r2 * 2  # x read + a16 write + mid_hl write
         e2e_ms = float(e2e.item())
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int4 (e4m3 MMA operands, fp32 accumulate)",
+            "vs_baseline": None,
+            "dtype": "fp16 MMA operands holding int4 code x group scale exactly, fp32 accumulate",
             "data": "synthetic (BASELINE recipe, seeded per rank), random-init weights",
             "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N, "rank": RANK, "group": GROUP,
-                       "l2": "flushed between timed steps (256 MiB memset outside the step events)",
+                       "l2": ("flushed between timed steps outside the step events: 256 MiB memset, then a "
+                              "256 MiB read so no dirty flush lines are written back inside a step"),
                        "parallelism": f"batch-sharded replicas x{world} (no collective on the data path)"},
             "roofline": {"bound": "tensor", "kernel": "linear_gemm_kernel", "achieved": round(achieved, 2),
                          "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                          "traffic": _ncu_traffic("linear_gemm_kernel"), "peak_source": peak_src,
                          "gemm_us": round(gemm_avg * 1e3, 2),
-                         "act_quant_us": round(statistics.mean(aq_ms) * 1e3, 2)},
+                         "flops_per_launch": OPS,
+                         "activation_pass": {"bound": "hbm", "kernels": "act_quant_kernel + mid_finalize_kernel",
+                                             "us": round(aq_avg * 1e3, 2), "bytes": aq_bytes,
+                                             "achieved": round(aq_bytes / (aq_avg * 1e-3) / 1e9, 1),
+                                             "peak": hbm, "unit": "GB/s",
+                                             "frac": round(aq_bytes / (aq_avg * 1e-3) / 1e9 / hbm, 4),
+                                             "traffic": _ncu_traffic("act_quant_kernel")}},
             "cpu_baseline": cpu_base,
             "e2e": {"value": round(world * OPS / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
                     "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
                     "ms_per_step": round(e2e_ms, 3),
                     "api": "SVDQuantLinear.forward with pinned host x -> device, y -> pinned host"},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -291,11 +317,13 @@ def run_ours(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-calls", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="minimum seconds of CPU work in the cpu_baseline sample")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
