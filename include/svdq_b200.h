@@ -101,6 +101,30 @@ int svdq_act_quant(const void* x, int64_t ldx, const void* smooth,
                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
+ * svdq_act_quant without a workspace argument: allocates nothing.  No
+ * counterpart in the reference (its activation quantization runs in torch /
+ * Triton and allocates through the framework).  For callers that cannot
+ * allocate device memory at the call site (an FFI host whose device memory is
+ * owned by another framework; a serving loop that forbids allocation after
+ * warm-up).  The K-slice scratch is a file-scope device array of
+ * svdq_act_quant_noalloc_scratch_bytes() (8 MiB) per device; a call needing
+ * more (svdq_act_quant_workspace_bytes() > 8 MiB) returns
+ * SVDQ_ERR_UNSUPPORTED.  The scratch address is looked up with
+ * cudaGetSymbolAddress on the first call on each device: if that first call
+ * would fall inside a stream capture, make one call before capturing.  All
+ * calls on a device share the scratch: calls that overlap in time race and
+ * must be serialized by the caller.  Arguments and results otherwise as
+ * svdq_act_quant.
+ */
+size_t svdq_act_quant_noalloc_scratch_bytes(void);
+int svdq_act_quant_noalloc(const void* x, int64_t ldx, const void* smooth,
+                           const void* l2, int rank,
+                           const void* lora_down, const float* lora_col_scale, int lora_rank,
+                           int M, int K_in, int K_pad, int a_group,
+                           void* out_packed, void* out_scales, void* out_a16,
+                           void* out_mid_hl, int R2, cudaStream_t stream);
+
+/*
  * Activation pass of the W4A16 linear: a16 = fp16(fp32(x) / fp32(smooth)) and
  * the low-rank/LoRA down-projection.  Replaces x / smooth and F.linear(x_hat, l2)
  * of the reference's float run (svd.py:122, 159) and the smoothing done by

@@ -28,6 +28,10 @@ SIGNATURES = {
     "svdq_act_quant": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
                         c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                         c_void_p, ctypes.c_size_t, c_void_p], c_int),
+    "svdq_act_quant_noalloc_scratch_bytes": ([], ctypes.c_size_t),
+    "svdq_act_quant_noalloc": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                                c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                c_void_p], c_int),
     "svdq_w4a16_prep": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
                          c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p, ctypes.c_size_t,
                          c_void_p], c_int),

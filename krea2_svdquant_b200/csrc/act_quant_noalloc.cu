@@ -1,0 +1,82 @@
+// svdq_act_quant_noalloc: the W4A4 activation pass with its K-slice scratch in
+// a file-scope device array instead of a caller-provided workspace.
+//
+// For callers that cannot allocate device memory at the call site: a C / FFI
+// host that binds only this ABI inside a process whose device memory belongs
+// to another framework, or a serving loop that forbids allocation after
+// warm-up so that no request can block on a synchronizing allocation or fail
+// on fragmentation.  The call allocates nothing: no cudaMalloc / cudaFree and
+// no other allocating routine.  The scratch address is looked up once per
+// device with cudaGetSymbolAddress on the first call on that device; when that
+// first call would otherwise fall inside a stream capture, make one call
+// before capturing.  The scratch holds kNoAllocScratchBytes; a call that needs
+// more is rejected with SVDQ_ERR_UNSUPPORTED and names the size it needs.
+// Nothing in the scratch has to start at zero: every K slice writes all of its
+// partial sums before the finalize launch reads them.  All calls on one device
+// share the one scratch array, so calls that overlap in time (on different
+// streams, or from different host threads) race on it and must be serialized
+// by the caller.
+#include <mutex>
+
+#include "svdq_common.cuh"
+
+extern "C" size_t svdq_act_quant_workspace_bytes(int M, int K_pad, int rank, int lora_rank);
+extern "C" int svdq_act_quant(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank,
+                              const void* lora_down, const float* lora_col_scale, int lora_rank, int M, int K_in,
+                              int K_pad, int a_group, void* out_packed, void* out_scales, void* out_a16,
+                              void* out_mid_hl, int R2, void* workspace, size_t workspace_bytes,
+                              cudaStream_t stream);
+
+namespace svdq {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device (looked up once per device).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  int st = check_cuda(cudaGetDevice(&dev), "svdq_act_quant_noalloc: current device");
+  if (st) return st;
+  if (dev < 0 || dev >= kMaxDevices) return set_error(SVDQ_ERR_UNSUPPORTED, "svdq_act_quant_noalloc: device ordinal");
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    st = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "svdq_act_quant_noalloc: scratch address");
+    if (st) return st;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return SVDQ_OK;
+}
+
+}  // namespace
+}  // namespace svdq
+
+extern "C" size_t svdq_act_quant_noalloc_scratch_bytes(void) { return svdq::kNoAllocScratchBytes; }
+
+extern "C" int svdq_act_quant_noalloc(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank,
+                                      const void* lora_down, const float* lora_col_scale, int lora_rank, int M,
+                                      int K_in, int K_pad, int a_group, void* out_packed, void* out_scales,
+                                      void* out_a16, void* out_mid_hl, int R2, cudaStream_t stream) {
+  using namespace svdq;
+  const size_t need = (out_mid_hl && rank + lora_rank > 0 && M > 0 && K_pad > 0 && rank >= 0 && lora_rank >= 0)
+                          ? svdq_act_quant_workspace_bytes(M, K_pad, rank, lora_rank)
+                          : 0;
+  if (need > kNoAllocScratchBytes)
+    return set_error(SVDQ_ERR_UNSUPPORTED, "svdq_act_quant_noalloc: this call needs " + std::to_string(need) +
+                                               " bytes of scratch but the static scratch holds " +
+                                               std::to_string(kNoAllocScratchBytes) +
+                                               " bytes; use svdq_act_quant with a caller-provided workspace");
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int st = noalloc_scratch(&scratch);
+    if (st) return st;
+  }
+  return svdq_act_quant(x, ldx, smooth, l2, rank, lora_down, lora_col_scale, lora_rank, M, K_in, K_pad, a_group,
+                        out_packed, out_scales, out_a16, out_mid_hl, R2, scratch, need, stream);
+}
