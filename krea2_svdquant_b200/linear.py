@@ -5,10 +5,14 @@ bias]``), attributes, ``add_lora_adapter``, ``state`` property and
 ``_forward_base`` / ``forward`` split.  The forward runs on the B200 CUDA
 library only:
 
-* ``b200`` (W4A4, the default): one activation pass (smoothing, INT4 codes,
-  low-rank + LoRA down-projection) and one fused tcgen05 GEMM (INT4 x INT4
-  residual with per-group rescale, low-rank/LoRA up-projection, bias, cast).
-* ``b200_w4a16``: bf16 activations against the INT4 weight.
+* ``b200`` (W4A4, the default): one activation pass (smoothing, dynamic INT4
+  codes per token and group, low-rank + LoRA down-projection) and one fused
+  tcgen05 GEMM.  The GEMM's operands are the dequantized codes ``q * scale``
+  of activations and weights, both exact in fp16, so the whole K reduction
+  accumulates in TMEM; the low-rank/LoRA up-projection, bias and cast are
+  fused into the same kernel.
+* ``b200_w4a16``: the activation pass only smooths (``fp16(x / s)``), the same
+  GEMM runs against the INT4 weight's exact fp16 dequantization.
 
 Errors raise; nothing falls back to another implementation (the reference
 swallows kernel errors and reruns its simulation, linear.py:133-154).
@@ -149,9 +153,10 @@ class SVDQuantLinear(nn.Module):
             a.multiplier for a in self.lora_adapters)
 
     def prepare(self, device: torch.device | str | None = None) -> PreparedOperands:
-        """Derive (once per device and buffer set) the kernel operands: e4m3
-        weight codes, transposed fp32 scales, ``[l1|lora_up]`` hi/lo operand,
-        padded smoothing / down-projection weights."""
+        """Derive (once per device and buffer set) the kernel operands: the fp16
+        weight operand ``w16 = q * weight_scale``, the ``[l1|lora_up]`` hi/lo
+        up-projection operand, padded smoothing / down-projection weights and
+        the stacked LoRA down weights with their per-row multipliers."""
         device = torch.device(device) if device is not None else self.qweight.device
         if device.type != "cuda":
             raise ValueError("SVDQuantLinear.prepare needs a CUDA device (no CPU path in this runtime)")
@@ -249,6 +254,10 @@ class SVDQuantLinear(nn.Module):
                 y = y + adapter(x)
             return y
         return self._run(x, include_lora=True)
+
+    def release_prepared(self) -> None:
+        """Drop the derived device operands (they are rebuilt on the next forward)."""
+        self._prepared = None
 
     def extra_repr(self) -> str:
         n, k = self.original_shape
