@@ -176,6 +176,33 @@ int svdq_linear_gemm(const void* a16, const void* w16,
                      int M, int N, int K_pad,
                      cudaStream_t stream);
 
+/*
+ * Block-weight prefetcher.  Replaces the synchronous per-tensor `.to(device)`
+ * uploads of the reference's block offloader
+ * (src/krea2_svdquant/runtime/block_offload.py:56-63, 157-173) with one
+ * cudaMemcpyAsync per block from a pinned host arena into a device slot, on a
+ * low-priority copy stream.  The caller owns the host arenas and the device
+ * slots.  Per slot, an upload waits on the GPU for the slot's last release on
+ * the compute stream; compute waits for the upload (and whatever the caller
+ * enqueued after it on the copy stream) through svdq_prefetch_wait.
+ *   create   -> copy stream + two events per slot (num_slots in [1, 64])
+ *   begin    -> enqueue the upload of `bytes` from pinned host_src into dev_dst
+ *   commit   -> mark the slot ready after everything on the copy stream so far
+ *   wait     -> order `compute` after the slot's ready mark; timeout_ms >= 0 also
+ *               blocks the host for at most timeout_ms (SVDQ_ERR_TIMEOUT after)
+ *   release  -> record the end of the slot's use on `compute`
+ *   sync     -> host wait (bounded by timeout_ms unless < 0) for all uploads
+ */
+typedef struct svdq_prefetcher svdq_prefetcher;
+int svdq_prefetcher_create(int device, int num_slots, svdq_prefetcher** out);
+int svdq_prefetcher_copy_stream(svdq_prefetcher* p, cudaStream_t* out);
+int svdq_prefetch_begin(svdq_prefetcher* p, int slot, void* dev_dst, const void* host_src, size_t bytes);
+int svdq_prefetch_commit(svdq_prefetcher* p, int slot);
+int svdq_prefetch_wait(svdq_prefetcher* p, int slot, cudaStream_t compute, int timeout_ms);
+int svdq_prefetch_release(svdq_prefetcher* p, int slot, cudaStream_t compute);
+int svdq_prefetcher_sync(svdq_prefetcher* p, int timeout_ms);
+int svdq_prefetcher_destroy(svdq_prefetcher* p);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,6 +35,14 @@ SIGNATURES = {
     "svdq_w4a16_prep": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
                          c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p, ctypes.c_size_t,
                          c_void_p], c_int),
+    "svdq_prefetcher_create": ([c_int, c_int, ctypes.POINTER(c_void_p)], c_int),
+    "svdq_prefetcher_copy_stream": ([c_void_p, ctypes.POINTER(c_void_p)], c_int),
+    "svdq_prefetch_begin": ([c_void_p, c_int, c_void_p, c_void_p, ctypes.c_size_t], c_int),
+    "svdq_prefetch_commit": ([c_void_p, c_int], c_int),
+    "svdq_prefetch_wait": ([c_void_p, c_int, c_void_p, c_int], c_int),
+    "svdq_prefetch_release": ([c_void_p, c_int, c_void_p], c_int),
+    "svdq_prefetcher_sync": ([c_void_p, c_int], c_int),
+    "svdq_prefetcher_destroy": ([c_void_p], c_int),
     "svdq_repack_weight": ([c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p], c_int),
     "svdq_build_up_hl": ([c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p], c_int),
     "svdq_linear_gemm": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
