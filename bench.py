@@ -162,6 +162,131 @@ def run_reference(args) -> None:
     }), flush=True)
 
 
+def _device_times(fn, iters: int, flush, warmup: int = 2) -> list[float]:
+    """Per-call device times (ms) of ``fn`` with CUDA events, L2 flushed before each call."""
+    import torch
+    for _ in range(warmup):
+        flush()
+        fn()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(iters):
+        flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        out.append(a.elapsed_time(b))
+    return out
+
+
+def measure_block_linears(dev, flush, iters: int) -> dict:
+    """the 8 quantized linears of one Krea2 block at M=4352 (4096 image +
+    256 text tokens), rank 32, group 64, W4A4; time = sum of the 8 module forwards."""
+    import torch
+
+    from krea2_svdquant_b200.linear import SVDQuantLinear
+    from krea2_svdquant_b200.quant import random_state
+    from krea2_svdquant_b200.transformer import Krea2StandInConfig
+
+    m_tok = 4352
+    gen = torch.Generator(device=dev).manual_seed(3)
+    per, total_ops, total_ms = {}, 0, 0.0
+    for name, (n, k) in Krea2StandInConfig().linear_shapes().items():
+        mod = SVDQuantLinear(random_state(n, k, 32, 64, device=dev, generator=gen), backend="b200")
+        x = torch.randn(m_tok, k, device=dev, generator=gen).bfloat16()
+        mod.prepare(dev)
+        ms = statistics.median(_device_times(lambda: mod(x), iters, flush))
+        ops_ = 2 * m_tok * n * k
+        per[name] = {"N": n, "K": k, "us": round(ms * 1e3, 1), "tops": round(ops_ / (ms * 1e-3) / 1e12, 1)}
+        total_ops += ops_
+        total_ms += ms
+        del mod, x
+    return {"config": "BASELINE config 3: 8 linears of one Krea2 block, M=4352, rank 32, group 64, W4A4",
+            "ops": total_ops, "ms": round(total_ms, 4), "tops": round(total_ops / (total_ms * 1e-3) / 1e12, 1),
+            "per_linear": per}
+
+
+def measure_w4a16_lora(dev, flush, iters: int) -> dict:
+    """W4A16 X[4096,6144] x INT4 W[16384,6144] (group 64, bf16 scales), rank-32
+    SVD branch + LoRA rank 64 (A, B ~ N(0, 0.01), scale 0.8)."""
+    import torch
+
+    from krea2_svdquant_b200.linear import SVDQuantLinear
+    from krea2_svdquant_b200.quant import random_state
+
+    gen = torch.Generator(device=dev).manual_seed(4)
+    mod = SVDQuantLinear(random_state(N, K, 32, 64, device=dev, generator=gen), backend="b200_w4a16")
+    mod.add_lora_adapter(torch.randn(64, K, device=dev, generator=gen).mul_(0.01).bfloat16(),
+                         torch.randn(N, 64, device=dev, generator=gen).mul_(0.01).bfloat16(), scale=0.8)
+    x = torch.randn(M, K, device=dev, generator=gen).bfloat16()
+    mod.prepare(dev)
+    ms = statistics.median(_device_times(lambda: mod(x), iters, flush))
+    lowrank = 2 * M * (K + N) * 32 + 2 * M * 64 * (K + N)
+    return {"config": "BASELINE config 4: W4A16 + rank-32 SVD branch + LoRA r64 (scale 0.8), M4096 K6144 N16384",
+            "ms": round(ms, 4), "tops": round(OPS / (ms * 1e-3) / 1e12, 1),
+            "lowrank_lora_ops": lowrank}
+
+
+def measure_forward28(world: int, rank: int, dev, args) -> dict:
+    """random-init Krea2-shaped 28-block transformer (hidden 6144, 48/12 heads x 128,
+    MLP 16384, every listed linear W4A4 rank 32 / group 64), 8 images of 4096 latent + 256 text tokens,
+    8 denoising steps (8 full forwards); the batch is sharded over the ranks, no collective on the
+    data path; block offload with the prefetcher on at 1 GPU.  images/s = 8 / max over ranks of the
+    device time of the 8 forwards."""
+    import torch
+    import torch.distributed as dist
+
+    from krea2_svdquant_b200.offload import enable_block_offload
+    from krea2_svdquant_b200.transformer import Krea2StandInConfig, Krea2StandInTransformer
+
+    cfg = Krea2StandInConfig()
+    images = 8
+    if images % world:
+        raise ValueError("the 8-image batch must split evenly over the ranks")
+    local = images // world
+    offload = world == 1 and not args.no_offload
+    model = Krea2StandInTransformer.random_svdquant(cfg, seed=0, init_device=dev,
+                                                    keep_on="cpu" if offload else dev)
+    off = None
+    if offload:
+        off = enable_block_offload(model, dev, num_blocks_on_gpu=1, pin_memory=True)
+    else:
+        model.to(dev)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    lat = torch.randn(local, cfg.image_tokens, cfg.in_channels, device=dev, generator=g).bfloat16()
+    txt = torch.randn(local, cfg.text_tokens, cfg.hidden, device=dev, generator=g).bfloat16()
+    with torch.no_grad():
+        model(lat, txt)  # warm-up step (derives the resident blocks' GEMM operands)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.forward_steps):
+            out = model(lat, txt)
+        b.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    finite = bool(torch.isfinite(out).all().item())
+    if off is not None:
+        off.remove()
+    del model
+    torch.cuda.empty_cache()
+    lin_ops = 2 * (cfg.image_tokens + cfg.text_tokens) * sum(n * k for n, k in cfg.linear_shapes().values())
+    return {"config": ("BASELINE config 5: Krea2-shaped stand-in, 28 blocks, 8 images x (4096+256) tokens, "
+                       f"{args.forward_steps} denoising steps, batch sharded over {world} GPU(s), "
+                       f"block offload {'on (prefetcher)' if offload else 'off'}"),
+            "images_per_s": round(images * 1.0 / (ms * 1e-3) * (8 / args.forward_steps), 4),
+            "ms_per_denoising_step": round(ms / args.forward_steps, 2), "images": images,
+            "images_per_rank": local, "steps_timed": args.forward_steps,
+            "linear_ops_per_image_step": lin_ops * cfg.num_layers, "output_finite": finite}
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -253,6 +378,16 @@ def run_ours(args) -> None:
         dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
         dist.barrier()
 
+    extra = {}
+    if not args.no_extra:
+        # configs 3-4 on every rank (independent), config 5 with the batch sharded over the ranks
+        extra["block_linears"] = measure_block_linears(dev, flush_l2, 10)
+        extra["w4a16_lora"] = measure_w4a16_lora(dev, flush_l2, 10)
+        torch.cuda.empty_cache()
+        extra["forward28"] = measure_forward28(world, rank, dev, args)
+        if _lib.device_error():
+            raise RuntimeError("device-side error during the extra measurements")
+
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from krea2_svdquant_b200.quant import SVDQuantLinearState
@@ -307,6 +442,7 @@ def run_ours(args) -> None:
                     "ms_per_step": round(e2e_ms, 3),
                     "api": "SVDQuantLinear.forward with pinned host x -> device, y -> pinned host"},
             "gpu_launches": 3 * args.steps,
+            **extra,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -321,6 +457,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the config 3/4/5 measurements (block linears, W4A16+LoRA, 28-block forward)")
+    ap.add_argument("--no-offload", action="store_true", help="28-block forward without block offload at 1 GPU")
+    ap.add_argument("--forward-steps", type=int, default=8, help="denoising steps timed in the 28-block forward")
     ap.add_argument("--cpu-calls", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="minimum seconds of CPU work in the cpu_baseline sample")

@@ -118,3 +118,24 @@ def make_synthetic_state(m: int, k: int, n: int, rank: int = 32, group: int = 64
                                       x, rank=rank, group_size=group, smooth_min=lo, smooth_max=hi,
                                       scale_dtype=scale_dtype)
     return x, st
+
+
+def random_state(n: int, k: int, rank: int = 32, group: int = 64, *, device: str | torch.device = "cpu",
+                 generator: torch.Generator | None = None, bias: bool = True,
+                 scale_dtype: torch.dtype = torch.bfloat16) -> SVDQuantLinearState:
+    """A random-init quantized layer with the statistics of a converted N(0, 0.02) weight:
+    uniform INT4 codes, group scales near absmax(N(0,0.02) over 64)/7, rank-``rank`` factors
+    of matching size, smoothing factors in [0.5, 2], bias ~ N(0, 0.01).  Used to build
+    random-init models of a given architecture without running the converter."""
+    dev = torch.device(device)
+    kw = dict(device=dev, generator=generator)
+    k_pad = (k + group - 1) // group * group
+    qweight = torch.randint(0, 256, (n, k_pad // 2), dtype=torch.uint8, **kw)
+    scales = (torch.rand((n, k_pad // group), **kw) * 0.004 + 0.005).to(scale_dtype)
+    l1 = (torch.randn((n, rank), **kw) * 0.05).to(torch.bfloat16)
+    l2 = (torch.randn((rank, k), **kw) * 0.05).to(torch.bfloat16)
+    smooth = (torch.rand((k,), **kw) * 1.5 + 0.5).to(torch.bfloat16)
+    b = (torch.randn((n,), **kw) * 0.01).to(torch.bfloat16) if bias else None
+    return SVDQuantLinearState(smooth_scale=smooth, qweight=qweight, weight_scales=scales, l1=l1, l2=l2, bias=b,
+                               group_size=group, original_shape=(n, k), qweight_packed=True,
+                               padded_in_features=k_pad)
