@@ -22,7 +22,6 @@ import json
 import os
 import statistics
 import sys
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -57,8 +56,27 @@ def _ncu_traffic(kernel: str) -> float | None:
     return None
 
 
+_SAMPLER_CHILD = r"""
+import select, sys, time
+import pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+while True:
+    if select.select([sys.stdin], [], [], 0.005)[0]:
+        break
+    try:
+        print(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+              pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+    except pynvml.NVMLError:
+        pass
+sys.stdout.flush()
+"""
+
+
 class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML while running."""
+    """Samples the SM clock and the clock-event reasons every 5 ms through NVML, in a child
+    process (a thread would share the GIL with the launch loop and miss samples)."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
@@ -66,43 +84,48 @@ class ClockSampler:
         0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
     }
 
-    def __init__(self, index: int):
+    def __init__(self, cuda_index: int):
         self.samples: list[int] = []
         self.reasons: set[str] = set()
         self.max_mhz = None
-        self._stop = threading.Event()
-        self._thread = None
+        self._proc = None
+        self._nvml_index = cuda_index
         try:
-            import pynvml
-            pynvml.nvmlInit()
-            self._nv = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            import torch
+            self._nvml_index = torch.cuda._get_nvml_device_index(cuda_index)
         except Exception:
-            self._nv = None
-
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
-                mask = self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                for bit, name in self.REASONS.items():
-                    if mask & bit and name != "gpu_idle":
-                        self.reasons.add(name)
-            except Exception:
-                pass
-            time.sleep(0.005)
+            pass
 
     def __enter__(self):
-        if self._nv is not None:
-            self._thread = threading.Thread(target=self._run, daemon=True)
-            self._thread.start()
+        import subprocess
+        try:
+            self._proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_CHILD, str(self._nvml_index)],
+                                          stdin=subprocess.PIPE, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                          text=True)
+            first = self._proc.stdout.readline().split()
+            if len(first) == 2 and first[0] == "max":
+                self.max_mhz = int(first[1])
+        except Exception:
+            self._proc = None
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
-        if self._thread:
-            self._thread.join()
+        if self._proc is None:
+            return
+        try:
+            out, _ = self._proc.communicate(input="stop\n", timeout=30)
+        except Exception:
+            self._proc.kill()
+            out = ""
+        for line in out.splitlines():
+            parts = line.split()
+            if len(parts) != 2:
+                continue
+            clk, mask = int(parts[0]), int(parts[1])
+            self.samples.append(clk)
+            for bit, name in self.REASONS.items():
+                if mask & bit and name != "gpu_idle":
+                    self.reasons.add(name)
 
     def summary(self) -> dict:
         busy = [s for s in self.samples if self.max_mhz is None or s > 0.3 * self.max_mhz] or self.samples
@@ -241,11 +264,11 @@ def measure_forward28(world: int, rank: int, dev, args) -> dict:
     from krea2_svdquant_b200.offload import enable_block_offload
     from krea2_svdquant_b200.transformer import Krea2StandInConfig, Krea2StandInTransformer
 
+    from krea2_svdquant_b200.shard import max_over_ranks, shard_range
+
     cfg = Krea2StandInConfig()
     images = 8
-    if images % world:
-        raise ValueError("the 8-image batch must split evenly over the ranks")
-    local = images // world
+    _, local = shard_range(images, world, rank)
     offload = world == 1 and not args.no_offload
     model = Krea2StandInTransformer.random_svdquant(cfg, seed=0, init_device=dev,
                                                     keep_on="cpu" if offload else dev)
@@ -268,10 +291,7 @@ def measure_forward28(world: int, rank: int, dev, args) -> dict:
             out = model(lat, txt)
         b.record()
         torch.cuda.synchronize()
-    t = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms = max_over_ranks(a.elapsed_time(b), dev)
     finite = bool(torch.isfinite(out).all().item())
     if off is not None:
         off.remove()
@@ -302,7 +322,7 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     x, st = make_synthetic_state(M, K, N, RANK, GROUP, seed=rank, device=dev)
     mod = SVDQuantLinear(st, backend="b200")
@@ -453,7 +473,7 @@ def run_ours(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
