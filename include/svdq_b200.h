@@ -177,6 +177,18 @@ int svdq_linear_gemm(const void* a16, const void* w16,
                      cudaStream_t stream);
 
 /*
+ * Converter weight quantization on the GPU: an fp32 layer residual w [N, K]
+ * (row stride ldw) -> packed INT4 codes [N, K_pad/2] (nibble q + 8, even k
+ * low) and group scales [N, K_pad/group] as fp32, fp16 or bf16, with
+ * K_pad = round_up(K, group).  Bit-exact with quantize_symmetric_int4 on fp32
+ * input + pack_int4 (src/krea2_svdquant/quant/pack.py:6-23, 47-56) as
+ * scripts/convert_simulated.py:197-203 calls them; fp16 / bf16 scales are the
+ * fp32 scales rounded once.  group in {64, 128}; out_packed 4-byte aligned.
+ */
+int svdq_quantize_weight(const float* w, int64_t ldw, int N, int K, int group,
+                         void* out_packed, void* out_scales, int scale_dtype, cudaStream_t stream);
+
+/*
  * Block-weight prefetcher.  Replaces the synchronous per-tensor `.to(device)`
  * uploads of the reference's block offloader
  * (src/krea2_svdquant/runtime/block_offload.py:56-63, 157-173) with one

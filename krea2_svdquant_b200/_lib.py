@@ -43,6 +43,7 @@ SIGNATURES = {
     "svdq_prefetch_release": ([c_void_p, c_int, c_void_p], c_int),
     "svdq_prefetcher_sync": ([c_void_p, c_int], c_int),
     "svdq_prefetcher_destroy": ([c_void_p], c_int),
+    "svdq_quantize_weight": ([c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p], c_int),
     "svdq_repack_weight": ([c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p], c_int),
     "svdq_build_up_hl": ([c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p], c_int),
     "svdq_linear_gemm": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,

@@ -129,6 +129,31 @@ def _(x, smooth, l2, lora_down, lora_col_scale, k_pad):
             x.new_empty((m, r2) if r2 else (0,), dtype=torch.bfloat16))
 
 
+# --------------------------------------------------------------------------- converter
+@torch.library.custom_op("svdq_b200::quantize_weight", mutates_args=())
+def quantize_weight(w: Tensor, group: int, scale_dtype: torch.dtype) -> tuple[Tensor, Tensor]:
+    """fp32 residual ``w [N, K]`` -> ``(packed [N, K_pad/2] u8, scales [N, K_pad/group])``, bit-exact with
+    the reference's ``pack_int4(quantize_symmetric_int4(w, group, dim=1))`` (scales rounded once to
+    ``scale_dtype``)."""
+    _need_cuda("quantize_weight", w)
+    _need(w.dim() == 2 and w.dtype == torch.float32 and w.stride(1) == 1, "quantize_weight: w must be fp32 [N, K]")
+    _need(scale_dtype in _DT, "quantize_weight: scale_dtype must be float32, float16 or bfloat16")
+    n, k = w.shape
+    k_pad = round_up(k, group)
+    packed = torch.empty((n, k_pad // 2), dtype=torch.uint8, device=w.device)
+    scales = torch.empty((n, k_pad // group), dtype=scale_dtype, device=w.device)
+    _lib.call("svdq_quantize_weight", _p(w), w.stride(0), n, k, group, _p(packed), _p(scales), _DT[scale_dtype],
+              _stream(w.device))
+    return packed, scales
+
+
+@quantize_weight.register_fake
+def _(w, group, scale_dtype):
+    n, k = w.shape
+    k_pad = round_up(k, group)
+    return (w.new_empty((n, k_pad // 2), dtype=torch.uint8), w.new_empty((n, k_pad // group), dtype=scale_dtype))
+
+
 # --------------------------------------------------------------------------- load-time operands
 @torch.library.custom_op("svdq_b200::repack_weight", mutates_args=())
 def repack_weight(qweight: Tensor, scales: Tensor, w_group: int) -> Tensor:

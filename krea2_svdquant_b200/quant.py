@@ -96,6 +96,31 @@ def quantize_linear_from_samples(weight: torch.Tensor, bias: torch.Tensor | None
                                qweight_packed=packed, padded_in_features=q.shape[-1] if packed else None)
 
 
+def quantize_linear_from_samples_cuda(weight: torch.Tensor, bias: torch.Tensor | None, x_samples: torch.Tensor,
+                                      rank: int = 32, group_size: int = 128, smooth_min: float | None = 0.25,
+                                      smooth_max: float | None = 4.0, scale_dtype: torch.dtype = torch.float16,
+                                      lowrank: tuple[torch.Tensor, torch.Tensor] | None = None
+                                      ) -> SVDQuantLinearState:
+    """GPU converter for one layer (scripts/convert_simulated.py:183-208 on the device): smoothing,
+    low-rank factors and residual with torch on the weight's CUDA device, then the residual's INT4
+    quantization and packing in the CUDA library (``svdq_quantize_weight``), bit-exact with the
+    reference's ``pack_int4(quantize_symmetric_int4(residual))``.  ``lowrank`` passes precomputed
+    ``(l1, l2)`` instead of running the randomized SVD.  Returns a packed state whose scales are
+    rounded once to ``scale_dtype`` (fp16 in the reference checkpoints)."""
+    from . import ops
+
+    if not weight.is_cuda:
+        raise ValueError("quantize_linear_from_samples_cuda needs a CUDA weight")
+    smooth = compute_smooth_scale(x_samples.float().abs().amax(dim=0), weight, smooth_min, smooth_max)
+    migrated = weight * smooth.unsqueeze(0)
+    l1, l2 = lowrank if lowrank is not None else svd_lowrank(migrated, rank)
+    residual = (migrated.float() - l1.float() @ l2.float()).contiguous()
+    qw, ws = ops.quantize_weight(residual, group_size, scale_dtype)
+    return SVDQuantLinearState(smooth_scale=smooth, qweight=qw, weight_scales=ws, l1=l1, l2=l2, bias=bias,
+                               group_size=group_size, original_shape=tuple(weight.shape), qweight_packed=True,
+                               padded_in_features=qw.shape[-1] * 2)
+
+
 def make_synthetic_state(m: int, k: int, n: int, rank: int = 32, group: int = 64, *, seed: int = 0,
                          bias: bool = True, device: str | torch.device = "cpu", outlier_frac: float = 0.01,
                          outlier_scale: float = 20.0, scale_dtype: torch.dtype = torch.bfloat16,

@@ -65,6 +65,7 @@ def baseline_inputs(m, k, n, rank, group, *, seed, bias=True, scale_dtype=torch.
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("KREA2_REF_SRC", "/root/reference/src"))
+    ap.add_argument("--only", default=None, help="write only this fixture (file stem)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     from krea2_svdquant.quant.pack import pack_int4, quantize_symmetric_int4, unpack_int4
@@ -115,6 +116,9 @@ def main() -> None:
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
         print("wrote", name, {k2: v.shape for k2, v in out.items()})
 
+    if args.only == "weight_quant_fp32":
+        weight_quant_case(quantize_symmetric_int4, pack_int4)
+        return
     # BASELINE recipe (config-1 distributions) at a fixture-friendly size.
     linear_case("linear_g64", 64, 1024, 256, 32, 64, seed=1, lora=(16, 0.8, 8.0))
     # K not a group multiple: padded to 192 inside quantize_symmetric_int4 (pack.py:12-16).
@@ -149,6 +153,29 @@ def main() -> None:
     out["scales_fp32_g32"] = sf.numpy()
     np.savez_compressed(os.path.join(HERE, "quant_edges.npz"), **out)
     print("wrote quant_edges")
+    weight_quant_case(quantize_symmetric_int4, pack_int4)
+
+
+def weight_quant_case(quantize_symmetric_int4, pack_int4) -> None:
+    """The converter's weight quantization (convert_simulated.py:197-203): an fp32 residual
+    quantized along K with fp32 scales, then packed; K = 200 is not a group multiple."""
+    g = torch.Generator().manual_seed(9)
+    w = torch.randn(48, 200, generator=g) * 0.02
+    w[:, ::37] *= 15.0                                   # outlier columns
+    w[3] = 0.0                                           # all-zero row -> 1e-8 clamp
+    w[4, :64] = torch.arange(64, dtype=torch.float32) % 15 - 7.0  # amax 7: scale exactly 1
+    w[4, 1:14] = torch.tensor([0.5, 1.5, 2.5, 3.5, 4.5, 5.5, 6.5, -0.5, -1.5, -2.5, -3.5, -4.5, -5.5])  # ties
+    w[5, :64] = -w[5, :64].abs()                         # negative maximum
+    w[6] = w[6] * 1e-6
+    out = {"w": w.numpy()}
+    for group in (64, 128):
+        q, sc = quantize_symmetric_int4(w, group_size=group, dim=1)
+        out[f"q_g{group}"] = q.numpy()
+        out[f"packed_g{group}"] = pack_int4(q).numpy()
+        out[f"scales_g{group}"] = sc.numpy()
+        out[f"scales_fp16_g{group}"] = sc.to(torch.float16).numpy()
+    np.savez_compressed(os.path.join(HERE, "weight_quant_fp32.npz"), **out)
+    print("wrote weight_quant_fp32")
 
 
 if __name__ == "__main__":

@@ -103,3 +103,14 @@ def test_bf16_round_matches_torch():
     a[:8] = [0.0, -0.0, np.inf, -np.inf, 1e-45, 3.4e38, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8]
     t = torch.from_numpy(a).bfloat16().float().numpy()
     assert np.array_equal(O.bf16_round(a).view(np.uint32), t.view(np.uint32))
+
+
+def test_weight_quant_fp32_matches_reference(golden):
+    """The converter's fp32 residual quantization (pack.py:6-23, 47-56 on fp32 input)."""
+    g = golden("weight_quant_fp32")
+    for group in (64, 128):
+        q, sc = O.quantize_symmetric_int4(g["w"], group, "fp32")
+        assert np.array_equal(q, g[f"q_g{group}"])
+        assert np.array_equal(sc.view(np.uint32), g[f"scales_g{group}"].view(np.uint32))
+        assert np.array_equal(O.pack_int4(q), g[f"packed_g{group}"])
+        assert np.array_equal(sc.astype(np.float16), g[f"scales_fp16_g{group}"])
