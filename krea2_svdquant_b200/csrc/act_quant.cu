@@ -42,12 +42,11 @@ constexpr int kWarps = 4;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kBM = 64;              // rows per CTA (16 per warp)
 constexpr int kBK = 64;              // columns per stage: one 128-byte swizzle row of bf16
-constexpr int kMaxSliceStages = 16;  // stages per CTA slice (bounds the reciprocal table)
+constexpr int kMaxSliceStages = 12;  // stages per CTA slice (bounds the reciprocal table)
 constexpr int kMinSliceStages = 2;
 constexpr int kTargetCtasPerSm = 4;
 constexpr uint32_t kXTileBytes = kBM * kBK * 2;   // 8 KB
 constexpr uint32_t kLrTileBytes = 8 * kBK * 2;    // 1 KB: 8 low-rank rows
-constexpr uint32_t kOutTileBytes = 16 * kBK * 2;  // 2 KB: one warp's a16 tile
 // a16 = q * scale is exact in fp16 while the group scale lies in [2^-17, 65504 / 7]:
 // above it a16 overflows (recorded as kErrA16Range in the device error word),
 // below it the smallest codes round in fp16's subnormal range (absolute error < 2^-25).
@@ -114,6 +113,25 @@ __device__ __forceinline__ float bf2_absmax_f(uint32_t m) {
   return fmaxf(fabsf(__uint_as_float(m << 16)), fabsf(__uint_as_float(m & 0xFFFF0000u)));
 }
 
+// Non-blocking check of an mbarrier phase.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Shared-memory counter increment with acquire-release ordering at CTA scope.
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t addr, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(addr), "r"(v) : "memory");
+  return old;
+}
+
 struct AqArgs {
   int M, K_in, K_pad;
   int rank, lora_rank, r_tot;
@@ -128,20 +146,23 @@ struct AqArgs {
   int* err;
 };
 
-struct AqSmem {
-  uint32_t xs, ws, ost, rst, bars;  // shared addresses
-};
-
 template <int STAGES, int NT>
 __host__ __device__ constexpr uint32_t aq_smem_layout_bytes() {
-  return 1024 /*align slack*/ + STAGES * kXTileBytes + STAGES * NT * kLrTileBytes + kWarps * kOutTileBytes +
+  return 1024 /*align slack*/ + STAGES * kXTileBytes + STAGES * NT * kLrTileBytes +
          kMaxSliceStages * 32 * 16 /*reciprocal table*/ + 256 /*barriers, counters*/;
 }
 
 // GS: stages per quantization group (1: G=64, 2: G=128).  NT: 8-column
 // low-rank tiles per CTA (0: no mid).  PACKED: also write reference-format
-// codes and scales.
-template <int GS, int STAGES, int NT, bool W4A16, bool PACKED>
+// codes and scales.  LORA: some low-rank rows of this launch are LoRA rows
+// (multiplied with raw x rather than x_hat).
+//
+// Each warp writes its 16 x 64 a16 tile in place over its own 16 rows of the
+// x stage (the rows it alone reads) and TMA-stores it from there, so a stage
+// is released only once that store has read it: stage c is released after
+// the store of stage c + 1 is issued (bulk wait_group.read 1), in the same
+// single-lane section.
+template <int GS, int STAGES, int NT, bool W4A16, bool PACKED, bool LORA>
 __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
     act_quant_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_l2,
                      const __grid_constant__ CUtensorMap tm_lora, const __grid_constant__ CUtensorMap tm_a16,
@@ -150,8 +171,7 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t xs = base;
   const uint32_t ws = xs + STAGES * kXTileBytes;
-  const uint32_t ost = ws + STAGES * NT * kLrTileBytes;
-  const uint32_t rst = ost + kWarps * kOutTileBytes;
+  const uint32_t rst = ws + STAGES * NT * kLrTileBytes;
   const uint32_t bars = rst + kMaxSliceStages * 32 * 16;
   uint8_t* gbase = smem_raw + (base - smem_u32(smem_raw));
   const float4* rst_p = reinterpret_cast<const float4*>(gbase + (rst - base));
@@ -219,7 +239,9 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
   const int wrow = warp * 16;              // first row of this warp within the CTA tile
   const int row_g = m0 + wrow + g;         // global rows held by this lane
   const int row_g8 = row_g + 8;
-  const uint32_t my_ost = ost + warp * kOutTileBytes;
+  const uint32_t my_rows = (uint32_t)warp * (16 * kBK * 2);  // this warp's 16 rows within an x stage
+  const bool write_a16 = a.write_a16 != 0;
+  const uint32_t cnt_base = smem_u32(cnt);
   bool ok = true;
   bool a16_range = false;  // some group scale of this lane exceeded kA16ScaleMax
 
@@ -230,24 +252,25 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
   const int b_row = (lane & 7) + ((lane >> 4) << 3);
   const int b_chk = (lane >> 3) & 1;
 
+  // k16 steps outermost so the NT accumulator chains advance side by side
   auto lowrank_mma = [&](const uint32_t (&fr)[4][4], int s, bool lora_pass) {
     if constexpr (NT > 0) {
+      constexpr bool kF16 = W4A16;
 #pragma unroll
-      for (int t = 0; t < NT; t += 2) {
-        const bool l0 = t < ntl && ((r0 + 8 * t >= a.rank) == lora_pass);
-        const bool l1 = t + 1 < ntl && ((r0 + 8 * (t + 1) >= a.rank) == lora_pass);
-        if (!(l0 || l1)) continue;
+      for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int t = 0; t < NT; t += 2) {
+          const bool l0 = t < ntl && (!LORA || ((r0 + 8 * t >= a.rank) == lora_pass));
+          const bool l1 = t + 1 < ntl && (!LORA || ((r0 + 8 * (t + 1) >= a.rank) == lora_pass));
+          if (!(l0 || l1)) continue;
           uint32_t b[4];
           ldmatrix_x4(ws + (s * NT + t) * kLrTileBytes + swz128(b_row, 2 * kk + b_chk), b);
-          constexpr bool kF16 = W4A16;
           if (l0) {
-            if (lora_pass) mma_16816<false>(acc[t], fr[kk], b[0], b[1]);
+            if (LORA && lora_pass) mma_16816<false>(acc[t], fr[kk], b[0], b[1]);
             else mma_16816<kF16>(acc[t], fr[kk], b[0], b[1]);
           }
-          if (NT > 1 && l1) {
-            if (lora_pass) mma_16816<false>(acc[t + 1], fr[kk], b[2], b[3]);
+          if (l1) {
+            if (LORA && lora_pass) mma_16816<false>(acc[t + 1], fr[kk], b[2], b[3]);
             else mma_16816<kF16>(acc[t + 1], fr[kk], b[2], b[3]);
           }
         }
@@ -255,20 +278,31 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
     }
   };
 
+  // lane 0: count this warp's release of stage-slot s (chunk c); the fourth release refills it
+  auto release = [&](int s, int c) {
+    const uint32_t old = atom_add_acq_rel(cnt_base + 4u * (uint32_t)s, 1u);
+    if ((old & (kWarps - 1)) == kWarps - 1) {
+      fence_proxy_async_smem();
+      if (c + STAGES < n_loc) issue(s, c + STAGES);
+    }
+  };
+  int pending = -1;  // chunk whose slot waits for its a16 store to finish reading
+
 #pragma unroll 1
   for (int c0 = 0; c0 < n_loc && ok; c0 += GS) {
     uint32_t fr[GS][4][4];  // x fragments, then x_hat fragments (bf16x2, or f16x2 in W4A16 mode)
-    uint32_t mx_g = 0, mx_g8 = 0;
+    uint32_t mxk[GS][4][2];  // per k16 block: |x_hat| max of rows g and g+8 (bf16x2 lanes)
 #pragma unroll
     for (int j = 0; j < GS; ++j) {
       const int c = c0 + j, s = c % STAGES;
-      if (!mbar_wait(full_bar(s), (uint32_t)((c / STAGES) & 1), abort_flag, a.err, 0x4100 + s)) {
+      const uint32_t par = (uint32_t)((c / STAGES) & 1);
+      if (!mbar_test(full_bar(s), par) && !mbar_wait(full_bar(s), par, abort_flag, a.err, 0x4100 + s)) {
         ok = false;
         break;
       }
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) ldmatrix_x4(xs + s * kXTileBytes + swz128(a_row, 2 * kk + a_chk), fr[j][kk]);
-      if (a.lora_rank > 0) lowrank_mma(fr[j], s, true);  // LoRA down-projection on raw x
+      if constexpr (LORA) lowrank_mma(fr[j], s, true);  // LoRA down-projection on raw x
       const float4* tb = rst_p + c * (kBK / 2) + t4;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
@@ -282,8 +316,8 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
           fr[j][kk][i] = W4A16 ? f2_to_h2(q) : f2_to_bf2(q);
         }
         if constexpr (!W4A16) {
-          mx_g = bf2_maxabs(bf2_maxabs(mx_g, fr[j][kk][0]), fr[j][kk][2]);
-          mx_g8 = bf2_maxabs(bf2_maxabs(mx_g8, fr[j][kk][1]), fr[j][kk][3]);
+          mxk[j][kk][0] = bf2_maxabs(fr[j][kk][0], fr[j][kk][2]);
+          mxk[j][kk][1] = bf2_maxabs(fr[j][kk][1], fr[j][kk][3]);
         }
       }
     }
@@ -293,7 +327,17 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
     uint64_t sc2[2], ys2[2], ns2[2];
     if constexpr (!W4A16) {
       if (emit) {
-        float am[2] = {bf2_absmax_f(mx_g), bf2_absmax_f(mx_g8)};
+        uint32_t mx[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t m01 = bf2_maxabs(mxk[0][0][h], mxk[0][1][h]), m23 = bf2_maxabs(mxk[0][2][h], mxk[0][3][h]);
+          if constexpr (GS == 2) {
+            m01 = bf2_maxabs(m01, bf2_maxabs(mxk[GS - 1][0][h], mxk[GS - 1][1][h]));
+            m23 = bf2_maxabs(m23, bf2_maxabs(mxk[GS - 1][2][h], mxk[GS - 1][3][h]));
+          }
+          mx[h] = bf2_maxabs(m01, m23);
+        }
+        float am[2] = {bf2_absmax_f(mx[0]), bf2_absmax_f(mx[1])};
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           am[h] = fmaxf(am[h], __shfl_xor_sync(0xffffffffu, am[h], 1));
@@ -319,11 +363,9 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
     for (int j = 0; j < GS; ++j) {
       const int c = c0 + j, s = c % STAGES;
       const int kcol = (st0 + c) * kBK;
+      const uint32_t my_tile = xs + s * kXTileBytes + my_rows;  // a16 overwrites this warp's x rows
+      const bool store = emit && write_a16;
       if (emit) {
-        if (a.write_a16) {
-          if (lane == 0) bulk_wait_read0();  // previous store of this warp's staging tile has read it
-          __syncwarp();
-        }
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           uint32_t o[4];
@@ -347,31 +389,33 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
               if (row_g8 < a.M) { prow_g8[0] = (uint8_t)nib[1]; prow_g8[4] = (uint8_t)nib[3]; }
             }
           }
-          if (a.write_a16) stmatrix_x4(my_ost + swz128(lane & 15, 2 * kk + (lane >> 4)), o[0], o[1], o[2], o[3]);
+          if (store) stmatrix_x4(my_tile + swz128(lane & 15, 2 * kk + (lane >> 4)), o[0], o[1], o[2], o[3]);
         }
-        if (a.write_a16) {
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && m0 + wrow < a.M) {
-            tma_store_2d(&tm_a16, my_ost, kcol, m0 + wrow);
-            bulk_commit();
-          }
-        }
+        if (store) fence_proxy_async_smem();
       }
       if (ntl > 0 && a.rank > 0 && r0 < a.rank) lowrank_mma(fr[j], s, false);  // l2 on x_hat
 
-      // release the stage; the last of the four warps refills it
+      // one single-lane section per stage: store this stage's a16, then release the
+      // previous stage once its store has read the tile (or this one, without a store)
       __syncwarp();
       if (lane == 0) {
-        __threadfence_block();
-        const int old = atomicAdd(&cnt[s], 1);
-        if ((old & (kWarps - 1)) == kWarps - 1) {
-          __threadfence_block();
-          fence_proxy_async_smem();
-          if (c + STAGES < n_loc) issue(s, c + STAGES);
+        if (store) {
+          if (m0 + wrow < a.M) tma_store_2d(&tm_a16, my_tile, kcol, m0 + wrow);
+          bulk_commit();
+          if (pending >= 0) {
+            bulk_wait_read<1>();
+            release(pending % STAGES, pending);
+          }
+        } else {
+          release(s, c);
         }
       }
+      pending = store ? c : -1;
     }
+  }
+  if (lane == 0 && pending >= 0) {
+    bulk_wait_read<0>();
+    release(pending % STAGES, pending);
   }
 
   // ---- fp32 partial of the low-rank projection over this K slice ----
@@ -432,29 +476,43 @@ struct Geometry {
 int pick_nt(int r_use) {
   if (r_use <= 0) return 0;
   const int tiles = r_use / 8;
-  return tiles <= 1 ? 1 : tiles <= 2 ? 2 : tiles <= 4 ? 4 : 8;
+  return tiles <= 2 ? 2 : tiles <= 4 ? 4 : 8;
 }
 
-Geometry geometry(int M, int K_pad, int r_use) {
+// K slices per row band: as many as one wave of CTAs holds (kTargetCtasPerSm per SM), each
+// slice a whole number of stages (a multiple of `step`: 2 for 128-column groups, so a group
+// never straddles two slices), between kMinSliceStages and kMaxSliceStages.  Among the slice
+// lengths that give the fewest waves the one that fills the most CTA slots is taken.
+Geometry geometry(int M, int K_pad, int r_use, int step) {
   Geometry gm;
   gm.nt = pick_nt(r_use);
   gm.nz = gm.nt ? (r_use + 8 * gm.nt - 1) / (8 * gm.nt) : 1;
   const int n_st = K_pad / kBK;
-  const int bands = (M + kBM - 1) / kBM;
+  const int layers = ((M + kBM - 1) / kBM) * gm.nz;  // CTAs per K slice
   const int slots = num_sms() * kTargetCtasPerSm;
-  const int want = std::max(1, slots / std::max(1, bands * gm.nz));
-  int slice = (n_st + want - 1) / want;
-  slice = (slice + 1) & ~1;  // even: a 128-column group never straddles two slices
-  slice = std::min(std::max(slice, kMinSliceStages), kMaxSliceStages);
-  gm.slice = slice;
-  gm.ksplit = (n_st + slice - 1) / slice;
+  int best_slice = kMaxSliceStages, best_waves = 1 << 30;
+  double best_fill = -1.0;
+  for (int slice = kMinSliceStages; slice <= kMaxSliceStages; slice += step) {
+    const int ksplit = (n_st + slice - 1) / slice;
+    const long long ctas = (long long)ksplit * layers;
+    const int waves = (int)((ctas + slots - 1) / slots);
+    const double fill = (double)ctas / ((double)waves * slots);
+    if (waves < best_waves || (waves == best_waves && fill > best_fill + 1e-9)) {
+      best_waves = waves;
+      best_fill = fill;
+      best_slice = slice;
+    }
+  }
+  gm.slice = best_slice;
+  gm.ksplit = (n_st + best_slice - 1) / best_slice;
   return gm;
 }
 
+// Covers both slice steps, so one size serves every group size and mode.
 size_t workspace_bytes(int M, int K_pad, int r_tot) {
   if (r_tot <= 0 || M <= 0 || K_pad <= 0) return 0;
-  const Geometry gm = geometry(M, K_pad, r_tot);
-  return sizeof(float) * (size_t)gm.ksplit * (size_t)M * (size_t)r_tot;
+  const int ksplit = std::max(geometry(M, K_pad, r_tot, 1).ksplit, geometry(M, K_pad, r_tot, 2).ksplit);
+  return sizeof(float) * (size_t)ksplit * (size_t)M * (size_t)r_tot;
 }
 
 struct LaunchSpec {
@@ -468,11 +526,11 @@ struct LaunchSpec {
   int R2;
 };
 
-template <int GS, int NT, bool W4A16, bool PACKED>
+template <int GS, int NT, bool W4A16, bool PACKED, bool LORA>
 int launch_t(const LaunchSpec& L, cudaStream_t stream) {
-  constexpr int STAGES = GS == 2 ? 4 : 3;
+  constexpr int STAGES = 4;
   constexpr uint32_t smem = aq_smem_layout_bytes<STAGES, NT>();
-  auto kern = act_quant_kernel<GS, STAGES, NT, W4A16, PACKED>;
+  auto kern = act_quant_kernel<GS, STAGES, NT, W4A16, PACKED, LORA>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "activation pass: shared memory attribute");
   const dim3 grid((L.args.M + kBM - 1) / kBM, L.gm.ksplit, L.gm.nz);
@@ -480,22 +538,25 @@ int launch_t(const LaunchSpec& L, cudaStream_t stream) {
   return check_launch("activation pass launch");
 }
 
-template <int GS, bool W4A16, bool PACKED>
+template <int GS, bool W4A16, bool PACKED, bool LORA>
 int launch_nt(const LaunchSpec& L, cudaStream_t stream) {
   switch (L.gm.nt) {
-    case 0: return launch_t<GS, 0, W4A16, PACKED>(L, stream);
-    case 1: return launch_t<GS, 1, W4A16, PACKED>(L, stream);
-    case 2: return launch_t<GS, 2, W4A16, PACKED>(L, stream);
-    case 4: return launch_t<GS, 4, W4A16, PACKED>(L, stream);
-    default: return launch_t<GS, 8, W4A16, PACKED>(L, stream);
+    case 0: return launch_t<GS, 0, W4A16, PACKED, false>(L, stream);
+    case 2: return launch_t<GS, 2, W4A16, PACKED, LORA>(L, stream);
+    case 4: return launch_t<GS, 4, W4A16, PACKED, LORA>(L, stream);
+    default: return launch_t<GS, 8, W4A16, PACKED, LORA>(L, stream);
   }
 }
 
+template <bool LORA>
+int launch_l(const LaunchSpec& L, cudaStream_t stream) {
+  if (L.w4a16) return launch_nt<1, true, false, LORA>(L, stream);
+  if (L.gs == 1) return L.packed ? launch_nt<1, false, true, LORA>(L, stream) : launch_nt<1, false, false, LORA>(L, stream);
+  return L.packed ? launch_nt<2, false, true, LORA>(L, stream) : launch_nt<2, false, false, LORA>(L, stream);
+}
+
 int launch(const LaunchSpec& L, cudaStream_t stream) {
-  int st;
-  if (L.w4a16) st = launch_nt<1, true, false>(L, stream);
-  else if (L.gs == 1) st = L.packed ? launch_nt<1, false, true>(L, stream) : launch_nt<1, false, false>(L, stream);
-  else st = L.packed ? launch_nt<2, false, true>(L, stream) : launch_nt<2, false, false>(L, stream);
+  const int st = L.args.lora_rank > 0 ? launch_l<true>(L, stream) : launch_l<false>(L, stream);
   if (st || !L.args.partial) return st;
   const int64_t items = (int64_t)L.args.M * (L.R2 - L.args.r_tot);
   const int blocks = (int)std::min<int64_t>((items + 255) / 256, (int64_t)num_sms() * 8);
@@ -540,7 +601,7 @@ int build_spec(LaunchSpec& L, const void* x, int64_t ldx, const void* smooth, co
   const int r_tot = rank + lora_rank;
   const bool want_mid = out_mid_hl && r_tot > 0;
   const int r_use = want_mid ? r_tot : 0;
-  L.gm = geometry(M, K_pad, r_use);
+  L.gm = geometry(M, K_pad, r_use, G == 128 ? 2 : 1);
   int st;
   if ((st = make_tma_2d(&L.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K_in, M, (uint64_t)ldx * 2, kBK, kBM,
                         CU_TENSOR_MAP_SWIZZLE_128B)))

@@ -55,18 +55,30 @@ def test_quantize_weight_large_vs_oracle(group):
 
 
 def test_cuda_converter_matches_torch_converter():
-    from krea2_svdquant_b200.quant import (quantize_linear_from_samples, quantize_linear_from_samples_cuda,
-                                           svd_lowrank)
+    """Same residual through both quantizers: bit-identical codes and scales.  (The residual is
+    computed once: two fp32 GEMMs of L1 L2 need not agree in the last bit.)"""
+    from krea2_svdquant_b200 import ops
+    from krea2_svdquant_b200.quant import (compute_smooth_scale, pack_int4, quantize_linear_from_samples_cuda,
+                                           quantize_symmetric_int4)
     gen = torch.Generator().manual_seed(3)
     w = (torch.randn(384, 1000, generator=gen) * 0.02).bfloat16().cuda()
     xs = torch.randn(64, 1000, generator=gen).bfloat16().cuda()
-    ref = quantize_linear_from_samples(w, None, xs, rank=32, group_size=128, scale_dtype=torch.float16)
-    got = quantize_linear_from_samples_cuda(w, None, xs, rank=32, group_size=128, scale_dtype=torch.float16,
-                                            lowrank=(ref.l1, ref.l2))
-    assert torch.equal(got.qweight, ref.qweight)
-    assert torch.equal(got.weight_scales, ref.weight_scales)
-    assert torch.equal(got.smooth_scale, ref.smooth_scale)
-    assert got.padded_in_features == ref.padded_in_features == 1024
-    # without precomputed factors the randomized SVD runs on the device
-    st = quantize_linear_from_samples_cuda(w, None, xs, rank=16, group_size=64)
-    assert st.qweight.shape == (384, 512) and st.l1.shape == (384, 16)
+    smooth = compute_smooth_scale(xs.float().abs().amax(0), w, 0.25, 4.0)
+    mig = w * smooth.unsqueeze(0)
+    l1 = (torch.randn(384, 32, generator=gen) * 0.02).bfloat16().cuda()
+    l2 = (torch.randn(32, 1000, generator=gen) * 0.02).bfloat16().cuda()
+    res = (mig.float() - l1.float() @ l2.float()).contiguous()
+    q, sc = quantize_symmetric_int4(res, 128)            # torch on the GPU
+    packed, sc16 = ops.quantize_weight(res, 128, torch.float16)
+    assert torch.equal(packed, pack_int4(q))
+    assert torch.equal(sc16, sc.to(torch.float16))
+    # the converter end to end (its own residual): shapes, smoothing and a sound quantization
+    st = quantize_linear_from_samples_cuda(w, None, xs, rank=32, group_size=128, lowrank=(l1, l2))
+    assert st.qweight.shape == (384, 512) and st.weight_scales.shape == (384, 8)
+    assert st.padded_in_features == 1024 and torch.equal(st.smooth_scale, smooth)
+    deq = (O.unpack_int4(st.qweight.cpu().numpy(), 1024).reshape(384, 8, 128).astype(np.float32)
+           * st.weight_scales.float().cpu().numpy()[:, :, None]).reshape(384, 1024)[:, :1000]
+    step = np.repeat(st.weight_scales.float().cpu().numpy(), 128, axis=1)[:, :1000]
+    assert np.all(np.abs(deq - res.cpu().numpy()) <= 0.5 * step * 1.01 + 1e-6)
+    st2 = quantize_linear_from_samples_cuda(w, None, xs, rank=16, group_size=64)
+    assert st2.qweight.shape == (384, 512) and st2.l1.shape == (384, 16)
