@@ -82,6 +82,8 @@ def act_quant(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Option
     mid = torch.empty((m, r2) if (emit_a16 and r2) else (0,), dtype=torch.bfloat16, device=dev)
     packed = torch.empty((m, k_pad // 2) if emit_packed else (0,), dtype=torch.uint8, device=dev)
     scales = torch.empty((m, k_pad // a_group) if emit_packed else (0,), dtype=torch.bfloat16, device=dev)
+    if m == 0:
+        return a16, mid, packed, scales
     ws = _workspace(m, k_pad, rank, lrank, dev) if mid.numel() else None
     _lib.call("svdq_act_quant", _p(x), x.stride(0), _p(smooth), _p(l2), rank, _p(lora_down),
               _p(lora_col_scale), lrank, m, k_in, k_pad, a_group, _p(packed), _p(scales), _p(a16),
@@ -114,6 +116,8 @@ def w4a16_prep(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Optio
     rank, lrank, r2 = _lowrank_args(l2, lora_down)
     a16 = torch.empty((m, k_pad), dtype=torch.float16, device=x.device)
     mid = torch.empty((m, r2) if r2 else (0,), dtype=torch.bfloat16, device=x.device)
+    if m == 0:
+        return a16, mid
     ws = _workspace(m, k_pad, rank, lrank, x.device) if r2 else None
     _lib.call("svdq_w4a16_prep", _p(x), x.stride(0), _p(smooth), _p(l2), rank, _p(lora_down),
               _p(lora_col_scale), lrank, m, k_in, k_pad, _p(a16), _p(mid), r2, _p(ws),
@@ -203,6 +207,8 @@ def linear_gemm(a16: Tensor, w16: Tensor, mid_hl: Optional[Tensor], up_hl: Optio
     r2 = 0 if mid_hl is None or mid_hl.numel() == 0 else mid_hl.shape[1]
     _need(r2 == 0 or (up_hl is not None and tuple(up_hl.shape) == (n, r2)), "linear_gemm: up_hl shape mismatch")
     out = torch.empty((m, n), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=a16.device)
+    if m == 0:
+        return out
     _lib.call("svdq_linear_gemm", _p(a16), _p(w16), _p(mid_hl) if r2 else None, _p(up_hl) if r2 else None, r2,
               _p(bias), _p(out), _lib.SVDQ_FP32 if out_fp32 else _lib.SVDQ_BF16, out.stride(0), m, n, k_pad,
               _stream(a16.device))

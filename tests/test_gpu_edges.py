@@ -1,0 +1,159 @@
+"""Edge shapes of the linear path on the GPU against the oracle: empty and single-row
+batches, ragged rows, tiny and strided K, the smallest N, the widest low-rank operand,
+leading batch dimensions, fp32 inputs, W4A16 with padding and LoRA, and invalid
+arguments reported as errors."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import svdq_oracle as O
+from tests._helpers import staged_oracle, state_numpy
+
+pytestmark = pytest.mark.gpu
+
+TOL_FP32 = 1e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib_ready():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from krea2_svdquant_b200 import _lib, build
+    build.build()
+    _lib.lib()
+    yield
+    assert _lib.device_error() == 0
+
+
+def _mod(st, backend="b200"):
+    from krea2_svdquant_b200.linear import SVDQuantLinear
+    m = SVDQuantLinear(st, backend=backend)
+    m.output_fp32 = True
+    return m
+
+
+def _check(mod, x, loras=()):
+    s = state_numpy(mod.state)
+    y = mod(x)
+    torch.cuda.synchronize()
+    ref, _ = staged_oracle(x.reshape(-1, x.shape[-1]).float().cpu().numpy(), s, loras)
+    got = y.reshape(-1, y.shape[-1]).float().cpu().numpy()
+    if ref.size == 0:
+        assert got.shape == ref.shape
+        return 0.0
+    return O.rel_fro(got, ref)
+
+
+def _state(m, k, n, r=16, grp=64, seed=0, bias=True):
+    from krea2_svdquant_b200.quant import make_synthetic_state
+    return make_synthetic_state(m, k, n, r, grp, seed=seed, bias=bias, device="cuda")
+
+
+@pytest.mark.parametrize("m", [1, 2, 63, 65, 129])
+def test_small_and_ragged_batches(m):
+    x, st = _state(max(m, 2), 512, 264, seed=m)
+    assert _check(_mod(st), x[:m].contiguous()) <= TOL_FP32
+
+
+def test_empty_batch():
+    x, st = _state(4, 256, 128)
+    mod = _mod(st)
+    y = mod(x[:0])
+    assert y.shape == (0, 128)
+    mod16 = _mod(st, "b200_w4a16")
+    assert mod16(x[:0]).shape == (0, 128)
+
+
+def test_tiny_k_and_smallest_n():
+    x, st = _state(40, 8, 8, r=8, grp=64, seed=3)
+    assert st.padded_in_features == 64
+    assert _check(_mod(st), x) <= TOL_FP32
+
+
+def test_strided_rows_and_leading_dims():
+    from krea2_svdquant_b200 import ops
+    x, st = _state(96, 384, 256, seed=4)
+    mod = _mod(st)
+    wide = torch.zeros(96, 512, dtype=torch.bfloat16, device="cuda")
+    wide[:, :384] = x
+    view = wide[:, :384]                       # row stride 512 > K
+    assert view.stride(0) == 512
+    y_view = mod(view)
+    y_cont = mod(x)
+    assert torch.equal(y_view, y_cont)
+    # the activation pass reads the strided rows directly (no copy): bit-identical outputs
+    p = mod.prepare()
+    a1 = ops.act_quant(view, p.smooth, p.l2, None, None, p.k_pad, 64, True, True)
+    a2 = ops.act_quant(x, p.smooth, p.l2, None, None, p.k_pad, 64, True, True)
+    for t1, t2 in zip(a1, a2):
+        assert torch.equal(t1.view(torch.uint8), t2.view(torch.uint8))
+    y3 = mod(x.view(4, 24, 384))
+    assert y3.shape == (4, 24, 256) and torch.equal(y3.reshape(96, 256), y_cont)
+
+
+def test_fp32_input_is_quantized_from_its_bf16_value():
+    x, st = _state(33, 256, 128, seed=5)
+    mod = _mod(st)
+    mod.output_fp32 = False
+    y32 = mod(x.float())
+    assert y32.dtype == torch.float32
+    y16 = mod(x)
+    assert torch.equal(y32, y16.float()) or O.rel_fro(y32.cpu().numpy(), y16.float().cpu().numpy()) < 5e-3
+
+
+def test_widest_lowrank_operand():
+    """rank 128 + two LoRA adapters of 64 = 256 low-rank columns (the ABI maximum)."""
+    x, st = _state(70, 640, 192, r=128, seed=6)
+    mod = _mod(st)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    loras = []
+    for i in range(2):
+        d = (torch.randn(64, 640, device="cuda", generator=g) * 0.05).bfloat16()
+        u = (torch.randn(192, 64, device="cuda", generator=g) * 0.05).bfloat16()
+        mod.add_lora_adapter(d, u, scale=0.5 + i, network_alpha=32.0)
+        loras.append((d.float().cpu().numpy(), u.float().cpu().numpy(), mod.lora_adapters[-1].multiplier))
+    assert _check(mod, x, loras) <= TOL_FP32
+    too_many = (torch.randn(8, 640, device="cuda") * 0.05).bfloat16(), torch.zeros(192, 8, device="cuda").bfloat16()
+    mod.add_lora_adapter(*too_many)
+    with pytest.raises(Exception):
+        mod(x)
+
+
+def test_long_k_small_m():
+    x, st = _state(16, 16384, 256, seed=8)
+    assert _check(_mod(st), x) <= TOL_FP32
+
+
+def test_w4a16_padding_and_lora():
+    x, st = _state(37, 200, 136, r=8, grp=64, seed=10)
+    mod = _mod(st, "b200_w4a16")
+    g = torch.Generator(device="cuda").manual_seed(2)
+    d = (torch.randn(16, 200, device="cuda", generator=g) * 0.05).bfloat16()
+    u = (torch.randn(136, 16, device="cuda", generator=g) * 0.05).bfloat16()
+    mod.add_lora_adapter(d, u, scale=0.8, network_alpha=8.0)
+    s = state_numpy(mod.state)
+    y = mod(x)
+    ref = O.w4a16_linear_fp32(x.float().cpu().numpy(), s["smooth"], s["qweight"], s["weight_scales"], s["l1"],
+                              s["l2"], s["bias"], group=s["group"], k_in=s["k_in"], k_pad=s["k_pad"],
+                              loras=[(d.float().cpu().numpy(), u.float().cpu().numpy(),
+                                      mod.lora_adapters[0].multiplier)])
+    assert O.rel_fro(y.float().cpu().numpy(), ref) <= TOL_FP32
+
+
+def test_invalid_arguments_raise():
+    from krea2_svdquant_b200 import ops
+    from krea2_svdquant_b200._lib import SVDQError
+    x, st = _state(8, 128, 64)
+    mod = _mod(st)
+    p = mod.prepare()
+    with pytest.raises(SVDQError):
+        ops.act_quant(x, p.smooth, p.l2, None, None, p.k_pad, 96, True, False)   # group 96
+    with pytest.raises(SVDQError):
+        a16 = torch.zeros(8, 96, dtype=torch.float16, device="cuda")
+        ops.linear_gemm(a16, torch.zeros(64, 96, dtype=torch.float16, device="cuda"), None, None, None, False)
+    with pytest.raises(ValueError):
+        mod(x.cpu())
+    with pytest.raises(ValueError):
+        mod(x[:, :100])
