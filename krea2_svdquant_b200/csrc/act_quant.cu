@@ -214,8 +214,10 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
-    for (int s = 0; s < STAGES && s < n_loc; ++s) issue(s, s);
   }
+  pdl_wait();  // inputs may come from the previous kernel on the stream
+  if (tid == 0)
+    for (int s = 0; s < STAGES && s < n_loc; ++s) issue(s, s);
   // reciprocal table of the slice: {RN(1/s_c), RN(1/s_c+1), -s_c, -s_c+1} per column pair
   {
     float4* tbl = reinterpret_cast<float4*>(gbase + (rst - base));
@@ -418,6 +420,8 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
     release(pending % STAGES, pending);
   }
 
+  pdl_trigger();  // the finalize launch may start its prologue
+
   // ---- fp32 partial of the low-rank projection over this K slice ----
   if constexpr (NT > 0) {
     if (ok && a.partial) {
@@ -450,6 +454,8 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
 __global__ void mid_finalize_kernel(const float* __restrict__ partial, int ksplit, int M, int rank, int r_tot,
                                     const float* __restrict__ lora_col_scale, __nv_bfloat16* __restrict__ mid_hl,
                                     int R2) {
+  pdl_wait();
+  pdl_trigger();
   const int w = R2 - r_tot;  // work items per row: r_tot (hi+lo pairs) + zero padding
   const int64_t total = (int64_t)M * w;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -533,8 +539,18 @@ int launch_t(const LaunchSpec& L, cudaStream_t stream) {
   auto kern = act_quant_kernel<GS, STAGES, NT, W4A16, PACKED, LORA>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "activation pass: shared memory attribute");
-  const dim3 grid((L.args.M + kBM - 1) / kBM, L.gm.ksplit, L.gm.nz);
-  kern<<<grid, kThreads, smem, stream>>>(L.tm_x, L.tm_l2, L.tm_lora, L.tm_a16, L.args);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((L.args.M + kBM - 1) / kBM, L.gm.ksplit, L.gm.nz);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, L.tm_x, L.tm_l2, L.tm_lora, L.tm_a16, L.args);
+  if (e != cudaSuccess) return check_cuda(e, "activation pass launch");
   return check_launch("activation pass launch");
 }
 
@@ -560,8 +576,18 @@ int launch(const LaunchSpec& L, cudaStream_t stream) {
   if (st || !L.args.partial) return st;
   const int64_t items = (int64_t)L.args.M * (L.R2 - L.args.r_tot);
   const int blocks = (int)std::min<int64_t>((items + 255) / 256, (int64_t)num_sms() * 8);
-  mid_finalize_kernel<<<blocks, 256, 0, stream>>>(L.args.partial, L.gm.ksplit, L.args.M, L.args.rank, L.args.r_tot,
-                                                  L.lora_col_scale, L.mid_hl, L.R2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, mid_finalize_kernel, (const float*)L.args.partial, L.gm.ksplit,
+                                           L.args.M, L.args.rank, L.args.r_tot, L.lora_col_scale, L.mid_hl, L.R2);
+  if (e != cudaSuccess) return check_cuda(e, "activation pass finalize");
   return check_launch("activation pass finalize");
 }
 

@@ -148,6 +148,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
+  // everything above touches no memory an earlier kernel writes; operands are read from here on
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -369,13 +372,15 @@ int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, con
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, tm_a, tm_w, tm_mid, tm_up, a);
   if (e != cudaSuccess) return check_cuda(e, (w + " launch").c_str());
   return check_launch((w + " launch").c_str());

@@ -437,6 +437,12 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t a_fmt, uint32_t b_fmt
 constexpr uint32_t kFmtBF16 = 1;  // kind::f16 format code
 constexpr uint32_t kFmtE4M3 = 0;  // kind::f8f6f4 format code
 
+// Programmatic dependent launch.  pdl_wait: block until the grids this launch depends on
+// have completed and their writes are visible (a no-op without a programmatic dependency).
+// pdl_trigger: allow the next programmatically dependent launch to start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(
