@@ -255,9 +255,23 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
   const int b_chk = (lane >> 3) & 1;
 
   // k16 steps outermost so the NT accumulator chains advance side by side
+  const bool all_l2 = !LORA && ntl == NT;  // every tile of this CTA is a live l2 tile (the common case)
   auto lowrank_mma = [&](const uint32_t (&fr)[4][4], int s, bool lora_pass) {
     if constexpr (NT > 0) {
       constexpr bool kF16 = W4A16;
+      if (!lora_pass && all_l2) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+          for (int t = 0; t < NT; t += 2) {
+            uint32_t b[4];
+            ldmatrix_x4(ws + (s * NT + t) * kLrTileBytes + swz128(b_row, 2 * kk + b_chk), b);
+            mma_16816<kF16>(acc[t], fr[kk], b[0], b[1]);
+            mma_16816<kF16>(acc[t + 1], fr[kk], b[2], b[3]);
+          }
+        }
+        return;
+      }
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
@@ -339,11 +353,13 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
           }
           mx[h] = bf2_maxabs(m01, m23);
         }
-        float am[2] = {bf2_absmax_f(mx[0]), bf2_absmax_f(mx[1])};
+        // both rows' maxima in one bf16x2 (row g low, row g+8 high), reduced over the 4 lanes of the row
+        uint32_t both = bf2_maxabs(__byte_perm(mx[0], mx[1], 0x5410), __byte_perm(mx[0], mx[1], 0x7632));
+        both = bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 1));
+        both = bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 2));
+        const float am[2] = {fabsf(__uint_as_float(both << 16)), fabsf(__uint_as_float(both & 0xFFFF0000u))};
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          am[h] = fmaxf(am[h], __shfl_xor_sync(0xffffffffu, am[h], 1));
-          am[h] = fmaxf(am[h], __shfl_xor_sync(0xffffffffu, am[h], 2));
           const float v = fmaxf(am[h], eps);
           const float q0 = v * y7;
           const float sc = __bfloat162float(__float2bfloat16_rn(fmaf(fmaf(-q0, 7.0f, v), y7, q0)));
