@@ -63,10 +63,19 @@ const char* svdq_version(void);
  * word instead of hanging.  Reads (and optionally clears) that word on the
  * current device; synchronizes the device.  *code == 0 means no failure.
  * Codes: 0x101-0x301 GEMM waits, 0x41xx activation-pass waits, 0x4200 an
- * activation group scale above 65504/7 (the fp16 GEMM operand a16 overflowed);
- * the first failure since the last clear is kept.
+ * activation group scale above 65504/7 (the fp16 GEMM operand a16 overflowed),
+ * 0x7E01 the diagnostic wait below; the first failure since the last clear is kept.
  */
 int svdq_device_error(int* code, int clear);
+
+/*
+ * Diagnostic for the bounded-wait machinery: one CTA waits on an mbarrier that
+ * nothing completes, with an in-kernel limit of limit_us microseconds
+ * (1 .. 5,000,000).  The wait gives up, records 0x7E01 in the device error
+ * word and the kernel exits; the CUDA context stays usable.  Asynchronous on
+ * `stream`; read the result with svdq_device_error.
+ */
+int svdq_selftest_bounded_wait(int limit_us, cudaStream_t stream);
 
 /*
  * Device workspace (bytes) the activation passes need for the low-rank

@@ -105,3 +105,36 @@ int svdq_device_error(int* code, int clear) {
 }
 
 }  // extern "C"
+
+namespace svdq {
+namespace {
+
+constexpr int kErrSelftestWait = 0x7E01;
+
+// One CTA waits on an mbarrier that nothing arrives on, through the same bounded
+// wait every kernel of this library uses, with a short limit.  The wait gives up,
+// records kErrSelftestWait and the kernel exits normally.
+__global__ void selftest_bounded_wait_kernel(unsigned long long limit_ns, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(smem_u32(&bar), 0, &abort_flag, err, kErrSelftestWait, limit_ns);
+  __syncthreads();
+}
+
+}  // namespace
+}  // namespace svdq
+
+extern "C" int svdq_selftest_bounded_wait(int limit_us, cudaStream_t stream) {
+  using namespace svdq;
+  SVDQ_REQUIRE(limit_us >= 1 && limit_us <= 5000000, "svdq_selftest_bounded_wait: limit_us must be in [1, 5e6]");
+  int* err = device_error_word();
+  if (!err) return set_error(SVDQ_ERR_CUDA, "svdq_selftest_bounded_wait: device error word unavailable");
+  selftest_bounded_wait_kernel<<<1, 32, 0, stream>>>((unsigned long long)limit_us * 1000ull, err);
+  return check_launch("svdq_selftest_bounded_wait launch");
+}

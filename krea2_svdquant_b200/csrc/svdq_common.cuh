@@ -138,12 +138,13 @@ __device__ __forceinline__ bool mbar_poll64(uint32_t bar, uint32_t parity) {
 // acquire, for barriers that also receive arrivals from the other CTA of a pair.
 template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
-                                          volatile int* abort_flag, int* err, int where) {
+                                          volatile int* abort_flag, int* err, int where,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_poll64<CLUSTER>(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicCAS(err, 0, where);
       return false;
