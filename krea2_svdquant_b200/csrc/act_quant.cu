@@ -109,9 +109,6 @@ __device__ __forceinline__ uint32_t bf2_maxabs(uint32_t m, uint32_t v) {
   asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(m), "r"(v));
   return d;
 }
-__device__ __forceinline__ float bf2_absmax_f(uint32_t m) {
-  return fmaxf(fabsf(__uint_as_float(m << 16)), fabsf(__uint_as_float(m & 0xFFFF0000u)));
-}
 
 // Non-blocking check of an mbarrier phase.
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
