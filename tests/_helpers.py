@@ -1,21 +1,10 @@
-"""Shared helpers for the GPU parity tests: golden/synthetic inputs, e4m3 decode,
-oracle evaluation."""
+"""Shared helpers for the GPU parity tests: golden/synthetic inputs and oracle evaluation."""
 from __future__ import annotations
 
 import numpy as np
 import torch
 
 from oracle import svdq_oracle as O
-
-
-def e4m3_decode(b: np.ndarray) -> np.ndarray:
-    """float32 values of e4m3 bytes (finite encodings)."""
-    b = np.asarray(b, np.uint8).astype(np.int32)
-    s = np.where(b & 0x80, -1.0, 1.0)
-    e = (b >> 3) & 0xF
-    m = (b & 7).astype(np.float64)
-    v = np.where(e == 0, m / 8.0 * 2.0 ** -6, (1.0 + m / 8.0) * 2.0 ** (e - 7.0))
-    return (s * v).astype(np.float32)
 
 
 def bf16_tensor(a, device="cuda") -> torch.Tensor:
