@@ -30,6 +30,7 @@ if ROOT not in sys.path:
 
 M, K, N, RANK, GROUP = 4096, 6144, 16384, 32, 64
 OPS = 2 * M * N * K  # dense-equivalent ops per step (svd.py:158 residual GEMM)
+REF_BUDGET_S = 240.0  # longest stretch of reference-arm (CPU) steps that is timed
 METRIC = "SVDQuantLinear TOPS @M4096 K6144 N16384"
 WORKLOAD = ("BASELINE config 2: W4A4 SVDQuantLinear forward (act-quant + fused tcgen05 GEMM with "
             "low-rank r32 + bias), M4096 K6144 N16384, group 64, bf16 in/out")
@@ -161,22 +162,41 @@ def cpu_reference_tops(calls: int, warmup: int, x_cpu, st_cpu, budget_s: float =
 
 
 def run_reference(args) -> None:
-    """--impl reference: the reference's own CPU implementation of the path on the host cores."""
+    """--impl reference: the reference's own CPU implementation of the path on the host cores.
+
+    Each step is one full config-2 call of the CPU path (it dequantizes the whole weight per
+    call, so smaller row samples would understate it), on all host threads.  At most
+    REF_BUDGET_S seconds of steps are timed; the line states how many."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     import torch
 
     from krea2_svdquant_b200.quant import make_synthetic_state
+    from oracle.svdq_oracle import svdquant_linear_sim_torch
 
     x, st = make_synthetic_state(M, K, N, RANK, GROUP, seed=0, device="cpu")
-    tops, cores, _ = cpu_reference_tops(args.steps, args.warmup, x, st)
-    ms = OPS / (tops * 1e12) * 1e3
-    sample = (f"each step one full config-2 call (M=4096), {args.warmup} warm-up steps, bf16, torch CPU "
-              f"restatement of svdquant_linear_sim (svd.py:119-163), {cores} threads")
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    fn_args = (st.smooth_scale, st.qweight, st.weight_scales, st.l1, st.l2, st.bias)
+    kw = dict(group=GROUP, k_in=K, k_pad=K)
+    with torch.no_grad():
+        tw = time.perf_counter()
+        for _ in range(args.warmup):
+            svdquant_linear_sim_torch(x, *fn_args, **kw)
+        per_call = (time.perf_counter() - tw) / max(1, args.warmup)
+        timed = max(1, min(args.steps, int(REF_BUDGET_S / max(per_call, 1e-6))))
+        t0 = time.perf_counter()
+        for _ in range(timed):
+            svdquant_linear_sim_torch(x, *fn_args, **kw)
+        dt = (time.perf_counter() - t0) / timed
+    tops = OPS / dt / 1e12
+    sample = (f"{timed} of the {args.steps} steps timed (at most {REF_BUDGET_S:.0f} s), each one full config-2 call "
+              f"(M=4096), {args.warmup} warm-up calls, bf16, torch CPU restatement of svdquant_linear_sim "
+              f"(svd.py:119-163), {cores} threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(tops, 4), "unit": "TOPS",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (BASELINE recipe, seeded)", "config": {"workload": WORKLOAD},
         "cpu_baseline": {"value": round(tops, 4), "unit": "TOPS", "cores": cores, "kind": "port",
