@@ -36,6 +36,18 @@ WORKLOAD = ("BASELINE config 2: W4A4 SVDQuantLinear forward (act-quant + fused t
             "low-rank r32 + bias), M4096 K6144 N16384, group 64, bf16 in/out")
 
 
+def cpu_model() -> str:
+    """The host CPU model name (Linux), for the CPU baselines' sample descriptions."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown CPU"
+
+
 def _peaks() -> dict:
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -157,7 +169,7 @@ def cpu_reference_tops(calls: int, warmup: int, x_cpu, st_cpu, budget_s: float =
         dt = (time.perf_counter() - t0) / done
         calls = done
     sample = (f"{calls} full config-2 calls (M=4096) after {warmup} warm-up, bf16, torch CPU "
-              f"restatement of svdquant_linear_sim (svd.py:119-163), {cores} threads")
+              f"restatement of svdquant_linear_sim (svd.py:119-163), {cores} threads on {cpu_model()}")
     return OPS / dt / 1e12, cores, sample
 
 
@@ -193,7 +205,7 @@ def run_reference(args) -> None:
     tops = OPS / dt / 1e12
     sample = (f"{timed} of the {args.steps} steps timed (at most {REF_BUDGET_S:.0f} s), each one full config-2 call "
               f"(M=4096), {args.warmup} warm-up calls, bf16, torch CPU restatement of svdquant_linear_sim "
-              f"(svd.py:119-163), {cores} threads")
+              f"(svd.py:119-163), {cores} threads on {cpu_model()}")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(tops, 4), "unit": "TOPS",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
