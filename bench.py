@@ -56,6 +56,11 @@ def _peaks() -> dict:
         return {}
 
 
+def _bf16_peak() -> float:
+    """Dense bf16/fp16 tensor peak (TFLOP/s): MEASURED_PEAKS.json burst figure, else the recipe fallback."""
+    return float(_peaks().get("bf16_tflops") or 1590.0)
+
+
 def _ncu_traffic(kernel: str) -> float | None:
     """DRAM bytes per launch of ``kernel`` from the committed ncu summary, if present."""
     path = os.path.join(ROOT, "profiles", "traffic.txt")
@@ -258,9 +263,10 @@ def measure_block_linears(dev, flush, iters: int) -> dict:
         total_ops += ops_
         total_ms += ms
         del mod, x
+    tops = total_ops / (total_ms * 1e-3) / 1e12
     return {"config": "BASELINE config 3: 8 linears of one Krea2 block, M=4352, rank 32, group 64, W4A4",
-            "ops": total_ops, "ms": round(total_ms, 4), "tops": round(total_ops / (total_ms * 1e-3) / 1e12, 1),
-            "per_linear": per}
+            "ops": total_ops, "ms": round(total_ms, 4), "tops": round(tops, 1),
+            "frac_of_measured_bf16_peak": round(tops / _bf16_peak(), 4), "per_linear": per}
 
 
 def measure_w4a16_lora(dev, flush, iters: int) -> dict:
@@ -279,8 +285,9 @@ def measure_w4a16_lora(dev, flush, iters: int) -> dict:
     mod.prepare(dev)
     ms = statistics.median(_device_times(lambda: mod(x), iters, flush))
     lowrank = 2 * M * (K + N) * 32 + 2 * M * 64 * (K + N)
+    tops = OPS / (ms * 1e-3) / 1e12
     return {"config": "BASELINE config 4: W4A16 + rank-32 SVD branch + LoRA r64 (scale 0.8), M4096 K6144 N16384",
-            "ms": round(ms, 4), "tops": round(OPS / (ms * 1e-3) / 1e12, 1),
+            "ms": round(ms, 4), "tops": round(tops, 1), "frac_of_measured_bf16_peak": round(tops / _bf16_peak(), 4),
             "lowrank_lora_ops": lowrank}
 
 

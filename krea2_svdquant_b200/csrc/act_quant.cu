@@ -233,8 +233,11 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
 
   const float eps = __bfloat162float(__float2bfloat16_rn(1e-8f));
   const float y7 = __frcp_rn(7.0f);
-  constexpr float kMagic = 12582920.0f;  // 1.5 * 2^23 + 8: rint and the offset-binary code in one add
-  const uint64_t mag2 = f2_pack(kMagic, kMagic), nmag2 = f2_pack(-kMagic, -kMagic);
+  // rint by one add: for |t| < 2^22, t + 1.5 * 2^23 rounds t to the nearest integer (ties to even)
+  // and the low mantissa bits hold rint(t) in two's complement.  kMagic * scale has at most 10
+  // significant bits, so fma(m, scale, -kMagic * scale) = rint(t) * scale exactly.
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t mag2 = f2_pack(kMagic, kMagic);
   const int wrow = warp * 16;              // first row of this warp within the CTA tile
   const int row_g = m0 + wrow + g;         // global rows held by this lane
   const int row_g8 = row_g + 8;
@@ -337,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
     if (!ok) break;
 
     // ---- group scale of rows g and g+8 (W4A4) ----
-    uint64_t sc2[2], ys2[2], ns2[2];
+    uint64_t sc2[2], ys2[2], ns2[2], nms2[2];  // scale, RN(1/scale), -scale, -kMagic * scale
     if constexpr (!W4A16) {
       if (emit) {
         uint32_t mx[2];
@@ -365,6 +368,7 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
           sc2[h] = f2_pack(sc, sc);
           ys2[h] = f2_pack(ys, ys);
           ns2[h] = f2_pack(-sc, -sc);
+          nms2[h] = f2_pack(-kMagic * sc, -kMagic * sc);
           if constexpr (PACKED) {
             const int row = h ? row_g8 : row_g;
             if (t4 == 0 && row < a.M && a.scales)
@@ -393,9 +397,10 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
             for (int i = 0; i < 4; ++i) {
               const int h = i & 1;
               const uint64_t q = div_f2(bf2_to_f2(fr[j][kk][i]), ys2[h], ns2[h]);
-              const uint64_t m = f2_add(q, mag2);        // low mantissa bits = rint(q) + 8
-              o[i] = f2_to_h2(f2_mul(f2_add(m, nmag2), sc2[h]));  // q * scale, exact in fp16
-              nib[i] = ((uint32_t)m & 0xFu) | (((uint32_t)(m >> 32) & 0xFu) << 4);
+              const uint64_t m = f2_add(q, mag2);                 // low mantissa bits = rint(q)
+              o[i] = f2_to_h2(f2_fma(m, sc2[h], nms2[h]));         // rint(q) * scale, exact in fp16
+              // offset-binary code q + 8 = two's-complement low nibble with its top bit flipped
+              nib[i] = (((uint32_t)m & 0xFu) | (((uint32_t)(m >> 32) & 0xFu) << 4)) ^ 0x88u;
             }
             if constexpr (PACKED) {
               uint8_t* prow_g = a.packed + (int64_t)row_g * (a.K_pad / 2) + (kcol + 16 * kk + 2 * t4) / 2;
