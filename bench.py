@@ -306,7 +306,7 @@ def measure_forward28(world: int, rank: int, dev, args) -> dict:
     from krea2_svdquant_b200.shard import max_over_ranks, shard_range
 
     cfg = Krea2StandInConfig()
-    images = 8
+    images = args.forward_images
     _, local = shard_range(images, world, rank)
     offload = world == 1 and not args.no_offload
     model = Krea2StandInTransformer.random_svdquant(cfg, seed=0, init_device=dev,
@@ -339,6 +339,7 @@ def measure_forward28(world: int, rank: int, dev, args) -> dict:
         if world > 1:
             dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("forward28_timed")  # lets a profiler capture just the timed steps
         a.record()
         for _ in range(args.forward_steps):
             if graph is not None:
@@ -346,6 +347,7 @@ def measure_forward28(world: int, rank: int, dev, args) -> dict:
             else:
                 out = model(lat, txt)
         b.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     ms = max_over_ranks(a.elapsed_time(b), dev)
     finite = bool(torch.isfinite(out).all().item())
@@ -355,14 +357,36 @@ def measure_forward28(world: int, rank: int, dev, args) -> dict:
     del graph, model
     torch.cuda.empty_cache()
     lin_ops = 2 * (cfg.image_tokens + cfg.text_tokens) * sum(n * k for n, k in cfg.linear_shapes().values())
-    return {"config": ("BASELINE config 5: Krea2-shaped stand-in, 28 blocks, 8 images x (4096+256) tokens, "
+    return {"config": (f"BASELINE config 5: Krea2-shaped stand-in, 28 blocks, {images} images x (4096+256) tokens, "
                        f"{args.forward_steps} denoising steps, batch sharded over {world} GPU(s), "
                        f"block offload {'on (prefetcher)' if offload else 'off'}, "
                        f"{'CUDA graph replay' if used_graph else 'eager launches'}"),
-            "images_per_s": round(images * 1.0 / (ms * 1e-3) * (8 / args.forward_steps), 4),
+            "images_per_s": round(images * 1.0 / (ms * 1e-3) * (args.forward_steps / 8), 4),
             "ms_per_denoising_step": round(ms / args.forward_steps, 2), "images": images,
             "images_per_rank": local, "steps_timed": args.forward_steps,
             "linear_ops_per_image_step": lin_ops * cfg.num_layers, "output_finite": finite}
+
+
+def run_forward_only(args) -> None:
+    """--only-forward: the 28-block forward measurement alone (one JSON line)."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    res = measure_forward28(world, rank, dev, args)
+    if rank == 0:
+        print(json.dumps({"metric": "28-block forward images/s", "value": res["images_per_s"], "unit": "images/s",
+                          "n_gpus": world, "higher_is_better": True, "scaling": "strong", "forward28": res}),
+              flush=True)
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def run_ours(args) -> None:
@@ -564,6 +588,8 @@ def main() -> None:
                     help="skip the config 3/4/5 measurements (block linears, W4A16+LoRA, 28-block forward)")
     ap.add_argument("--no-offload", action="store_true", help="28-block forward without block offload at 1 GPU")
     ap.add_argument("--forward-steps", type=int, default=8, help="denoising steps timed in the 28-block forward")
+    ap.add_argument("--forward-images", type=int, default=8, help="images in the 28-block forward batch")
+    ap.add_argument("--only-forward", action="store_true", help="run only the 28-block forward measurement")
     ap.add_argument("--graph", action="store_true",
                     help="replay the resident 28-block forward from a CUDA graph (host launch cost is not on the "
                          "critical path at these sizes, so eager launches are the default)")
@@ -575,6 +601,8 @@ def main() -> None:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.only_forward:
+        run_forward_only(args)
     else:
         run_ours(args)
 
