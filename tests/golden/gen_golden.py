@@ -119,6 +119,9 @@ def main() -> None:
     if args.only == "weight_quant_fp32":
         weight_quant_case(quantize_symmetric_int4, pack_int4)
         return
+    if args.only == "ckpt_small":
+        checkpoint_case()
+        return
     # BASELINE recipe (config-1 distributions) at a fixture-friendly size.
     linear_case("linear_g64", 64, 1024, 256, 32, 64, seed=1, lora=(16, 0.8, 8.0))
     # K not a group multiple: padded to 192 inside quantize_symmetric_int4 (pack.py:12-16).
@@ -154,6 +157,80 @@ def main() -> None:
     np.savez_compressed(os.path.join(HERE, "quant_edges.npz"), **out)
     print("wrote quant_edges")
     weight_quant_case(quantize_symmetric_int4, pack_int4)
+    checkpoint_case()
+
+
+def checkpoint_case() -> None:
+    """A two-layer transformer-only checkpoint in the converter's on-disk layout
+    (scripts/convert_simulated.py:136-221): per layer the reference's smoothing, low-rank
+    factors and INT4 residual (fp16 scales), saved with safetensors plus svdquant_config.json.
+    The reference's own loader (runtime/load.py:52-132) reads it back into a toy transformer
+    and its pytorch_sim modules give the recorded fp32 outputs."""
+    import json
+    import shutil
+
+    from safetensors.torch import save_file
+    from torch import nn
+
+    from krea2_svdquant.quant.pack import pack_int4, quantize_symmetric_int4
+    from krea2_svdquant.quant.svd import compute_smooth_scale, svd_lowrank
+    from krea2_svdquant.runtime.linear import SVDQuantLinear
+    from krea2_svdquant.runtime.load import load_svdquant_transformer
+
+    out_dir = os.path.join(HERE, "ckpt_small")
+    shutil.rmtree(out_dir, ignore_errors=True)
+    os.makedirs(out_dir)
+    g = torch.Generator().manual_seed(21)
+    layers = {"transformer_blocks.0.attn.to_q": (96, 128, 16, True), "transformer_blocks.0.ff.down": (128, 192, 32, False)}
+    tensors, meta = {}, {"base_model": "krea/Krea-2-Turbo", "format": "krea2-svdquant-transformer-v1",
+                         "target_component": "transformer", "weight_bits": 4, "activation_bits": 16,
+                         "group_size": 64, "layers": {}}
+    inputs = {}
+    for name, (n, k, rank, bias) in layers.items():
+        w = (torch.randn(n, k, generator=g) * 0.02).bfloat16()
+        x = torch.randn(24, k, generator=g)
+        x[:, ::17] *= 10.0
+        smooth = compute_smooth_scale(x.abs().amax(0), w, 0.25, 4.0).cpu()
+        mig = w * smooth.unsqueeze(0)
+        l1, l2 = svd_lowrank(mig, rank)
+        res = mig.float() - l1.float() @ l2.float()
+        q, sc = quantize_symmetric_int4(res, group_size=64, dim=1)
+        key = name.replace(".", "__")
+        tensors[f"{key}.qweight_packed"] = pack_int4(q)
+        tensors[f"{key}.weight_scales"] = sc.to(torch.float16)
+        tensors[f"{key}.smooth_scale"] = smooth.to(torch.bfloat16)
+        tensors[f"{key}.l1"] = l1.to(torch.bfloat16)
+        tensors[f"{key}.l2"] = l2.to(torch.bfloat16)
+        if bias:
+            tensors[f"{key}.bias"] = (torch.randn(n, generator=g) * 0.01).bfloat16()
+        meta["layers"][name] = {"rank": rank, "group_size": 64, "shape": [n, k], "calibrated": True}
+        inputs[name] = x.bfloat16()
+    save_file(tensors, os.path.join(out_dir, "transformer_svdquant.safetensors"))
+    with open(os.path.join(out_dir, "svdquant_config.json"), "w") as f:
+        json.dump(meta, f, indent=2)
+
+    class Toy(nn.Module):
+        def __init__(self):
+            super().__init__()
+            blk = nn.Module()
+            blk.attn = nn.Module()
+            blk.attn.to_q = nn.Linear(128, 96)
+            blk.ff = nn.Module()
+            blk.ff.down = nn.Linear(192, 128)
+            self.transformer_blocks = nn.ModuleList([blk])
+
+    toy = Toy()
+    report = load_svdquant_transformer(toy, out_dir, backend="pytorch_sim")
+    assert report["_load_report"]["replaced"] == list(layers)
+    outs = {}
+    for name in layers:
+        mod = toy.get_submodule(name)
+        assert isinstance(mod, SVDQuantLinear)
+        with torch.no_grad():
+            outs[name.replace(".", "__") + "__x"] = inputs[name].float().numpy()
+            outs[name.replace(".", "__") + "__y_fp32"] = mod(inputs[name].float()).numpy()
+    np.savez_compressed(os.path.join(out_dir, "reference_outputs.npz"), **outs)
+    print("wrote ckpt_small")
 
 
 def weight_quant_case(quantize_symmetric_int4, pack_int4) -> None:

@@ -157,3 +157,41 @@ def test_invalid_arguments_raise():
         mod(x.cpu())
     with pytest.raises(ValueError):
         mod(x[:, :100])
+
+
+def test_reference_written_checkpoint_outputs():
+    """Layers loaded from the reference-written checkpoint reproduce the reference's own fp32
+    pytorch_sim outputs (W4A16) and the staged oracle (W4A4)."""
+    import os
+
+    from torch import nn
+
+    from krea2_svdquant_b200.load import load_svdquant_transformer
+    ck = os.path.join(os.path.dirname(__file__), "golden", "ckpt_small")
+    ref = np.load(os.path.join(ck, "reference_outputs.npz"))
+
+    def toy():
+        m = nn.Module()
+        blk = nn.Module()
+        blk.attn = nn.Module()
+        blk.attn.to_q = nn.Linear(128, 96)
+        blk.ff = nn.Module()
+        blk.ff.down = nn.Linear(192, 128)
+        m.transformer_blocks = nn.ModuleList([blk])
+        return m
+
+    for backend in ("b200_w4a16", "b200"):
+        model = toy()
+        load_svdquant_transformer(model, ck, backend=backend)
+        model.cuda()
+        for name in ("transformer_blocks.0.attn.to_q", "transformer_blocks.0.ff.down"):
+            key = name.replace(".", "__")
+            mod = model.get_submodule(name)
+            mod.output_fp32 = True
+            x = torch.from_numpy(ref[key + "__x"]).cuda().bfloat16()
+            y = mod(x).float().cpu().numpy()
+            if backend == "b200_w4a16":
+                assert O.rel_fro(y, ref[key + "__y_fp32"]) <= TOL_FP32
+            else:
+                want, _ = staged_oracle(x.float().cpu().numpy(), state_numpy(mod.state))
+                assert O.rel_fro(y, want) <= TOL_FP32

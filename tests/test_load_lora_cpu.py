@@ -179,3 +179,38 @@ def test_checkpoint_missing_tensors(tmp_path):
 def test_reference_backend_names_rejected():
     with pytest.raises(ValueError):
         _svdq_linear().__class__(_svdq_linear().state, backend="pytorch_sim")
+
+
+GOLDEN_CKPT = __import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "ckpt_small")
+
+
+class _CkptToy(nn.Module):
+    """The module tree the reference-written fixture checkpoint addresses."""
+
+    def __init__(self):
+        super().__init__()
+        blk = nn.Module()
+        blk.attn = nn.Module()
+        blk.attn.to_q = nn.Linear(128, 96)
+        blk.ff = nn.Module()
+        blk.ff.down = nn.Linear(192, 128)
+        self.transformer_blocks = nn.ModuleList([blk])
+
+
+def test_loads_reference_written_checkpoint():
+    """A checkpoint in the converter's layout, built and read back by the reference
+    (tests/golden/gen_golden.py checkpoint_case), loads here unchanged."""
+    from safetensors.torch import load_file
+    model = _CkptToy()
+    cfg = load_svdquant_transformer(model, GOLDEN_CKPT, backend="b200_w4a16")
+    assert cfg["_load_report"]["replaced"] == ["transformer_blocks.0.attn.to_q", "transformer_blocks.0.ff.down"]
+    t = load_file(GOLDEN_CKPT + "/transformer_svdquant.safetensors")
+    q = model.transformer_blocks[0].attn.to_q
+    d = model.transformer_blocks[0].ff.down
+    assert torch.equal(q.qweight, t["transformer_blocks__0__attn__to_q.qweight_packed"])
+    assert q.weight_scales.dtype == torch.float16 and torch.equal(q.weight_scales,
+                                                                 t["transformer_blocks__0__attn__to_q.weight_scales"])
+    assert q.bias is not None and d.bias is None
+    assert q.original_shape == (96, 128) and d.original_shape == (128, 192)
+    assert q.padded_in_features == 128 and d.padded_in_features == 192
+    assert q.group_size == 64 and d.l1.shape == (128, 32)
