@@ -90,6 +90,21 @@ __device__ __forceinline__ void advance(int& idx, uint32_t& phase, int n) {
   }
 }
 
+// Tile t -> (row block, column block).  Row blocks advance along N in groups of kGroupM, so the
+// tiles live at one time share about 8 A slabs and a few W slabs, which stay in L2: at
+// M4096 N16384 K6144 this reads 570 MB of DRAM against 707 MB for plain column-major order
+// (groups of 4: 989 MB, groups of 12: 633 MB and 2% slower).
+constexpr int kGroupM = 8;
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = kGroupM * num_n;
+  const int first_m = (t / per_group) * kGroupM;
+  const int r = t % per_group;
+  const int gm = min(num_m - first_m, kGroupM);
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
 template <bool OUT_F32>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     linear_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
@@ -160,8 +175,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t filled = 0, par = 0;
       bool ok = true;
       for (int t = pair; ok && t < num_tiles; t += num_pairs) {
-        const int m0 = (t % args.num_m_blocks) * (2 * BM) + (int)rank * BM;
-        const int n0 = (t / args.num_m_blocks) * BN + (int)rank * BN_HALF;
+        int mb, nb;
+        tile_coords(t, args.num_m_blocks, args.num_n_blocks, mb, nb);
+        const int m0 = mb * (2 * BM) + (int)rank * BM;
+        const int n0 = nb * BN + (int)rank * BN_HALF;
         const int total = args.n_k + args.n_lr;
         for (int s = 0; ok && s < total; ++s) {
           if (!(ok = mbar_wait<true>(empty_bar(stage), phase ^ 1u, abort_flag, args.err, kWaitProdEmpty))) break;
@@ -232,8 +249,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t tb_ph = 0;
     bool ok = true;
     for (int t = pair; ok && t < num_tiles; t += num_pairs) {
-      const int m0 = (t % args.num_m_blocks) * (2 * BM) + (int)rank * BM;
-      const int n0 = (t / args.num_m_blocks) * BN;
+      int mb, nb;
+      tile_coords(t, args.num_m_blocks, args.num_n_blocks, mb, nb);
+      const int m0 = mb * (2 * BM) + (int)rank * BM;
+      const int n0 = nb * BN;
       if (!(ok = mbar_wait<true>(tm_full(tb), tb_ph, abort_flag, args.err, kWaitEpiTmemFull))) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + col0);
