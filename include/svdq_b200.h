@@ -62,7 +62,8 @@ const char* svdq_version(void);
  * In-kernel bounded waits record the place they gave up in a device-side
  * word instead of hanging.  Reads (and optionally clears) that word on the
  * current device; synchronizes the device.  *code == 0 means no failure.
- * Codes: 0x101-0x301 GEMM waits, 0x41xx activation-pass waits, 0x4200 an
+ * Codes: 0x101-0x303 GEMM waits (0x302: a split tile's owner waited for a
+ * partial), 0x41xx activation-pass waits, 0x4200 an
  * activation group scale above 65504/7 (the fp16 GEMM operand a16 overflowed),
  * 0x7E01 the diagnostic wait below; the first failure since the last clear is kept.
  */
@@ -184,6 +185,41 @@ int svdq_linear_gemm(const void* a16, const void* w16,
                      void* out, int out_dtype, int64_t ldo,
                      int M, int N, int K_pad,
                      cudaStream_t stream);
+
+/*
+ * Bytes of the split-tail workspace of svdq_linear_gemm_ws on the current
+ * device (sync words plus one fp32 256x128 partial tile per CTA of a full grid).
+ */
+size_t svdq_linear_gemm_workspace_bytes(void);
+
+/*
+ * svdq_linear_gemm with a workspace.  When the output tiles leave a last wave
+ * that would keep most CTA pairs idle, that wave's K iterations are split into
+ * equal ranges over all pairs; the pair holding the start of a tile adds the
+ * other ranges' fp32 partials in K order, so results are deterministic (for a
+ * given shape and device) but differ from svdq_linear_gemm in fp32 summation
+ * order.  Same computation and arguments as svdq_linear_gemm otherwise.
+ *   workspace: 256-byte aligned, at least svdq_linear_gemm_workspace_bytes(),
+ *   ZERO-FILLED before its first use; each launch leaves it ready for the next.
+ *   One launch at a time per workspace (launches ordered on one stream are
+ *   fine).  workspace == NULL gives svdq_linear_gemm.
+ */
+int svdq_linear_gemm_ws(const void* a16, const void* w16,
+                        const void* mid_hl, const void* up_hl, int R2,
+                        const void* bias,
+                        void* out, int out_dtype, int64_t ldo,
+                        int M, int N, int K_pad,
+                        void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream);
+
+/*
+ * The launch plan of svdq_linear_gemm (with_workspace == 0) or
+ * svdq_linear_gemm_ws (with_workspace != 0) for a shape on the current device:
+ * out4 = {CTA pairs, tiles computed whole, K iterations per pair in the split
+ * tail, tail iterations in total (0: no split)}.  A K iteration is 64 columns
+ * of K_pad or of R2.  Host-only apart from the device attribute queries.
+ */
+int svdq_linear_gemm_schedule(int M, int N, int K_pad, int R2, int with_workspace, int* out4);
 
 /*
  * Converter weight quantization on the GPU: an fp32 layer residual w [N, K]

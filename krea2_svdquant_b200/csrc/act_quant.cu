@@ -217,12 +217,24 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
     for (int s = 0; s < STAGES && s < n_loc; ++s) issue(s, s);
   // reciprocal table of the slice: {RN(1/s_c), RN(1/s_c+1), -s_c, -s_c+1} per column pair
   {
+    // every load first (one round trip for the whole table), then the reciprocals
+    constexpr int kTblIters = kMaxSliceStages * (kBK / 2) / kThreads;
+    static_assert(kTblIters * kThreads == kMaxSliceStages * (kBK / 2), "table entries per thread");
     float4* tbl = reinterpret_cast<float4*>(gbase + (rst - base));
-    for (int i = tid; i < n_loc * (kBK / 2); i += kThreads) {
+    float sv[kTblIters][2];
+#pragma unroll
+    for (int u = 0; u < kTblIters; ++u) {
+      const int i = tid + u * kThreads;
       const int col = st0 * kBK + 2 * i;
-      const float s0 = col < a.K_in ? __bfloat162float(a.smooth[col]) : 1.f;
-      const float s1 = col + 1 < a.K_in ? __bfloat162float(a.smooth[col + 1]) : 1.f;
-      tbl[i] = make_float4(__frcp_rn(s0), __frcp_rn(s1), -s0, -s1);
+      const bool live = i < n_loc * (kBK / 2);
+      sv[u][0] = live && col < a.K_in ? __bfloat162float(a.smooth[col]) : 1.f;
+      sv[u][1] = live && col + 1 < a.K_in ? __bfloat162float(a.smooth[col + 1]) : 1.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kTblIters; ++u) {
+      const int i = tid + u * kThreads;
+      if (i < n_loc * (kBK / 2))
+        tbl[i] = make_float4(__frcp_rn(sv[u][0]), __frcp_rn(sv[u][1]), -sv[u][0], -sv[u][1]);
     }
   }
   __syncthreads();

@@ -29,6 +29,20 @@
 // Every mbarrier wait is bounded; a wait that runs out sets a CTA abort flag and
 // the library's device error word, and all roles leave their loops, so both
 // CTAs always reach the closing cluster barrier.
+//
+// Split tail.  Whole tiles fill as many complete waves over the pairs as they
+// can; when the remaining tiles would leave most pairs idle for a last wave,
+// their K iterations (residual stages, then low-rank stages) are laid end to
+// end and cut into equal contiguous ranges, one per pair.  A range that starts
+// inside a tile is the pair's first unit: it writes its fp32 partial tile to the
+// workspace and publishes a flag.  The unit that holds the start of a tile is the
+// last unit of its pair: it waits (bounded) for the flags of the following pairs
+// whose ranges cover the rest of the tile, adds their partials in K order (a
+// fixed order, so results are deterministic), and runs the bias/cast epilogue.
+// Flags carry a generation number kept in the workspace and advanced by the
+// last CTA of each launch, so flags of an earlier or aborted launch never match.
+#include <algorithm>
+
 #include "svdq_common.cuh"
 
 namespace svdq {
@@ -55,6 +69,7 @@ struct Barriers {
   uint64_t tmem_full[NUM_ACC];
   uint64_t tmem_empty[NUM_ACC];  // used in the even CTA (16 arrivals: 8 warps per CTA)
   uint64_t mma_done;
+  uint64_t part_done;          // epilogue warps of this CTA have written a tail partial (8 arrivals)
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -69,8 +84,23 @@ struct GemmArgs {
   int n_k;   // K_pad / 64 residual stages
   int n_lr;  // R2 / 64 low-rank stages
   int num_m_blocks, num_n_blocks;  // pair tiles: 256 rows x 256 columns
+  int iters;       // K iterations of one tile: n_k + n_lr
+  int dp_tiles;    // tiles [0, dp_tiles) are computed whole, round-robin over the pairs
+  int tail_len;    // K iterations per pair in the split tail
+  int tail_total;  // (num_tiles - dp_tiles) * iters; 0 = no split tail
+  float* partial;  // [2 * pairs][BM * BN] fp32 partial tiles of the split tail
+  uint32_t* sync;  // [0] generation, [1] CTAs done, [2 + 2 * pair + rank] partial-ready flags
   int* err;
 };
+
+// Workspace of the split tail: sync words, then one fp32 partial tile per CTA.
+constexpr size_t kPartialFloats = (size_t)BM * BN;
+inline size_t sync_bytes(int max_pairs) { return ((size_t)(2 + 2 * max_pairs) * 4 + 1023) / 1024 * 1024; }
+inline size_t workspace_bytes_for(int max_pairs) {
+  return sync_bytes(max_pairs) + (size_t)2 * max_pairs * kPartialFloats * sizeof(float);
+}
+constexpr int kMaxParts = 4;       // a tail tile is cut into at most this many K ranges
+constexpr int kMinSplitIters = 8;  // and no range is shorter than this many K iterations
 
 // Wait sites recorded in the device error word.
 enum : int {
@@ -79,6 +109,8 @@ enum : int {
   kWaitMmaTmemEmpty = 0x202,
   kWaitMmaDone = 0x203,
   kWaitEpiTmemFull = 0x301,
+  kWaitEpiPartial = 0x302,   // the owner of a split tile waited for a partial
+  kWaitEpiPartDone = 0x303,  // a CTA waited for its own epilogue warps' partial stores
 };
 
 constexpr uint32_t kFmtF16 = 0;  // kind::f16 format code for fp16
@@ -105,6 +137,75 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
   nb = r / gm;
 }
 
+// The units of one pair, in order: whole tiles pair, pair + pairs, ... below
+// dp_tiles, then the pieces of its tail range [pair * tail_len, +tail_len),
+// cut at tile boundaries.  A unit is (tile, K iterations [k0, k1)).
+struct Walk {
+  int j, g, gend;
+};
+__device__ __forceinline__ void walk_init(Walk& w, const GemmArgs& a, int pair) {
+  w.j = 0;
+  w.g = a.tail_total > 0 ? min(pair * a.tail_len, a.tail_total) : 0;
+  w.gend = a.tail_total > 0 ? min(w.g + a.tail_len, a.tail_total) : 0;
+}
+__device__ __forceinline__ bool walk_next(Walk& w, const GemmArgs& a, int pair, int num_pairs, int& t, int& k0,
+                                          int& k1) {
+  const int td = pair + w.j * num_pairs;
+  if (td < a.dp_tiles) {
+    ++w.j;
+    t = td;
+    k0 = 0;
+    k1 = a.iters;
+    return true;
+  }
+  if (w.g >= w.gend) return false;
+  const int tt = w.g / a.iters;
+  k0 = w.g - tt * a.iters;
+  k1 = min(a.iters, k0 + (w.gend - w.g));
+  t = a.dp_tiles + tt;
+  w.g += k1 - k0;
+  return true;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_local(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Element (row, col) of a CTA's partial tile: 4-column groups outermost, so the
+// 32 lanes of a warp (32 consecutive rows) touch 512 contiguous bytes.
+__device__ __forceinline__ size_t part_index(int row, int col) {
+  return ((size_t)(col >> 2) * BM + row) * 4 + (col & 3);
+}
+
+// An owner streams the partials it adds through the operand ring, idle by then
+// (its unit is the pair's last): per epilogue warp kPartSlots groups of 8 x 512
+// bytes, one group = one 32-column chunk of one partial for the warp's 32 rows.
+constexpr int kPartSlots = 6;
+constexpr uint32_t kPartWarpBytes = kPartSlots * 8 * 512;
+static_assert(8 * kPartWarpBytes <= (uint32_t)STAGES * AB_BYTES, "partial staging fits the operand ring");
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
 template <bool OUT_F32>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     linear_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
@@ -124,7 +225,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
-  const int num_tiles = args.num_m_blocks * args.num_n_blocks;
 
   auto full_bar = [&](int s) { return smem_u32(&bars->full[s]); };
   auto empty_bar = [&](int s) { return smem_u32(&bars->empty[s]); };
@@ -143,6 +243,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(tm_empty(b), 16);  // epilogue warps of both CTAs
     }
     mbar_init(smem_u32(&bars->mma_done), 1);
+    mbar_init(smem_u32(&bars->part_done), 8);  // one arrival per epilogue warp
     bars->abort_flag = 0;
     fence_mbar_init();
   }
@@ -174,13 +275,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       uint32_t filled = 0, par = 0;
       bool ok = true;
-      for (int t = pair; ok && t < num_tiles; t += num_pairs) {
+      Walk wk;
+      walk_init(wk, args, pair);
+      int t, k0, k1;
+      while (ok && walk_next(wk, args, pair, num_pairs, t, k0, k1)) {
         int mb, nb;
         tile_coords(t, args.num_m_blocks, args.num_n_blocks, mb, nb);
         const int m0 = mb * (2 * BM) + (int)rank * BM;
         const int n0 = nb * BN + (int)rank * BN_HALF;
-        const int total = args.n_k + args.n_lr;
-        for (int s = 0; ok && s < total; ++s) {
+        for (int s = k0; ok && s < k1; ++s) {
           if (!(ok = mbar_wait<true>(empty_bar(stage), phase ^ 1u, abort_flag, args.err, kWaitProdEmpty))) break;
           const uint32_t full_c = mapa_shared(full_bar(stage), 0);
           if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * AB_BYTES);
@@ -210,12 +313,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int stage = 0, tb = 0;
       uint32_t phase = 0, tb_ph = 0;
       bool ok = true;
-      for (int t = pair; ok && t < num_tiles; t += num_pairs) {
+      Walk wk;
+      walk_init(wk, args, pair);
+      int t, k0, k1;
+      while (ok && walk_next(wk, args, pair, num_pairs, t, k0, k1)) {
         if (!(ok = mbar_wait<true>(tm_empty(tb), tb_ph ^ 1u, abort_flag, args.err, kWaitMmaTmemEmpty))) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(tb * BN);
-        const int total = args.n_k + args.n_lr;
-        for (int s = 0; ok && s < total; ++s) {
+        for (int s = k0; ok && s < k1; ++s) {
           if (!(ok = mbar_wait<true>(full_bar(stage), phase, abort_flag, args.err, kWaitMmaFull))) break;
           tc_fence_after();
           const uint64_t da = desc_k_sw128(stage_a(stage));
@@ -223,7 +328,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t idesc = s < args.n_k ? idesc_f16 : idesc_bf16;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)  // 4 x K=16 = 128 bytes
-            umma_f16_pair(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (s > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_pair(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (s > k0 || kk > 0) ? 1u : 0u);
           umma_commit_pair(empty_bar(stage));
           advance(stage, phase, STAGES);
         }
@@ -245,16 +350,72 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int col0 = (ew >> 2) * EPI_COLS;  // warpgroup's column half
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    // flag value of this launch: flags of earlier launches hold older generations
+    const uint32_t epoch = args.tail_total > 0 ? *reinterpret_cast<volatile uint32_t*>(args.sync) + 1u : 0u;
     int tb = 0;
     uint32_t tb_ph = 0;
     bool ok = true;
-    for (int t = pair; ok && t < num_tiles; t += num_pairs) {
+    Walk wk;
+    walk_init(wk, args, pair);
+    int t, k0, k1;
+    while (ok && walk_next(wk, args, pair, num_pairs, t, k0, k1)) {
       int mb, nb;
       tile_coords(t, args.num_m_blocks, args.num_n_blocks, mb, nb);
       const int m0 = mb * (2 * BM) + (int)rank * BM;
       const int n0 = nb * BN;
+      const bool contrib = k0 > 0;  // a later piece of a split tile: hand the partial to its owner
+      int n_parts = 0;              // owner of a split tile: partials of pairs pair+1 .. pair+n_parts
+      if (k0 == 0 && k1 < args.iters) {
+        const int tile_end = (t - args.dp_tiles + 1) * args.iters;
+        for (int c = pair + 1; c < num_pairs && c * args.tail_len < tile_end; ++c) ++n_parts;
+      }
+      // bias of the warpgroup's 128 columns: lane l < 16 holds columns 8l .. 8l+7, loaded
+      // before the accumulator wait so its latency hides behind the MMAs
+      uint4 bias_lane = make_uint4(0u, 0u, 0u, 0u);
+      if (args.bias && !contrib && lane < 16 && n0 + col0 + 8 * lane < args.N)
+        bias_lane = *reinterpret_cast<const uint4*>(args.bias + n0 + col0 + 8 * lane);
       if (!(ok = mbar_wait<true>(tm_full(tb), tb_ph, abort_flag, args.err, kWaitEpiTmemFull))) break;
       tc_fence_after();
+      if (n_parts > 0) {
+        // lane 0 waits for each flag (bounded); then every lane acquires it itself
+        int good = 1;
+        if (lane == 0) {
+          for (int c = 1; c <= n_parts && good; ++c) {
+            const uint32_t* f = args.sync + 2 + 2 * (pair + c) + rank;
+            if (ld_acquire_gpu(f) == epoch) continue;
+            const unsigned long long t0 = globaltimer();
+            while (ld_acquire_gpu(f) != epoch) {
+              if (*abort_flag) { good = 0; break; }
+              if (globaltimer() - t0 > kWaitLimitNs) {
+                *abort_flag = 1;
+                atomicCAS(args.err, 0, kWaitEpiPartial);
+                good = 0;
+                break;
+              }
+            }
+          }
+        }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!(ok = good != 0)) break;
+        for (int c = 1; c <= n_parts; ++c) (void)ld_acquire_gpu(args.sync + 2 + 2 * (pair + c) + rank);
+      }
+      // owner: groups (chunk c, partial pc) in the order they are added, kPartSlots in flight;
+      // each lane copies and later reads only its own 16-byte pieces (no cross-lane hazards)
+      const uint32_t wreg = smem_base + (uint32_t)ew * kPartWarpBytes;
+      const int n_groups = 4 * n_parts;
+      auto issue_group = [&](int g) {
+        if (g < n_groups) {
+          const int c = g / n_parts, pc = g - c * n_parts + 1;
+          const float* src = args.partial + (size_t)(2 * (pair + pc) + (int)rank) * kPartialFloats +
+                             part_index(row, col0 + c * 32);
+          const uint32_t dst = wreg + (uint32_t)(g % kPartSlots) * (8 * 512) + (uint32_t)lane * 16;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) cp_async16(dst + (uint32_t)i * 512, src + (size_t)i * 4 * BM);
+        }
+        cp_async_commit();
+      };
+      if (n_parts > 0)
+        for (int g = 0; g < kPartSlots; ++g) issue_group(g);
       const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + col0);
       const int grow = m0 + row;
       const int64_t rbase = (int64_t)grow * args.ldo;
@@ -273,7 +434,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(mapa_shared(tm_empty(tb), 0));
         }
-        const int nc = n0 + col0 + c * 32;
+        const int cc = col0 + c * 32;  // tile column of cur[0]
+        if (contrib) {
+          float4* slot = reinterpret_cast<float4*>(args.partial + (size_t)(2 * pair + (int)rank) * kPartialFloats);
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            __stcg(slot + part_index(row, cc + i) / 4, make_float4(__uint_as_float(cur[i]), __uint_as_float(cur[i + 1]),
+                                                                   __uint_as_float(cur[i + 2]), __uint_as_float(cur[i + 3])));
+          continue;
+        }
+        // owner of a split tile: add the other ranges' partials in K order
+        for (int pc = 1; pc <= n_parts; ++pc) {
+          const int g = c * n_parts + pc - 1;
+          cp_async_wait<kPartSlots - 1>();  // groups up to g have landed
+          const uint32_t sl = wreg + (uint32_t)(g % kPartSlots) * (8 * 512) + (uint32_t)lane * 16;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 pv = ld_shared_f4(sl + (uint32_t)i * 512);
+            cur[4 * i] = __float_as_uint(__uint_as_float(cur[4 * i]) + pv.x);
+            cur[4 * i + 1] = __float_as_uint(__uint_as_float(cur[4 * i + 1]) + pv.y);
+            cur[4 * i + 2] = __float_as_uint(__uint_as_float(cur[4 * i + 2]) + pv.z);
+            cur[4 * i + 3] = __float_as_uint(__uint_as_float(cur[4 * i + 3]) + pv.w);
+          }
+          issue_group(g + kPartSlots);  // reuses the slot just read (its values are in registers)
+        }
+        const int nc = n0 + cc;
+        uint32_t bw[4][4];  // bias words of this chunk's four 8-column groups
+#pragma unroll
+        for (int ii = 0; ii < 4; ++ii) {
+          bw[ii][0] = __shfl_sync(0xffffffffu, bias_lane.x, c * 4 + ii);
+          bw[ii][1] = __shfl_sync(0xffffffffu, bias_lane.y, c * 4 + ii);
+          bw[ii][2] = __shfl_sync(0xffffffffu, bias_lane.z, c * 4 + ii);
+          bw[ii][3] = __shfl_sync(0xffffffffu, bias_lane.w, c * 4 + ii);
+        }
         if (grow < args.M) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
@@ -283,8 +476,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
               for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(cur[i + e]);
               if (args.bias) {
-                const uint4 braw = *reinterpret_cast<const uint4*>(args.bias + n);
-                const __nv_bfloat162* bb = reinterpret_cast<const __nv_bfloat162*>(&braw);
+                const __nv_bfloat162* bb = reinterpret_cast<const __nv_bfloat162*>(bw[i / 8]);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const float2 f = __bfloat1622float2(bb[e]);
@@ -310,6 +502,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
+      if (contrib) {
+        // publish the partial: each warp's arrival (release at CTA scope) orders its stores
+        // before the publishing thread's acquire, whose GPU-scope release then covers them
+        __syncwarp();
+        if (lane == 0) mbar_arrive_local(smem_u32(&bars->part_done));
+        int good = 1;
+        if (ew == 0) {
+          if (lane == 0) {
+            if (mbar_wait<false>(smem_u32(&bars->part_done), 0, abort_flag, args.err, kWaitEpiPartDone)) {
+              __threadfence();
+              st_release_gpu(args.sync + 2 + 2 * pair + rank, epoch);
+            } else {
+              good = 0;
+            }
+          }
+          good = __shfl_sync(0xffffffffu, good, 0);
+        }
+        if (!(ok = good != 0)) break;
+      }
       advance(tb, tb_ph, NUM_ACC);
     }
   }
@@ -324,13 +535,78 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
+  if (args.tail_total > 0 && threadIdx.x == 0) {
+    // the last CTA of the launch advances the generation (every CTA has read it by now)
+    __threadfence();
+    if (atomicAdd(args.sync + 1, 1u) == gridDim.x - 1) {
+      args.sync[1] = 0;
+      args.sync[0] = args.sync[0] + 1u;
+      __threadfence();
+    }
+  }
 }
 
 }  // namespace
 
+// Pairs of this kernel that can be resident at once on the current device.  The
+// split tail's owners wait for other pairs, so its grid never exceeds this.
+int max_resident_pairs(const void* kern) {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int fallback = num_sms() / 2;
+  if (dev < 0 || dev >= 64) return fallback;
+  if (cache[dev] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * fallback, 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = fallback;
+    }
+    cache[dev] = n < fallback ? n : fallback;
+  }
+  return cache[dev];
+}
+
+struct Schedule {
+  int pairs, dp_tiles, tail_len, tail_total;
+};
+
+// Whole tiles round-robin; a last partial wave filling at most 11/20 of the pairs
+// is split into equal K ranges when the workspace allows (see the kernel comment).
+// A split tail costs about three tile epilogues of fixed time (partial stores,
+// flag hand-off, partial loads), so fuller last waves stay whole: measured on
+// B200 at M 4352, K 6144, a tail of 0.38 of a wave ran 8% faster split, one of
+// 0.70 ran 1% slower.
+Schedule plan_schedule(int tiles, int iters, int max_pairs, bool can_split) {
+  Schedule s{tiles < max_pairs ? tiles : max_pairs, tiles, 0, 0};
+  if (!can_split || tiles <= 0) return s;
+  const int full = tiles / max_pairs, tail = tiles - full * max_pairs;
+  if (tail == 0 || tail * 20 > max_pairs * 11) return s;
+  const int tail_total = tail * iters;
+  int len = (tail_total + max_pairs - 1) / max_pairs;
+  len = std::max(len, std::max(kMinSplitIters, (iters + kMaxParts - 1) / kMaxParts));
+  if (len >= iters) return s;
+  s.dp_tiles = full * max_pairs;
+  s.tail_len = len;
+  s.tail_total = tail_total;
+  s.pairs = full > 0 ? max_pairs : (tail_total + len - 1) / len;
+  return s;
+}
+
 int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, const void* up_hl, int R2,
                        const void* bias, void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
-                       cudaStream_t stream, const char* who) {
+                       void* workspace, size_t workspace_bytes, cudaStream_t stream, const char* who) {
   const std::string w(who);
   if (!(a16 && w16 && out)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": null operand pointer");
   if (!(M >= 0 && N > 0 && K_pad > 0)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": bad M/N/K_pad");
@@ -379,13 +655,23 @@ int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, con
   a.n_lr = R2 / 64;
   a.num_m_blocks = (M + 2 * BM - 1) / (2 * BM);
   a.num_n_blocks = (N + BN - 1) / BN;
+  a.iters = a.n_k + a.n_lr;
   a.err = err;
   auto kern = out_dtype == SVDQ_FP32 ? linear_gemm_kernel<true> : linear_gemm_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
   if (e != cudaSuccess) return check_cuda(e, (w + ": shared memory attribute").c_str());
   const int tiles = a.num_m_blocks * a.num_n_blocks;
-  const int max_pairs = num_sms() / 2;
-  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  const int max_pairs = max_resident_pairs(reinterpret_cast<const void*>(kern));
+  const bool can_split = workspace != nullptr && workspace_bytes >= workspace_bytes_for(num_sms() / 2) &&
+                         (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0;
+  const Schedule sc = plan_schedule(tiles, a.iters, max_pairs, can_split);
+  a.dp_tiles = sc.dp_tiles;
+  a.tail_len = sc.tail_len;
+  a.tail_total = sc.tail_total;
+  a.sync = static_cast<uint32_t*>(workspace);
+  a.partial = workspace ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + sync_bytes(num_sms() / 2))
+                        : nullptr;
+  const int pairs = sc.pairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
@@ -410,6 +696,38 @@ int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, con
 extern "C" int svdq_linear_gemm(const void* a16, const void* w16, const void* mid_hl, const void* up_hl, int R2,
                                 const void* bias, void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
                                 cudaStream_t stream) {
-  return svdq::launch_linear_gemm(a16, w16, mid_hl, up_hl, R2, bias, out, out_dtype, ldo, M, N, K_pad, stream,
-                                  "svdq_linear_gemm");
+  return svdq::launch_linear_gemm(a16, w16, mid_hl, up_hl, R2, bias, out, out_dtype, ldo, M, N, K_pad, nullptr, 0,
+                                  stream, "svdq_linear_gemm");
+}
+
+extern "C" size_t svdq_linear_gemm_workspace_bytes(void) { return svdq::workspace_bytes_for(svdq::num_sms() / 2); }
+
+extern "C" int svdq_linear_gemm_ws(const void* a16, const void* w16, const void* mid_hl, const void* up_hl, int R2,
+                                   const void* bias, void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
+                                   void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_linear_gemm_ws: workspace must be 256-byte aligned");
+  if (workspace && workspace_bytes < svdq::workspace_bytes_for(svdq::num_sms() / 2))
+    return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT,
+                           "svdq_linear_gemm_ws: workspace smaller than svdq_linear_gemm_workspace_bytes()");
+  return svdq::launch_linear_gemm(a16, w16, mid_hl, up_hl, R2, bias, out, out_dtype, ldo, M, N, K_pad, workspace,
+                                  workspace_bytes, stream, "svdq_linear_gemm_ws");
+}
+
+extern "C" int svdq_linear_gemm_schedule(int M, int N, int K_pad, int R2, int with_workspace, int* out4) {
+  if (!out4) return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_linear_gemm_schedule: out4 is NULL");
+  if (!(M >= 0 && N > 0 && K_pad > 0 && K_pad % 64 == 0 && R2 >= 0 && R2 % 64 == 0))
+    return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_linear_gemm_schedule: bad M/N/K_pad/R2");
+  auto kern = svdq::linear_gemm_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)svdq::SMEM_BYTES);
+  if (e != cudaSuccess) return svdq::check_cuda(e, "svdq_linear_gemm_schedule: shared memory attribute");
+  const int tiles = ((M + 2 * svdq::BM - 1) / (2 * svdq::BM)) * ((N + svdq::BN - 1) / svdq::BN);
+  const svdq::Schedule sc = svdq::plan_schedule(tiles, K_pad / 64 + R2 / 64,
+                                                svdq::max_resident_pairs(reinterpret_cast<const void*>(kern)),
+                                                with_workspace != 0);
+  out4[0] = sc.pairs;
+  out4[1] = sc.dp_tiles;
+  out4[2] = sc.tail_len;
+  out4[3] = sc.tail_total;
+  return SVDQ_OK;
 }

@@ -8,6 +8,7 @@ CPU implementation behind these ops.
 from __future__ import annotations
 
 import ctypes
+import threading
 from typing import Optional
 
 import torch
@@ -195,6 +196,31 @@ def _(l1, lora_up, r2):
 
 
 # --------------------------------------------------------------------------- GEMM
+_gemm_ws: dict = {}
+_gemm_ws_lock = threading.Lock()
+
+
+def _gemm_workspace(dev: torch.device) -> Optional[Tensor]:
+    """Zero-filled split-tail workspace of ``svdq_linear_gemm_ws``, one per (device, stream).
+
+    Launches on one stream run in order, so a stream's launches share its workspace; each
+    launch leaves it ready for the next (the sync words are never re-zeroed).  Inside a CUDA
+    graph capture no workspace is created (the launch runs unsplit), so a graph never owns
+    or re-zeroes one."""
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    ws = _gemm_ws.get(key)
+    if ws is None and torch.cuda.is_current_stream_capturing():
+        return None
+    if ws is None:
+        with _gemm_ws_lock:
+            ws = _gemm_ws.get(key)
+            if ws is None:
+                n = int(_lib.lib().svdq_linear_gemm_workspace_bytes())
+                ws = torch.zeros((n,), dtype=torch.uint8, device=dev)
+                _gemm_ws[key] = ws
+    return ws
+
+
 @torch.library.custom_op("svdq_b200::linear_gemm", mutates_args=())
 def linear_gemm(a16: Tensor, w16: Tensor, mid_hl: Optional[Tensor], up_hl: Optional[Tensor],
                 bias: Optional[Tensor], out_fp32: bool) -> Tensor:
@@ -209,9 +235,10 @@ def linear_gemm(a16: Tensor, w16: Tensor, mid_hl: Optional[Tensor], up_hl: Optio
     out = torch.empty((m, n), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=a16.device)
     if m == 0:
         return out
-    _lib.call("svdq_linear_gemm", _p(a16), _p(w16), _p(mid_hl) if r2 else None, _p(up_hl) if r2 else None, r2,
+    ws = _gemm_workspace(a16.device)
+    _lib.call("svdq_linear_gemm_ws", _p(a16), _p(w16), _p(mid_hl) if r2 else None, _p(up_hl) if r2 else None, r2,
               _p(bias), _p(out), _lib.SVDQ_FP32 if out_fp32 else _lib.SVDQ_BF16, out.stride(0), m, n, k_pad,
-              _stream(a16.device))
+              _p(ws), 0 if ws is None else ws.numel(), _stream(a16.device))
     return out
 
 
