@@ -257,7 +257,9 @@ def measure_block_linears(dev, flush, iters: int) -> dict:
         mod = SVDQuantLinear(random_state(n, k, 32, 64, device=dev, generator=gen), backend="b200")
         x = torch.randn(m_tok, k, device=dev, generator=gen).bfloat16()
         mod.prepare(dev)
+        torch.cuda.nvtx.range_push(f"block_linear:{name}")  # lets a profiler capture one layer's launches
         ms = statistics.median(_device_times(lambda: mod(x), iters, flush))
+        torch.cuda.nvtx.range_pop()
         ops_ = 2 * m_tok * n * k
         per[name] = {"N": n, "K": k, "us": round(ms * 1e3, 1), "tops": round(ops_ / (ms * 1e-3) / 1e12, 1)}
         total_ops += ops_
@@ -387,6 +389,28 @@ def run_forward_only(args) -> None:
               flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_block_linears_only(args) -> None:
+    """--only-block-linears: the config-3 measurement alone on one GPU (one JSON line)."""
+    import torch
+
+    from krea2_svdquant_b200 import _lib
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    flush_w = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(32 * 1024 * 1024, dtype=torch.int64, device=dev)
+
+    def flush_l2():  # the same L2 flush as the headline measurement
+        flush_w.zero_()
+        return flush_r.sum()
+
+    res = measure_block_linears(dev, flush_l2, max(args.warmup, 3))
+    if _lib.device_error():
+        raise RuntimeError("device-side error during the block-linears measurement")
+    print(json.dumps({"metric": "Krea2 block linears TOPS @M4352", "value": res["tops"], "unit": "TOPS",
+                      "n_gpus": 1, "higher_is_better": True, "block_linears": res}), flush=True)
 
 
 def run_ours(args) -> None:
@@ -590,6 +614,8 @@ def main() -> None:
     ap.add_argument("--forward-steps", type=int, default=8, help="denoising steps timed in the 28-block forward")
     ap.add_argument("--forward-images", type=int, default=8, help="images in the 28-block forward batch")
     ap.add_argument("--only-forward", action="store_true", help="run only the 28-block forward measurement")
+    ap.add_argument("--only-block-linears", action="store_true",
+                    help="run only the config-3 block-linears measurement (one GPU)")
     ap.add_argument("--graph", action="store_true",
                     help="replay the resident 28-block forward from a CUDA graph (host launch cost is not on the "
                          "critical path at these sizes, so eager launches are the default)")
@@ -603,6 +629,8 @@ def main() -> None:
         run_reference(args)
     elif args.only_forward:
         run_forward_only(args)
+    elif args.only_block_linears:
+        run_block_linears_only(args)
     else:
         run_ours(args)
 
