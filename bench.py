@@ -163,19 +163,25 @@ def cpu_reference_tops(calls: int, warmup: int, x_cpu, st_cpu, budget_s: float =
     torch.set_num_threads(cores)
     args = (st_cpu.smooth_scale, st_cpu.qweight, st_cpu.weight_scales, st_cpu.l1, st_cpu.l2, st_cpu.bias)
     kw = dict(group=GROUP, k_in=K, k_pad=K)
+    per = {}  # dtype -> (seconds per call, calls)
     with torch.no_grad():
-        for _ in range(warmup):
-            svdquant_linear_sim_torch(x_cpu, *args, **kw)
-        t0 = time.perf_counter()
-        done = 0
-        while done < calls or time.perf_counter() - t0 < budget_s:
-            svdquant_linear_sim_torch(x_cpu, *args, **kw)
-            done += 1
-        dt = (time.perf_counter() - t0) / done
-        calls = done
-    sample = (f"{calls} full config-2 calls (M=4096) after {warmup} warm-up, bf16, torch CPU "
-              f"restatement of svdquant_linear_sim (svd.py:119-163), {cores} threads on {cpu_model()}")
-    return OPS / dt / 1e12, cores, sample
+        # the reference's bf16 run and its fp32 run; the faster one is the baseline
+        for name, xd in (("bf16", x_cpu), ("fp32", x_cpu.float())):
+            for _ in range(warmup):
+                svdquant_linear_sim_torch(xd, *args, **kw)
+            t0 = time.perf_counter()
+            done = 0
+            while done < calls or time.perf_counter() - t0 < budget_s / 2:
+                svdquant_linear_sim_torch(xd, *args, **kw)
+                done += 1
+            per[name] = ((time.perf_counter() - t0) / done, done)
+    best = min(per, key=lambda n: per[n][0])
+    tops = {n: OPS / v[0] / 1e12 for n, v in per.items()}
+    sample = (f"full config-2 calls (M=4096) of the torch CPU restatement of svdquant_linear_sim "
+              f"(svd.py:119-163) after {warmup} warm-up each: bf16 {per['bf16'][1]} calls "
+              f"{tops['bf16']:.3f} TOPS, fp32 {per['fp32'][1]} calls {tops['fp32']:.3f} TOPS; value = {best}; "
+              f"{cores} threads on {cpu_model()}")
+    return tops[best], cores, sample
 
 
 def run_reference(args) -> None:
@@ -241,6 +247,21 @@ def _device_times(fn, iters: int, flush, warmup: int = 2) -> list[float]:
     return out
 
 
+def _gemm_waves(m: int, n: int, k_pad: int, r2: int) -> dict:
+    """Wave efficiency of the GEMM's 256x256 pair tiles and whether its last wave is split."""
+    import ctypes
+
+    from krea2_svdquant_b200 import _lib
+
+    out = (ctypes.c_int * 4)()
+    _lib.call("svdq_linear_gemm_schedule", m, n, k_pad, r2, 1, out)
+    pairs, dp_tiles, tail_len, tail_total = tuple(out)
+    tiles = -(-m // 256) * -(-n // 256)
+    full = -(-tiles // pairs) * pairs
+    return {"tiles": tiles, "pairs": pairs, "wave_efficiency_whole_tiles": round(tiles / full, 3),
+            "split_tail": tail_total > 0}
+
+
 def measure_block_linears(dev, flush, iters: int) -> dict:
     """the 8 quantized linears of one Krea2 block at M=4352 (4096 image +
     256 text tokens), rank 32, group 64, W4A4; time = sum of the 8 module forwards."""
@@ -256,12 +277,13 @@ def measure_block_linears(dev, flush, iters: int) -> dict:
     for name, (n, k) in Krea2StandInConfig().linear_shapes().items():
         mod = SVDQuantLinear(random_state(n, k, 32, 64, device=dev, generator=gen), backend="b200")
         x = torch.randn(m_tok, k, device=dev, generator=gen).bfloat16()
-        mod.prepare(dev)
+        prep = mod.prepare(dev)
         torch.cuda.nvtx.range_push(f"block_linear:{name}")  # lets a profiler capture one layer's launches
         ms = statistics.median(_device_times(lambda: mod(x), iters, flush))
         torch.cuda.nvtx.range_pop()
         ops_ = 2 * m_tok * n * k
-        per[name] = {"N": n, "K": k, "us": round(ms * 1e3, 1), "tops": round(ops_ / (ms * 1e-3) / 1e12, 1)}
+        per[name] = {"N": n, "K": k, "us": round(ms * 1e3, 1), "tops": round(ops_ / (ms * 1e-3) / 1e12, 1),
+                     **_gemm_waves(m_tok, n, prep.k_pad, 0 if prep.up_hl is None else prep.up_hl.shape[1])}
         total_ops += ops_
         total_ms += ms
         del mod, x
