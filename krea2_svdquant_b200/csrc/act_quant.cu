@@ -42,9 +42,16 @@ constexpr int kWarps = 4;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kBM = 64;              // rows per CTA (16 per warp)
 constexpr int kBK = 64;              // columns per stage: one 128-byte swizzle row of bf16
-constexpr int kMaxSliceStages = 12;  // stages per CTA slice (bounds the reciprocal table)
-constexpr int kMinSliceStages = 2;
 constexpr int kTargetCtasPerSm = 4;
+// x / low-rank ring depth: 4, or 3 with twelve low-rank tiles so that three CTAs still fit an SM.
+__host__ __device__ constexpr int ring_stages(int nt) { return nt >= 12 ? 3 : 4; }
+// Stages per CTA slice, which bounds the reciprocal table: 16 with eight or more low-rank tiles
+// (their CTAs fit three per SM either way), else 12 (a 16-stage table would push the CTA past a
+// quarter of the SM's shared memory).
+__host__ __device__ constexpr int max_slice_stages(int nt) { return nt >= 8 ? 16 : 12; }
+// CTAs per SM the launch bound plans registers for.
+__host__ __device__ constexpr int min_ctas(int nt) { return nt >= 8 ? 3 : kTargetCtasPerSm; }
+constexpr int kMinSliceStages = 2;
 constexpr uint32_t kXTileBytes = kBM * kBK * 2;   // 8 KB
 constexpr uint32_t kLrTileBytes = 8 * kBK * 2;    // 1 KB: 8 low-rank rows
 // a16 = q * scale is exact in fp16 while the group scale lies in [2^-17, 65504 / 7]:
@@ -146,7 +153,7 @@ struct AqArgs {
 template <int STAGES, int NT>
 __host__ __device__ constexpr uint32_t aq_smem_layout_bytes() {
   return 1024 /*align slack*/ + STAGES * kXTileBytes + STAGES * NT * kLrTileBytes +
-         kMaxSliceStages * 32 * 16 /*reciprocal table*/ + 256 /*barriers, counters*/;
+         max_slice_stages(NT) * 32 * 16 /*reciprocal table*/ + 256 /*barriers, counters*/;
 }
 
 // GS: stages per quantization group (1: G=64, 2: G=128).  NT: 8-column
@@ -160,7 +167,7 @@ __host__ __device__ constexpr uint32_t aq_smem_layout_bytes() {
 // the store of stage c + 1 is issued (bulk wait_group.read 1), in the same
 // single-lane section.
 template <int GS, int STAGES, int NT, bool W4A16, bool PACKED, bool LORA>
-__global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
+__global__ void __launch_bounds__(kThreads, min_ctas(NT))
     act_quant_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_l2,
                      const __grid_constant__ CUtensorMap tm_lora, const __grid_constant__ CUtensorMap tm_a16,
                      const AqArgs a) {
@@ -169,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
   const uint32_t xs = base;
   const uint32_t ws = xs + STAGES * kXTileBytes;
   const uint32_t rst = ws + STAGES * NT * kLrTileBytes;
-  const uint32_t bars = rst + kMaxSliceStages * 32 * 16;
+  const uint32_t bars = rst + max_slice_stages(NT) * 32 * 16;
   uint8_t* gbase = smem_raw + (base - smem_u32(smem_raw));
   const float4* rst_p = reinterpret_cast<const float4*>(gbase + (rst - base));
   int* cnt = reinterpret_cast<int*>(gbase + (bars - base) + 8 * STAGES);        // releases per stage
@@ -218,8 +225,8 @@ __global__ void __launch_bounds__(kThreads, kTargetCtasPerSm)
   // reciprocal table of the slice: {RN(1/s_c), RN(1/s_c+1), -s_c, -s_c+1} per column pair
   {
     // every load first (one round trip for the whole table), then the reciprocals
-    constexpr int kTblIters = kMaxSliceStages * (kBK / 2) / kThreads;
-    static_assert(kTblIters * kThreads == kMaxSliceStages * (kBK / 2), "table entries per thread");
+    constexpr int kTblIters = max_slice_stages(NT) * (kBK / 2) / kThreads;
+    static_assert(kTblIters * kThreads == max_slice_stages(NT) * (kBK / 2), "table entries per thread");
     float4* tbl = reinterpret_cast<float4*>(gbase + (rst - base));
     float sv[kTblIters][2];
 #pragma unroll
@@ -512,12 +519,40 @@ struct Geometry {
 int pick_nt(int r_use) {
   if (r_use <= 0) return 0;
   const int tiles = r_use / 8;
-  return tiles <= 2 ? 2 : tiles <= 4 ? 4 : 8;
+  return tiles <= 2 ? 2 : tiles <= 4 ? 4 : tiles <= 8 ? 8 : tiles <= 12 ? 12 : 8;
 }
 
-// K slices per row band: as many as one wave of CTAs holds (kTargetCtasPerSm per SM), each
-// slice a whole number of stages (a multiple of `step`: 2 for 128-column groups, so a group
-// never straddles two slices), between kMinSliceStages and kMaxSliceStages.  Among the slice
+// CTAs of the activation pass that fit on one SM, from its shared memory (registers never
+// bind: the launch bound plans them for min_ctas(nt) CTAs, which the shared memory also allows).
+int ctas_per_sm(int nt) {
+  static int cache[64][5] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int slot = nt == 0 ? 0 : nt == 2 ? 1 : nt == 4 ? 2 : nt == 8 ? 3 : 4;
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev][slot] == 0) {
+    const uint32_t smem = slot == 0   ? aq_smem_layout_bytes<ring_stages(0), 0>()
+                          : slot == 1 ? aq_smem_layout_bytes<ring_stages(2), 2>()
+                          : slot == 2 ? aq_smem_layout_bytes<ring_stages(4), 4>()
+                          : slot == 3 ? aq_smem_layout_bytes<ring_stages(8), 8>()
+                                      : aq_smem_layout_bytes<ring_stages(12), 12>();
+    int per_sm = 0, reserved = 0;
+    if (cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+        per_sm <= 0)
+      per_sm = 233472;
+    if (cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess ||
+        reserved < 0)
+      reserved = 1024;
+    (void)cudaGetLastError();
+    const int n = per_sm / (int)(smem + (uint32_t)reserved);
+    cache[dev][slot] = std::max(1, std::min(kTargetCtasPerSm, n));
+  }
+  return cache[dev][slot];
+}
+
+// K slices per row band: as many as one wave of CTAs holds (ctas_per_sm per SM), each slice a
+// whole number of stages (a multiple of `step`: 2 for 128-column groups, so a group never
+// straddles two slices), between kMinSliceStages and max_slice_stages.  Among the slice
 // lengths that give the fewest waves the one that fills the most CTA slots is taken.
 Geometry geometry(int M, int K_pad, int r_use, int step) {
   Geometry gm;
@@ -525,10 +560,11 @@ Geometry geometry(int M, int K_pad, int r_use, int step) {
   gm.nz = gm.nt ? (r_use + 8 * gm.nt - 1) / (8 * gm.nt) : 1;
   const int n_st = K_pad / kBK;
   const int layers = ((M + kBM - 1) / kBM) * gm.nz;  // CTAs per K slice
-  const int slots = num_sms() * kTargetCtasPerSm;
-  int best_slice = kMaxSliceStages, best_waves = 1 << 30;
+  const int slots = num_sms() * ctas_per_sm(gm.nt);
+  const int max_slice = max_slice_stages(gm.nt);
+  int best_slice = max_slice, best_waves = 1 << 30;
   double best_fill = -1.0;
-  for (int slice = kMinSliceStages; slice <= kMaxSliceStages; slice += step) {
+  for (int slice = kMinSliceStages; slice <= max_slice; slice += step) {
     const int ksplit = (n_st + slice - 1) / slice;
     const long long ctas = (long long)ksplit * layers;
     const int waves = (int)((ctas + slots - 1) / slots);
@@ -564,7 +600,7 @@ struct LaunchSpec {
 
 template <int GS, int NT, bool W4A16, bool PACKED, bool LORA>
 int launch_t(const LaunchSpec& L, cudaStream_t stream) {
-  constexpr int STAGES = 4;
+  constexpr int STAGES = ring_stages(NT);
   constexpr uint32_t smem = aq_smem_layout_bytes<STAGES, NT>();
   auto kern = act_quant_kernel<GS, STAGES, NT, W4A16, PACKED, LORA>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -590,7 +626,8 @@ int launch_nt(const LaunchSpec& L, cudaStream_t stream) {
     case 0: return launch_t<GS, 0, W4A16, PACKED, false>(L, stream);
     case 2: return launch_t<GS, 2, W4A16, PACKED, LORA>(L, stream);
     case 4: return launch_t<GS, 4, W4A16, PACKED, LORA>(L, stream);
-    default: return launch_t<GS, 8, W4A16, PACKED, LORA>(L, stream);
+    case 8: return launch_t<GS, 8, W4A16, PACKED, LORA>(L, stream);
+    default: return launch_t<GS, 12, W4A16, PACKED, LORA>(L, stream);
   }
 }
 

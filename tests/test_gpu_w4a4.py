@@ -134,6 +134,55 @@ def test_act_quant_wide_lowrank():
     assert np.all(mid_np[:, 2 * rt:] == 0)
 
 
+@pytest.mark.parametrize("r,rl,ag", [(8, 0, 64), (32, 0, 64), (64, 0, 64), (32, 64, 64), (64, 24, 128),
+                                     (72, 32, 64)])
+def test_act_quant_lowrank_width_buckets(r, rl, ag):
+    """Every CTA low-rank width: 2, 4, 8 and 12 tiles of 8 columns in one CTA (the 12-tile
+    CTAs run a 3-deep ring), and widths over 96 split across CTAs; ragged rows; both groups."""
+    torch.manual_seed(r + rl)
+    m, k = 200, 1280
+    x = (torch.randn(m, k) * 2).bfloat16().cuda()
+    s = (torch.rand(k) * 3 + 0.25).bfloat16().cuda()
+    l2 = (torch.randn(r, k) * 0.05).bfloat16().cuda()
+    a = (torch.randn(rl, k) * 0.05).bfloat16().cuda() if rl else None
+    cs = torch.full((rl,), 0.8, device="cuda") if rl else None
+    a16, mid, packed, scales = _act(x, s, l2, a, cs, k_pad=k, a_group=ag)
+    torch.cuda.synchronize()
+    xh, q, pk, sa = O.act_quant(x.float().cpu().numpy(), s.float().cpu().numpy(), ag)
+    assert np.array_equal(packed.cpu().numpy(), pk)
+    assert np.array_equal(a16.float().cpu().numpy(), _dequant_np(q, sa, ag))
+    mid_np = mid.float().cpu().numpy()
+    rt = r + rl
+    got = mid_np[:, :rt] + mid_np[:, rt:2 * rt]
+    ref = O.lowrank_down(xh, l2.float().cpu().numpy())
+    if rl:
+        ref = np.concatenate([ref, 0.8 * O.lowrank_down(x.float().cpu().numpy(), a.float().cpu().numpy())], 1)
+    assert O.rel_fro(got, ref) < TOL_MID
+    assert np.all(mid_np[:, 2 * rt:] == 0)
+
+
+def test_w4a16_prep_twelve_tile_width():
+    """The W4A16 activation pass at rank 32 + LoRA 64 (config 4's 96 low-rank columns)."""
+    from krea2_svdquant_b200 import ops
+    torch.manual_seed(12)
+    m, k, r, rl = 150, 1024, 32, 64
+    x = (torch.randn(m, k) * 2).bfloat16().cuda()
+    s = (torch.rand(k) * 3 + 0.25).bfloat16().cuda()
+    l2 = (torch.randn(r, k) * 0.05).bfloat16().cuda()
+    a = (torch.randn(rl, k) * 0.05).bfloat16().cuda()
+    cs = torch.full((rl,), 0.8, device="cuda")
+    a16, mid = ops.w4a16_prep(x, s, l2.half(), a, cs, k)
+    torch.cuda.synchronize()
+    xh = (x.float().cpu().numpy() / s.float().cpu().numpy()).astype(np.float32).astype(np.float16)
+    assert np.array_equal(a16.cpu().numpy(), xh)
+    mid_np = mid.float().cpu().numpy()
+    rt = r + rl
+    got = mid_np[:, :rt] + mid_np[:, rt:2 * rt]
+    ref = np.concatenate([O.lowrank_down(xh.astype(np.float32), l2.half().float().cpu().numpy()),
+                          0.8 * O.lowrank_down(x.float().cpu().numpy(), a.float().cpu().numpy())], 1)
+    assert O.rel_fro(got, ref) < TOL_MID
+
+
 def test_act_quant_ragged_rows_and_lora():
     torch.manual_seed(0)
     m, k, r, rl = 37, 320, 16, 24
