@@ -602,6 +602,11 @@ def run_ours(args) -> None:
                          "traffic": _ncu_traffic("linear_gemm_kernel"), "peak_source": peak_src,
                          "gemm_us": round(gemm_avg * 1e3, 2),
                          "flops_per_launch": OPS,
+                         # the timed loop runs ~0.6 s of back-to-back GEMMs under the power cap, between
+                         # the burst figure (peak) and the 4 s sustained cuBLAS figure (reported here)
+                         "peak_sustained": peaks.get("bf16_tflops_sustained"),
+                         "frac_sustained": (round(achieved / float(peaks["bf16_tflops_sustained"]), 4)
+                                            if peaks.get("bf16_tflops_sustained") else None),
                          "activation_pass": {"bound": "hbm", "kernels": "act_quant_kernel + mid_finalize_kernel",
                                              "us": round(aq_avg * 1e3, 2), "bytes": aq_bytes,
                                              "achieved": round(aq_bytes / (aq_avg * 1e-3) / 1e9, 1),
