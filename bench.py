@@ -617,6 +617,9 @@ def run_ours(args) -> None:
             "e2e": {"value": round(world * OPS / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
                     "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
                     "ms_per_step": round(e2e_ms, 3),
+                    # the device-to-host copy of y is the bound: its achieved link rate per step
+                    "d2h_gbs": round(M * N * 2 / (e2e_ms * 1e-3) / 1e9, 1),
+                    "h2d_gbs": round(M * K * 2 / (e2e_ms * 1e-3) / 1e9, 1),
                     "api": ("SVDQuantLinear.forward; per step x pinned host -> device and y -> pinned host, "
                             "uploads / forwards / downloads of consecutive steps overlapped on two copy streams")},
             "gpu_launches": 3 * args.steps,
