@@ -222,6 +222,13 @@ int svdq_linear_gemm_ws(const void* a16, const void* w16,
 int svdq_linear_gemm_schedule(int M, int N, int K_pad, int R2, int with_workspace, int* out4);
 
 /*
+ * The planner behind svdq_linear_gemm_schedule for a given number of 256x256
+ * tiles, K iterations per tile and co-resident CTA pairs; same out4.  Host
+ * only: makes no CUDA call.
+ */
+int svdq_linear_gemm_plan(int tiles, int iters, int max_pairs, int with_workspace, int* out4);
+
+/*
  * Converter weight quantization on the GPU: an fp32 layer residual w [N, K]
  * (row stride ldw) -> packed INT4 codes [N, K_pad/2] (nibble q + 8, even k
  * low) and group scales [N, K_pad/group] as fp32, fp16 or bf16, with

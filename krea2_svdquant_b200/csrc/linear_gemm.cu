@@ -714,6 +714,18 @@ extern "C" int svdq_linear_gemm_ws(const void* a16, const void* w16, const void*
                                   workspace_bytes, stream, "svdq_linear_gemm_ws");
 }
 
+extern "C" int svdq_linear_gemm_plan(int tiles, int iters, int max_pairs, int with_workspace, int* out4) {
+  if (!out4) return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_linear_gemm_plan: out4 is NULL");
+  if (!(tiles >= 0 && iters > 0 && max_pairs > 0))
+    return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_linear_gemm_plan: bad tiles/iters/max_pairs");
+  const svdq::Schedule sc = svdq::plan_schedule(tiles, iters, max_pairs, with_workspace != 0);
+  out4[0] = sc.pairs;
+  out4[1] = sc.dp_tiles;
+  out4[2] = sc.tail_len;
+  out4[3] = sc.tail_total;
+  return SVDQ_OK;
+}
+
 extern "C" int svdq_linear_gemm_schedule(int M, int N, int K_pad, int R2, int with_workspace, int* out4) {
   if (!out4) return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_linear_gemm_schedule: out4 is NULL");
   if (!(M >= 0 && N > 0 && K_pad > 0 && K_pad % 64 == 0 && R2 >= 0 && R2 % 64 == 0))
