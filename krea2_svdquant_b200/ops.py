@@ -7,6 +7,7 @@ CPU implementation behind these ops.
 """
 from __future__ import annotations
 
+import collections
 import ctypes
 import threading
 from typing import Optional
@@ -196,8 +197,9 @@ def _(l1, lora_up, r2):
 
 
 # --------------------------------------------------------------------------- GEMM
-_gemm_ws: dict = {}
+_gemm_ws: "collections.OrderedDict[tuple, Tensor]" = collections.OrderedDict()
 _gemm_ws_lock = threading.Lock()
+_GEMM_WS_KEEP = 8  # workspaces kept (most recently used (device, stream) pairs)
 
 
 def _gemm_workspace(dev: torch.device) -> Optional[Tensor]:
@@ -208,16 +210,20 @@ def _gemm_workspace(dev: torch.device) -> Optional[Tensor]:
     graph capture no workspace is created (the launch runs unsplit), so a graph never owns
     or re-zeroes one."""
     key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
-    ws = _gemm_ws.get(key)
-    if ws is None and torch.cuda.is_current_stream_capturing():
-        return None
-    if ws is None:
-        with _gemm_ws_lock:
-            ws = _gemm_ws.get(key)
-            if ws is None:
-                n = int(_lib.lib().svdq_linear_gemm_workspace_bytes())
-                ws = torch.zeros((n,), dtype=torch.uint8, device=dev)
-                _gemm_ws[key] = ws
+    with _gemm_ws_lock:
+        ws = _gemm_ws.get(key)
+        if ws is not None:
+            _gemm_ws.move_to_end(key)
+            return ws
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        n = int(_lib.lib().svdq_linear_gemm_workspace_bytes())
+        ws = torch.zeros((n,), dtype=torch.uint8, device=dev)
+        _gemm_ws[key] = ws
+        # An evicted workspace returns to the caching allocator, which reuses it only after the
+        # work already queued on its stream.
+        while len(_gemm_ws) > _GEMM_WS_KEEP:
+            _gemm_ws.popitem(last=False)
     return ws
 
 
