@@ -38,9 +38,10 @@
 namespace svdq {
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = 32 * kWarps;
-constexpr int kBM = 64;              // rows per CTA (16 per warp)
+// Warps per CTA, each owning 16 rows: 8 (128 rows) with eight or more low-rank tiles, so each
+// stage's low-rank boxes serve twice the rows; else 4 (64 rows), which keeps more CTAs per SM.
+__host__ __device__ constexpr int cta_warps(int nt) { return nt >= 8 ? 8 : 4; }
+__host__ __device__ constexpr int cta_rows(int nt) { return 16 * cta_warps(nt); }
 constexpr int kBK = 64;              // columns per stage: one 128-byte swizzle row of bf16
 constexpr int kTargetCtasPerSm = 4;
 // x / low-rank ring depth: 4, or 3 with twelve low-rank tiles so that three CTAs still fit an SM.
@@ -50,9 +51,10 @@ __host__ __device__ constexpr int ring_stages(int nt) { return nt >= 12 ? 3 : 4;
 // quarter of the SM's shared memory).
 __host__ __device__ constexpr int max_slice_stages(int nt) { return nt >= 8 ? 16 : 12; }
 // CTAs per SM the launch bound plans registers for.
-__host__ __device__ constexpr int min_ctas(int nt) { return nt >= 8 ? 3 : kTargetCtasPerSm; }
+__host__ __device__ constexpr int min_ctas(int nt) { return nt >= 8 ? 2 : kTargetCtasPerSm; }
 constexpr int kMinSliceStages = 2;
-constexpr uint32_t kXTileBytes = kBM * kBK * 2;   // 8 KB
+// x stage: the CTA's rows x 64 columns of bf16 (8 or 16 KB)
+__host__ __device__ constexpr uint32_t x_tile_bytes(int nt) { return (uint32_t)cta_rows(nt) * kBK * 2; }
 constexpr uint32_t kLrTileBytes = 8 * kBK * 2;    // 1 KB: 8 low-rank rows
 // a16 = q * scale is exact in fp16 while the group scale lies in [2^-17, 65504 / 7]:
 // above it a16 overflows (recorded as kErrA16Range in the device error word),
@@ -152,7 +154,7 @@ struct AqArgs {
 
 template <int STAGES, int NT>
 __host__ __device__ constexpr uint32_t aq_smem_layout_bytes() {
-  return 1024 /*align slack*/ + STAGES * kXTileBytes + STAGES * NT * kLrTileBytes +
+  return 1024 /*align slack*/ + STAGES * x_tile_bytes(NT) + STAGES * NT * kLrTileBytes +
          max_slice_stages(NT) * 32 * 16 /*reciprocal table*/ + 256 /*barriers, counters*/;
 }
 
@@ -167,10 +169,14 @@ __host__ __device__ constexpr uint32_t aq_smem_layout_bytes() {
 // the store of stage c + 1 is issued (bulk wait_group.read 1), in the same
 // single-lane section.
 template <int GS, int STAGES, int NT, bool W4A16, bool PACKED, bool LORA>
-__global__ void __launch_bounds__(kThreads, min_ctas(NT))
+__global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
     act_quant_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_l2,
                      const __grid_constant__ CUtensorMap tm_lora, const __grid_constant__ CUtensorMap tm_a16,
                      const AqArgs a) {
+  constexpr int kWarps = cta_warps(NT);
+  constexpr int kThreads = 32 * kWarps;
+  constexpr int kBM = cta_rows(NT);
+  constexpr uint32_t kXTileBytes = x_tile_bytes(NT);
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t xs = base;
@@ -559,7 +565,7 @@ Geometry geometry(int M, int K_pad, int r_use, int step) {
   gm.nt = pick_nt(r_use);
   gm.nz = gm.nt ? (r_use + 8 * gm.nt - 1) / (8 * gm.nt) : 1;
   const int n_st = K_pad / kBK;
-  const int layers = ((M + kBM - 1) / kBM) * gm.nz;  // CTAs per K slice
+  const int layers = ((M + cta_rows(gm.nt) - 1) / cta_rows(gm.nt)) * gm.nz;  // CTAs per K slice
   const int slots = num_sms() * ctas_per_sm(gm.nt);
   const int max_slice = max_slice_stages(gm.nt);
   int best_slice = max_slice, best_waves = 1 << 30;
@@ -606,8 +612,8 @@ int launch_t(const LaunchSpec& L, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "activation pass: shared memory attribute");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((L.args.M + kBM - 1) / kBM, L.gm.ksplit, L.gm.nz);
-  cfg.blockDim = dim3(kThreads);
+  cfg.gridDim = dim3((L.args.M + cta_rows(NT) - 1) / cta_rows(NT), L.gm.ksplit, L.gm.nz);
+  cfg.blockDim = dim3(32 * cta_warps(NT));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -696,7 +702,8 @@ int build_spec(LaunchSpec& L, const void* x, int64_t ldx, const void* smooth, co
   const int r_use = want_mid ? r_tot : 0;
   L.gm = geometry(M, K_pad, r_use, G == 128 ? 2 : 1);
   int st;
-  if ((st = make_tma_2d(&L.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K_in, M, (uint64_t)ldx * 2, kBK, kBM,
+  if ((st = make_tma_2d(&L.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K_in, M, (uint64_t)ldx * 2, kBK,
+                        cta_rows(L.gm.nt),
                         CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
   L.tm_l2 = L.tm_x;
