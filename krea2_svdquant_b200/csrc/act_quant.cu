@@ -10,10 +10,11 @@
 // W4A16 mode: a16 = fp16(fp32(x) / fp32(smooth)) (the reference's fp32 run of
 // svd.py:122) and mid from that fp16 x_hat against l2 given in fp16.
 //
-// Work decomposition.  A CTA owns 64 rows x one K slice (a whole number of
-// 64-column stages) x up to 64 low-rank columns; each of its 4 warps owns 16
-// rows.  TMA brings each stage's x tile (64 x 64) and low-rank rows (8-row
-// boxes) into a ring of shared-memory stages with 128-byte swizzle.  A warp
+// Work decomposition.  A CTA owns 64 rows (4 warps) or, with 64 or more
+// low-rank columns, 128 rows (8 warps) x one K slice (a whole number of
+// 64-column stages) x up to 96 low-rank columns; each warp owns 16 rows.  TMA
+// brings each stage's x tile (rows x 64) and low-rank rows (8-row boxes) into
+// a ring of shared-memory stages with 128-byte swizzle.  A warp
 // loads its 16 x 64 x tile straight into mma.sync A-fragment registers with
 // ldmatrix and does all per-element work on those registers: the LoRA
 // down-projection MMAs on raw x, the division and group quantization, the
