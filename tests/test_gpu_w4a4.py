@@ -260,6 +260,27 @@ def test_w4a4_linear_lora_golden(golden):
     assert e16 <= TOL_BF16, e16
 
 
+def test_w4a4_linear_split_tail_block_shape_with_lora():
+    """A block-shaped layer (M 4352, N 1536, so 102 tiles on 74 CTA pairs) whose last wave the GEMM
+    splits along K, through the module with a LoRA adapter, against the staged oracle."""
+    import ctypes
+
+    from krea2_svdquant_b200 import _lib
+    from krea2_svdquant_b200.quant import random_state
+    m, k, n = 4352, 1024, 1536
+    g = torch.Generator(device="cuda").manual_seed(21)
+    st = random_state(n, k, 32, 64, device="cuda", generator=g)
+    x = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    loras = [((torch.randn(16, k, device="cuda", generator=g) * 0.05).bfloat16(),
+              (torch.randn(n, 16, device="cuda", generator=g) * 0.05).bfloat16(), 0.8, 16.0)]
+    sched = (ctypes.c_int * 4)()
+    _lib.call("svdq_linear_gemm_schedule", m, n, k, 128, 1, sched)  # rank 32 + LoRA 16 -> R2 = 128
+    assert sched[3] > 0, "this shape must take the split tail"
+    e32, e16 = _linear_vs_oracle(st, x, loras)
+    assert e32 <= TOL_FP32, e32
+    assert e16 <= TOL_BF16, e16
+
+
 @pytest.mark.parametrize("m,k,n,r,grp,bias", [
     (256, 1024, 2048, 32, 64, True),    # BASELINE config 1
     (200, 1024, 520, 32, 64, True),     # ragged M and N (N % 256 != 0)
