@@ -33,6 +33,7 @@
 // whose quotient stays below 2^126; rint(x_hat / scale) and the /7 of the scale
 // agree for all bf16 inputs with a normal scale (the scale is >= 1.4e-9).
 #include <algorithm>
+#include <atomic>
 
 #include "svdq_common.cuh"
 
@@ -532,12 +533,13 @@ int pick_nt(int r_use) {
 // CTAs of the activation pass that fit on one SM, from its shared memory (registers never
 // bind: the launch bound plans them for min_ctas(nt) CTAs, which the shared memory also allows).
 int ctas_per_sm(int nt) {
-  static int cache[64][5] = {};
+  static std::atomic<int> cache[64][5];  // per device and width; concurrent fillers agree
   int dev = 0;
   cudaGetDevice(&dev);
   const int slot = nt == 0 ? 0 : nt == 2 ? 1 : nt == 4 ? 2 : nt == 8 ? 3 : 4;
   if (dev < 0 || dev >= 64) dev = 0;
-  if (cache[dev][slot] == 0) {
+  int c = cache[dev][slot].load(std::memory_order_relaxed);
+  if (c == 0) {
     const uint32_t smem = slot == 0   ? aq_smem_layout_bytes<ring_stages(0), 0>()
                           : slot == 1 ? aq_smem_layout_bytes<ring_stages(2), 2>()
                           : slot == 2 ? aq_smem_layout_bytes<ring_stages(4), 4>()
@@ -552,9 +554,10 @@ int ctas_per_sm(int nt) {
       reserved = 1024;
     (void)cudaGetLastError();
     const int n = per_sm / (int)(smem + (uint32_t)reserved);
-    cache[dev][slot] = std::max(1, std::min(kTargetCtasPerSm, n));
+    c = std::max(1, std::min(kTargetCtasPerSm, n));
+    cache[dev][slot].store(c, std::memory_order_relaxed);
   }
-  return cache[dev][slot];
+  return c;
 }
 
 // K slices per row band: as many as one wave of CTAs holds (ctas_per_sm per SM), each slice a

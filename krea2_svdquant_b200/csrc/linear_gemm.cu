@@ -42,6 +42,7 @@
 // Flags carry a generation number kept in the workspace and advanced by the
 // last CTA of each launch, so flags of an earlier or aborted launch never match.
 #include <algorithm>
+#include <atomic>
 
 #include "svdq_common.cuh"
 
@@ -551,12 +552,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // Pairs of this kernel that can be resident at once on the current device.  The
 // split tail's owners wait for other pairs, so its grid never exceeds this.
 int max_resident_pairs(const void* kern) {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];  // per device; concurrent fillers store the same value
   int dev = 0;
   cudaGetDevice(&dev);
   const int fallback = num_sms() / 2;
   if (dev < 0 || dev >= 64) return fallback;
-  if (cache[dev] == 0) {
+  int c = cache[dev].load(std::memory_order_relaxed);
+  if (c == 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * fallback, 1, 1);
     cfg.blockDim = dim3(NUM_THREADS, 1, 1);
@@ -573,9 +575,10 @@ int max_resident_pairs(const void* kern) {
       (void)cudaGetLastError();
       n = fallback;
     }
-    cache[dev] = n < fallback ? n : fallback;
+    c = n < fallback ? n : fallback;
+    cache[dev].store(c, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return c;
 }
 
 struct Schedule {

@@ -1,5 +1,6 @@
 // Host runtime pieces shared by all entry points: error strings, the device
 // error word, tensor-map encoding through the driver entry point, SM count.
+#include <atomic>
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -12,15 +13,18 @@ namespace svdq {
 static __device__ int g_device_error = 0;
 
 int* device_error_word() {
-  static int* cache[64] = {nullptr};
+  // per-device caches: every thread that fills an entry stores the same value
+  static std::atomic<int*> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!cache[dev]) {
+  int* c = cache[dev].load(std::memory_order_relaxed);
+  if (!c) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
-    cache[dev] = static_cast<int*>(p);
+    c = static_cast<int*>(p);
+    cache[dev].store(c, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return c;
 }
 
 static thread_local std::string t_last_error;
@@ -69,16 +73,18 @@ int make_tma_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, u
 }
 
 int num_sms() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
+  int c = cache[dev].load(std::memory_order_relaxed);
+  if (c == 0) {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev] = n > 0 ? n : 148;
+    c = n > 0 ? n : 148;
+    cache[dev].store(c, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return c;
 }
 
 }  // namespace svdq
