@@ -207,16 +207,16 @@ def _gemm_workspace(dev: torch.device) -> Optional[Tensor]:
 
     Launches on one stream run in order, so a stream's launches share its workspace; each
     launch leaves it ready for the next (the sync words are never re-zeroed).  Inside a CUDA
-    graph capture no workspace is created (the launch runs unsplit), so a graph never owns
-    or re-zeroes one."""
+    graph capture no workspace is used at all (the launch runs unsplit): a captured graph would
+    keep the workspace's address after this cache had evicted and freed it."""
+    if torch.cuda.is_current_stream_capturing():
+        return None
     key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
     with _gemm_ws_lock:
         ws = _gemm_ws.get(key)
         if ws is not None:
             _gemm_ws.move_to_end(key)
             return ws
-        if torch.cuda.is_current_stream_capturing():
-            return None
         n = int(_lib.lib().svdq_linear_gemm_workspace_bytes())
         ws = torch.zeros((n,), dtype=torch.uint8, device=dev)
         _gemm_ws[key] = ws

@@ -153,13 +153,16 @@ def test_module_path_uses_split_tail_and_matches_oracle_tolerance():
     ref = _reference(a16, w16, mid, up, bias)
     torch.cuda.synchronize()
     assert ((y.double() - ref).norm() / ref.norm()).item() < 1e-5
-    # under graph capture no workspace is created: the captured launch runs unsplit
+    # under graph capture no workspace is used, even one the stream already has: the captured
+    # launch runs unsplit
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
+        y_eager = ops.linear_gemm(a16, w16, mid, up, bias, True)  # creates the stream's workspace
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             yg = ops.linear_gemm(a16, w16, mid, up, bias, True)
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(yg, _gemm(a16, w16, mid, up, bias, True))
+    assert torch.equal(y_eager, y)
