@@ -149,7 +149,9 @@ class SVDQuantLinear(nn.Module):
         bufs = [self.smooth_scale, self.qweight, self.weight_scales, self.l1, self.l2, self.bias]
         for a in self.lora_adapters:
             bufs += [a.down_weight, a.up_weight]
-        return (device,) + tuple((None if b is None else (b.data_ptr(), b.device)) for b in bufs) + tuple(
+        # the version counter changes on every in-place write (load_state_dict copies into the
+        # existing buffers), so updated weights are re-derived rather than served stale
+        return (device,) + tuple((None if b is None else (b.data_ptr(), b.device, b._version)) for b in bufs) + tuple(
             a.multiplier for a in self.lora_adapters)
 
     def prepare(self, device: torch.device | str | None = None) -> PreparedOperands:

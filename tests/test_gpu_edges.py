@@ -142,6 +142,21 @@ def test_w4a16_padding_and_lora():
     assert O.rel_fro(y.float().cpu().numpy(), ref) <= TOL_FP32
 
 
+def test_in_place_weight_update_is_not_served_stale():
+    """load_state_dict copies into the existing buffers: the next forward must use the new weights."""
+    x, st = _state(64, 256, 128, seed=11)
+    _, st2 = _state(64, 256, 128, seed=12)
+    mod = _mod(st)
+    y_old = mod(x)
+    fresh = _mod(st2)
+    y_new = fresh(x)
+    mod.load_state_dict(fresh.state_dict())
+    y_after = mod(x)
+    torch.cuda.synchronize()
+    assert not torch.equal(y_old, y_new)
+    assert torch.equal(y_after, y_new)
+
+
 def test_invalid_arguments_raise():
     from krea2_svdquant_b200 import ops
     from krea2_svdquant_b200._lib import SVDQError
