@@ -17,7 +17,7 @@ class BackendKind(str, Enum):
     TRITON_BLACKWELL = "triton_blackwell"
     GLUON_BLACKWELL = "gluon_blackwell"
     B200 = "b200"              # W4A4: dynamic INT4 activations, tcgen05 GEMM, fused low-rank/LoRA
-    B200_W4A16 = "b200_w4a16"  # W4A16: bf16 activations, in-kernel INT4 weight dequant
+    B200_W4A16 = "b200_w4a16"  # W4A16: smoothed fp16 activations x the INT4 weight's exact fp16 values
 
 
 B200_BACKENDS = (BackendKind.B200, BackendKind.B200_W4A16)

@@ -1,7 +1,7 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
 Run in a container where the reference project is importable (its ``src``
-directory on ``sys.path``; default location given by ``--ref``).  The script
+directory on ``sys.path``: ``--ref`` or the ``KREA2_REF_SRC`` environment variable).  The script
 imports the reference's own functions and records their inputs and outputs:
 
 * ``quantize_symmetric_int4`` / ``pack_int4`` / ``unpack_int4``
@@ -64,7 +64,8 @@ def baseline_inputs(m, k, n, rank, group, *, seed, bias=True, scale_dtype=torch.
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("KREA2_REF_SRC", "/root/reference/src"))
+    ap.add_argument("--ref", default=os.environ.get("KREA2_REF_SRC"), required="KREA2_REF_SRC" not in os.environ,
+                    help="the reference checkout's src directory (or set KREA2_REF_SRC)")
     ap.add_argument("--only", default=None, help="write only this fixture (file stem)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)

@@ -22,16 +22,46 @@ def test_traffic_comes_from_committed_profile():
     assert bench._ncu_traffic("no_such_kernel") is None
 
 
-def test_cpu_baseline_times_both_dtypes(monkeypatch):
+@pytest.mark.parametrize("use_ref", [False, True])
+def test_cpu_baseline_times_both_dtypes(monkeypatch, use_ref):
     import bench
     from krea2_svdquant_b200.quant import make_synthetic_state
+    if use_ref and bench.reference_linear_fn() is None:
+        pytest.skip("the reference is not installed in baseline/_ref")
+    if not use_ref:
+        monkeypatch.setattr(bench, "reference_linear_fn", lambda: None)
     m, k, n = 32, 128, 64
     monkeypatch.setattr(bench, "K", k)
     monkeypatch.setattr(bench, "OPS", 2 * m * n * k)
     x, st = make_synthetic_state(m, k, n, 8, 64, seed=0, device="cpu")
-    tops, cores, sample = bench.cpu_reference_tops(2, 1, x, st, budget_s=0.05)
+    tops, cores, sample, kind = bench.cpu_reference_tops(2, 1, x, st, budget_s=0.05)
     assert tops > 0 and cores >= 1
     assert "bf16" in sample and "fp32" in sample and "value = " in sample
+    assert kind == ("reference" if use_ref else "port")
+
+
+def test_reference_install_matches_port():
+    """The reference's own svdquant_linear_sim (baseline/_ref) and the oracle's torch restatement
+    that stands in for it give the same bf16 result on a small case."""
+    import bench
+    import torch
+    from krea2_svdquant_b200.quant import make_synthetic_state
+    from oracle.svdq_oracle import svdquant_linear_sim_torch
+    ref = bench.reference_linear_fn()
+    if ref is None:
+        pytest.skip("the reference is not installed in baseline/_ref")
+    sim, make_state = ref
+    x, st = make_synthetic_state(32, 128, 64, 8, 64, seed=0, device="cpu")
+    want = sim(x, make_state(st))
+    got = svdquant_linear_sim_torch(x, st.smooth_scale, st.qweight, st.weight_scales, st.l1, st.l2, st.bias,
+                                    group=64, k_in=128, k_pad=128)
+    assert torch.equal(got, want)
+
+
+def test_both_arms_share_config():
+    import bench
+    assert bench.bench_config(2) == bench.bench_config(2)
+    assert {"workload", "M", "K", "N", "rank", "group", "l2", "parallelism"} <= set(bench.bench_config(1))
 
 
 def test_clock_summary_ignores_idle_samples():

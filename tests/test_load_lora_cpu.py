@@ -14,7 +14,7 @@ from torch import nn
 
 from krea2_svdquant_b200.linear import SVDQuantLinear
 from krea2_svdquant_b200.load import load_svdquant_transformer, save_svdquant_checkpoint
-from krea2_svdquant_b200.lora import load_svdquant_lora_adapters, module_matches, split_lora_pairs
+from krea2_svdquant_b200.lora import ModuleIndex, addresses, load_svdquant_lora_adapters, parse_lora_keys
 from krea2_svdquant_b200.quant import SVDQuantLinearState, make_synthetic_state
 from krea2_svdquant_b200.replace import get_parent_module, iter_named_linears, replace_module
 
@@ -106,12 +106,32 @@ def test_lora_shape_checks():
 
 
 def test_key_matching_helpers():
-    assert module_matches("base_model.model.transformer_blocks.3.ff.up", "transformer_blocks.3.ff.up")
-    assert module_matches("lora_unet_transformer_blocks_3_ff_up", "transformer_blocks.3.ff.up")
-    assert not module_matches("transformer_blocks.13.ff.up", "transformer_blocks.3.ff.up")
-    pairs = split_lora_pairs({"a.lora_linear_layer.down.weight": torch.zeros(1), "a.lora_linear_layer.up.weight":
-                              torch.zeros(1), "a.network_alpha": torch.tensor(2.0)})
-    assert set(pairs["a"]) == {"down", "up", "alpha"} and pairs["a"]["alpha"] == 2.0
+    assert addresses("base_model.model.transformer_blocks.3.ff.up", "transformer_blocks.3.ff.up")
+    assert addresses("lora_unet_transformer_blocks_3_ff_up", "transformer_blocks.3.ff.up")
+    assert not addresses("transformer_blocks.13.ff.up", "transformer_blocks.3.ff.up")
+    entries = parse_lora_keys({"a.lora_linear_layer.down.weight": torch.zeros(1), "a.lora_linear_layer.up.weight":
+                               torch.zeros(1), "a.network_alpha": torch.tensor(2.0),
+                               "b.lora.down.weight": torch.zeros(1), "b.alpha": torch.zeros(2)})
+    assert set(entries) == {"a", "b"}  # longest suffix wins: "b.lora.down.weight" is path "b"
+    assert entries["a"].complete and entries["a"].alpha == 2.0
+    assert not entries["b"].complete and entries["b"].alpha is None  # a non-scalar alpha is ignored
+
+
+def test_module_index_resolves_like_a_scan():
+    """The index lookup over "_"-boundary suffixes finds exactly the modules a scan of every
+    module with the matching rule would find."""
+    model = nn.Module()
+    model.transformer_blocks = nn.ModuleList()
+    for _ in range(12):
+        blk = nn.Module()
+        blk.attn = nn.Module()
+        blk.attn.to_q = _svdq_linear()
+        model.transformer_blocks.append(blk)
+    idx = ModuleIndex.of(model)
+    for path in ["transformer.transformer_blocks.1.attn.to_q", "lora_unet_transformer_blocks_11_attn_to_q",
+                 "transformer_blocks.1.attn.to_k", "blocks.1.attn.to_q", "base_model.model.transformer_blocks.10.attn.to_q"]:
+        scan = sorted(n for n in idx.modules if addresses(path, n))
+        assert idx.resolve(path) == scan, path
 
 
 class _DenseToy(nn.Module):
