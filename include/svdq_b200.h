@@ -92,9 +92,13 @@ size_t svdq_act_quant_workspace_bytes(int M, int K_pad, int rank, int lora_rank)
  *   F.linear(x_hat, l2)                                 (svd.py:159, low-rank down)
  *   F.linear(x, lora_down) * multiplier                 (src/krea2_svdquant/runtime/linear.py:38-45)
  * in one pass over x.  Codes, packing and scales are bit-exact with the
- * reference.  a16 = q * scale is exact while every group scale lies in
+ * reference for every finite input: x / smooth and x_hat / scale follow IEEE
+ * division (a fast correctly rounded quotient where it is proven equal, IEEE
+ * division for tiny x, huge quotients and non-normal smoothing factors).
+ * a16 = q * scale is exact while every group scale lies in
  * [2^-17, 65504/7] (group max |x_hat| up to ~65000); larger scales overflow
- * fp16 and are reported through svdq_device_error (code 0x4200).  Optional outputs may be NULL: out_packed / out_scales (the
+ * fp16 and are reported through svdq_device_error (code 0x4200).  Optional
+ * outputs may be NULL: out_packed / out_scales (the
  * reference-format codes), out_a16 (the GEMM operand), out_mid_hl (needs
  * rank + lora_rank > 0 and a workspace of svdq_act_quant_workspace_bytes()).
  * out_packed and out_scales are written together (both NULL or both set).
@@ -120,10 +124,12 @@ int svdq_act_quant(const void* x, int64_t ldx, const void* smooth,
  * svdq_act_quant_noalloc_scratch_bytes() (8 MiB) per device; a call needing
  * more (svdq_act_quant_workspace_bytes() > 8 MiB) returns
  * SVDQ_ERR_UNSUPPORTED.  The scratch address is looked up with
- * cudaGetSymbolAddress on the first call on each device: if that first call
- * would fall inside a stream capture, make one call before capturing.  All
- * calls on a device share the scratch: calls that overlap in time race and
- * must be serialized by the caller.  Arguments and results otherwise as
+ * cudaGetSymbolAddress on the first call in each CUDA context (the device's
+ * primary context or another context the host made current), whatever that
+ * call's arguments: if that first call would fall inside a stream capture,
+ * make one call of any shape before capturing.  All calls on a device share
+ * the scratch: calls that overlap in time race and must be serialized by the
+ * caller.  Arguments and results otherwise as
  * svdq_act_quant.
  */
 size_t svdq_act_quant_noalloc_scratch_bytes(void);

@@ -103,3 +103,20 @@ def device_error(clear: bool = True) -> int:
     code = c_int(0)
     check(lib().svdq_device_error(ctypes.byref(code), 1 if clear else 0))
     return code.value
+
+
+class DeviceWaitError(RuntimeError):
+    """A bounded in-kernel wait ran out: the results of the launches since the last check are
+    incomplete.  ``code`` is the device error word (see ``svdq_device_error`` in the header)."""
+
+    def __init__(self, code: int, where: str):
+        super().__init__(f"device-side wait error 0x{code:x} ({where}): the outputs of the kernels since the "
+                         "last check are incomplete")
+        self.code = code
+
+
+def raise_on_device_error(where: str) -> None:
+    """Synchronize, read and clear the device error word; raise :class:`DeviceWaitError` if set."""
+    code = device_error(clear=True)
+    if code:
+        raise DeviceWaitError(code, where)

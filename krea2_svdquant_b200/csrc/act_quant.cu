@@ -32,6 +32,11 @@
 // for every finite x with |x| >= 2^-118 or x == 0 and every normal smooth
 // whose quotient stays below 2^126; rint(x_hat / scale) and the /7 of the scale
 // agree for all bf16 inputs with a normal scale (the scale is >= 1.4e-9).
+// Outside that domain the kernel divides with IEEE division (__fdiv_rn): a warp
+// redoes a whole stage that way when one of its elements has 0 < |x| < 2^-118
+// or a quotient that is inf, NaN or (bf16) >= 2^126, and a CTA whose slice has
+// a zero, subnormal or non-finite smoothing factor does so for every stage.  So
+// x_hat (and fp16(x / s) in W4A16 mode) equals IEEE division for every input.
 #include <algorithm>
 #include <atomic>
 
@@ -113,6 +118,20 @@ __device__ __forceinline__ uint64_t div_f2(uint64_t a, uint64_t y, uint64_t nb) 
   const uint64_t q0 = f2_mul(a, y);
   const uint64_t r = f2_fma(q0, nb, a);
   return f2_fma(r, y, q0);
+}
+// Elements where the Markstein quotient above may differ from IEEE division, as bits 15 / 31 of
+// the result (other bits are don't-care): x with 0 < |x| < 2^-118 (the residual r loses bits
+// below fp32's normal range), or a result that is inf / NaN or, in bf16, at least 2^126 (the
+// product a * y can overflow).  xv: the bf16x2 input; out: the bf16x2 (or f16x2) quotient.
+// Each 16-bit half is tested with one add: h + c sets bit 15 iff h >= 0x8000 - c, and no half
+// carries into the next (h <= 0x7FFF).
+template <bool F16OUT>
+__device__ __forceinline__ uint32_t outside_fast_division(uint32_t xv, uint32_t out) {
+  const uint32_t t = xv & 0x7FFF7FFFu;
+  const uint32_t nonzero = t + 0x7FFF7FFFu;       // bit 15: |x| bits >= 0x0001
+  const uint32_t not_tiny = t + 0x7B807B80u;      // bit 15: |x| bits >= 0x0480 (2^-118)
+  const uint32_t big = (out & 0x7FFF7FFFu) + (F16OUT ? 0x04000400u : 0x01800180u);  // f16 >= inf; bf16 >= 2^126
+  return (nonzero & ~not_tiny) | big;
 }
 // running max of |.| over bf16x2 lanes (the sign bit of the result is meaningless)
 __device__ __forceinline__ uint32_t bf2_maxabs(uint32_t m, uint32_t v) {
@@ -230,7 +249,9 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
   pdl_wait();  // inputs may come from the previous kernel on the stream
   if (tid == 0)
     for (int s = 0; s < STAGES && s < n_loc; ++s) issue(s, s);
-  // reciprocal table of the slice: {RN(1/s_c), RN(1/s_c+1), -s_c, -s_c+1} per column pair
+  // reciprocal table of the slice: {RN(1/s_c), RN(1/s_c+1), -s_c, -s_c+1} per column pair.  A slice
+  // with a smoothing factor outside the normal range divides with IEEE division throughout.
+  bool slice_ieee;
   {
     // every load first (one round trip for the whole table), then the reciprocals
     constexpr int kTblIters = max_slice_stages(NT) * (kBK / 2) / kThreads;
@@ -245,14 +266,21 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
       sv[u][0] = live && col < a.K_in ? __bfloat162float(a.smooth[col]) : 1.f;
       sv[u][1] = live && col + 1 < a.K_in ? __bfloat162float(a.smooth[col + 1]) : 1.f;
     }
+    int odd_smooth = 0;  // a smoothing factor outside the normal range (zero, subnormal, inf, NaN)
 #pragma unroll
     for (int u = 0; u < kTblIters; ++u) {
       const int i = tid + u * kThreads;
-      if (i < n_loc * (kBK / 2))
+      if (i < n_loc * (kBK / 2)) {
         tbl[i] = make_float4(__frcp_rn(sv[u][0]), __frcp_rn(sv[u][1]), -sv[u][0], -sv[u][1]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float m = fabsf(sv[u][h]);
+          odd_smooth |= !(m >= 1.17549435e-38f && m <= 3.40282347e38f);
+        }
+      }
     }
+    slice_ieee = __syncthreads_or(odd_smooth) != 0;
   }
-  __syncthreads();
 
   float acc[NT > 0 ? NT : 1][4];
 #pragma unroll
@@ -347,6 +375,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
       for (int kk = 0; kk < 4; ++kk) ldmatrix_x4(xs + s * kXTileBytes + swz128(a_row, 2 * kk + a_chk), fr[j][kk]);
       if constexpr (LORA) lowrank_mma(fr[j], s, true);  // LoRA down-projection on raw x
       const float4* tb = rst_p + c * (kBK / 2) + t4;
+      uint32_t off_domain = 0;  // bit 15 / 31 set: some element of this stage needs IEEE division
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const float4 cA = tb[8 * kk], cB = tb[8 * kk + 4];
@@ -355,10 +384,31 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
         // fragment regs: 0 = (row g, cols A), 1 = (row g+8, cols A), 2 = (row g, cols B), 3 = (row g+8, cols B)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint64_t q = div_f2(bf2_to_f2(fr[j][kk][i]), i < 2 ? yA : yB, i < 2 ? nA : nB);
+          const uint32_t xv = fr[j][kk][i];
+          const uint64_t q = div_f2(bf2_to_f2(xv), i < 2 ? yA : yB, i < 2 ? nA : nB);
           fr[j][kk][i] = W4A16 ? f2_to_h2(q) : f2_to_bf2(q);
+          off_domain |= outside_fast_division<W4A16>(xv, fr[j][kk][i]);
         }
-        if constexpr (!W4A16) {
+      }
+      if (slice_ieee || __any_sync(0xffffffffu, (off_domain & 0x80008000u) != 0)) {
+        // rare: redo the whole stage with IEEE division (the x tile is still in shared memory)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          uint32_t xr[4];
+          ldmatrix_x4(xs + s * kXTileBytes + swz128(a_row, 2 * kk + a_chk), xr);
+          const float4 cA = tb[8 * kk], cB = tb[8 * kk + 4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float s0 = i < 2 ? -cA.z : -cB.z, s1 = i < 2 ? -cA.w : -cB.w;
+            const uint64_t q = f2_pack(__fdiv_rn(__uint_as_float(xr[i] << 16), s0),
+                                       __fdiv_rn(__uint_as_float(xr[i] & 0xFFFF0000u), s1));
+            fr[j][kk][i] = W4A16 ? f2_to_h2(q) : f2_to_bf2(q);
+          }
+        }
+      }
+      if constexpr (!W4A16) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
           mxk[j][kk][0] = bf2_maxabs(fr[j][kk][0], fr[j][kk][2]);
           mxk[j][kk][1] = bf2_maxabs(fr[j][kk][1], fr[j][kk][3]);
         }

@@ -6,18 +6,18 @@
 // to another framework, or a serving loop that forbids allocation after
 // warm-up so that no request can block on a synchronizing allocation or fail
 // on fragmentation.  The call allocates nothing: no cudaMalloc / cudaFree and
-// no other allocating routine.  The scratch address is looked up once per
-// device with cudaGetSymbolAddress on the first call on that device; when that
-// first call would otherwise fall inside a stream capture, make one call
-// before capturing.  The scratch holds kNoAllocScratchBytes; a call that needs
-// more is rejected with SVDQ_ERR_UNSUPPORTED and names the size it needs.
+// no other allocating routine.  The scratch address is looked up with
+// cudaGetSymbolAddress on the first call in each CUDA context (the device's
+// primary context, or any other context the host made current), whatever
+// that call's shape; when that first call would otherwise fall inside a
+// stream capture, make one call of any shape before capturing.  The scratch
+// holds kNoAllocScratchBytes; a call that needs more is rejected with
+// SVDQ_ERR_UNSUPPORTED and names the size it needs.
 // Nothing in the scratch has to start at zero: every K slice writes all of its
 // partial sums before the finalize launch reads them.  All calls on one device
 // share the one scratch array, so calls that overlap in time (on different
 // streams, or from different host threads) race on it and must be serialized
 // by the caller.
-#include <mutex>
-
 #include "svdq_common.cuh"
 
 extern "C" size_t svdq_act_quant_workspace_bytes(int M, int K_pad, int rank, int lora_rank);
@@ -33,25 +33,11 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mutex;
-void* g_scratch_ptr[kMaxDevices] = {nullptr};
-
-// Device address of the scratch array on the current device (looked up once per device).
+// Device address of the scratch array in the current context.  The first call in a context looks
+// it up with cudaGetSymbolAddress (with that context's device current); later calls reuse it.
 int noalloc_scratch(void** out) {
-  int dev = 0;
-  int st = check_cuda(cudaGetDevice(&dev), "svdq_act_quant_noalloc: current device");
-  if (st) return st;
-  if (dev < 0 || dev >= kMaxDevices) return set_error(SVDQ_ERR_UNSUPPORTED, "svdq_act_quant_noalloc: device ordinal");
-  std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    st = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "svdq_act_quant_noalloc: scratch address");
-    if (st) return st;
-    g_scratch_ptr[dev] = p;
-  }
-  *out = g_scratch_ptr[dev];
-  return SVDQ_OK;
+  return symbol_address(reinterpret_cast<const void*>(&g_noalloc_scratch), out,
+                        "svdq_act_quant_noalloc: scratch address");
 }
 
 }  // namespace
@@ -72,11 +58,11 @@ extern "C" int svdq_act_quant_noalloc(const void* x, int64_t ldx, const void* sm
                                                " bytes of scratch but the static scratch holds " +
                                                std::to_string(kNoAllocScratchBytes) +
                                                " bytes; use svdq_act_quant with a caller-provided workspace");
+  // looked up on every call, whether or not this call uses the scratch, so the one-time set-up of a
+  // context happens on its first call of any shape
   void* scratch = nullptr;
-  if (need > 0) {
-    const int st = noalloc_scratch(&scratch);
-    if (st) return st;
-  }
+  const int st = noalloc_scratch(&scratch);
+  if (st) return st;
   return svdq_act_quant(x, ldx, smooth, l2, rank, lora_down, lora_col_scale, lora_rank, M, K_in, K_pad, a_group,
-                        out_packed, out_scales, out_a16, out_mid_hl, R2, scratch, need, stream);
+                        out_packed, out_scales, out_a16, out_mid_hl, R2, need > 0 ? scratch : nullptr, need, stream);
 }

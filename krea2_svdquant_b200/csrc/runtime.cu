@@ -12,19 +12,69 @@ namespace svdq {
 
 static __device__ int g_device_error = 0;
 
-int* device_error_word() {
-  // per-device caches: every thread that fills an entry stores the same value
-  static std::atomic<int*> cache[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  int* c = cache[dev].load(std::memory_order_relaxed);
+namespace {
+using PFN_ctx_get = CUresult (*)(CUcontext*);
+PFN_ctx_get g_ctx_get = nullptr;
+std::once_flag g_ctx_once;
+
+// Symbol addresses cached per CUDA context: a device's primary context and any other context an
+// FFI host makes current hold separate module instances, so the address of one is not valid in another.
+struct CtxAddr {
+  CUcontext ctx;
+  const void* symbol;
+  void* addr;
+};
+constexpr int kMaxCtxAddrs = 256;
+CtxAddr g_ctx_addrs[kMaxCtxAddrs];
+int g_ctx_addr_count = 0;
+std::mutex g_ctx_addr_mutex;
+}  // namespace
+
+int current_context(CUcontext* out) {
+  std::call_once(g_ctx_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_get = reinterpret_cast<PFN_ctx_get>(fn);
+  });
+  if (!g_ctx_get) return set_error(SVDQ_ERR_CUDA, "cuCtxGetCurrent entry point not found");
+  CUcontext c = nullptr;
+  if (g_ctx_get(&c) != CUDA_SUCCESS) return set_error(SVDQ_ERR_CUDA, "cuCtxGetCurrent failed");
   if (!c) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
-    c = static_cast<int*>(p);
-    cache[dev].store(c, std::memory_order_relaxed);
+    // nothing current yet on this thread: cudaSetDevice makes the device's primary context current
+    int dev = 0;
+    int st = check_cuda(cudaGetDevice(&dev), "current device");
+    if (!st) st = check_cuda(cudaSetDevice(dev), "binding the current device's primary context");
+    if (st) return st;
+    if (g_ctx_get(&c) != CUDA_SUCCESS || !c) return set_error(SVDQ_ERR_CUDA, "no current CUDA context");
   }
-  return c;
+  *out = c;
+  return SVDQ_OK;
+}
+
+int symbol_address(const void* symbol, void** out, const char* what) {
+  CUcontext ctx = nullptr;
+  int st = current_context(&ctx);
+  if (st) return st;
+  std::lock_guard<std::mutex> lock(g_ctx_addr_mutex);
+  for (int i = 0; i < g_ctx_addr_count; ++i)
+    if (g_ctx_addrs[i].ctx == ctx && g_ctx_addrs[i].symbol == symbol) {
+      *out = g_ctx_addrs[i].addr;
+      return SVDQ_OK;
+    }
+  void* p = nullptr;
+  st = check_cuda(cudaGetSymbolAddress(&p, symbol), what);
+  if (st) return st;
+  if (g_ctx_addr_count < kMaxCtxAddrs) g_ctx_addrs[g_ctx_addr_count++] = CtxAddr{ctx, symbol, p};
+  *out = p;
+  return SVDQ_OK;
+}
+
+int* device_error_word() {
+  void* p = nullptr;
+  if (symbol_address(reinterpret_cast<const void*>(&g_device_error), &p, "device error word address")) return nullptr;
+  return static_cast<int*>(p);
 }
 
 static thread_local std::string t_last_error;

@@ -34,6 +34,14 @@ int make_tma_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
 // Number of SMs on the current device (cached per device).
 int num_sms();
 
+// The calling thread's current CUDA context (the runtime's primary context of the current
+// device unless the caller made another context current).
+int current_context(CUcontext* out);
+
+// Device address of a file-scope __device__ variable in the current context, looked up with
+// cudaGetSymbolAddress once per (context, symbol) and cached.
+int symbol_address(const void* symbol, void** out, const char* what);
+
 // Device address of this library's error word on the current device: bounded
 // in-kernel waits record there where they gave up (kernels take it as a
 // parameter).  Returns nullptr if the symbol address cannot be obtained.

@@ -25,7 +25,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from . import ops
+from . import _lib, ops
 from .config import BackendKind, resolve_backend
 from .quant import SVDQuantLinearState
 
@@ -91,7 +91,16 @@ def _pad_cols(t: torch.Tensor, cols: int, value: float = 0.0) -> torch.Tensor:
 
 
 class SVDQuantLinear(nn.Module):
-    """Runtime SVDQuant linear on the B200 kernels (see module docstring)."""
+    """Runtime SVDQuant linear on the B200 kernels (see module docstring).
+
+    ``check_device_errors`` (class default False): after every forward, synchronize and raise
+    :class:`~krea2_svdquant_b200._lib.DeviceWaitError` if a bounded in-kernel wait gave up (for
+    example when another stream's long kernels kept a split GEMM's CTA pairs from running
+    together for seconds).  Off by default because it synchronizes; production callers that
+    leave it off should poll ``_lib.raise_on_device_error`` (``svdq_device_error``) once per step.
+    """
+
+    check_device_errors = False
 
     def __init__(self, state: SVDQuantLinearState, backend: BackendKind | str = BackendKind.AUTO,
                  *, act_group_size: int = 64):
@@ -241,6 +250,8 @@ class SVDQuantLinear(nn.Module):
                                            self.act_group_size, True, False)
         y = ops.linear_gemm(a16, p.w16, mid if mid.numel() else None, up_hl if mid.numel() else None,
                             p.bias, out_fp32)
+        if self.check_device_errors:
+            _lib.raise_on_device_error(f"SVDQuantLinear {tuple(self.original_shape)}")
         return y.reshape(*lead, n)
 
     def _forward_base(self, x: torch.Tensor) -> torch.Tensor:

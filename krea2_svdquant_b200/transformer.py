@@ -170,10 +170,12 @@ class Krea2StandInTransformer(nn.Module):
     @classmethod
     def random_svdquant(cls, cfg: Krea2StandInConfig, *, rank: int = 32, group: int = 64,
                         backend: BackendKind | str = BackendKind.B200, seed: int = 0,
-                        init_device: str | torch.device = "cpu", keep_on: str | torch.device = "cpu"
-                        ) -> "Krea2StandInTransformer":
+                        init_device: str | torch.device = "cpu", keep_on: str | torch.device = "cpu",
+                        dtype: torch.dtype = torch.bfloat16) -> "Krea2StandInTransformer":
         """Every listed linear a random-init SVDQuant layer (rank ``rank``, group ``group``).
-        States are drawn on ``init_device`` and kept on ``keep_on``."""
+        States are drawn on ``init_device`` and kept on ``keep_on``.  ``dtype`` is the dtype of the
+        glue (embedding, norms, projection) and so of the activations between the linears: the
+        quantized linears take bf16 or fp32 activations and return the same dtype."""
         gen = torch.Generator(device=init_device).manual_seed(seed)
         shapes = cfg.linear_shapes()
 
@@ -185,7 +187,7 @@ class Krea2StandInTransformer(nn.Module):
             return SVDQuantLinear(st, backend=backend)
 
         torch.manual_seed(seed)
-        return cls(cfg, make)
+        return cls(cfg, make, dtype)
 
     def forward(self, latents: torch.Tensor, text: torch.Tensor) -> torch.Tensor:
         """``latents`` [B, image_tokens, in_channels], ``text`` [B, text_tokens, hidden] -> [B, image_tokens,

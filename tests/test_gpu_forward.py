@@ -14,8 +14,9 @@ from tests._helpers import staged_oracle, state_numpy
 pytestmark = pytest.mark.gpu
 
 TOL_LINEAR_BF16 = 2e-3   # in-situ linear (bf16 output) vs bf16(staged fp32 oracle)
-TOL_MODEL = 3e-2         # whole model vs oracle-linear model: both run bf16 glue, so small input
-                         # differences flip activation codes at rounding boundaries downstream
+TOL_BLOCK_FP32 = 1e-3    # fp32-glue block with fp32-output linears vs the same block with oracle linears
+TOL_MODEL = 3e-2         # smoke check only: whole bf16 model vs oracle-linear model; both run bf16
+                         # glue, so small input differences flip activation codes downstream
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -54,6 +55,56 @@ class _OracleLinear(nn.Module):
     def forward(self, x):
         y, _ = staged_oracle(x.reshape(-1, x.shape[-1]).float().cpu().numpy(), self.s)
         return torch.from_numpy(y.astype(np.float32)).to(x.device).to(x.dtype).reshape(*x.shape[:-1], self.n)
+
+
+class _OracleLinearF32(nn.Module):
+    """The staged oracle of one SVDQuant layer on fp32 activations, as the module treats them:
+    the input rounded to bf16 (the activation pass reads bf16), float64 evaluation, fp32 output."""
+
+    def __init__(self, mod):
+        super().__init__()
+        self.s = state_numpy(mod.state)
+        self.n = mod.original_shape[0]
+
+    def forward(self, x):
+        xb = O.bf16_round(x.reshape(-1, x.shape[-1]).float().cpu().numpy())
+        y, _ = staged_oracle(xb, self.s)
+        return torch.from_numpy(y.astype(np.float32)).to(x.device).reshape(*x.shape[:-1], self.n)
+
+
+def _fp32_model(num_layers: int):
+    from krea2_svdquant_b200.transformer import Krea2StandInConfig, Krea2StandInTransformer
+    cfg = Krea2StandInConfig(num_layers=num_layers, hidden=512, heads=4, kv_heads=2, head_dim=128, mlp=1024,
+                             in_channels=64, image_tokens=192, text_tokens=64)
+    model = Krea2StandInTransformer.random_svdquant(cfg, rank=32, group=64, seed=5, dtype=torch.float32).cuda()
+    return cfg, model
+
+
+@pytest.mark.parametrize("num_layers", [1, 2])
+def test_fp32_block_vs_oracle_linears(num_layers):
+    """Krea2 stand-in block(s) with fp32 glue (norms, attention, gates, residuals) and fp32-output
+    SVDQuant linears, against the same block(s) with every linear replaced by the staged float64
+    oracle: relative Frobenius <= 1e-3 on the block output."""
+    from krea2_svdquant_b200.linear import SVDQuantLinear
+    from krea2_svdquant_b200.replace import replace_module
+    cfg, model = _fp32_model(num_layers)
+    g = torch.Generator(device="cuda").manual_seed(12)
+    x = torch.randn(2, cfg.image_tokens + cfg.text_tokens, cfg.hidden, device="cuda", generator=g)
+    with torch.no_grad():
+        got = x
+        for blk in model.transformer_blocks:
+            got = blk(got)
+        assert got.dtype == torch.float32
+        for n in [n for n, m in model.named_modules() if isinstance(m, SVDQuantLinear)]:
+            replace_module(model, n, _OracleLinearF32(model.get_submodule(n)))
+        want = x
+        for blk in model.transformer_blocks:
+            want = blk(want)
+    err = O.rel_fro(got.cpu().numpy(), want.cpu().numpy())
+    # the part of the output the blocks add (the residual stream carries x unchanged)
+    err_delta = O.rel_fro((got - x).cpu().numpy(), (want - x).cpu().numpy())
+    assert err <= TOL_BLOCK_FP32, err
+    assert err_delta <= TOL_BLOCK_FP32, err_delta
 
 
 def test_forward_linears_in_situ():

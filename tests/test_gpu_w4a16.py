@@ -71,6 +71,21 @@ def test_w4a16_prep_division_sweep():
     assert np.array_equal(a16.cpu().numpy(), ref)
 
 
+def test_w4a16_prep_every_finite_bf16():
+    """a16 = fp16(fp32(x) / fp32(s)) for every finite bf16 x, smoothing factors in [2^-6, 2^6]
+    (quotients overflow fp16 and fp32; tiny x take the kernel's IEEE-division path)."""
+    from krea2_svdquant_b200 import ops
+    k = 512
+    xn = bf16_sweep(k, lo_exp=-127, hi_exp=128)
+    rng = np.random.default_rng(9)
+    sn = torch.tensor(2.0 ** rng.uniform(-6, 6, k)).bfloat16().float().numpy()
+    a16, _ = ops.w4a16_prep(bf16_tensor(xn), bf16_tensor(sn), None, None, None, k)
+    torch.cuda.synchronize()
+    with np.errstate(over="ignore"):
+        ref = (xn / sn[None, :]).astype(np.float32).astype(np.float16)
+    assert np.array_equal(a16.cpu().numpy(), ref)
+
+
 @pytest.mark.parametrize("case", LINEAR_CASES)
 def test_w4a16_linear_golden(golden, case):
     g = golden(case)

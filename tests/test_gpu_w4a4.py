@@ -103,6 +103,50 @@ def test_act_quant_division_sweep(ag):
     assert _lib.device_error(clear=True) == 0x4200
 
 
+@pytest.mark.parametrize("ag", [64, 128])
+def test_act_quant_every_finite_bf16(ag):
+    """Every finite bf16 x (subnormals, zeros and values up to the bf16 maximum) divided by
+    smoothing factors in [1, 64]: codes, scales and x_hat equal IEEE division bit for bit.  Tiny x
+    (|x| < 2^-118) and quotients >= 2^126 take the kernel's IEEE-division path."""
+    from krea2_svdquant_b200 import _lib
+    k = 512
+    xn = bf16_sweep(k, lo_exp=-127, hi_exp=128)
+    assert np.isfinite(xn).all() and (xn.view(np.uint32) & 0x7F800000 == 0).sum() > 200  # subnormals present
+    rng = np.random.default_rng(7)
+    sn = torch.tensor(2.0 ** rng.uniform(0, 6, k)).bfloat16().float().numpy()
+    a16, mid, packed, scales = _act(bf16_tensor(xn), bf16_tensor(sn), k_pad=k, a_group=ag)
+    torch.cuda.synchronize()
+    xh, q, pk, sa = O.act_quant(xn, sn, ag)
+    assert np.isfinite(sa).all()
+    assert np.array_equal(packed.cpu().numpy(), pk)
+    assert np.array_equal(scales.float().cpu().numpy(), sa)
+    _lib.device_error(clear=True)  # large groups overflow the fp16 operand (0x4200), checked elsewhere
+
+
+def test_act_quant_x_hat_ieee_with_odd_smoothing():
+    """Smoothing factors that are subnormal or huge: the kernel's x_hat (seen through the W4A16
+    operand, fp16(x / s)) and the W4A4 codes still follow IEEE division."""
+    from krea2_svdquant_b200 import ops
+    k = 256
+    rng = np.random.default_rng(8)
+    sn = torch.tensor(2.0 ** rng.uniform(-6, 6, k)).bfloat16().float().numpy()
+    sn[::7] = (np.arange(1, k // 7 + 2, dtype=np.uint32)[: len(sn[::7])] << 16).view(np.float32)  # bf16 subnormals
+    sn[3::11] = np.float32(2.0 ** 120)
+    xn = torch.tensor(rng.standard_normal((64, k)) * 2.0 ** rng.uniform(-130, -100, (64, k))).bfloat16().float().numpy()
+    xn[:32] = torch.tensor(rng.standard_normal((32, k))).bfloat16().float().numpy()
+    a16, _ = ops.w4a16_prep(bf16_tensor(xn), bf16_tensor(sn), None, None, None, k)
+    torch.cuda.synchronize()
+    with np.errstate(over="ignore", divide="ignore", invalid="ignore"):
+        ref = (xn / sn[None, :]).astype(np.float32).astype(np.float16)
+    assert np.array_equal(a16.cpu().numpy(), ref)
+    keep = np.isfinite(O.smooth_bf16(xn, sn)).all(axis=1)  # rows whose x_hat stays finite
+    _, _, packed, scales = _act(bf16_tensor(xn[keep]), bf16_tensor(sn), k_pad=k)
+    torch.cuda.synchronize()
+    _, _, pk, sa = O.act_quant(xn[keep], sn, 64)
+    assert np.array_equal(packed.cpu().numpy(), pk)
+    assert np.array_equal(scales.float().cpu().numpy(), sa)
+
+
 def test_act_quant_no_range_flag_in_domain():
     from krea2_svdquant_b200 import _lib
     x = (torch.randn(64, 256) * 1000).bfloat16().cuda()
