@@ -14,7 +14,7 @@ from tests._helpers import staged_oracle, state_numpy
 pytestmark = pytest.mark.gpu
 
 TOL_LINEAR_BF16 = 2e-3   # in-situ linear (bf16 output) vs bf16(staged fp32 oracle)
-TOL_BLOCK_FP32 = 1e-3    # fp32-glue block with fp32-output linears vs the same block with oracle linears
+TOL_BLOCK_FP32 = 1e-3    # fp32-glue block with fp32-output linears vs the same block with staged oracle linears
 TOL_MODEL = 3e-2         # smoke check only: whole bf16 model vs oracle-linear model; both run bf16
                          # glue, so small input differences flip activation codes downstream
 
@@ -57,54 +57,78 @@ class _OracleLinear(nn.Module):
         return torch.from_numpy(y.astype(np.float32)).to(x.device).to(x.dtype).reshape(*x.shape[:-1], self.n)
 
 
-class _OracleLinearF32(nn.Module):
-    """The staged oracle of one SVDQuant layer on fp32 activations, as the module treats them:
-    the input rounded to bf16 (the activation pass reads bf16), float64 evaluation, fp32 output."""
+class _StagedOracleLinear(nn.Module):
+    """One SVDQuant layer's float64 oracle, evaluated on the input the KERNEL layer at the same
+    place received (recorded in call order): the staged W4A4 formula (README.md:64) for ``b200``, the
+    reference's fp32 run of svdquant_linear_sim (svd.py:119-163) for ``b200_w4a16``.  The input is
+    rounded to bf16 first, as the module's activation pass reads bf16.  Returns fp32."""
 
-    def __init__(self, mod):
+    def __init__(self, mod, inputs: list, w4a16: bool):
         super().__init__()
         self.s = state_numpy(mod.state)
         self.n = mod.original_shape[0]
+        self.inputs = inputs
+        self.w4a16 = w4a16
 
     def forward(self, x):
-        xb = O.bf16_round(x.reshape(-1, x.shape[-1]).float().cpu().numpy())
-        y, _ = staged_oracle(xb, self.s)
+        xr = self.inputs.pop(0)
+        assert xr.shape == x.shape
+        xb = O.bf16_round(xr.reshape(-1, xr.shape[-1]).float().cpu().numpy())
+        s = self.s
+        if self.w4a16:
+            y = O.w4a16_linear_fp32(xb, s["smooth"], s["qweight"], s["weight_scales"], s["l1"], s["l2"], s["bias"],
+                                    group=s["group"], k_in=s["k_in"], k_pad=s["k_pad"])
+        else:
+            y, _ = staged_oracle(xb, s)
         return torch.from_numpy(y.astype(np.float32)).to(x.device).reshape(*x.shape[:-1], self.n)
 
 
-def _fp32_model(num_layers: int):
+def _fp32_model(num_layers: int, backend: str):
     from krea2_svdquant_b200.transformer import Krea2StandInConfig, Krea2StandInTransformer
     cfg = Krea2StandInConfig(num_layers=num_layers, hidden=512, heads=4, kv_heads=2, head_dim=128, mlp=1024,
                              in_channels=64, image_tokens=192, text_tokens=64)
-    model = Krea2StandInTransformer.random_svdquant(cfg, rank=32, group=64, seed=5, dtype=torch.float32).cuda()
+    model = Krea2StandInTransformer.random_svdquant(cfg, rank=32, group=64, seed=5, dtype=torch.float32,
+                                                    backend=backend).cuda()
     return cfg, model
 
 
-@pytest.mark.parametrize("num_layers", [1, 2])
-def test_fp32_block_vs_oracle_linears(num_layers):
-    """Krea2 stand-in block(s) with fp32 glue (norms, attention, gates, residuals) and fp32-output
-    SVDQuant linears, against the same block(s) with every linear replaced by the staged float64
-    oracle: relative Frobenius <= 1e-3 on the block output."""
+@pytest.mark.parametrize("backend", ["b200", "b200_w4a16"])
+def test_fp32_blocks_vs_staged_oracle(backend):
+    """Three Krea2 stand-in blocks with fp32 glue (norms, attention, gates, residuals) and fp32-output
+    SVDQuant linears.  Each block is compared with the same block whose linears are the float64
+    oracle evaluated on the inputs the kernel linears received (staged, as for a single linear):
+    relative Frobenius <= 1e-3 on every block's output and on the part it adds to the residual
+    stream.  Staging is needed because every linear input passes a quantizer (bf16 rounding, and
+    INT4 codes in W4A4): a free-running oracle chain fed its own 1e-5-level different values flips
+    roundings, each flip worth a whole quantization step (tests/test_oracle_golden.py::
+    test_w4a4_input_sensitivity measures this on the oracle alone)."""
+    import copy
+
     from krea2_svdquant_b200.linear import SVDQuantLinear
     from krea2_svdquant_b200.replace import replace_module
-    cfg, model = _fp32_model(num_layers)
+    cfg, model = _fp32_model(3, backend)
+    names = [n for n, m in model.named_modules() if isinstance(m, SVDQuantLinear)]
+    recorded = {n: [] for n in names}
+    hooks = [model.get_submodule(n).register_forward_hook(
+        lambda mod, args, out, n=n: recorded[n].append(args[0].detach().clone())) for n in names]
+    oracle = copy.deepcopy(model)
+    for n in names:
+        replace_module(oracle, n, _StagedOracleLinear(oracle.get_submodule(n), recorded[n], backend == "b200_w4a16"))
     g = torch.Generator(device="cuda").manual_seed(12)
-    x = torch.randn(2, cfg.image_tokens + cfg.text_tokens, cfg.hidden, device="cuda", generator=g)
+    h = torch.randn(2, cfg.image_tokens + cfg.text_tokens, cfg.hidden, device="cuda", generator=g)
     with torch.no_grad():
-        got = x
-        for blk in model.transformer_blocks:
-            got = blk(got)
-        assert got.dtype == torch.float32
-        for n in [n for n, m in model.named_modules() if isinstance(m, SVDQuantLinear)]:
-            replace_module(model, n, _OracleLinearF32(model.get_submodule(n)))
-        want = x
-        for blk in model.transformer_blocks:
-            want = blk(want)
-    err = O.rel_fro(got.cpu().numpy(), want.cpu().numpy())
-    # the part of the output the blocks add (the residual stream carries x unchanged)
-    err_delta = O.rel_fro((got - x).cpu().numpy(), (want - x).cpu().numpy())
-    assert err <= TOL_BLOCK_FP32, err
-    assert err_delta <= TOL_BLOCK_FP32, err_delta
+        for i, (blk, blk_o) in enumerate(zip(model.transformer_blocks, oracle.transformer_blocks)):
+            got = blk(h)
+            want = blk_o(h)
+            assert got.dtype == torch.float32
+            err = O.rel_fro(got.cpu().numpy(), want.cpu().numpy())
+            err_delta = O.rel_fro((got - h).cpu().numpy(), (want - h).cpu().numpy())
+            assert err <= TOL_BLOCK_FP32, (i, err)
+            assert err_delta <= TOL_BLOCK_FP32, (i, err_delta)
+            h = got
+    for hk in hooks:
+        hk.remove()
+    assert all(not v for v in recorded.values())  # every recorded input was used once
 
 
 def test_forward_linears_in_situ():

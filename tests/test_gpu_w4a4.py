@@ -145,6 +145,8 @@ def test_act_quant_x_hat_ieee_with_odd_smoothing():
     _, _, pk, sa = O.act_quant(xn[keep], sn, 64)
     assert np.array_equal(packed.cpu().numpy(), pk)
     assert np.array_equal(scales.float().cpu().numpy(), sa)
+    from krea2_svdquant_b200 import _lib
+    _lib.device_error(clear=True)  # scales above 65504/7 overflow the fp16 operand (0x4200), checked elsewhere
 
 
 def test_act_quant_no_range_flag_in_domain():
