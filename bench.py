@@ -368,6 +368,62 @@ def measure_w4a16_lora(dev, flush, iters: int) -> dict:
             "lowrank_lora_ops": lowrank}
 
 
+def measure_small_batch(dev, flush, iters: int) -> dict:
+    """The config-2/4 layer (K6144 N16384, rank 32, group 64, bias) at small batches, where the
+    weight bytes bound the GEMM: the packed-weight GEMM (half-byte codes + fp16 scales converted in
+    shared memory) against the fp16-weight GEMM on the same activation operand, each against its
+    roofline max(bytes / HBM peak, 2MNK / bf16 peak).  Kernel times with the L2 flushed."""
+    import torch
+
+    from krea2_svdquant_b200 import ops
+    from krea2_svdquant_b200.linear import SVDQuantLinear
+    from krea2_svdquant_b200.quant import make_synthetic_state
+
+    peaks = _peaks()
+    hbm = float(peaks.get("hbm_gbs") or 6650.0) * 1e9
+    tc = _bf16_peak() * 1e12
+    _, st = make_synthetic_state(256, K, N, RANK, GROUP, seed=9, device=dev)
+    mod = SVDQuantLinear(st, backend="b200", weight_operand="auto")
+    p = mod.prepare(dev)
+    r2 = p.up_hl.shape[1]
+    out = {}
+    for m in (16, 64, 256):
+        x = torch.randn(m, K, device=dev).bfloat16()
+        a16, mid, _, _ = ops.act_quant(x, p.smooth, p.l2, None, None, p.k_pad, 64, True, False)
+        t_pk = statistics.median(_device_times(
+            lambda: ops.packed_gemm(a16, p.codes, p.scales16, GROUP, mid, p.up_hl, p.bias, False), iters, flush))
+        t_16 = statistics.median(_device_times(
+            lambda: ops.linear_gemm(a16, p.w16, mid, p.up_hl, p.bias, False), iters, flush))
+        t_lin = statistics.median(_device_times(lambda: mod(x), iters, flush))
+        act_out = m * K * 2 + m * N * 2 + m * r2 * 2 + N * r2 * 2 + N * 2  # a16, out, mid_hl, up_hl, bias
+        b_pk = N * K // 2 + N * (K // GROUP) * 2 + act_out
+        b_16 = N * K * 2 + act_out
+        flops = 2 * m * N * K
+        roof_pk = max(b_pk / hbm, flops / tc)
+        roof_16 = max(b_16 / hbm, flops / tc)
+        out[f"M{m}"] = {
+            "packed_gemm_us": round(t_pk * 1e3, 2), "packed_bytes": b_pk,
+            "packed_bound": "hbm" if b_pk / hbm >= flops / tc else "tensor",
+            "packed_roofline_us": round(roof_pk * 1e6, 2), "packed_frac": round(roof_pk / (t_pk * 1e-3), 3),
+            "packed_achieved_gbs": round(b_pk / (t_pk * 1e-3) / 1e9, 1),
+            "fp16_gemm_us": round(t_16 * 1e3, 2), "fp16_roofline_us": round(roof_16 * 1e6, 2),
+            "fp16_frac": round(roof_16 / (t_16 * 1e-3), 3),
+            "linear_us": round(t_lin * 1e3, 2), "linear_tops": round(flops / (t_lin * 1e-3) / 1e12, 1)}
+    return {"config": "K6144 N16384 rank 32 group 64 bias, W4A4, small batches (BASELINE config 4's HBM regime)",
+            "hbm_peak_gbs": hbm / 1e9, "per_batch": out,
+            "plan_tn_ks_grid_ctas_per_sm": {f"M{m}": _packed_plan(m, N, K) for m in (16, 64, 256)}}
+
+
+def _packed_plan(m: int, n: int, k: int) -> list[int]:
+    import ctypes
+
+    from krea2_svdquant_b200 import _lib
+
+    out = (ctypes.c_int * 4)()
+    _lib.call("svdq_packed_gemm_plan", m, n, k, out)
+    return list(out)
+
+
 def measure_forward28(world: int, rank: int, dev, args, offload: bool | None = None) -> dict:
     """random-init Krea2-shaped 28-block transformer (hidden 6144, 48/12 heads x 128,
     MLP 16384, every listed linear W4A4 rank 32 / group 64), 8 images of 4096 latent + 256 text tokens,
@@ -465,6 +521,27 @@ def run_forward_only(args) -> None:
               flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_small_batch_only(args) -> None:
+    """--only-small-batch: the small-batch packed-weight measurement alone on one GPU (one JSON line)."""
+    import torch
+
+    from krea2_svdquant_b200 import _lib
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    flush_w = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(32 * 1024 * 1024, dtype=torch.int64, device=dev)
+
+    def flush_l2():
+        flush_w.zero_()
+        return flush_r.sum()
+
+    res = measure_small_batch(dev, flush_l2, max(args.warmup, 20))
+    if _lib.device_error():
+        raise RuntimeError("device-side error during the small-batch measurement")
+    print(json.dumps({"metric": "small-batch SVDQuantLinear K6144 N16384", "small_batch": res}), flush=True)
 
 
 def run_block_linears_only(args) -> None:
@@ -609,6 +686,7 @@ def run_ours(args) -> None:
         # configs 3-4 on every rank (independent), config 5 with the batch sharded over the ranks
         extra["block_linears"] = measure_block_linears(dev, flush_l2, 10)
         extra["w4a16_lora"] = measure_w4a16_lora(dev, flush_l2, 10)
+        extra["small_batch"] = measure_small_batch(dev, flush_l2, 20)
         torch.cuda.empty_cache()
         extra["forward28"] = measure_forward28(world, rank, dev, args)
         if world == 1 and not args.no_offload:
@@ -704,6 +782,8 @@ def main() -> None:
     ap.add_argument("--only-forward", action="store_true", help="run only the 28-block forward measurement")
     ap.add_argument("--only-block-linears", action="store_true",
                     help="run only the config-3 block-linears measurement (one GPU)")
+    ap.add_argument("--only-small-batch", action="store_true",
+                    help="run only the small-batch (M 16/64/256) packed-weight measurement (one GPU)")
     ap.add_argument("--graph", action="store_true",
                     help="replay the resident 28-block forward from a CUDA graph (host launch cost is not on the "
                          "critical path at these sizes, so eager launches are the default)")
@@ -719,6 +799,8 @@ def main() -> None:
         run_forward_only(args)
     elif args.only_block_linears:
         run_block_linears_only(args)
+    elif args.only_small_batch:
+        run_small_batch_only(args)
     else:
         run_ours(args)
 

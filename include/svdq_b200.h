@@ -235,6 +235,47 @@ int svdq_linear_gemm_schedule(int M, int N, int K_pad, int R2, int with_workspac
 int svdq_linear_gemm_plan(int tiles, int iters, int max_pairs, int with_workspace, int* out4);
 
 /*
+ * Load-time preparation of the packed-weight GEMM's operands (replaces, like svdq_repack_weight,
+ * the per-call unpack + dequantize of src/krea2_svdquant/quant/svd.py:128-135 and
+ * quant/pack.py:26-70, but keeps the weight at half a byte per element):
+ *   out_codes    [N, K_pad/2] u8: the checkpoint's codes (nibble q + 8, pack.py:47-56) with the
+ *                nibbles of every 32-bit word reordered to [k0 k2 k4 k6 | k1 k3 k5 k7]
+ *                (16-byte aligned);
+ *   out_scales16 [N, K_pad/w_group] fp16: the group scales rounded to fp16.
+ * inexact (device int, may be NULL; not cleared here) is set to 1 when some scale or its
+ * sixteenth is not an fp16 value; otherwise svdq_packed_gemm's weights equal svdq_repack_weight's
+ * w16 bit for bit (bf16 scales in [2^-10, 8188], fp16 scales >= 2^-10, all group-scale zeros).
+ *   w_group % 32 == 0, K_pad % w_group == 0, K_pad % 64 == 0; qweight 4-byte aligned.
+ */
+int svdq_prepare_packed(const void* qweight, const void* scales, int scale_dtype, int N, int K_pad,
+                        int w_group, void* out_codes, void* out_scales16, int* inexact,
+                        cudaStream_t stream);
+
+/*
+ * Packed-weight SVDQuant linear GEMM: the same computation as svdq_linear_gemm, with the weight
+ * read as the half-byte codes + fp16 group scales of svdq_prepare_packed and converted to fp16
+ * in shared memory (exactly, see above) inside the kernel; no fp16 weight is allocated.  Weight
+ * rows are the tcgen05 MMA's M dimension and tokens its N (16 to 128 per tile), so small
+ * batches run small MMAs and read 4x fewer weight bytes.  When the tiles leave SMs idle, a
+ * cluster of 2, 4 or 8 CTAs splits K and sums its fp32 partials through distributed shared
+ * memory in a fixed order (deterministic).  Replaces F.linear(x_hat, w_res) + F.linear(mid, l1)
+ * + bias of svd.py:158-162 and the in-loop dequantization of kernels/triton/generic_int4.py:19-133.
+ *   a16 [M, K_pad] fp16; K_pad % 64 == 0; w_group as above; N % 8 == 0, ldo % 8 == 0;
+ *   R2 % 64 == 0 (may be 0); out_dtype in {SVDQ_BF16, SVDQ_FP32}; bias may be NULL.
+ */
+int svdq_packed_gemm(const void* a16, const void* codes, const void* scales16, int w_group,
+                     const void* mid_hl, const void* up_hl, int R2, const void* bias,
+                     void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
+                     cudaStream_t stream);
+
+/*
+ * The launch plan of svdq_packed_gemm for a shape on the current device: out4 = {token tile TN,
+ * CTAs per cluster along K, CTAs in the grid, CTAs per SM}.  Host only apart from device
+ * attribute queries.
+ */
+int svdq_packed_gemm_plan(int M, int N, int K_pad, int* out4);
+
+/*
  * Converter weight quantization on the GPU: an fp32 layer residual w [N, K]
  * (row stride ldw) -> packed INT4 codes [N, K_pad/2] (nibble q + 8, even k
  * low) and group scales [N, K_pad/group] as fp32, fp16 or bf16, with

@@ -54,6 +54,11 @@ SIGNATURES = {
                              c_int64, c_int, c_int, c_int, c_void_p, ctypes.c_size_t, c_void_p], c_int),
     "svdq_linear_gemm_schedule": ([c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)], c_int),
     "svdq_linear_gemm_plan": ([c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)], c_int),
+    "svdq_prepare_packed": ([c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                             c_void_p], c_int),
+    "svdq_packed_gemm": ([c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                          c_int64, c_int, c_int, c_int, c_void_p], c_int),
+    "svdq_packed_gemm_plan": ([c_int, c_int, c_int, ctypes.POINTER(c_int)], c_int),
 }
 
 SVDQ_BF16, SVDQ_FP16, SVDQ_FP32 = 0, 1, 2

@@ -1,0 +1,611 @@
+// Packed-weight SVDQuant linear GEMM for sm_100a (tcgen05 + TMA + TMEM).
+//
+//   out[m, n] = sum_k a16[m,k] * (q_w[n,k] * s_w[n, k/G]) + sum_j mid_hl[m,j] up_hl[n,j] + bias[n]
+//
+// The INT4 weight stays packed in HBM (half a byte per weight, the checkpoint's size): each CTA
+// streams its rows' codes with TMA and converts them to fp16 in shared memory, where the tensor
+// core reads them.  No fp16 copy of the weight exists, so a layer costs its packed bytes in memory,
+// and a small batch reads 4x fewer weight bytes than a kernel over a dequantized weight.
+//
+// Orientation (swap AB): the weight rows are the MMA's M (128 TMEM lanes per CTA) and the tokens
+// its N (TN columns, 16 to 128), so 16 tokens cost a 128x16 MMA instead of most of a 128x256 tile.
+// The result tile lands in TMEM as [weight row][token] and leaves transposed.
+//
+// Conversion.  The load-time preparation (svdq_prepare_packed) reorders the nibbles of each 32-bit
+// word to [k0 k2 k4 k6 | k1 k3 k5 k7] (low half-word holds the even k), so one AND/OR per pair puts
+// two codes into the mantissas of an fp16x2 pair with exponent 2^10: 1024 + n (even pair) or
+// 1024 + 16 n (odd pair, whose nibbles sit 4 bits higher).  One subtraction gives the exact code
+// (n - 8 or 16 (n - 8)), one multiplication the exact product with the group scale (s or s / 16):
+// q * s has at most 3 + 8 significant bits for a bf16-valued scale, so it is exact in fp16, and
+// equals the load-time fp16 operand of the other GEMM bit for bit.  13 instructions per 8 weights.
+//
+// Split K.  When the tiles would leave SMs idle, a cluster of KS CTAs (KS in {1, 2, 4, 8}) shares a
+// tile, each taking one contiguous K range; the last one also takes the low-rank stages.  Each
+// CTA parks its fp32 partial in its own shared memory, and after a cluster barrier each CTA sums
+// one slice of rows over all KS partials through distributed shared memory, in rank order (a
+// fixed order: results are deterministic), adds the bias and stores.
+//
+// Roles (12 warps): warp 0 TMA of packed codes (8-deep ring of 128 rows x 64 k); warp 2 TMA of
+// the token tile (a16, or mid_hl with up_hl for the low-rank stages; 4-deep ring); warp 1 TMEM
+// allocation and the MMA issue; warps 4-11 conversion into the A ring; warps 4-7 the epilogue.
+// Every wait is bounded (error word codes 0x51xx-0x54xx); a wait that runs out raises the CTA's
+// abort flag and every role leaves its loop, so all CTAs still meet at the cluster barriers.
+#include <algorithm>
+
+#include "svdq_common.cuh"
+
+namespace svdq {
+namespace {
+
+constexpr int PW_ROWS = 128;                          // weight rows per CTA
+constexpr int PW_KB = 64;                             // k per stage
+constexpr int PW_PSTAGES = 8;                         // packed-code ring
+constexpr int PW_ASTAGES = 4;                         // operand ring
+constexpr uint32_t PW_P_BYTES = PW_ROWS * PW_KB / 2;  // 4 KiB of codes
+constexpr uint32_t PW_A_BYTES = PW_ROWS * PW_KB * 2;  // 16 KiB of fp16 weights
+constexpr int PW_CONV_WARPS = 8;
+constexpr int PW_THREADS = 32 * (4 + PW_CONV_WARPS);
+static_assert(PW_CONV_WARPS * 32 * 16 == (int)PW_P_BYTES, "one 16-byte piece of codes per converter thread");
+
+template <int TN>
+struct PwLayout {
+  static constexpr uint32_t kB = (uint32_t)TN * PW_KB * 2;  // token tile bytes per stage
+  static constexpr uint32_t kOffB = PW_ASTAGES * PW_A_BYTES;
+  static constexpr uint32_t kOffP = kOffB + PW_ASTAGES * kB;
+  static constexpr uint32_t kOffBar = kOffP + PW_PSTAGES * PW_P_BYTES;
+  static constexpr uint32_t kSmem = kOffBar + 256 + 1024;   // barriers + alignment slack
+  static constexpr uint32_t kTmemCols = TN < 32 ? 32 : TN;
+  static_assert(kB % 1024 == 0, "token tiles keep 1 KiB alignment for the 128-byte swizzle");
+  static_assert((uint32_t)PW_ROWS * TN * 4 <= PW_ASTAGES * PW_A_BYTES, "split-K partial fits the A ring");
+};
+
+struct PwBars {
+  uint64_t full_p[PW_PSTAGES];   // codes landed (TMA bytes)
+  uint64_t empty_p[PW_PSTAGES];  // codes read (one arrival per converter warp)
+  uint64_t full_ab[PW_ASTAGES];  // token tile (and low-rank A) landed (TMA bytes)
+  uint64_t conv[PW_ASTAGES];     // A stage written (one arrival per converter warp)
+  uint64_t empty_ab[PW_ASTAGES]; // MMAs of the stage done (commit)
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(PwBars) <= 256, "barrier block");
+
+struct PwArgs {
+  const __half* scales16;  // [N, nG] fp16 group scales
+  const __nv_bfloat16* bias;
+  void* out;
+  int64_t ldo;
+  int M, N;
+  int n_k, n_lr;   // residual and low-rank stages
+  int nG, w_group;
+  int ks;          // CTAs per cluster along K
+  int units_n;     // 128-row weight tiles
+  int* err;
+};
+
+enum : int {
+  kPwWaitPackedEmpty = 0x5101,
+  kPwWaitTileEmpty = 0x5102,
+  kPwWaitConvPacked = 0x5201,
+  kPwWaitConvEmpty = 0x5202,
+  kPwWaitMmaFull = 0x5301,
+  kPwWaitMmaConv = 0x5302,
+  kPwWaitMmaDrain = 0x5303,
+  kPwWaitEpilogue = 0x5401,
+};
+
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t h2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint4 ld_shared_u4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void st_shared_u4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void mbar_arrive_cta(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Eight codes of one native-order word -> four fp16x2 pairs (k0 k1, k2 k3, k4 k5, k6 k7), exact.
+__device__ __forceinline__ uint4 convert_word(uint32_t w, uint32_t s_lo, uint32_t s_hi) {
+  constexpr uint32_t kExp = 0x64006400u;  // fp16x2 {1024, 1024}
+  constexpr uint32_t kOffLo = 0x64086408u;  // {1032, 1032}: 1024 + the nibble offset 8
+  constexpr uint32_t kOffHi = 0x64806480u;  // {1152, 1152}: 1024 + 16 * 8
+  const uint32_t w8 = w >> 8;
+  uint4 o;
+  o.x = h2_mul(h2_sub((w & 0x000F000Fu) | kExp, kOffLo), s_lo);
+  o.y = h2_mul(h2_sub((w & 0x00F000F0u) | kExp, kOffHi), s_hi);
+  o.z = h2_mul(h2_sub((w8 & 0x000F000Fu) | kExp, kOffLo), s_lo);
+  o.w = h2_mul(h2_sub((w8 & 0x00F000F0u) | kExp, kOffHi), s_hi);
+  return o;
+}
+
+template <int TN, bool OUT_F32>
+__global__ void __launch_bounds__(PW_THREADS, TN <= 32 ? 2 : 1)
+    packed_gemm_kernel(const __grid_constant__ CUtensorMap tm_a16, const __grid_constant__ CUtensorMap tm_codes,
+                       const __grid_constant__ CUtensorMap tm_mid, const __grid_constant__ CUtensorMap tm_up,
+                       const PwArgs args) {
+  using L = PwLayout<TN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  PwBars* bars = reinterpret_cast<PwBars*>(gbase + L::kOffBar);
+  volatile int* abort_flag = &bars->abort_flag;
+  const uint32_t a_ring = base, b_ring = base + L::kOffB, p_ring = base + L::kOffP;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ks = args.ks;
+  const int crank = (int)(blockIdx.x % (unsigned)ks);
+  const int unit = (int)(blockIdx.x / (unsigned)ks);
+  const int nb = unit % args.units_n, mb = unit / args.units_n;
+  const int n0 = nb * PW_ROWS, m0 = mb * TN;
+  const int kb0 = (int)((int64_t)crank * args.n_k / ks), kb1 = (int)((int64_t)(crank + 1) * args.n_k / ks);
+  const int n_res = kb1 - kb0;
+  const int iters = n_res + (crank == ks - 1 ? args.n_lr : 0);
+
+  auto bar = [&](const uint64_t& b) { return smem_u32(&b); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PW_PSTAGES; ++s) {
+      mbar_init(bar(bars->full_p[s]), 1);
+      mbar_init(bar(bars->empty_p[s]), PW_CONV_WARPS);
+    }
+    for (int s = 0; s < PW_ASTAGES; ++s) {
+      mbar_init(bar(bars->full_ab[s]), 1);
+      mbar_init(bar(bars->conv[s]), PW_CONV_WARPS);
+      mbar_init(bar(bars->empty_ab[s]), 1);
+    }
+    mbar_init(bar(bars->mma_done), 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tma_desc(&tm_a16);
+    prefetch_tma_desc(&tm_codes);
+    if (args.n_lr > 0) {
+      prefetch_tma_desc(&tm_mid);
+      prefetch_tma_desc(&tm_up);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_1(smem_u32(&bars->tmem_base), L::kTmemCols);
+    tmem_relinquish_1();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  pdl_wait();  // operands may come from the previous kernel on the stream
+  pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ packed codes (residual stages only)
+      uint32_t filled = 0, par = 0;
+      bool ok = true;
+      for (int it = 0; it < n_res && ok; ++it) {
+        const int s = it % PW_PSTAGES;
+        const uint32_t ph = (uint32_t)(it / PW_PSTAGES) & 1u;
+        if (!(ok = mbar_wait(bar(bars->empty_p[s]), ph ^ 1u, abort_flag, args.err, kPwWaitPackedEmpty))) break;
+        mbar_arrive_expect_tx(bar(bars->full_p[s]), PW_P_BYTES);
+        tma_load_2d(p_ring + (uint32_t)s * PW_P_BYTES, &tm_codes, bar(bars->full_p[s]), (kb0 + it) * (PW_KB / 2), n0);
+        filled |= 1u << s;
+        par = (par & ~(1u << s)) | (ph << s);
+      }
+      if (!ok)
+        for (int s = 0; s < PW_PSTAGES; ++s)
+          if (filled & (1u << s)) mbar_wait_drain(bar(bars->full_p[s]), (par >> s) & 1u, 100000000ull);
+    }
+  } else if (warp == 2) {
+    if (lane == 0) {
+      // ------------------------------------------------ token tiles (+ low-rank A)
+      uint32_t filled = 0, par = 0;
+      bool ok = true;
+      for (int it = 0; it < iters && ok; ++it) {
+        const int s = it % PW_ASTAGES;
+        const uint32_t ph = (uint32_t)(it / PW_ASTAGES) & 1u;
+        if (!(ok = mbar_wait(bar(bars->empty_ab[s]), ph ^ 1u, abort_flag, args.err, kPwWaitTileEmpty))) break;
+        const uint32_t fb = bar(bars->full_ab[s]);
+        const uint32_t bdst = b_ring + (uint32_t)s * L::kB;
+        if (it < n_res) {
+          mbar_arrive_expect_tx(fb, L::kB);
+          tma_load_2d(bdst, &tm_a16, fb, (kb0 + it) * PW_KB, m0);
+        } else {
+          const int j = it - n_res;
+          mbar_arrive_expect_tx(fb, L::kB + PW_A_BYTES);
+          tma_load_2d(a_ring + (uint32_t)s * PW_A_BYTES, &tm_up, fb, j * PW_KB, n0);
+          tma_load_2d(bdst, &tm_mid, fb, j * PW_KB, m0);
+        }
+        filled |= 1u << s;
+        par = (par & ~(1u << s)) | (ph << s);
+      }
+      if (!ok)
+        for (int s = 0; s < PW_ASTAGES; ++s)
+          if (filled & (1u << s)) mbar_wait_drain(bar(bars->full_ab[s]), (par >> s) & 1u, 100000000ull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issue
+      const uint32_t idesc_res = make_idesc(0u /*f16*/, 0u, PW_ROWS, TN);
+      const uint32_t idesc_lr = make_idesc(kFmtBF16, kFmtBF16, PW_ROWS, TN);
+      bool ok = true;
+      for (int it = 0; it < iters && ok; ++it) {
+        const int s = it % PW_ASTAGES;
+        const uint32_t ph = (uint32_t)(it / PW_ASTAGES) & 1u;
+        if (!(ok = mbar_wait(bar(bars->full_ab[s]), ph, abort_flag, args.err, kPwWaitMmaFull))) break;
+        if (!(ok = mbar_wait(bar(bars->conv[s]), ph, abort_flag, args.err, kPwWaitMmaConv))) break;
+        tc_fence_after();
+        const uint64_t da = desc_k_sw128(a_ring + (uint32_t)s * PW_A_BYTES);
+        const uint64_t db = desc_k_sw128(b_ring + (uint32_t)s * L::kB);
+        const uint32_t idesc = it < n_res ? idesc_res : idesc_lr;
+#pragma unroll
+        for (int kk = 0; kk < PW_KB / 16; ++kk)
+          umma_f16_1(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (it > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_1(bar(bars->empty_ab[s]));
+      }
+      // the epilogue reads the accumulator after every issued MMA has completed; this thread also
+      // waits for that, so no MMA is in flight when the CTA frees TMEM or exits
+      umma_commit_1(bar(bars->mma_done));
+      if (!mbar_wait_drain(bar(bars->mma_done), 0, 1000000000ull)) {
+        *abort_flag = 1;
+        atomicCAS(args.err, 0, kPwWaitMmaDrain);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------ conversion: codes -> fp16 A stages
+    const int ct = threadIdx.x - 128;  // 0 .. 255
+    const int row = ct >> 1, half = ct & 1;
+    const int n_row = n0 + row;
+    const uint32_t a_row = (uint32_t)row * 128u;
+    const uint32_t r7 = (uint32_t)(row & 7);
+    const __half* srow = args.scales16 + (int64_t)min(n_row, args.N - 1) * args.nG;
+    bool ok = true;
+    for (int it = 0; it < iters && ok; ++it) {
+      const int s = it % PW_ASTAGES;
+      const uint32_t ph = (uint32_t)(it / PW_ASTAGES) & 1u;
+      if (it < n_res) {
+        const int kb = kb0 + it;
+        const int ps = it % PW_PSTAGES;
+        const uint32_t pph = (uint32_t)(it / PW_PSTAGES) & 1u;
+        const uint32_t sbits = n_row < args.N ? (uint32_t)__half_as_ushort(srow[(kb * PW_KB + 32 * half) / args.w_group])
+                                              : 0u;
+        ok = mbar_wait(bar(bars->empty_ab[s]), ph ^ 1u, abort_flag, args.err, kPwWaitConvEmpty) &&
+             mbar_wait(bar(bars->full_p[ps]), pph, abort_flag, args.err, kPwWaitConvPacked);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;  // the lanes of a warp leave together
+        const uint4 pk = ld_shared_u4(p_ring + (uint32_t)ps * PW_P_BYTES + (uint32_t)ct * 16u);
+        const uint32_t s_lo = sbits | (sbits << 16);
+        const uint32_t s16 = (uint32_t)__half_as_ushort(__hmul(__ushort_as_half((unsigned short)sbits),
+                                                               __float2half_rn(0.0625f)));
+        const uint32_t s_hi = s16 | (s16 << 16);
+        const uint32_t dst = a_ring + (uint32_t)s * PW_A_BYTES + a_row;
+        const uint32_t words[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 o = convert_word(words[j], s_lo, s_hi);
+          st_shared_u4(dst + ((((uint32_t)(4 * half + j)) ^ r7) << 4), o.x, o.y, o.z, o.w);
+        }
+        fence_proxy_async_smem();  // the tensor core (async proxy) reads what these stores wrote
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_cta(bar(bars->empty_p[ps]));
+          mbar_arrive_cta(bar(bars->conv[s]));
+        }
+      } else {
+        // low-rank stage: its A rows come by TMA; the converters only keep the stage's count
+        ok = mbar_wait(bar(bars->empty_ab[s]), ph ^ 1u, abort_flag, args.err, kPwWaitConvEmpty);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        if (lane == 0) mbar_arrive_cta(bar(bars->conv[s]));
+      }
+    }
+    if (warp < 8) {
+      // ---------------------------------------------- epilogue: TMEM -> registers -> out or partial
+      const int q = warp & 3;
+      const int erow = q * 32 + lane;
+      const int n = n0 + erow;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+      const bool done = mbar_wait(bar(bars->mma_done), 0, abort_flag, args.err, kPwWaitEpilogue) && !*abort_flag;
+      if (__all_sync(0xffffffffu, done)) {
+        tc_fence_after();
+        float bias_v = 0.f;
+        if (ks == 1 && args.bias && n < args.N) bias_v = __bfloat162float(args.bias[n]);
+        float* part = reinterpret_cast<float*>(gbase);  // [TN][128] over the A ring (all MMAs are done)
+#pragma unroll 1
+        for (int c0 = 0; c0 < TN; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(taddr + (uint32_t)c0, v);
+          tmem_ld_wait_regs16(v);
+          if (ks > 1) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) part[(c0 + e) * PW_ROWS + erow] = __uint_as_float(v[e]);
+          } else if (n < args.N) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int m = m0 + c0 + e;
+              if (m < args.M) {
+                const float y = __uint_as_float(v[e]) + bias_v;
+                if constexpr (OUT_F32) static_cast<float*>(args.out)[(int64_t)m * args.ldo + n] = y;
+                else static_cast<__nv_bfloat16*>(args.out)[(int64_t)m * args.ldo + n] = __float2bfloat16_rn(y);
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (ks > 1) {
+    // ------------------------------------------------ split-K: sum the cluster's partials
+    cluster_sync();  // every CTA's partial is in its shared memory
+    const int rows = PW_ROWS / ks;
+    const uint32_t part_local = base;
+    for (int o = threadIdx.x; o < rows * TN; o += PW_THREADS) {
+      const int rl = o % rows, col = o / rows;
+      const int row = crank * rows + rl;
+      const int n = n0 + row, m = m0 + col;
+      const uint32_t off = (uint32_t)(col * PW_ROWS + row) * 4u;
+      float y = 0.f;
+      for (int c = 0; c < ks; ++c) y += ld_dsmem_f32(mapa_shared(part_local + off, (uint32_t)c));
+      if (n < args.N && m < args.M && !*abort_flag) {
+        if (args.bias) y += __bfloat162float(args.bias[n]);
+        if constexpr (OUT_F32) static_cast<float*>(args.out)[(int64_t)m * args.ldo + n] = y;
+        else static_cast<__nv_bfloat16*>(args.out)[(int64_t)m * args.ldo + n] = __float2bfloat16_rn(y);
+      }
+    }
+    cluster_sync();  // no CTA leaves while another still reads its shared memory
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_1(tmem, L::kTmemCols);
+  }
+}
+
+// Native nibble order: natural word [k0 k1 k2 k3 k4 k5 k6 k7] (nibble i at bits 4i) ->
+// [k0 k2 k4 k6 | k1 k3 k5 k7].
+__global__ void prepare_codes_kernel(const uint32_t* __restrict__ in, uint32_t* __restrict__ out, int64_t words) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < words; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t w = in[i];
+    uint32_t o = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o |= ((w >> (4 * j)) & 0xFu) << ((j & 1) ? 16 + 4 * (j >> 1) : 4 * (j >> 1));
+    out[i] = o;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float scale_f32(T v);
+template <>
+__device__ __forceinline__ float scale_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float scale_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float scale_f32<float>(float v) { return v; }
+
+// Group scales -> fp16.  *inexact (when given) is set when a scale is not an fp16 value or its
+// sixteenth is not: the kernel's weights then round the scale once more than fp16(q * s) does
+// (relative error at most 2^-11 on the weights of such groups).
+template <typename T>
+__global__ void prepare_scales_kernel(const T* __restrict__ in, __half* __restrict__ out, int64_t count,
+                                      int* __restrict__ inexact) {
+  int bad = 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+    const float s = scale_f32<T>(in[i]);
+    const __half h = __float2half_rn(s);
+    const __half h16 = __hmul(h, __float2half_rn(0.0625f));
+    bad |= (__half2float(h) != s) || (__half2float(h16) * 16.0f != __half2float(h));
+    out[i] = h;
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0 && inexact) atomicExch(inexact, 1);
+}
+
+int pw_ctas_per_sm(uint32_t smem) {
+  int dev = 0, per_sm = 0, reserved = 0;
+  cudaGetDevice(&dev);
+  if (cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess || per_sm <= 0)
+    per_sm = 233472;
+  if (cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess || reserved < 0)
+    reserved = 1024;
+  (void)cudaGetLastError();
+  return std::max(1, std::min(2, per_sm / (int)(smem + (uint32_t)reserved)));
+}
+
+struct PwPlan {
+  int tn, ks, units_n, units_m;
+};
+
+int pick_tn(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+
+uint32_t pw_smem(int tn) {
+  switch (tn) {
+    case 16: return PwLayout<16>::kSmem;
+    case 32: return PwLayout<32>::kSmem;
+    case 64: return PwLayout<64>::kSmem;
+    default: return PwLayout<128>::kSmem;
+  }
+}
+
+// Split factor: the KS in {1, 2, 4, 8} whose grid fills the CTA slots best (fewest idle slots in
+// the last wave), with at least two residual stages per CTA; ties go to the smaller KS.
+PwPlan plan_packed(int M, int N, int K_pad) {
+  PwPlan p;
+  p.tn = pick_tn(M);
+  p.units_n = (N + PW_ROWS - 1) / PW_ROWS;
+  p.units_m = (M + p.tn - 1) / p.tn;
+  const int n_k = K_pad / PW_KB;
+  const long long units = (long long)p.units_n * p.units_m;
+  const long long slots = (long long)num_sms() * pw_ctas_per_sm(pw_smem(p.tn));
+  p.ks = 1;
+  double best = -1.0;
+  for (int ks = 1; ks <= 8 && n_k / ks >= 2; ks *= 2) {
+    const long long ctas = units * ks;
+    const long long waves = (ctas + slots - 1) / slots;
+    const double fill = (double)ctas / (double)(waves * slots);
+    if (fill > best + 1e-9) {
+      best = fill;
+      p.ks = ks;
+    }
+  }
+  return p;
+}
+
+template <int TN, bool OUT_F32>
+int launch_pw(const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMap& tmid, const CUtensorMap& tup,
+              const PwArgs& a, int grid, cudaStream_t stream) {
+  auto kern = packed_gemm_kernel<TN, OUT_F32>;
+  constexpr uint32_t smem = PwLayout<TN>::kSmem;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return check_cuda(e, "svdq_packed_gemm: shared memory attribute");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(PW_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = a.ks;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tc, tmid, tup, a);
+  if (e != cudaSuccess) return check_cuda(e, "svdq_packed_gemm launch");
+  return check_launch("svdq_packed_gemm launch");
+}
+
+template <bool OUT_F32>
+int launch_pw_tn(int tn, const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMap& tmid, const CUtensorMap& tup,
+                 const PwArgs& a, int grid, cudaStream_t stream) {
+  switch (tn) {
+    case 16: return launch_pw<16, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
+    case 32: return launch_pw<32, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
+    case 64: return launch_pw<64, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
+    default: return launch_pw<128, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
+  }
+}
+
+}  // namespace
+}  // namespace svdq
+
+extern "C" int svdq_prepare_packed(const void* qweight, const void* scales, int scale_dtype, int N, int K_pad,
+                                   int w_group, void* out_codes, void* out_scales16, int* inexact,
+                                   cudaStream_t stream) {
+  using namespace svdq;
+  SVDQ_REQUIRE(qweight && scales && out_codes && out_scales16, "svdq_prepare_packed: null pointer");
+  SVDQ_REQUIRE(N > 0 && K_pad > 0 && K_pad % 64 == 0, "svdq_prepare_packed: K_pad must be a positive multiple of 64");
+  SVDQ_REQUIRE(w_group > 0 && w_group % 32 == 0 && K_pad % w_group == 0,
+               "svdq_prepare_packed: w_group must be a multiple of 32 dividing K_pad");
+  SVDQ_REQUIRE((reinterpret_cast<uintptr_t>(qweight) & 3u) == 0 && (reinterpret_cast<uintptr_t>(out_codes) & 15u) == 0,
+               "svdq_prepare_packed: qweight must be 4-byte and out_codes 16-byte aligned");
+  const int64_t words = (int64_t)N * K_pad / 8;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)std::min<int64_t>((words + threads - 1) / threads, (int64_t)num_sms() * 32);
+  prepare_codes_kernel<<<blocks, threads, 0, stream>>>(static_cast<const uint32_t*>(qweight),
+                                                       static_cast<uint32_t*>(out_codes), words);
+  int st = check_launch("svdq_prepare_packed: codes");
+  if (st) return st;
+  const int64_t count = (int64_t)N * (K_pad / w_group);
+  const unsigned sblocks = (unsigned)std::min<int64_t>((count + threads - 1) / threads, (int64_t)num_sms() * 8);
+  __half* o = static_cast<__half*>(out_scales16);
+  switch (scale_dtype) {
+    case SVDQ_BF16:
+      prepare_scales_kernel<<<sblocks, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(scales), o, count, inexact);
+      break;
+    case SVDQ_FP16:
+      prepare_scales_kernel<<<sblocks, threads, 0, stream>>>(static_cast<const __half*>(scales), o, count, inexact);
+      break;
+    case SVDQ_FP32:
+      prepare_scales_kernel<<<sblocks, threads, 0, stream>>>(static_cast<const float*>(scales), o, count, inexact);
+      break;
+    default:
+      return set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_prepare_packed: scale_dtype must be bf16, fp16 or fp32");
+  }
+  return check_launch("svdq_prepare_packed: scales");
+}
+
+extern "C" int svdq_packed_gemm_plan(int M, int N, int K_pad, int* out4) {
+  using namespace svdq;
+  SVDQ_REQUIRE(out4, "svdq_packed_gemm_plan: out4 is NULL");
+  SVDQ_REQUIRE(M > 0 && N > 0 && K_pad > 0 && K_pad % 64 == 0, "svdq_packed_gemm_plan: bad M/N/K_pad");
+  const PwPlan p = plan_packed(M, N, K_pad);
+  out4[0] = p.tn;
+  out4[1] = p.ks;
+  out4[2] = p.units_n * p.units_m * p.ks;
+  out4[3] = pw_ctas_per_sm(pw_smem(p.tn));
+  return SVDQ_OK;
+}
+
+extern "C" int svdq_packed_gemm(const void* a16, const void* codes, const void* scales16, int w_group,
+                                const void* mid_hl, const void* up_hl, int R2, const void* bias, void* out,
+                                int out_dtype, int64_t ldo, int M, int N, int K_pad, cudaStream_t stream) {
+  using namespace svdq;
+  SVDQ_REQUIRE(a16 && codes && scales16 && out, "svdq_packed_gemm: null operand pointer");
+  SVDQ_REQUIRE(M >= 0 && N > 0 && K_pad > 0 && K_pad % 64 == 0, "svdq_packed_gemm: bad M/N/K_pad");
+  SVDQ_REQUIRE(w_group > 0 && w_group % 32 == 0 && K_pad % w_group == 0,
+               "svdq_packed_gemm: w_group must be a multiple of 32 dividing K_pad");
+  SVDQ_REQUIRE(N % 8 == 0 && ldo >= N && ldo % 8 == 0, "svdq_packed_gemm: N and ldo must be multiples of 8, ldo >= N");
+  SVDQ_REQUIRE(R2 >= 0 && R2 % 64 == 0, "svdq_packed_gemm: R2 must be a multiple of 64");
+  SVDQ_REQUIRE(R2 == 0 || (mid_hl && up_hl), "svdq_packed_gemm: mid_hl/up_hl are NULL");
+  SVDQ_REQUIRE(out_dtype == SVDQ_BF16 || out_dtype == SVDQ_FP32, "svdq_packed_gemm: out_dtype must be bf16 or fp32");
+  SVDQ_REQUIRE(!bias || (reinterpret_cast<uintptr_t>(bias) & 1u) == 0, "svdq_packed_gemm: bias must be 2-byte aligned");
+  if (M == 0) return SVDQ_OK;
+  int* err = device_error_word();
+  if (!err) return set_error(SVDQ_ERR_CUDA, "svdq_packed_gemm: device error word unavailable");
+  const PwPlan p = plan_packed(M, N, K_pad);
+  CUtensorMap ta, tc, tmid, tup;
+  int st;
+  if ((st = make_tma_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a16, K_pad, M, (uint64_t)K_pad * 2, PW_KB, p.tn,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if ((st = make_tma_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, K_pad / 2, N, (uint64_t)K_pad / 2, PW_KB / 2,
+                        PW_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return st;
+  if (R2 > 0) {
+    if ((st = make_tma_2d(&tmid, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, mid_hl, R2, M, (uint64_t)R2 * 2, PW_KB, p.tn,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+    if ((st = make_tma_2d(&tup, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, up_hl, R2, N, (uint64_t)R2 * 2, PW_KB, PW_ROWS,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+  } else {
+    tmid = ta;
+    tup = ta;
+  }
+  PwArgs a;
+  a.scales16 = static_cast<const __half*>(scales16);
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.out = out;
+  a.ldo = ldo;
+  a.M = M;
+  a.N = N;
+  a.n_k = K_pad / PW_KB;
+  a.n_lr = R2 / PW_KB;
+  a.nG = K_pad / w_group;
+  a.w_group = w_group;
+  a.ks = p.ks;
+  a.units_n = p.units_n;
+  a.err = err;
+  const int grid = p.units_n * p.units_m * p.ks;
+  return out_dtype == SVDQ_FP32 ? launch_pw_tn<true>(p.tn, ta, tc, tmid, tup, a, grid, stream)
+                                : launch_pw_tn<false>(p.tn, ta, tc, tmid, tup, a, grid, stream);
+}

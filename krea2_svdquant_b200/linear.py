@@ -78,7 +78,9 @@ class PreparedOperands:
     lora_col_scale: torch.Tensor | None  # [rl8] fp32 multiplier per stacked row
     up_hl: torch.Tensor | None     # [n, R2] bf16, [l1 | lora_up] hi/lo operand
     up_hl_base: torch.Tensor | None  # same without the LoRA columns (for _forward_base)
-    w16: torch.Tensor              # [n, k_pad] fp16 = q * weight scale
+    w16: torch.Tensor | None       # [n, k_pad] fp16 = q * weight scale (weight_operand "fp16" / "auto")
+    codes: torch.Tensor | None     # [n, k_pad/2] u8 kernel-order codes (weight_operand "packed" / "auto")
+    scales16: torch.Tensor | None  # [n, k_pad/group] fp16 group scales (with codes)
     bias: torch.Tensor | None      # [n] bf16
 
 
@@ -101,11 +103,20 @@ class SVDQuantLinear(nn.Module):
     """
 
     check_device_errors = False
+    # "auto": both weight operands, the packed-weight GEMM for batches of at most
+    # PACKED_MAX_TOKENS tokens (it reads 4x fewer weight bytes), the fp16-weight GEMM above;
+    # "fp16": only the load-time fp16 weight (4x the packed bytes); "packed": only the packed
+    # codes + fp16 scales (no fp16 weight is allocated; every batch size runs the packed GEMM).
+    WEIGHT_OPERANDS = ("auto", "fp16", "packed")
+    PACKED_MAX_TOKENS = 64
 
     def __init__(self, state: SVDQuantLinearState, backend: BackendKind | str = BackendKind.AUTO,
-                 *, act_group_size: int = 64):
+                 *, act_group_size: int = 64, weight_operand: str = "auto"):
         super().__init__()
         self.backend = resolve_backend(backend)
+        if weight_operand not in self.WEIGHT_OPERANDS:
+            raise ValueError(f"weight_operand must be one of {self.WEIGHT_OPERANDS}, got {weight_operand!r}")
+        self.weight_operand = weight_operand
         self.group_size = int(state.group_size)
         self.original_shape = tuple(int(v) for v in state.original_shape)
         self.qweight_packed = bool(state.qweight_packed)
@@ -160,12 +171,14 @@ class SVDQuantLinear(nn.Module):
             bufs += [a.down_weight, a.up_weight]
         # the version counter changes on every in-place write (load_state_dict copies into the
         # existing buffers), so updated weights are re-derived rather than served stale
-        return (device,) + tuple((None if b is None else (b.data_ptr(), b.device, b._version)) for b in bufs) + tuple(
+        return (device, self.weight_operand) + tuple(
+            (None if b is None else (b.data_ptr(), b.device, b._version)) for b in bufs) + tuple(
             a.multiplier for a in self.lora_adapters)
 
     def prepare(self, device: torch.device | str | None = None) -> PreparedOperands:
         """Derive (once per device and buffer set) the kernel operands: the fp16
-        weight operand ``w16 = q * weight_scale``, the ``[l1|lora_up]`` hi/lo
+        weight operand ``w16 = q * weight_scale`` and/or the packed-weight GEMM's
+        kernel-order codes and fp16 scales (per ``weight_operand``), the ``[l1|lora_up]`` hi/lo
         up-projection operand, padded smoothing / down-projection weights and
         the stacked LoRA down weights with their per-row multipliers."""
         device = torch.device(device) if device is not None else self.qweight.device
@@ -214,13 +227,19 @@ class SVDQuantLinear(nn.Module):
                 up_hl_base = ops.build_up_hl(l1_in, None, r2b) if r2b else None
             qw = self.qweight.to(device=device).contiguous()
             ws = self.weight_scales.to(device=device).contiguous()
-            w16 = ops.repack_weight(qw, ws, self.group_size)
+            w16 = ops.repack_weight(qw, ws, self.group_size) if self.weight_operand != "packed" else None
+            codes = scales16 = None
+            if self.weight_operand != "fp16":
+                if self.group_size % 32:
+                    raise ValueError(f"the packed-weight GEMM needs a weight group size divisible by 32, "
+                                     f"got {self.group_size} (use weight_operand='fp16')")
+                codes, scales16, _ = ops.prepare_packed(qw, ws, self.group_size)
             bias = None if self.bias is None else self.bias.to(device=device, dtype=bf).contiguous()
         self._prepared = PreparedOperands(device=device, key=key, k_in=k_in, k_pad=k_pad, n=n, smooth=smooth,
                                           l2=l2, l2_f16=None if l2 is None else l2.to(torch.float16),
                                           lora_down=lora_down, lora_col_scale=col_scale, up_hl=up_hl,
                                           up_hl_base=up_hl_base,
-                                          w16=w16, bias=bias)
+                                          w16=w16, codes=codes, scales16=scales16, bias=bias)
         return self._prepared
 
     # ------------------------------------------------------------------ forward
@@ -248,8 +267,11 @@ class SVDQuantLinear(nn.Module):
         else:
             a16, mid, _, _ = ops.act_quant(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
                                            self.act_group_size, True, False)
-        y = ops.linear_gemm(a16, p.w16, mid if mid.numel() else None, up_hl if mid.numel() else None,
-                            p.bias, out_fp32)
+        lowrank = (mid, up_hl) if mid.numel() else (None, None)
+        if p.w16 is None or (p.codes is not None and x2.shape[0] <= self.PACKED_MAX_TOKENS):
+            y = ops.packed_gemm(a16, p.codes, p.scales16, self.group_size, *lowrank, p.bias, out_fp32)
+        else:
+            y = ops.linear_gemm(a16, p.w16, *lowrank, p.bias, out_fp32)
         if self.check_device_errors:
             _lib.raise_on_device_error(f"SVDQuantLinear {tuple(self.original_shape)}")
         return y.reshape(*lead, n)

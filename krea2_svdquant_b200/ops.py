@@ -251,3 +251,57 @@ def linear_gemm(a16: Tensor, w16: Tensor, mid_hl: Optional[Tensor], up_hl: Optio
 @linear_gemm.register_fake
 def _(a16, w16, mid_hl, up_hl, bias, out_fp32):
     return a16.new_empty((a16.shape[0], w16.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
+
+
+# --------------------------------------------------------------------------- packed-weight GEMM
+@torch.library.custom_op("svdq_b200::prepare_packed", mutates_args=())
+def prepare_packed(qweight: Tensor, scales: Tensor, w_group: int) -> tuple[Tensor, Tensor, Tensor]:
+    """Checkpoint INT4 weight -> the packed-weight GEMM's operands: ``codes [N, K_pad/2]`` u8 in the
+    kernel's nibble order, ``scales16 [N, K_pad/w_group]`` fp16, and a one-element int32 flag that is
+    1 when some scale (or its sixteenth) is not an fp16 value (the GEMM's weights then differ from
+    ``repack_weight``'s by one more rounding of the scale)."""
+    _need_cuda("prepare_packed", qweight, scales)
+    _need(qweight.dtype == torch.uint8 and qweight.dim() == 2 and qweight.is_contiguous(),
+          "prepare_packed: qweight must be contiguous uint8 [N, K_pad/2]")
+    _need(scales.dtype in _DT and scales.is_contiguous(), "prepare_packed: scales must be contiguous bf16/fp16/fp32")
+    n, k_pad = qweight.shape[0], qweight.shape[1] * 2
+    codes = torch.empty_like(qweight)
+    scales16 = torch.empty((n, k_pad // w_group), dtype=torch.float16, device=qweight.device)
+    flag = torch.zeros((1,), dtype=torch.int32, device=qweight.device)
+    _lib.call("svdq_prepare_packed", _p(qweight), _p(scales), _DT[scales.dtype], n, k_pad, w_group, _p(codes),
+              _p(scales16), _p(flag), _stream(qweight.device))
+    return codes, scales16, flag
+
+
+@prepare_packed.register_fake
+def _(qweight, scales, w_group):
+    n, k_pad = qweight.shape[0], qweight.shape[1] * 2
+    return (torch.empty_like(qweight), qweight.new_empty((n, k_pad // w_group), dtype=torch.float16),
+            qweight.new_empty((1,), dtype=torch.int32))
+
+
+@torch.library.custom_op("svdq_b200::packed_gemm", mutates_args=())
+def packed_gemm(a16: Tensor, codes: Tensor, scales16: Tensor, w_group: int, mid_hl: Optional[Tensor],
+                up_hl: Optional[Tensor], bias: Optional[Tensor], out_fp32: bool) -> Tensor:
+    """``a16 @ (q * s)^T + mid_hl @ up_hl^T + bias`` with the weight read as packed codes and converted
+    to fp16 in shared memory (tcgen05, fp32 accumulation)."""
+    _need_cuda("packed_gemm", a16, codes, scales16, mid_hl, up_hl, bias)
+    _need(a16.dtype == torch.float16 and a16.is_contiguous(), "packed_gemm: a16 must be contiguous fp16")
+    _need(codes.dtype == torch.uint8 and scales16.dtype == torch.float16, "packed_gemm: codes u8, scales16 fp16")
+    m, k_pad = a16.shape
+    n = codes.shape[0]
+    _need(codes.shape[1] * 2 == k_pad, "packed_gemm: activation / weight K mismatch")
+    r2 = 0 if mid_hl is None or mid_hl.numel() == 0 else mid_hl.shape[1]
+    _need(r2 == 0 or (up_hl is not None and tuple(up_hl.shape) == (n, r2)), "packed_gemm: up_hl shape mismatch")
+    out = torch.empty((m, n), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=a16.device)
+    if m == 0:
+        return out
+    _lib.call("svdq_packed_gemm", _p(a16), _p(codes), _p(scales16), w_group, _p(mid_hl) if r2 else None,
+              _p(up_hl) if r2 else None, r2, _p(bias), _p(out), _lib.SVDQ_FP32 if out_fp32 else _lib.SVDQ_BF16,
+              out.stride(0), m, n, k_pad, _stream(a16.device))
+    return out
+
+
+@packed_gemm.register_fake
+def _(a16, codes, scales16, w_group, mid_hl, up_hl, bias, out_fp32):
+    return a16.new_empty((a16.shape[0], codes.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
