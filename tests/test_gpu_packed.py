@@ -61,7 +61,7 @@ def test_prepare_packed_layout():
     assert np.array_equal(codes.cpu().numpy(), _native_order_np(st.qweight.cpu().numpy()))
     assert torch.equal(s16.float(), st.weight_scales.float())
     assert int(flag.item()) == 0
-    st.weight_scales[0, 0] = 1e-4  # a scale whose sixteenth is not an fp16 value
+    st.weight_scales[0, 0] = 1.1e-4  # bf16 value 0.000110149...: its sixteenth is not an fp16 value
     _, _, flag = ops.prepare_packed(st.qweight, st.weight_scales, 64)
     assert int(flag.item()) == 1
 
