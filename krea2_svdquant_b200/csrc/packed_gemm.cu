@@ -3,13 +3,20 @@
 //   out[m, n] = sum_k a16[m,k] * (q_w[n,k] * s_w[n, k/G]) + sum_j mid_hl[m,j] up_hl[n,j] + bias[n]
 //
 // The INT4 weight stays packed in HBM (half a byte per weight, the checkpoint's size): each CTA
-// streams its rows' codes with TMA and converts them to fp16 in shared memory, where the tensor
-// core reads them.  No fp16 copy of the weight exists, so a layer costs its packed bytes in memory,
-// and a small batch reads 4x fewer weight bytes than a kernel over a dequantized weight.
+// streams its rows' codes with TMA, converts them to fp16 in registers and stores them into tensor
+// memory, where the tensor core reads its A operand.  No fp16 copy of the weight exists, so a layer
+// costs its packed bytes in memory, and a small batch reads 4x fewer weight bytes than a kernel
+// over a dequantized weight.
 //
 // Orientation (swap AB): the weight rows are the MMA's M (128 TMEM lanes per CTA) and the tokens
 // its N (TN columns, 16 to 128), so 16 tokens cost a 128x16 MMA instead of most of a 128x256 tile.
-// The result tile lands in TMEM as [weight row][token] and leaves transposed.
+// The accumulator lands in TMEM as [weight row][token] and leaves transposed.
+//
+// Tensor memory holds the accumulator (columns [0, TN)) and a ring of converted weight stages
+// (32 columns = 64 fp16 of K per row each): 12 to 15 stages deep, so the conversion runs well
+// ahead of the MMAs and no stage waits for a full convert -> MMA -> release round trip.  A
+// converter thread owns one weight row (its TMEM lane) and half of a stage's K; tcgen05.st moves
+// its 32 fp16 values straight from registers to its lane, so the weights never touch shared memory.
 //
 // Conversion.  The load-time preparation (svdq_prepare_packed) reorders the nibbles of each 32-bit
 // word to [k0 k2 k4 k6 | k1 k3 k5 k7] (low half-word holds the even k), so one AND/OR per pair puts
@@ -19,15 +26,18 @@
 // q * s has at most 3 + 8 significant bits for a bf16-valued scale, so it is exact in fp16, and
 // equals the load-time fp16 operand of the other GEMM bit for bit.  13 instructions per 8 weights.
 //
+// Low-rank stages (mid_hl x up_hl, bf16) take their A operand from shared memory (TMA), as the
+// other GEMM does.
+//
 // Split K.  When the tiles would leave SMs idle, a cluster of KS CTAs (KS in {1, 2, 4, 8}) shares a
 // tile, each taking one contiguous K range; the last one also takes the low-rank stages.  Each
 // CTA parks its fp32 partial in its own shared memory, and after a cluster barrier each CTA sums
 // one slice of rows over all KS partials through distributed shared memory, in rank order (a
 // fixed order: results are deterministic), adds the bias and stores.
 //
-// Roles (12 warps): warp 0 TMA of packed codes (8-deep ring of 128 rows x 64 k); warp 2 TMA of
-// the token tile (a16, or mid_hl with up_hl for the low-rank stages; 4-deep ring); warp 1 TMEM
-// allocation and the MMA issue; warps 4-11 conversion into the A ring; warps 4-7 the epilogue.
+// Roles (12 warps): warp 0 TMA of packed codes (16-deep ring of 128 rows x 64 k); warp 2 TMA of
+// the token tiles (a16, or mid_hl with up_hl for the low-rank stages); warp 1 TMEM allocation and
+// the MMA issue; warps 4-11 conversion (two warps per TMEM lane quarter); warps 4-7 the epilogue.
 // Every wait is bounded (error word codes 0x51xx-0x54xx); a wait that runs out raises the CTA's
 // abort flag and every role leaves its loop, so all CTAs still meet at the cluster barriers.
 #include <algorithm>
@@ -37,39 +47,47 @@
 namespace svdq {
 namespace {
 
-constexpr int PW_ROWS = 128;                          // weight rows per CTA
+constexpr int PW_ROWS = 128;                          // weight rows per CTA (TMEM lanes)
 constexpr int PW_KB = 64;                             // k per stage
-constexpr int PW_PSTAGES = 8;                         // packed-code ring
-constexpr int PW_ASTAGES = 4;                         // operand ring
+constexpr int PW_PSTAGES = 16;                        // packed-code ring (shared memory)
+constexpr int PW_LSTAGES = 2;                         // low-rank A ring (shared memory)
 constexpr uint32_t PW_P_BYTES = PW_ROWS * PW_KB / 2;  // 4 KiB of codes
-constexpr uint32_t PW_A_BYTES = PW_ROWS * PW_KB * 2;  // 16 KiB of fp16 weights
+constexpr uint32_t PW_A_BYTES = PW_ROWS * PW_KB * 2;  // 16 KiB: a low-rank A stage
 constexpr int PW_CONV_WARPS = 8;
 constexpr int PW_THREADS = 32 * (4 + PW_CONV_WARPS);
+constexpr uint32_t PW_TMEM_COLS = 512;
+constexpr uint32_t PW_STAGE_COLS = PW_KB / 2;         // TMEM columns of one converted stage
 static_assert(PW_CONV_WARPS * 32 * 16 == (int)PW_P_BYTES, "one 16-byte piece of codes per converter thread");
 
 template <int TN>
 struct PwLayout {
-  static constexpr uint32_t kB = (uint32_t)TN * PW_KB * 2;  // token tile bytes per stage
-  static constexpr uint32_t kOffB = PW_ASTAGES * PW_A_BYTES;
-  static constexpr uint32_t kOffP = kOffB + PW_ASTAGES * kB;
+  static constexpr uint32_t kAccCols = TN < 32 ? 32 : TN;                     // accumulator columns
+  static constexpr int kAStages = std::min<int>(12, (PW_TMEM_COLS - kAccCols) / PW_STAGE_COLS);
+  static constexpr uint32_t kB = (uint32_t)TN * PW_KB * 2;                    // token tile bytes per stage
+  static constexpr int kBStages = kB <= 2048 ? 16 : kB <= 4096 ? 12 : 6;
+  static constexpr uint32_t kOffL = 0;                                        // low-rank A ring
+  static constexpr uint32_t kOffB = kOffL + PW_LSTAGES * PW_A_BYTES;
+  static constexpr uint32_t kOffP = kOffB + kBStages * kB;
   static constexpr uint32_t kOffBar = kOffP + PW_PSTAGES * PW_P_BYTES;
-  static constexpr uint32_t kSmem = kOffBar + 256 + 1024;   // barriers + alignment slack
-  static constexpr uint32_t kTmemCols = TN < 32 ? 32 : TN;
+  static constexpr uint32_t kSmem = kOffBar + 1024 + 1024;                   // barriers + alignment slack
   static_assert(kB % 1024 == 0, "token tiles keep 1 KiB alignment for the 128-byte swizzle");
-  static_assert((uint32_t)PW_ROWS * TN * 4 <= PW_ASTAGES * PW_A_BYTES, "split-K partial fits the A ring");
+  static_assert((uint32_t)PW_ROWS * TN * 4 <= kOffP, "split-K partial fits over the low-rank and token rings");
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
 };
 
 struct PwBars {
   uint64_t full_p[PW_PSTAGES];   // codes landed (TMA bytes)
   uint64_t empty_p[PW_PSTAGES];  // codes read (one arrival per converter warp)
-  uint64_t full_ab[PW_ASTAGES];  // token tile (and low-rank A) landed (TMA bytes)
-  uint64_t conv[PW_ASTAGES];     // A stage written (one arrival per converter warp)
-  uint64_t empty_ab[PW_ASTAGES]; // MMAs of the stage done (commit)
+  uint64_t full_b[16];           // token tile (and, for a low-rank stage, its A) landed (TMA bytes)
+  uint64_t empty_b[16];          // MMAs reading the token slot done (commit)
+  uint64_t conv[12];             // TMEM weight stage written (one arrival per converter warp)
+  uint64_t empty_a[12];          // MMAs reading the TMEM weight stage done (commit)
+  uint64_t empty_l[PW_LSTAGES];  // MMAs reading the low-rank A slot done (commit)
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
 };
-static_assert(sizeof(PwBars) <= 256, "barrier block");
+static_assert(sizeof(PwBars) <= 1024, "barrier block");
 
 struct PwArgs {
   const __half* scales16;  // [N, nG] fp16 group scales
@@ -87,9 +105,10 @@ struct PwArgs {
 enum : int {
   kPwWaitPackedEmpty = 0x5101,
   kPwWaitTileEmpty = 0x5102,
+  kPwWaitLowrankEmpty = 0x5103,
   kPwWaitConvPacked = 0x5201,
   kPwWaitConvEmpty = 0x5202,
-  kPwWaitMmaFull = 0x5301,
+  kPwWaitMmaTile = 0x5301,
   kPwWaitMmaConv = 0x5302,
   kPwWaitMmaDrain = 0x5303,
   kPwWaitEpilogue = 0x5401,
@@ -110,9 +129,6 @@ __device__ __forceinline__ uint4 ld_shared_u4(uint32_t addr) {
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
-__device__ __forceinline__ void st_shared_u4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
@@ -123,32 +139,31 @@ __device__ __forceinline__ void mbar_arrive_cta(uint32_t bar) {
 }
 
 // Eight codes of one native-order word -> four fp16x2 pairs (k0 k1, k2 k3, k4 k5, k6 k7), exact.
-__device__ __forceinline__ uint4 convert_word(uint32_t w, uint32_t s_lo, uint32_t s_hi) {
-  constexpr uint32_t kExp = 0x64006400u;  // fp16x2 {1024, 1024}
+__device__ __forceinline__ void convert_word(uint32_t w, uint32_t s_lo, uint32_t s_hi, uint32_t* o) {
+  constexpr uint32_t kExp = 0x64006400u;    // fp16x2 {1024, 1024}
   constexpr uint32_t kOffLo = 0x64086408u;  // {1032, 1032}: 1024 + the nibble offset 8
   constexpr uint32_t kOffHi = 0x64806480u;  // {1152, 1152}: 1024 + 16 * 8
   const uint32_t w8 = w >> 8;
-  uint4 o;
-  o.x = h2_mul(h2_sub((w & 0x000F000Fu) | kExp, kOffLo), s_lo);
-  o.y = h2_mul(h2_sub((w & 0x00F000F0u) | kExp, kOffHi), s_hi);
-  o.z = h2_mul(h2_sub((w8 & 0x000F000Fu) | kExp, kOffLo), s_lo);
-  o.w = h2_mul(h2_sub((w8 & 0x00F000F0u) | kExp, kOffHi), s_hi);
-  return o;
+  o[0] = h2_mul(h2_sub((w & 0x000F000Fu) | kExp, kOffLo), s_lo);
+  o[1] = h2_mul(h2_sub((w & 0x00F000F0u) | kExp, kOffHi), s_hi);
+  o[2] = h2_mul(h2_sub((w8 & 0x000F000Fu) | kExp, kOffLo), s_lo);
+  o[3] = h2_mul(h2_sub((w8 & 0x00F000F0u) | kExp, kOffHi), s_hi);
 }
 
 template <int TN, bool OUT_F32>
-__global__ void __launch_bounds__(PW_THREADS, TN <= 32 ? 2 : 1)
+__global__ void __launch_bounds__(PW_THREADS, 1)
     packed_gemm_kernel(const __grid_constant__ CUtensorMap tm_a16, const __grid_constant__ CUtensorMap tm_codes,
                        const __grid_constant__ CUtensorMap tm_mid, const __grid_constant__ CUtensorMap tm_up,
                        const PwArgs args) {
   using L = PwLayout<TN>;
+  constexpr int AS = L::kAStages, BS = L::kBStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   PwBars* bars = reinterpret_cast<PwBars*>(gbase + L::kOffBar);
   volatile int* abort_flag = &bars->abort_flag;
-  const uint32_t a_ring = base, b_ring = base + L::kOffB, p_ring = base + L::kOffP;
+  const uint32_t l_ring = base + L::kOffL, b_ring = base + L::kOffB, p_ring = base + L::kOffP;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ks = args.ks;
@@ -167,11 +182,15 @@ __global__ void __launch_bounds__(PW_THREADS, TN <= 32 ? 2 : 1)
       mbar_init(bar(bars->full_p[s]), 1);
       mbar_init(bar(bars->empty_p[s]), PW_CONV_WARPS);
     }
-    for (int s = 0; s < PW_ASTAGES; ++s) {
-      mbar_init(bar(bars->full_ab[s]), 1);
-      mbar_init(bar(bars->conv[s]), PW_CONV_WARPS);
-      mbar_init(bar(bars->empty_ab[s]), 1);
+    for (int s = 0; s < BS; ++s) {
+      mbar_init(bar(bars->full_b[s]), 1);
+      mbar_init(bar(bars->empty_b[s]), 1);
     }
+    for (int s = 0; s < AS; ++s) {
+      mbar_init(bar(bars->conv[s]), PW_CONV_WARPS);
+      mbar_init(bar(bars->empty_a[s]), 1);
+    }
+    for (int s = 0; s < PW_LSTAGES; ++s) mbar_init(bar(bars->empty_l[s]), 1);
     mbar_init(bar(bars->mma_done), 1);
     bars->abort_flag = 0;
     fence_mbar_init();
@@ -185,7 +204,7 @@ __global__ void __launch_bounds__(PW_THREADS, TN <= 32 ? 2 : 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc_1(smem_u32(&bars->tmem_base), L::kTmemCols);
+    tmem_alloc_1(smem_u32(&bars->tmem_base), PW_TMEM_COLS);
     tmem_relinquish_1();
   }
   tc_fence_before();
@@ -219,26 +238,28 @@ __global__ void __launch_bounds__(PW_THREADS, TN <= 32 ? 2 : 1)
       uint32_t filled = 0, par = 0;
       bool ok = true;
       for (int it = 0; it < iters && ok; ++it) {
-        const int s = it % PW_ASTAGES;
-        const uint32_t ph = (uint32_t)(it / PW_ASTAGES) & 1u;
-        if (!(ok = mbar_wait(bar(bars->empty_ab[s]), ph ^ 1u, abort_flag, args.err, kPwWaitTileEmpty))) break;
-        const uint32_t fb = bar(bars->full_ab[s]);
+        const int s = it % BS;
+        const uint32_t ph = (uint32_t)(it / BS) & 1u;
+        if (!(ok = mbar_wait(bar(bars->empty_b[s]), ph ^ 1u, abort_flag, args.err, kPwWaitTileEmpty))) break;
+        const uint32_t fb = bar(bars->full_b[s]);
         const uint32_t bdst = b_ring + (uint32_t)s * L::kB;
         if (it < n_res) {
           mbar_arrive_expect_tx(fb, L::kB);
           tma_load_2d(bdst, &tm_a16, fb, (kb0 + it) * PW_KB, m0);
         } else {
-          const int j = it - n_res;
+          const int j = it - n_res, ls = j % PW_LSTAGES;
+          const uint32_t lph = (uint32_t)(j / PW_LSTAGES) & 1u;
+          if (!(ok = mbar_wait(bar(bars->empty_l[ls]), lph ^ 1u, abort_flag, args.err, kPwWaitLowrankEmpty))) break;
           mbar_arrive_expect_tx(fb, L::kB + PW_A_BYTES);
-          tma_load_2d(a_ring + (uint32_t)s * PW_A_BYTES, &tm_up, fb, j * PW_KB, n0);
+          tma_load_2d(l_ring + (uint32_t)ls * PW_A_BYTES, &tm_up, fb, j * PW_KB, n0);
           tma_load_2d(bdst, &tm_mid, fb, j * PW_KB, m0);
         }
         filled |= 1u << s;
         par = (par & ~(1u << s)) | (ph << s);
       }
       if (!ok)
-        for (int s = 0; s < PW_ASTAGES; ++s)
-          if (filled & (1u << s)) mbar_wait_drain(bar(bars->full_ab[s]), (par >> s) & 1u, 100000000ull);
+        for (int s = 0; s < BS; ++s)
+          if (filled & (1u << s)) mbar_wait_drain(bar(bars->full_b[s]), (par >> s) & 1u, 100000000ull);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -247,18 +268,31 @@ __global__ void __launch_bounds__(PW_THREADS, TN <= 32 ? 2 : 1)
       const uint32_t idesc_lr = make_idesc(kFmtBF16, kFmtBF16, PW_ROWS, TN);
       bool ok = true;
       for (int it = 0; it < iters && ok; ++it) {
-        const int s = it % PW_ASTAGES;
-        const uint32_t ph = (uint32_t)(it / PW_ASTAGES) & 1u;
-        if (!(ok = mbar_wait(bar(bars->full_ab[s]), ph, abort_flag, args.err, kPwWaitMmaFull))) break;
-        if (!(ok = mbar_wait(bar(bars->conv[s]), ph, abort_flag, args.err, kPwWaitMmaConv))) break;
-        tc_fence_after();
-        const uint64_t da = desc_k_sw128(a_ring + (uint32_t)s * PW_A_BYTES);
-        const uint64_t db = desc_k_sw128(b_ring + (uint32_t)s * L::kB);
-        const uint32_t idesc = it < n_res ? idesc_res : idesc_lr;
+        const int bs = it % BS;
+        const uint32_t bph = (uint32_t)(it / BS) & 1u;
+        if (!(ok = mbar_wait(bar(bars->full_b[bs]), bph, abort_flag, args.err, kPwWaitMmaTile))) break;
+        const uint64_t db = desc_k_sw128(b_ring + (uint32_t)bs * L::kB);
+        if (it < n_res) {
+          const int as = it % AS;
+          if (!(ok = mbar_wait(bar(bars->conv[as]), (uint32_t)(it / AS) & 1u, abort_flag, args.err, kPwWaitMmaConv)))
+            break;
+          tc_fence_after();
+          const uint32_t ta = tmem + L::kAccCols + (uint32_t)as * PW_STAGE_COLS;
 #pragma unroll
-        for (int kk = 0; kk < PW_KB / 16; ++kk)
-          umma_f16_1(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (it > 0 || kk > 0) ? 1u : 0u);
-        umma_commit_1(bar(bars->empty_ab[s]));
+          for (int kk = 0; kk < PW_KB / 16; ++kk)
+            umma_f16_1_tmem_a(tmem, ta + (uint32_t)(kk * 8), db + (uint64_t)(kk * 2), idesc_res,
+                              (it > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_1(bar(bars->empty_a[as]));
+        } else {
+          const int ls = (it - n_res) % PW_LSTAGES;
+          tc_fence_after();
+          const uint64_t da = desc_k_sw128(l_ring + (uint32_t)ls * PW_A_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < PW_KB / 16; ++kk)
+            umma_f16_1(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc_lr, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_1(bar(bars->empty_l[ls]));
+        }
+        umma_commit_1(bar(bars->empty_b[bs]));
       }
       // the epilogue reads the accumulator after every issued MMA has completed; this thread also
       // waits for that, so no MMA is in flight when the CTA frees TMEM or exits
@@ -270,63 +304,54 @@ __global__ void __launch_bounds__(PW_THREADS, TN <= 32 ? 2 : 1)
       if (!ok) *abort_flag = 1;
     }
   } else if (warp >= 4) {
-    // ------------------------------------------------ conversion: codes -> fp16 A stages
-    const int ct = threadIdx.x - 128;  // 0 .. 255
-    const int row = ct >> 1, half = ct & 1;
+    // ------------------------------------------------ conversion: codes -> fp16 weights in TMEM
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int half = (warp - 4) >> 2;  // which 32 of a stage's 64 k
+    const int row = q * 32 + lane;
     const int n_row = n0 + row;
-    const uint32_t a_row = (uint32_t)row * 128u;
-    const uint32_t r7 = (uint32_t)(row & 7);
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const uint32_t code_off = (uint32_t)row * (PW_KB / 2) + 16u * (uint32_t)half;
     const __half* srow = args.scales16 + (int64_t)min(n_row, args.N - 1) * args.nG;
     bool ok = true;
-    for (int it = 0; it < iters && ok; ++it) {
-      const int s = it % PW_ASTAGES;
-      const uint32_t ph = (uint32_t)(it / PW_ASTAGES) & 1u;
-      if (it < n_res) {
-        const int kb = kb0 + it;
-        const int ps = it % PW_PSTAGES;
-        const uint32_t pph = (uint32_t)(it / PW_PSTAGES) & 1u;
-        const uint32_t sbits = n_row < args.N ? (uint32_t)__half_as_ushort(srow[(kb * PW_KB + 32 * half) / args.w_group])
-                                              : 0u;
-        ok = mbar_wait(bar(bars->empty_ab[s]), ph ^ 1u, abort_flag, args.err, kPwWaitConvEmpty) &&
-             mbar_wait(bar(bars->full_p[ps]), pph, abort_flag, args.err, kPwWaitConvPacked);
-        if (!(ok = __all_sync(0xffffffffu, ok))) break;  // the lanes of a warp leave together
-        const uint4 pk = ld_shared_u4(p_ring + (uint32_t)ps * PW_P_BYTES + (uint32_t)ct * 16u);
-        const uint32_t s_lo = sbits | (sbits << 16);
-        const uint32_t s16 = (uint32_t)__half_as_ushort(__hmul(__ushort_as_half((unsigned short)sbits),
-                                                               __float2half_rn(0.0625f)));
-        const uint32_t s_hi = s16 | (s16 << 16);
-        const uint32_t dst = a_ring + (uint32_t)s * PW_A_BYTES + a_row;
-        const uint32_t words[4] = {pk.x, pk.y, pk.z, pk.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint4 o = convert_word(words[j], s_lo, s_hi);
-          st_shared_u4(dst + ((((uint32_t)(4 * half + j)) ^ r7) << 4), o.x, o.y, o.z, o.w);
-        }
-        fence_proxy_async_smem();  // the tensor core (async proxy) reads what these stores wrote
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_cta(bar(bars->empty_p[ps]));
-          mbar_arrive_cta(bar(bars->conv[s]));
-        }
-      } else {
-        // low-rank stage: its A rows come by TMA; the converters only keep the stage's count
-        ok = mbar_wait(bar(bars->empty_ab[s]), ph ^ 1u, abort_flag, args.err, kPwWaitConvEmpty);
-        if (!(ok = __all_sync(0xffffffffu, ok))) break;
-        if (lane == 0) mbar_arrive_cta(bar(bars->conv[s]));
-      }
+    for (int it = 0; it < n_res && ok; ++it) {
+      const int kb = kb0 + it;
+      const int ps = it % PW_PSTAGES, as = it % AS;
+      const uint32_t sbits = n_row < args.N ? (uint32_t)__half_as_ushort(srow[(kb * PW_KB + 32 * half) / args.w_group])
+                                            : 0u;
+      ok = mbar_wait(bar(bars->full_p[ps]), (uint32_t)(it / PW_PSTAGES) & 1u, abort_flag, args.err, kPwWaitConvPacked);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;  // the lanes of a warp leave together
+      const uint4 pk = ld_shared_u4(p_ring + (uint32_t)ps * PW_P_BYTES + code_off);
+      const uint32_t s_lo = sbits | (sbits << 16);
+      const uint32_t s16 = (uint32_t)__half_as_ushort(__hmul(__ushort_as_half((unsigned short)sbits),
+                                                             __float2half_rn(0.0625f)));
+      const uint32_t s_hi = s16 | (s16 << 16);
+      uint32_t v[16];
+      convert_word(pk.x, s_lo, s_hi, v);
+      convert_word(pk.y, s_lo, s_hi, v + 4);
+      convert_word(pk.z, s_lo, s_hi, v + 8);
+      convert_word(pk.w, s_lo, s_hi, v + 12);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(bar(bars->empty_p[ps]));  // every lane has consumed its codes
+      ok = mbar_wait(bar(bars->empty_a[as]), ((uint32_t)(it / AS) & 1u) ^ 1u, abort_flag, args.err, kPwWaitConvEmpty);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      tc_fence_after();
+      tmem_st16(tmem + lane_off + L::kAccCols + (uint32_t)as * PW_STAGE_COLS + 16u * (uint32_t)half, v);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(bar(bars->conv[as]));
     }
     if (warp < 8) {
       // ---------------------------------------------- epilogue: TMEM -> registers -> out or partial
-      const int q = warp & 3;
       const int erow = q * 32 + lane;
       const int n = n0 + erow;
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+      const uint32_t taddr = tmem + lane_off;
       const bool done = mbar_wait(bar(bars->mma_done), 0, abort_flag, args.err, kPwWaitEpilogue) && !*abort_flag;
       if (__all_sync(0xffffffffu, done)) {
         tc_fence_after();
         float bias_v = 0.f;
         if (ks == 1 && args.bias && n < args.N) bias_v = __bfloat162float(args.bias[n]);
-        float* part = reinterpret_cast<float*>(gbase);  // [TN][128] over the A ring (all MMAs are done)
+        float* part = reinterpret_cast<float*>(gbase);  // [TN][128] over the low-rank/token rings (all MMAs are done)
 #pragma unroll 1
         for (int c0 = 0; c0 < TN; c0 += 16) {
           uint32_t v[16];
@@ -375,7 +400,7 @@ __global__ void __launch_bounds__(PW_THREADS, TN <= 32 ? 2 : 1)
   }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_1(tmem, L::kTmemCols);
+    tmem_dealloc_1(tmem, PW_TMEM_COLS);
   }
 }
 
@@ -417,16 +442,8 @@ __global__ void prepare_scales_kernel(const T* __restrict__ in, __half* __restri
   if (__syncthreads_or(bad) && threadIdx.x == 0 && inexact) atomicExch(inexact, 1);
 }
 
-int pw_ctas_per_sm(uint32_t smem) {
-  int dev = 0, per_sm = 0, reserved = 0;
-  cudaGetDevice(&dev);
-  if (cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess || per_sm <= 0)
-    per_sm = 233472;
-  if (cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess || reserved < 0)
-    reserved = 1024;
-  (void)cudaGetLastError();
-  return std::max(1, std::min(2, per_sm / (int)(smem + (uint32_t)reserved)));
-}
+// One CTA per SM: each allocates all 512 TMEM columns.
+int pw_ctas_per_sm(uint32_t) { return 1; }
 
 struct PwPlan {
   int tn, ks, units_n, units_m;
