@@ -35,11 +35,14 @@
 // one slice of rows over all KS partials through distributed shared memory, in rank order (a
 // fixed order: results are deterministic), adds the bias and stores.
 //
-// Roles (12 warps): warp 0 TMA of packed codes (16-deep ring of 128 rows x 64 k); warp 2 TMA of
+// Roles (12 warps): warp 0 TMA of packed codes (4-deep ring of 128 rows x 256 k groups, 128-byte
+// swizzle so the converters' shared loads are free of bank conflicts); warp 2 TMA of
 // the token tiles (a16, or mid_hl with up_hl for the low-rank stages); warp 1 TMEM allocation and
 // the MMA issue; warps 4-11 conversion (two warps per TMEM lane quarter); warps 4-7 the epilogue.
-// Every wait is bounded (error word codes 0x51xx-0x54xx); a wait that runs out raises the CTA's
-// abort flag and every role leaves its loop, so all CTAs still meet at the cluster barriers.
+// Waits spin on mbarrier.test_wait (a blocking try_wait costs a fraction of a microsecond even on a
+// completed phase, more than a stage here) and are bounded (error word codes 0x51xx-0x54xx); a wait
+// that runs out raises the CTA's abort flag and every role leaves its loop, so all CTAs still meet
+// at the cluster barriers.
 #include <algorithm>
 
 #include "svdq_common.cuh"
@@ -49,20 +52,21 @@ namespace {
 
 constexpr int PW_ROWS = 128;                          // weight rows per CTA (TMEM lanes)
 constexpr int PW_KB = 64;                             // k per stage
-constexpr int PW_PSTAGES = 16;                        // packed-code ring (shared memory)
+constexpr int PW_SUB = 4;                             // 64-k stages per code group (one TMA box)
+constexpr int PW_PSTAGES = 4;                         // code-group ring (shared memory)
 constexpr int PW_LSTAGES = 2;                         // low-rank A ring (shared memory)
-constexpr uint32_t PW_P_BYTES = PW_ROWS * PW_KB / 2;  // 4 KiB of codes
+constexpr uint32_t PW_P_BYTES = PW_ROWS * PW_SUB * PW_KB / 2;  // 16 KiB of codes: 128 rows x 128 bytes
 constexpr uint32_t PW_A_BYTES = PW_ROWS * PW_KB * 2;  // 16 KiB: a low-rank A stage
 constexpr int PW_CONV_WARPS = 8;
 constexpr int PW_THREADS = 32 * (4 + PW_CONV_WARPS);
 constexpr uint32_t PW_TMEM_COLS = 512;
 constexpr uint32_t PW_STAGE_COLS = PW_KB / 2;         // TMEM columns of one converted stage
-static_assert(PW_CONV_WARPS * 32 * 16 == (int)PW_P_BYTES, "one 16-byte piece of codes per converter thread");
+static_assert(PW_CONV_WARPS * 32 * 16 * PW_SUB == (int)PW_P_BYTES, "four 16-byte pieces of codes per converter thread");
 
 template <int TN>
 struct PwLayout {
   static constexpr uint32_t kAccCols = TN < 32 ? 32 : TN;                     // accumulator columns
-  static constexpr int kAStages = std::min<int>(12, (PW_TMEM_COLS - kAccCols) / PW_STAGE_COLS);
+  static constexpr int kAStages = std::min<int>(12, (PW_TMEM_COLS - kAccCols) / PW_STAGE_COLS) / PW_SUB * PW_SUB;
   static constexpr uint32_t kB = (uint32_t)TN * PW_KB * 2;                    // token tile bytes per stage
   static constexpr int kBStages = kB <= 2048 ? 16 : kB <= 4096 ? 12 : 6;
   static constexpr uint32_t kOffL = 0;                                        // low-rank A ring
@@ -71,13 +75,14 @@ struct PwLayout {
   static constexpr uint32_t kOffBar = kOffP + PW_PSTAGES * PW_P_BYTES;
   static constexpr uint32_t kSmem = kOffBar + 1024 + 1024;                   // barriers + alignment slack
   static_assert(kB % 1024 == 0, "token tiles keep 1 KiB alignment for the 128-byte swizzle");
+  static_assert(kAStages >= 2 * PW_SUB, "the TMEM weight ring holds at least two code groups");
   static_assert((uint32_t)PW_ROWS * TN * 4 <= kOffP, "split-K partial fits over the low-rank and token rings");
   static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
 };
 
 struct PwBars {
-  uint64_t full_p[PW_PSTAGES];   // codes landed (TMA bytes)
-  uint64_t empty_p[PW_PSTAGES];  // codes read (one arrival per converter warp)
+  uint64_t full_p[PW_PSTAGES];   // code group landed (TMA bytes)
+  uint64_t empty_p[PW_PSTAGES];  // code group read (one arrival per converter warp)
   uint64_t full_b[16];           // token tile (and, for a low-rank stage, its A) landed (TMA bytes)
   uint64_t empty_b[16];          // MMAs reading the token slot done (commit)
   uint64_t conv[12];             // TMEM weight stage written (one arrival per converter warp)
@@ -171,8 +176,12 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
   const int unit = (int)(blockIdx.x / (unsigned)ks);
   const int nb = unit % args.units_n, mb = unit / args.units_n;
   const int n0 = nb * PW_ROWS, m0 = mb * TN;
-  const int kb0 = (int)((int64_t)crank * args.n_k / ks), kb1 = (int)((int64_t)(crank + 1) * args.n_k / ks);
+  // K ranges are whole code groups (4 stages of 64 k); only the layer's last group may be short
+  const int n_grp = (args.n_k + PW_SUB - 1) / PW_SUB;
+  const int g0 = (int)((int64_t)crank * n_grp / ks), g1 = (int)((int64_t)(crank + 1) * n_grp / ks);
+  const int kb0 = g0 * PW_SUB, kb1 = min(g1 * PW_SUB, args.n_k);
   const int n_res = kb1 - kb0;
+  const int n_groups = g1 - g0;
   const int iters = n_res + (crank == ks - 1 ? args.n_lr : 0);
 
   auto bar = [&](const uint64_t& b) { return smem_u32(&b); };
@@ -216,15 +225,16 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ------------------------------------------------ packed codes (residual stages only)
+      // ------------------------------------------------ packed codes: one 128-row x 256-k group per box
       uint32_t filled = 0, par = 0;
       bool ok = true;
-      for (int it = 0; it < n_res && ok; ++it) {
+      for (int it = 0; it < n_groups && ok; ++it) {
         const int s = it % PW_PSTAGES;
         const uint32_t ph = (uint32_t)(it / PW_PSTAGES) & 1u;
-        if (!(ok = mbar_wait(bar(bars->empty_p[s]), ph ^ 1u, abort_flag, args.err, kPwWaitPackedEmpty))) break;
+        if (!(ok = mbar_spin_wait(bar(bars->empty_p[s]), ph ^ 1u, abort_flag, args.err, kPwWaitPackedEmpty))) break;
         mbar_arrive_expect_tx(bar(bars->full_p[s]), PW_P_BYTES);
-        tma_load_2d(p_ring + (uint32_t)s * PW_P_BYTES, &tm_codes, bar(bars->full_p[s]), (kb0 + it) * (PW_KB / 2), n0);
+        tma_load_2d(p_ring + (uint32_t)s * PW_P_BYTES, &tm_codes, bar(bars->full_p[s]), (g0 + it) * (PW_SUB * PW_KB / 2),
+                    n0);
         filled |= 1u << s;
         par = (par & ~(1u << s)) | (ph << s);
       }
@@ -240,7 +250,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
       for (int it = 0; it < iters && ok; ++it) {
         const int s = it % BS;
         const uint32_t ph = (uint32_t)(it / BS) & 1u;
-        if (!(ok = mbar_wait(bar(bars->empty_b[s]), ph ^ 1u, abort_flag, args.err, kPwWaitTileEmpty))) break;
+        if (!(ok = mbar_spin_wait(bar(bars->empty_b[s]), ph ^ 1u, abort_flag, args.err, kPwWaitTileEmpty))) break;
         const uint32_t fb = bar(bars->full_b[s]);
         const uint32_t bdst = b_ring + (uint32_t)s * L::kB;
         if (it < n_res) {
@@ -249,7 +259,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
         } else {
           const int j = it - n_res, ls = j % PW_LSTAGES;
           const uint32_t lph = (uint32_t)(j / PW_LSTAGES) & 1u;
-          if (!(ok = mbar_wait(bar(bars->empty_l[ls]), lph ^ 1u, abort_flag, args.err, kPwWaitLowrankEmpty))) break;
+          if (!(ok = mbar_spin_wait(bar(bars->empty_l[ls]), lph ^ 1u, abort_flag, args.err, kPwWaitLowrankEmpty))) break;
           mbar_arrive_expect_tx(fb, L::kB + PW_A_BYTES);
           tma_load_2d(l_ring + (uint32_t)ls * PW_A_BYTES, &tm_up, fb, j * PW_KB, n0);
           tma_load_2d(bdst, &tm_mid, fb, j * PW_KB, m0);
@@ -270,11 +280,11 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
       for (int it = 0; it < iters && ok; ++it) {
         const int bs = it % BS;
         const uint32_t bph = (uint32_t)(it / BS) & 1u;
-        if (!(ok = mbar_wait(bar(bars->full_b[bs]), bph, abort_flag, args.err, kPwWaitMmaTile))) break;
+        if (!(ok = mbar_spin_wait(bar(bars->full_b[bs]), bph, abort_flag, args.err, kPwWaitMmaTile))) break;
         const uint64_t db = desc_k_sw128(b_ring + (uint32_t)bs * L::kB);
         if (it < n_res) {
           const int as = it % AS;
-          if (!(ok = mbar_wait(bar(bars->conv[as]), (uint32_t)(it / AS) & 1u, abort_flag, args.err, kPwWaitMmaConv)))
+          if (!(ok = mbar_spin_wait(bar(bars->conv[as]), (uint32_t)(it / AS) & 1u, abort_flag, args.err, kPwWaitMmaConv)))
             break;
           tc_fence_after();
           const uint32_t ta = tmem + L::kAccCols + (uint32_t)as * PW_STAGE_COLS;
@@ -305,48 +315,73 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------ conversion: codes -> fp16 weights in TMEM
-    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    // Per code group (up to 4 stages): the thread's four 16-byte pieces (row `row`, k half `half`
+    // of each stage) are loaded and converted together, then stored to the four TMEM stages.
+    const int q = warp & 3;            // TMEM lane quarter this warp may access
     const int half = (warp - 4) >> 2;  // which 32 of a stage's 64 k
     const int row = q * 32 + lane;
     const int n_row = n0 + row;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    const uint32_t code_off = (uint32_t)row * (PW_KB / 2) + 16u * (uint32_t)half;
+    const uint32_t code_row = (uint32_t)row * 128u;
+    const uint32_t r7 = (uint32_t)(row & 7);
     const __half* srow = args.scales16 + (int64_t)min(n_row, args.N - 1) * args.nG;
     bool ok = true;
-    for (int it = 0; it < n_res && ok; ++it) {
-      const int kb = kb0 + it;
-      const int ps = it % PW_PSTAGES, as = it % AS;
-      const uint32_t sbits = n_row < args.N ? (uint32_t)__half_as_ushort(srow[(kb * PW_KB + 32 * half) / args.w_group])
-                                            : 0u;
-      ok = mbar_wait(bar(bars->full_p[ps]), (uint32_t)(it / PW_PSTAGES) & 1u, abort_flag, args.err, kPwWaitConvPacked);
+    for (int gi = 0; gi < n_groups && ok; ++gi) {
+      const int ps = gi % PW_PSTAGES;
+      const int it0 = gi * PW_SUB;                 // first stage of the group (CTA-relative)
+      const int nsub = min(PW_SUB, n_res - it0);
+      uint32_t sb[PW_SUB];
+#pragma unroll
+      for (int j = 0; j < PW_SUB; ++j) {
+        const int kb = kb0 + it0 + j;
+        sb[j] = (j < nsub && n_row < args.N) ? (uint32_t)__half_as_ushort(srow[(kb * PW_KB + 32 * half) / args.w_group])
+                                             : 0u;
+      }
+      ok = mbar_spin_wait(bar(bars->full_p[ps]), (uint32_t)(gi / PW_PSTAGES) & 1u, abort_flag, args.err,
+                          kPwWaitConvPacked);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;  // the lanes of a warp leave together
-      const uint4 pk = ld_shared_u4(p_ring + (uint32_t)ps * PW_P_BYTES + code_off);
-      const uint32_t s_lo = sbits | (sbits << 16);
-      const uint32_t s16 = (uint32_t)__half_as_ushort(__hmul(__ushort_as_half((unsigned short)sbits),
-                                                             __float2half_rn(0.0625f)));
-      const uint32_t s_hi = s16 | (s16 << 16);
-      uint32_t v[16];
-      convert_word(pk.x, s_lo, s_hi, v);
-      convert_word(pk.y, s_lo, s_hi, v + 4);
-      convert_word(pk.z, s_lo, s_hi, v + 8);
-      convert_word(pk.w, s_lo, s_hi, v + 12);
+      uint4 pk[PW_SUB];
+#pragma unroll
+      for (int j = 0; j < PW_SUB; ++j)  // 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r % 8)
+        pk[j] = ld_shared_u4(p_ring + (uint32_t)ps * PW_P_BYTES + code_row + ((((uint32_t)(2 * j + half)) ^ r7) << 4));
+      uint32_t v[PW_SUB][16];
+#pragma unroll
+      for (int j = 0; j < PW_SUB; ++j) {
+        const uint32_t s_lo = sb[j] | (sb[j] << 16);
+        const uint32_t s16 = (uint32_t)__half_as_ushort(__hmul(__ushort_as_half((unsigned short)sb[j]),
+                                                               __float2half_rn(0.0625f)));
+        const uint32_t s_hi = s16 | (s16 << 16);
+        convert_word(pk[j].x, s_lo, s_hi, v[j]);
+        convert_word(pk[j].y, s_lo, s_hi, v[j] + 4);
+        convert_word(pk[j].z, s_lo, s_hi, v[j] + 8);
+        convert_word(pk[j].w, s_lo, s_hi, v[j] + 12);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive_cta(bar(bars->empty_p[ps]));  // every lane has consumed its codes
-      ok = mbar_wait(bar(bars->empty_a[as]), ((uint32_t)(it / AS) & 1u) ^ 1u, abort_flag, args.err, kPwWaitConvEmpty);
-      if (!(ok = __all_sync(0xffffffffu, ok))) break;
-      tc_fence_after();
-      tmem_st16(tmem + lane_off + L::kAccCols + (uint32_t)as * PW_STAGE_COLS + 16u * (uint32_t)half, v);
+#pragma unroll
+      for (int j = 0; j < PW_SUB; ++j) {
+        if (j < nsub) {
+          const int it = it0 + j, as = it % AS;
+          ok = mbar_spin_wait(bar(bars->empty_a[as]), ((uint32_t)(it / AS) & 1u) ^ 1u, abort_flag, args.err,
+                              kPwWaitConvEmpty);
+          if (!(ok = __all_sync(0xffffffffu, ok))) break;
+          tc_fence_after();
+          tmem_st16(tmem + lane_off + L::kAccCols + (uint32_t)as * PW_STAGE_COLS + 16u * (uint32_t)half, v[j]);
+        }
+      }
+      if (!ok) break;
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cta(bar(bars->conv[as]));
+      if (lane == 0)
+        for (int j = 0; j < nsub; ++j) mbar_arrive_cta(bar(bars->conv[(it0 + j) % AS]));
     }
     if (warp < 8) {
       // ---------------------------------------------- epilogue: TMEM -> registers -> out or partial
       const int erow = q * 32 + lane;
       const int n = n0 + erow;
       const uint32_t taddr = tmem + lane_off;
-      const bool done = mbar_wait(bar(bars->mma_done), 0, abort_flag, args.err, kPwWaitEpilogue) && !*abort_flag;
+      const bool done = mbar_spin_wait(bar(bars->mma_done), 0, abort_flag, args.err, kPwWaitEpilogue) && !*abort_flag;
       if (__all_sync(0xffffffffu, done)) {
         tc_fence_after();
         float bias_v = 0.f;
@@ -472,7 +507,8 @@ PwPlan plan_packed(int M, int N, int K_pad) {
   const long long slots = (long long)num_sms() * pw_ctas_per_sm(pw_smem(p.tn));
   p.ks = 1;
   double best = -1.0;
-  for (int ks = 1; ks <= 8 && n_k / ks >= 2; ks *= 2) {
+  const int n_grp = (n_k + PW_SUB - 1) / PW_SUB;
+  for (int ks = 1; ks <= 8 && n_grp / ks >= 2; ks *= 2) {
     const long long ctas = units * ks;
     const long long waves = (ctas + slots - 1) / slots;
     const double fill = (double)ctas / (double)(waves * slots);
@@ -594,8 +630,8 @@ extern "C" int svdq_packed_gemm(const void* a16, const void* codes, const void* 
   if ((st = make_tma_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a16, K_pad, M, (uint64_t)K_pad * 2, PW_KB, p.tn,
                         CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
-  if ((st = make_tma_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, K_pad / 2, N, (uint64_t)K_pad / 2, PW_KB / 2,
-                        PW_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE)))
+  if ((st = make_tma_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, K_pad / 2, N, (uint64_t)K_pad / 2,
+                        PW_SUB * PW_KB / 2, PW_ROWS, CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
   if (R2 > 0) {
     if ((st = make_tma_2d(&tmid, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, mid_hl, R2, M, (uint64_t)R2 * 2, PW_KB, p.tn,
