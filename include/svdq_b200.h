@@ -241,11 +241,14 @@ int svdq_linear_gemm_plan(int tiles, int iters, int max_pairs, int with_workspac
  *   out_codes    [N, K_pad/2] u8: the checkpoint's codes (nibble q + 8, pack.py:47-56) with the
  *                nibbles of every 32-bit word reordered to [k0 k2 k4 k6 | k1 k3 k5 k7]
  *                (16-byte aligned);
- *   out_scales16 [N, K_pad/w_group] fp16: the group scales rounded to fp16.
+ *   out_scales16 fp16, the group scales rounded to fp16 in tile order: for each 128-row tile t
+ *                and each 256-k code group c, [128 rows][256 / w_group] contiguous at element
+ *                ((t * ceil(K_pad / 256) + c) * 128 + row) * (256 / w_group); zero past N and K_pad
+ *                (ceil(N / 128) * ceil(K_pad / 256) * 128 * (256 / w_group) elements, 16-byte aligned).
  * inexact (device int, may be NULL; not cleared here) is set to 1 when some scale or its
  * sixteenth is not an fp16 value; otherwise svdq_packed_gemm's weights equal svdq_repack_weight's
  * w16 bit for bit (bf16 scales in [2^-10, 8188], fp16 scales >= 2^-10, all group-scale zeros).
- *   w_group % 32 == 0, K_pad % w_group == 0, K_pad % 64 == 0; qweight 4-byte aligned.
+ *   w_group in {32, 64, 128, 256}, K_pad % w_group == 0, K_pad % 64 == 0; qweight 4-byte aligned.
  */
 int svdq_prepare_packed(const void* qweight, const void* scales, int scale_dtype, int N, int K_pad,
                         int w_group, void* out_codes, void* out_scales16, int* inexact,
@@ -260,7 +263,8 @@ int svdq_prepare_packed(const void* qweight, const void* scales, int scale_dtype
  * cluster of 2, 4 or 8 CTAs splits K and sums its fp32 partials through distributed shared
  * memory in a fixed order (deterministic).  Replaces F.linear(x_hat, w_res) + F.linear(mid, l1)
  * + bias of svd.py:158-162 and the in-loop dequantization of kernels/triton/generic_int4.py:19-133.
- *   a16 [M, K_pad] fp16; K_pad % 64 == 0; w_group as above; N % 8 == 0, ldo % 8 == 0;
+ *   a16 [M, K_pad] fp16; K_pad % 64 == 0; w_group and the layouts of codes and scales16 as
+ *   svdq_prepare_packed writes them; N % 8 == 0, ldo % 8 == 0;
  *   R2 % 64 == 0 (may be 0); out_dtype in {SVDQ_BF16, SVDQ_FP32}; bias may be NULL.
  */
 int svdq_packed_gemm(const void* a16, const void* codes, const void* scales16, int w_group,

@@ -56,6 +56,8 @@ constexpr int PW_SUB = 4;                             // 64-k stages per code gr
 constexpr int PW_PSTAGES = 4;                         // code-group ring (shared memory)
 constexpr int PW_LSTAGES = 2;                         // low-rank A ring (shared memory)
 constexpr uint32_t PW_P_BYTES = PW_ROWS * PW_SUB * PW_KB / 2;  // 16 KiB of codes: 128 rows x 128 bytes
+constexpr int PW_GROUP_K = PW_SUB * PW_KB;                      // 256 k per code group
+constexpr uint32_t PW_S_BYTES = PW_ROWS * (PW_GROUP_K / 32) * 2;  // group scales of a code group (G >= 32)
 constexpr uint32_t PW_A_BYTES = PW_ROWS * PW_KB * 2;  // 16 KiB: a low-rank A stage
 constexpr int PW_CONV_WARPS = 8;
 constexpr int PW_THREADS = 32 * (4 + PW_CONV_WARPS);
@@ -72,7 +74,8 @@ struct PwLayout {
   static constexpr uint32_t kOffL = 0;                                        // low-rank A ring
   static constexpr uint32_t kOffB = kOffL + PW_LSTAGES * PW_A_BYTES;
   static constexpr uint32_t kOffP = kOffB + kBStages * kB;
-  static constexpr uint32_t kOffBar = kOffP + PW_PSTAGES * PW_P_BYTES;
+  static constexpr uint32_t kOffS = kOffP + PW_PSTAGES * PW_P_BYTES;         // group-scale ring
+  static constexpr uint32_t kOffBar = kOffS + PW_PSTAGES * PW_S_BYTES;
   static constexpr uint32_t kSmem = kOffBar + 1024 + 1024;                   // barriers + alignment slack
   static_assert(kB % 1024 == 0, "token tiles keep 1 KiB alignment for the 128-byte swizzle");
   static_assert(kAStages >= 2 * PW_SUB, "the TMEM weight ring holds at least two code groups");
@@ -81,7 +84,7 @@ struct PwLayout {
 };
 
 struct PwBars {
-  uint64_t full_p[PW_PSTAGES];   // code group landed (TMA bytes)
+  uint64_t full_p[PW_PSTAGES];   // code group and its scales landed (TMA bytes)
   uint64_t empty_p[PW_PSTAGES];  // code group read (one arrival per converter warp)
   uint64_t full_b[16];           // token tile (and, for a low-rank stage, its A) landed (TMA bytes)
   uint64_t empty_b[16];          // MMAs reading the token slot done (commit)
@@ -95,13 +98,13 @@ struct PwBars {
 static_assert(sizeof(PwBars) <= 1024, "barrier block");
 
 struct PwArgs {
-  const __half* scales16;  // [N, nG] fp16 group scales
+  const __half* scales16;  // fp16 group scales in tile order (svdq_prepare_packed)
   const __nv_bfloat16* bias;
   void* out;
   int64_t ldo;
   int M, N;
   int n_k, n_lr;   // residual and low-rank stages
-  int nG, w_group;
+  int spg;         // scales per row per code group: 256 / w_group
   int ks;          // CTAs per cluster along K
   int units_n;     // 128-row weight tiles
   int* err;
@@ -133,6 +136,17 @@ __device__ __forceinline__ uint4 ld_shared_u4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
+}
+__device__ __forceinline__ uint32_t ld_shared_u16(uint32_t addr) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+// Contiguous global -> shared copy counted on an mbarrier (16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
 }
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
   float v;
@@ -168,7 +182,8 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
   uint8_t* gbase = smem_raw + (base - raw);
   PwBars* bars = reinterpret_cast<PwBars*>(gbase + L::kOffBar);
   volatile int* abort_flag = &bars->abort_flag;
-  const uint32_t l_ring = base + L::kOffL, b_ring = base + L::kOffB, p_ring = base + L::kOffP;
+  const uint32_t l_ring = base + L::kOffL, b_ring = base + L::kOffB, p_ring = base + L::kOffP,
+                 s_ring = base + L::kOffS;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ks = args.ks;
@@ -232,9 +247,12 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
         const int s = it % PW_PSTAGES;
         const uint32_t ph = (uint32_t)(it / PW_PSTAGES) & 1u;
         if (!(ok = mbar_spin_wait(bar(bars->empty_p[s]), ph ^ 1u, abort_flag, args.err, kPwWaitPackedEmpty))) break;
-        mbar_arrive_expect_tx(bar(bars->full_p[s]), PW_P_BYTES);
+        const uint32_t sbytes = (uint32_t)(PW_ROWS * args.spg * 2);
+        mbar_arrive_expect_tx(bar(bars->full_p[s]), PW_P_BYTES + sbytes);
         tma_load_2d(p_ring + (uint32_t)s * PW_P_BYTES, &tm_codes, bar(bars->full_p[s]), (g0 + it) * (PW_SUB * PW_KB / 2),
                     n0);
+        bulk_load(s_ring + (uint32_t)s * PW_S_BYTES,
+                  args.scales16 + ((int64_t)nb * n_grp + g0 + it) * PW_ROWS * args.spg, sbytes, bar(bars->full_p[s]));
         filled |= 1u << s;
         par = (par & ~(1u << s)) | (ph << s);
       }
@@ -324,22 +342,19 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const uint32_t code_row = (uint32_t)row * 128u;
     const uint32_t r7 = (uint32_t)(row & 7);
-    const __half* srow = args.scales16 + (int64_t)min(n_row, args.N - 1) * args.nG;
+    const int spg = args.spg, gshift = spg == 8 ? 5 : spg == 4 ? 6 : spg == 2 ? 7 : 8;  // log2(G)
     bool ok = true;
     for (int gi = 0; gi < n_groups && ok; ++gi) {
       const int ps = gi % PW_PSTAGES;
       const int it0 = gi * PW_SUB;                 // first stage of the group (CTA-relative)
       const int nsub = min(PW_SUB, n_res - it0);
-      uint32_t sb[PW_SUB];
-#pragma unroll
-      for (int j = 0; j < PW_SUB; ++j) {
-        const int kb = kb0 + it0 + j;
-        sb[j] = (j < nsub && n_row < args.N) ? (uint32_t)__half_as_ushort(srow[(kb * PW_KB + 32 * half) / args.w_group])
-                                             : 0u;
-      }
       ok = mbar_spin_wait(bar(bars->full_p[ps]), (uint32_t)(gi / PW_PSTAGES) & 1u, abort_flag, args.err,
                           kPwWaitConvPacked);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;  // the lanes of a warp leave together
+      uint32_t sb[PW_SUB];
+      const uint32_t srow = s_ring + (uint32_t)ps * PW_S_BYTES + (uint32_t)(row * spg) * 2u;
+#pragma unroll
+      for (int j = 0; j < PW_SUB; ++j) sb[j] = ld_shared_u16(srow + (uint32_t)(((j * PW_KB + 32 * half) >> gshift) * 2));
       uint4 pk[PW_SUB];
 #pragma unroll
       for (int j = 0; j < PW_SUB; ++j)  // 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r % 8)
@@ -423,8 +438,12 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
       const int row = crank * rows + rl;
       const int n = n0 + row, m = m0 + col;
       const uint32_t off = (uint32_t)(col * PW_ROWS + row) * 4u;
+      float pv[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) pv[c] = c < ks ? ld_dsmem_f32(mapa_shared(part_local + off, (uint32_t)c)) : 0.f;
       float y = 0.f;
-      for (int c = 0; c < ks; ++c) y += ld_dsmem_f32(mapa_shared(part_local + off, (uint32_t)c));
+#pragma unroll
+      for (int c = 0; c < 8; ++c) y += pv[c];  // rank order
       if (n < args.N && m < args.M && !*abort_flag) {
         if (args.bias) y += __bfloat162float(args.bias[n]);
         if constexpr (OUT_F32) static_cast<float*>(args.out)[(int64_t)m * args.ldo + n] = y;
@@ -460,24 +479,35 @@ __device__ __forceinline__ float scale_f32<__half>(__half v) { return __half2flo
 template <>
 __device__ __forceinline__ float scale_f32<float>(float v) { return v; }
 
-// Group scales -> fp16.  *inexact (when given) is set when a scale is not an fp16 value or its
-// sixteenth is not: the kernel's weights then round the scale once more than fp16(q * s) does
-// (relative error at most 2^-11 on the weights of such groups).
+// Group scales -> fp16 in the kernel's tile order: for each 128-row tile and each 256-k code group,
+// [128 rows][256 / G scales] contiguous (rows past N and groups past K_pad are zero), so one bulk
+// copy brings a code group's scales with its codes.  *inexact (when given) is set when a scale is
+// not an fp16 value or its sixteenth is not: the kernel's weights then round the scale once more
+// than fp16(q * s) does (relative error at most 2^-11 on the weights of such groups).
 template <typename T>
-__global__ void prepare_scales_kernel(const T* __restrict__ in, __half* __restrict__ out, int64_t count,
-                                      int* __restrict__ inexact) {
+__global__ void prepare_scales_kernel(const T* __restrict__ in, __half* __restrict__ out, int N, int nG, int n_grp,
+                                      int spg, int* __restrict__ inexact) {
+  const int64_t count = (int64_t)((N + PW_ROWS - 1) / PW_ROWS) * n_grp * PW_ROWS * spg;
   int bad = 0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
-    const float s = scale_f32<T>(in[i]);
-    const __half h = __float2half_rn(s);
-    const __half h16 = __hmul(h, __float2half_rn(0.0625f));
-    bad |= (__half2float(h) != s) || (__half2float(h16) * 16.0f != __half2float(h));
+    const int j = (int)(i % spg);
+    const int r = (int)((i / spg) % PW_ROWS);
+    const int64_t tg = i / ((int64_t)spg * PW_ROWS);
+    const int grp = (int)(tg % n_grp);
+    const int n = (int)(tg / n_grp) * PW_ROWS + r;
+    const int g = grp * spg + j;  // weight group along K
+    __half h = __float2half_rn(0.f);
+    if (n < N && g < nG) {
+      const float s = scale_f32<T>(in[(int64_t)n * nG + g]);
+      h = __float2half_rn(s);
+      const __half h16 = __hmul(h, __float2half_rn(0.0625f));
+      bad |= (__half2float(h) != s) || (__half2float(h16) * 16.0f != __half2float(h));
+    }
     out[i] = h;
   }
   if (__syncthreads_or(bad) && threadIdx.x == 0 && inexact) atomicExch(inexact, 1);
 }
 
-// One CTA per SM: each allocates all 512 TMEM columns.
 int pw_ctas_per_sm(uint32_t) { return 1; }
 
 struct PwPlan {
@@ -495,8 +525,9 @@ uint32_t pw_smem(int tn) {
   }
 }
 
-// Split factor: the KS in {1, 2, 4, 8} whose grid fills the CTA slots best (fewest idle slots in
-// the last wave), with at least two residual stages per CTA; ties go to the smaller KS.
+// Split factor: among KS in {1, 2, 4, 8} (at least two code groups per CTA), the fewest waves of
+// CTAs, then the fullest last wave; ties go to the smaller KS.  Each CTA has a fixed cost (set-up,
+// pipeline fill, epilogue, cluster reduction), so an extra wave costs more than idle SMs.
 PwPlan plan_packed(int M, int N, int K_pad) {
   PwPlan p;
   p.tn = pick_tn(M);
@@ -507,12 +538,14 @@ PwPlan plan_packed(int M, int N, int K_pad) {
   const long long slots = (long long)num_sms() * pw_ctas_per_sm(pw_smem(p.tn));
   p.ks = 1;
   double best = -1.0;
+  long long best_waves = 1ll << 40;
   const int n_grp = (n_k + PW_SUB - 1) / PW_SUB;
-  for (int ks = 1; ks <= 8 && n_grp / ks >= 2; ks *= 2) {
+  for (int ks = 1; ks <= 8 && (ks == 1 || n_grp / ks >= 2); ks *= 2) {
     const long long ctas = units * ks;
     const long long waves = (ctas + slots - 1) / slots;
     const double fill = (double)ctas / (double)(waves * slots);
-    if (fill > best + 1e-9) {
+    if (waves < best_waves || (waves == best_waves && fill > best + 1e-9)) {
+      best_waves = waves;
       best = fill;
       p.ks = ks;
     }
@@ -566,8 +599,8 @@ extern "C" int svdq_prepare_packed(const void* qweight, const void* scales, int 
   using namespace svdq;
   SVDQ_REQUIRE(qweight && scales && out_codes && out_scales16, "svdq_prepare_packed: null pointer");
   SVDQ_REQUIRE(N > 0 && K_pad > 0 && K_pad % 64 == 0, "svdq_prepare_packed: K_pad must be a positive multiple of 64");
-  SVDQ_REQUIRE(w_group > 0 && w_group % 32 == 0 && K_pad % w_group == 0,
-               "svdq_prepare_packed: w_group must be a multiple of 32 dividing K_pad");
+  SVDQ_REQUIRE((w_group == 32 || w_group == 64 || w_group == 128 || w_group == 256) && K_pad % w_group == 0,
+               "svdq_prepare_packed: w_group must be 32, 64, 128 or 256 and divide K_pad");
   SVDQ_REQUIRE((reinterpret_cast<uintptr_t>(qweight) & 3u) == 0 && (reinterpret_cast<uintptr_t>(out_codes) & 15u) == 0,
                "svdq_prepare_packed: qweight must be 4-byte and out_codes 16-byte aligned");
   const int64_t words = (int64_t)N * K_pad / 8;
@@ -577,18 +610,22 @@ extern "C" int svdq_prepare_packed(const void* qweight, const void* scales, int 
                                                        static_cast<uint32_t*>(out_codes), words);
   int st = check_launch("svdq_prepare_packed: codes");
   if (st) return st;
-  const int64_t count = (int64_t)N * (K_pad / w_group);
+  const int nG = K_pad / w_group, n_grp = (K_pad + PW_GROUP_K - 1) / PW_GROUP_K, spg = PW_GROUP_K / w_group;
+  const int64_t count = (int64_t)((N + PW_ROWS - 1) / PW_ROWS) * n_grp * PW_ROWS * spg;
   const unsigned sblocks = (unsigned)std::min<int64_t>((count + threads - 1) / threads, (int64_t)num_sms() * 8);
   __half* o = static_cast<__half*>(out_scales16);
   switch (scale_dtype) {
     case SVDQ_BF16:
-      prepare_scales_kernel<<<sblocks, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(scales), o, count, inexact);
+      prepare_scales_kernel<<<sblocks, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(scales), o, N, nG, n_grp,
+                                                             spg, inexact);
       break;
     case SVDQ_FP16:
-      prepare_scales_kernel<<<sblocks, threads, 0, stream>>>(static_cast<const __half*>(scales), o, count, inexact);
+      prepare_scales_kernel<<<sblocks, threads, 0, stream>>>(static_cast<const __half*>(scales), o, N, nG, n_grp, spg,
+                                                             inexact);
       break;
     case SVDQ_FP32:
-      prepare_scales_kernel<<<sblocks, threads, 0, stream>>>(static_cast<const float*>(scales), o, count, inexact);
+      prepare_scales_kernel<<<sblocks, threads, 0, stream>>>(static_cast<const float*>(scales), o, N, nG, n_grp, spg,
+                                                             inexact);
       break;
     default:
       return set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_prepare_packed: scale_dtype must be bf16, fp16 or fp32");
@@ -614,8 +651,9 @@ extern "C" int svdq_packed_gemm(const void* a16, const void* codes, const void* 
   using namespace svdq;
   SVDQ_REQUIRE(a16 && codes && scales16 && out, "svdq_packed_gemm: null operand pointer");
   SVDQ_REQUIRE(M >= 0 && N > 0 && K_pad > 0 && K_pad % 64 == 0, "svdq_packed_gemm: bad M/N/K_pad");
-  SVDQ_REQUIRE(w_group > 0 && w_group % 32 == 0 && K_pad % w_group == 0,
-               "svdq_packed_gemm: w_group must be a multiple of 32 dividing K_pad");
+  SVDQ_REQUIRE((w_group == 32 || w_group == 64 || w_group == 128 || w_group == 256) && K_pad % w_group == 0,
+               "svdq_packed_gemm: w_group must be 32, 64, 128 or 256 and divide K_pad");
+  SVDQ_REQUIRE((reinterpret_cast<uintptr_t>(scales16) & 15u) == 0, "svdq_packed_gemm: scales16 must be 16-byte aligned");
   SVDQ_REQUIRE(N % 8 == 0 && ldo >= N && ldo % 8 == 0, "svdq_packed_gemm: N and ldo must be multiples of 8, ldo >= N");
   SVDQ_REQUIRE(R2 >= 0 && R2 % 64 == 0, "svdq_packed_gemm: R2 must be a multiple of 64");
   SVDQ_REQUIRE(R2 == 0 || (mid_hl && up_hl), "svdq_packed_gemm: mid_hl/up_hl are NULL");
@@ -653,8 +691,7 @@ extern "C" int svdq_packed_gemm(const void* a16, const void* codes, const void* 
   a.N = N;
   a.n_k = K_pad / PW_KB;
   a.n_lr = R2 / PW_KB;
-  a.nG = K_pad / w_group;
-  a.w_group = w_group;
+  a.spg = PW_GROUP_K / w_group;
   a.ks = p.ks;
   a.units_n = p.units_n;
   a.err = err;

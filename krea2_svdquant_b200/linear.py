@@ -80,7 +80,7 @@ class PreparedOperands:
     up_hl_base: torch.Tensor | None  # same without the LoRA columns (for _forward_base)
     w16: torch.Tensor | None       # [n, k_pad] fp16 = q * weight scale (weight_operand "fp16" / "auto")
     codes: torch.Tensor | None     # [n, k_pad/2] u8 kernel-order codes (weight_operand "packed" / "auto")
-    scales16: torch.Tensor | None  # [n, k_pad/group] fp16 group scales (with codes)
+    scales16: torch.Tensor | None  # fp16 group scales in the packed GEMM's tile order (with codes)
     bias: torch.Tensor | None      # [n] bf16
 
 
@@ -229,10 +229,10 @@ class SVDQuantLinear(nn.Module):
             ws = self.weight_scales.to(device=device).contiguous()
             w16 = ops.repack_weight(qw, ws, self.group_size) if self.weight_operand != "packed" else None
             codes = scales16 = None
-            if self.weight_operand != "fp16":
-                if self.group_size % 32:
-                    raise ValueError(f"the packed-weight GEMM needs a weight group size divisible by 32, "
-                                     f"got {self.group_size} (use weight_operand='fp16')")
+            if self.weight_operand == "packed" and self.group_size not in ops.PACKED_GROUP_SIZES:
+                raise ValueError(f"the packed-weight GEMM takes weight group sizes {ops.PACKED_GROUP_SIZES}, "
+                                 f"got {self.group_size} (use weight_operand='fp16')")
+            if self.weight_operand != "fp16" and self.group_size in ops.PACKED_GROUP_SIZES:
                 codes, scales16, _ = ops.prepare_packed(qw, ws, self.group_size)
             bias = None if self.bias is None else self.bias.to(device=device, dtype=bf).contiguous()
         self._prepared = PreparedOperands(device=device, key=key, k_in=k_in, k_pad=k_pad, n=n, smooth=smooth,

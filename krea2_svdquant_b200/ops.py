@@ -257,7 +257,9 @@ def _(a16, w16, mid_hl, up_hl, bias, out_fp32):
 @torch.library.custom_op("svdq_b200::prepare_packed", mutates_args=())
 def prepare_packed(qweight: Tensor, scales: Tensor, w_group: int) -> tuple[Tensor, Tensor, Tensor]:
     """Checkpoint INT4 weight -> the packed-weight GEMM's operands: ``codes [N, K_pad/2]`` u8 in the
-    kernel's nibble order, ``scales16 [N, K_pad/w_group]`` fp16, and a one-element int32 flag that is
+    kernel's nibble order, ``scales16`` fp16 in the kernel's tile order (``packed_scales_numel``
+    elements: per 128-row tile and 256-k code group, [128 rows][256 / w_group]), and a one-element
+    int32 flag that is
     1 when some scale (or its sixteenth) is not an fp16 value (the GEMM's weights then differ from
     ``repack_weight``'s by one more rounding of the scale)."""
     _need_cuda("prepare_packed", qweight, scales)
@@ -266,7 +268,7 @@ def prepare_packed(qweight: Tensor, scales: Tensor, w_group: int) -> tuple[Tenso
     _need(scales.dtype in _DT and scales.is_contiguous(), "prepare_packed: scales must be contiguous bf16/fp16/fp32")
     n, k_pad = qweight.shape[0], qweight.shape[1] * 2
     codes = torch.empty_like(qweight)
-    scales16 = torch.empty((n, k_pad // w_group), dtype=torch.float16, device=qweight.device)
+    scales16 = torch.empty((packed_scales_numel(n, k_pad, w_group),), dtype=torch.float16, device=qweight.device)
     flag = torch.zeros((1,), dtype=torch.int32, device=qweight.device)
     _lib.call("svdq_prepare_packed", _p(qweight), _p(scales), _DT[scales.dtype], n, k_pad, w_group, _p(codes),
               _p(scales16), _p(flag), _stream(qweight.device))
@@ -276,8 +278,18 @@ def prepare_packed(qweight: Tensor, scales: Tensor, w_group: int) -> tuple[Tenso
 @prepare_packed.register_fake
 def _(qweight, scales, w_group):
     n, k_pad = qweight.shape[0], qweight.shape[1] * 2
-    return (torch.empty_like(qweight), qweight.new_empty((n, k_pad // w_group), dtype=torch.float16),
+    return (torch.empty_like(qweight), qweight.new_empty((packed_scales_numel(n, k_pad, w_group),),
+                                                         dtype=torch.float16),
             qweight.new_empty((1,), dtype=torch.int32))
+
+
+PACKED_GROUP_SIZES = (32, 64, 128, 256)
+
+
+def packed_scales_numel(n: int, k_pad: int, w_group: int) -> int:
+    """Elements of the packed GEMM's tile-ordered fp16 scales: per 128-row tile and 256-k code group,
+    [128 rows][256 / w_group] (padded with zeros past N and K_pad)."""
+    return -(-n // 128) * -(-k_pad // 256) * 128 * (256 // w_group)
 
 
 @torch.library.custom_op("svdq_b200::packed_gemm", mutates_args=())

@@ -51,6 +51,15 @@ def _native_order_np(qweight: np.ndarray) -> np.ndarray:
     return out.view(np.uint8).reshape(qweight.shape)
 
 
+def _tile_order_scales_np(scales: np.ndarray, group: int) -> np.ndarray:
+    """Per 128-row tile and 256-k code group, [128 rows][256 / group] (zero padded)."""
+    n, ng = scales.shape
+    spg, tiles, grps = 256 // group, -(-n // 128), -(-ng * group // 256)
+    pad = np.zeros((tiles * 128, grps * spg), np.float32)
+    pad[:n, :ng] = scales
+    return pad.reshape(tiles, 128, grps, spg).transpose(0, 2, 1, 3).reshape(-1)
+
+
 def test_prepare_packed_layout():
     from krea2_svdquant_b200 import ops
     from krea2_svdquant_b200.quant import random_state
@@ -59,7 +68,7 @@ def test_prepare_packed_layout():
     codes, s16, flag = ops.prepare_packed(st.qweight, st.weight_scales, 64)
     torch.cuda.synchronize()
     assert np.array_equal(codes.cpu().numpy(), _native_order_np(st.qweight.cpu().numpy()))
-    assert torch.equal(s16.float(), st.weight_scales.float())
+    assert np.array_equal(s16.float().cpu().numpy(), _tile_order_scales_np(st.weight_scales.float().cpu().numpy(), 64))
     assert int(flag.item()) == 0
     st.weight_scales[0, 0] = 1.1e-4  # bf16 value 0.000110149...: its sixteenth is not an fp16 value
     _, _, flag = ops.prepare_packed(st.qweight, st.weight_scales, 64)
