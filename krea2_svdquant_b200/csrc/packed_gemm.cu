@@ -15,8 +15,8 @@
 // Tensor memory holds the accumulator (columns [0, TN)) and a ring of converted weight stages
 // (32 columns = 64 fp16 of K per row each): 12 to 15 stages deep, so the conversion runs well
 // ahead of the MMAs and no stage waits for a full convert -> MMA -> release round trip.  A
-// converter thread owns one weight row (its TMEM lane) and half of a stage's K; tcgen05.st moves
-// its 32 fp16 values straight from registers to its lane, so the weights never touch shared memory.
+// converter thread owns one weight row (its TMEM lane) and a quarter of a stage's K; tcgen05.st moves
+// its 16 fp16 values straight from registers to its lane, so the weights never touch shared memory.
 //
 // Conversion.  The load-time preparation (svdq_prepare_packed) reorders the nibbles of each 32-bit
 // word to [k0 k2 k4 k6 | k1 k3 k5 k7] (low half-word holds the even k), so one AND/OR per pair puts
@@ -38,7 +38,7 @@
 // Roles (12 warps): warp 0 TMA of packed codes (4-deep ring of 128 rows x 256 k groups, 128-byte
 // swizzle so the converters' shared loads are free of bank conflicts); warp 2 TMA of
 // the token tiles (a16, or mid_hl with up_hl for the low-rank stages); warp 1 TMEM allocation and
-// the MMA issue; warps 4-11 conversion (two warps per TMEM lane quarter); warps 4-7 the epilogue.
+// the MMA issue; warps 4-19 conversion (four warps per TMEM lane quarter); warps 4-7 the epilogue.
 // Waits spin on mbarrier.test_wait (a blocking try_wait costs a fraction of a microsecond even on a
 // completed phase, more than a stage here) and are bounded (error word codes 0x51xx-0x54xx); a wait
 // that runs out raises the CTA's abort flag and every role leaves its loop, so all CTAs still meet
@@ -59,11 +59,11 @@ constexpr uint32_t PW_P_BYTES = PW_ROWS * PW_SUB * PW_KB / 2;  // 16 KiB of code
 constexpr int PW_GROUP_K = PW_SUB * PW_KB;                      // 256 k per code group
 constexpr uint32_t PW_S_BYTES = PW_ROWS * (PW_GROUP_K / 32) * 2;  // group scales of a code group (G >= 32)
 constexpr uint32_t PW_A_BYTES = PW_ROWS * PW_KB * 2;  // 16 KiB: a low-rank A stage
-constexpr int PW_CONV_WARPS = 8;
+constexpr int PW_CONV_WARPS = 16;
 constexpr int PW_THREADS = 32 * (4 + PW_CONV_WARPS);
 constexpr uint32_t PW_TMEM_COLS = 512;
 constexpr uint32_t PW_STAGE_COLS = PW_KB / 2;         // TMEM columns of one converted stage
-static_assert(PW_CONV_WARPS * 32 * 16 * PW_SUB == (int)PW_P_BYTES, "four 16-byte pieces of codes per converter thread");
+static_assert(PW_CONV_WARPS * 32 * 8 * PW_SUB == (int)PW_P_BYTES, "four 8-byte pieces of codes per converter thread");
 
 template <int TN>
 struct PwLayout {
@@ -135,6 +135,11 @@ __device__ __forceinline__ uint32_t h2_mul(uint32_t a, uint32_t b) {
 __device__ __forceinline__ uint4 ld_shared_u4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint2 ld_shared_u2(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
   return v;
 }
 __device__ __forceinline__ uint32_t ld_shared_u16(uint32_t addr) {
@@ -333,12 +338,12 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------ conversion: codes -> fp16 weights in TMEM
-    // Per code group (up to 4 stages): the thread's four 16-byte pieces (row `row`, k half `half`
-    // of each stage) are loaded and converted together, then stored to the four TMEM stages.
+    // Four warps per TMEM lane quarter, each owning 16 of a stage's 64 k for its 32 rows.  Per code
+    // group (up to 4 stages) a thread loads its four 8-byte pieces, converts them together and
+    // stores them to the four TMEM stages.
     const int q = warp & 3;            // TMEM lane quarter this warp may access
-    const int half = (warp - 4) >> 2;  // which 32 of a stage's 64 k
+    const int part = (warp - 4) >> 2;  // which 16 of a stage's 64 k
     const int row = q * 32 + lane;
-    const int n_row = n0 + row;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const uint32_t code_row = (uint32_t)row * 128u;
     const uint32_t r7 = (uint32_t)(row & 7);
@@ -351,15 +356,17 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
       ok = mbar_spin_wait(bar(bars->full_p[ps]), (uint32_t)(gi / PW_PSTAGES) & 1u, abort_flag, args.err,
                           kPwWaitConvPacked);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;  // the lanes of a warp leave together
-      uint32_t sb[PW_SUB];
       const uint32_t srow = s_ring + (uint32_t)ps * PW_S_BYTES + (uint32_t)(row * spg) * 2u;
+      const uint32_t prow = p_ring + (uint32_t)ps * PW_P_BYTES + code_row + 8u * (uint32_t)(part & 1);
+      uint2 pk[PW_SUB];
+      uint32_t sb[PW_SUB];
 #pragma unroll
-      for (int j = 0; j < PW_SUB; ++j) sb[j] = ld_shared_u16(srow + (uint32_t)(((j * PW_KB + 32 * half) >> gshift) * 2));
-      uint4 pk[PW_SUB];
-#pragma unroll
-      for (int j = 0; j < PW_SUB; ++j)  // 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r % 8)
-        pk[j] = ld_shared_u4(p_ring + (uint32_t)ps * PW_P_BYTES + code_row + ((((uint32_t)(2 * j + half)) ^ r7) << 4));
-      uint32_t v[PW_SUB][16];
+      for (int j = 0; j < PW_SUB; ++j) {
+        // 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r % 8); this piece is half of chunk 2j + part/2
+        pk[j] = ld_shared_u2(prow + ((((uint32_t)(2 * j + (part >> 1))) ^ r7) << 4));
+        sb[j] = ld_shared_u16(srow + (uint32_t)(((j * PW_KB + 16 * part) >> gshift) * 2));
+      }
+      uint32_t v[PW_SUB][8];
 #pragma unroll
       for (int j = 0; j < PW_SUB; ++j) {
         const uint32_t s_lo = sb[j] | (sb[j] << 16);
@@ -368,8 +375,6 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
         const uint32_t s_hi = s16 | (s16 << 16);
         convert_word(pk[j].x, s_lo, s_hi, v[j]);
         convert_word(pk[j].y, s_lo, s_hi, v[j] + 4);
-        convert_word(pk[j].z, s_lo, s_hi, v[j] + 8);
-        convert_word(pk[j].w, s_lo, s_hi, v[j] + 12);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive_cta(bar(bars->empty_p[ps]));  // every lane has consumed its codes
@@ -381,7 +386,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
                               kPwWaitConvEmpty);
           if (!(ok = __all_sync(0xffffffffu, ok))) break;
           tc_fence_after();
-          tmem_st16(tmem + lane_off + L::kAccCols + (uint32_t)as * PW_STAGE_COLS + 16u * (uint32_t)half, v[j]);
+          tmem_st8(tmem + lane_off + L::kAccCols + (uint32_t)as * PW_STAGE_COLS + 8u * (uint32_t)part, v[j]);
         }
       }
       if (!ok) break;
