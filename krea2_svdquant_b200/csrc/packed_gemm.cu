@@ -35,7 +35,10 @@
 // one slice of rows over all KS partials through distributed shared memory, in rank order (a
 // fixed order: results are deterministic), adds the bias and stores.
 //
-// Roles (12 warps): warp 0 TMA of packed codes (4-deep ring of 128 rows x 256 k groups, 128-byte
+// The converters are software-pipelined: a group's TMEM stores drain while the next group
+// converts, and are published (tcgen05.wait::st, then the stage barriers) after it.
+//
+// Roles (20 warps): warp 0 TMA of packed codes (4-deep ring of 128 rows x 256 k groups, 128-byte
 // swizzle so the converters' shared loads are free of bank conflicts); warp 2 TMA of
 // the token tiles (a16, or mid_hl with up_hl for the low-rank stages); warp 1 TMEM allocation and
 // the MMA issue; warps 4-19 conversion (four warps per TMEM lane quarter); warps 4-7 the epilogue.
@@ -78,7 +81,7 @@ struct PwLayout {
   static constexpr uint32_t kOffBar = kOffS + PW_PSTAGES * PW_S_BYTES;
   static constexpr uint32_t kSmem = kOffBar + 1024 + 1024;                   // barriers + alignment slack
   static_assert(kB % 1024 == 0, "token tiles keep 1 KiB alignment for the 128-byte swizzle");
-  static_assert(kAStages >= 2 * PW_SUB, "the TMEM weight ring holds at least two code groups");
+  static_assert(kAStages >= 2 * PW_SUB, "the TMEM weight ring holds at least two code groups (one converting, one draining)");
   static_assert((uint32_t)PW_ROWS * TN * 4 <= kOffP, "split-K partial fits over the low-rank and token rings");
   static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
 };
@@ -349,6 +352,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
     const uint32_t r7 = (uint32_t)(row & 7);
     const int spg = args.spg, gshift = spg == 8 ? 5 : spg == 4 ? 6 : spg == 2 ? 7 : 8;  // log2(G)
     bool ok = true;
+    int prev_nsub = 0;  // stages of the previous group whose TMEM stores are not yet published
     for (int gi = 0; gi < n_groups && ok; ++gi) {
       const int ps = gi % PW_PSTAGES;
       const int it0 = gi * PW_SUB;                 // first stage of the group (CTA-relative)
@@ -378,6 +382,14 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive_cta(bar(bars->empty_p[ps]));  // every lane has consumed its codes
+      // the previous group's TMEM stores drained while this group converted: publish them
+      if (gi > 0) {
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+          for (int j = 0; j < prev_nsub; ++j) mbar_arrive_cta(bar(bars->conv[(it0 - PW_SUB + j) % AS]));
+      }
 #pragma unroll
       for (int j = 0; j < PW_SUB; ++j) {
         if (j < nsub) {
@@ -390,11 +402,14 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
         }
       }
       if (!ok) break;
+      prev_nsub = nsub;
+    }
+    if (ok && n_groups > 0) {
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0)
-        for (int j = 0; j < nsub; ++j) mbar_arrive_cta(bar(bars->conv[(it0 + j) % AS]));
+        for (int j = 0; j < prev_nsub; ++j) mbar_arrive_cta(bar(bars->conv[((n_groups - 1) * PW_SUB + j) % AS]));
     }
     if (warp < 8) {
       // ---------------------------------------------- epilogue: TMEM -> registers -> out or partial
