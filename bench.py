@@ -383,15 +383,16 @@ def measure_small_batch(dev, flush, iters: int) -> dict:
     hbm = float(peaks.get("hbm_gbs") or 6650.0) * 1e9
     tc = _bf16_peak() * 1e12
     _, st = make_synthetic_state(256, K, N, RANK, GROUP, seed=9, device=dev)
-    mod = SVDQuantLinear(st, backend="b200", weight_operand="auto")
+    mod = SVDQuantLinear(st, backend="b200", weight_operand="fp16")
     p = mod.prepare(dev)
+    pk = SVDQuantLinear(st, backend="b200", weight_operand="packed").prepare(dev)
     r2 = p.up_hl.shape[1]
     out = {}
     for m in (16, 64, 256):
         x = torch.randn(m, K, device=dev).bfloat16()
         a16, mid, _, _ = ops.act_quant(x, p.smooth, p.l2, None, None, p.k_pad, 64, True, False)
         t_pk = statistics.median(_device_times(
-            lambda: ops.packed_gemm(a16, p.codes, p.scales16, GROUP, mid, p.up_hl, p.bias, False), iters, flush))
+            lambda: ops.packed_gemm(a16, pk.codes, pk.scales16, GROUP, mid, p.up_hl, p.bias, False), iters, flush))
         t_16 = statistics.median(_device_times(
             lambda: ops.linear_gemm(a16, p.w16, mid, p.up_hl, p.bias, False), iters, flush))
         t_lin = statistics.median(_device_times(lambda: mod(x), iters, flush))

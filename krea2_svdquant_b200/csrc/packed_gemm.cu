@@ -42,10 +42,11 @@
 // swizzle so the converters' shared loads are free of bank conflicts); warp 2 TMA of
 // the token tiles (a16, or mid_hl with up_hl for the low-rank stages); warp 1 TMEM allocation and
 // the MMA issue; warps 4-19 conversion (four warps per TMEM lane quarter); warps 4-7 the epilogue.
-// Waits spin on mbarrier.test_wait (a blocking try_wait costs a fraction of a microsecond even on a
-// completed phase, more than a stage here) and are bounded (error word codes 0x51xx-0x54xx); a wait
-// that runs out raises the CTA's abort flag and every role leaves its loop, so all CTAs still meet
-// at the cluster barriers.
+// The single-thread roles (TMA producers, MMA issue) wait by spinning on mbarrier.test_wait; the 16
+// converter warps and the epilogue wait with try_wait, which suspends them, so that waiting
+// converters do not take issue slots and shared-memory bandwidth from the MMA thread on their SMSP.
+// Every wait is bounded (error word codes 0x51xx-0x54xx); a wait that runs out raises the CTA's
+// abort flag and every role leaves its loop, so all CTAs still meet at the cluster barriers.
 #include <algorithm>
 
 #include "svdq_common.cuh"
@@ -357,7 +358,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
       const int ps = gi % PW_PSTAGES;
       const int it0 = gi * PW_SUB;                 // first stage of the group (CTA-relative)
       const int nsub = min(PW_SUB, n_res - it0);
-      ok = mbar_spin_wait(bar(bars->full_p[ps]), (uint32_t)(gi / PW_PSTAGES) & 1u, abort_flag, args.err,
+      ok = mbar_wait(bar(bars->full_p[ps]), (uint32_t)(gi / PW_PSTAGES) & 1u, abort_flag, args.err,
                           kPwWaitConvPacked);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;  // the lanes of a warp leave together
       const uint32_t srow = s_ring + (uint32_t)ps * PW_S_BYTES + (uint32_t)(row * spg) * 2u;
@@ -394,7 +395,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
       for (int j = 0; j < PW_SUB; ++j) {
         if (j < nsub) {
           const int it = it0 + j, as = it % AS;
-          ok = mbar_spin_wait(bar(bars->empty_a[as]), ((uint32_t)(it / AS) & 1u) ^ 1u, abort_flag, args.err,
+          ok = mbar_wait(bar(bars->empty_a[as]), ((uint32_t)(it / AS) & 1u) ^ 1u, abort_flag, args.err,
                               kPwWaitConvEmpty);
           if (!(ok = __all_sync(0xffffffffu, ok))) break;
           tc_fence_after();
@@ -416,7 +417,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
       const int erow = q * 32 + lane;
       const int n = n0 + erow;
       const uint32_t taddr = tmem + lane_off;
-      const bool done = mbar_spin_wait(bar(bars->mma_done), 0, abort_flag, args.err, kPwWaitEpilogue) && !*abort_flag;
+      const bool done = mbar_wait(bar(bars->mma_done), 0, abort_flag, args.err, kPwWaitEpilogue) && !*abort_flag;
       if (__all_sync(0xffffffffu, done)) {
         tc_fence_after();
         float bias_v = 0.f;

@@ -78,8 +78,8 @@ class PreparedOperands:
     lora_col_scale: torch.Tensor | None  # [rl8] fp32 multiplier per stacked row
     up_hl: torch.Tensor | None     # [n, R2] bf16, [l1 | lora_up] hi/lo operand
     up_hl_base: torch.Tensor | None  # same without the LoRA columns (for _forward_base)
-    w16: torch.Tensor | None       # [n, k_pad] fp16 = q * weight scale (weight_operand "fp16" / "auto")
-    codes: torch.Tensor | None     # [n, k_pad/2] u8 kernel-order codes (weight_operand "packed" / "auto")
+    w16: torch.Tensor | None       # [n, k_pad] fp16 = q * weight scale (weight_operand "fp16")
+    codes: torch.Tensor | None     # [n, k_pad/2] u8 kernel-order codes (weight_operand "packed")
     scales16: torch.Tensor | None  # fp16 group scales in the packed GEMM's tile order (with codes)
     bias: torch.Tensor | None      # [n] bf16
 
@@ -103,15 +103,14 @@ class SVDQuantLinear(nn.Module):
     """
 
     check_device_errors = False
-    # "auto": both weight operands, the packed-weight GEMM for batches of at most
-    # PACKED_MAX_TOKENS tokens (it reads 4x fewer weight bytes), the fp16-weight GEMM above;
-    # "fp16": only the load-time fp16 weight (4x the packed bytes); "packed": only the packed
-    # codes + fp16 scales (no fp16 weight is allocated; every batch size runs the packed GEMM).
-    WEIGHT_OPERANDS = ("auto", "fp16", "packed")
-    PACKED_MAX_TOKENS = 64
+    # "fp16" (default): the load-time fp16 weight q * s (4x the packed bytes) and the fp16-weight
+    # GEMM, the faster one at every batch size measured; "packed": only the kernel-order codes and
+    # fp16 scales (no fp16 weight is allocated: a quarter of the weight memory) and the
+    # packed-weight GEMM, which converts the codes on chip.
+    WEIGHT_OPERANDS = ("fp16", "packed")
 
     def __init__(self, state: SVDQuantLinearState, backend: BackendKind | str = BackendKind.AUTO,
-                 *, act_group_size: int = 64, weight_operand: str = "auto"):
+                 *, act_group_size: int = 64, weight_operand: str = "fp16"):
         super().__init__()
         self.backend = resolve_backend(backend)
         if weight_operand not in self.WEIGHT_OPERANDS:
@@ -227,12 +226,13 @@ class SVDQuantLinear(nn.Module):
                 up_hl_base = ops.build_up_hl(l1_in, None, r2b) if r2b else None
             qw = self.qweight.to(device=device).contiguous()
             ws = self.weight_scales.to(device=device).contiguous()
-            w16 = ops.repack_weight(qw, ws, self.group_size) if self.weight_operand != "packed" else None
-            codes = scales16 = None
-            if self.weight_operand == "packed" and self.group_size not in ops.PACKED_GROUP_SIZES:
-                raise ValueError(f"the packed-weight GEMM takes weight group sizes {ops.PACKED_GROUP_SIZES}, "
-                                 f"got {self.group_size} (use weight_operand='fp16')")
-            if self.weight_operand != "fp16" and self.group_size in ops.PACKED_GROUP_SIZES:
+            w16 = codes = scales16 = None
+            if self.weight_operand == "fp16":
+                w16 = ops.repack_weight(qw, ws, self.group_size)
+            else:
+                if self.group_size not in ops.PACKED_GROUP_SIZES:
+                    raise ValueError(f"the packed-weight GEMM takes weight group sizes {ops.PACKED_GROUP_SIZES}, "
+                                     f"got {self.group_size} (use weight_operand='fp16')")
                 codes, scales16, _ = ops.prepare_packed(qw, ws, self.group_size)
             bias = None if self.bias is None else self.bias.to(device=device, dtype=bf).contiguous()
         self._prepared = PreparedOperands(device=device, key=key, k_in=k_in, k_pad=k_pad, n=n, smooth=smooth,
@@ -268,7 +268,7 @@ class SVDQuantLinear(nn.Module):
             a16, mid, _, _ = ops.act_quant(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
                                            self.act_group_size, True, False)
         lowrank = (mid, up_hl) if mid.numel() else (None, None)
-        if p.w16 is None or (p.codes is not None and x2.shape[0] <= self.PACKED_MAX_TOKENS):
+        if p.w16 is None:
             y = ops.packed_gemm(a16, p.codes, p.scales16, self.group_size, *lowrank, p.bias, out_fp32)
         else:
             y = ops.linear_gemm(a16, p.w16, *lowrank, p.bias, out_fp32)

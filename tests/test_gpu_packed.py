@@ -143,16 +143,20 @@ def test_split_k_plans_are_exercised():
     assert len(seen - {1}) >= 2, seen
 
 
-def test_auto_dispatch_by_batch_size():
-    """weight_operand="auto" runs the packed GEMM up to PACKED_MAX_TOKENS tokens and the fp16-weight
-    GEMM above; both agree with their single-operand modules bit for bit."""
+def test_weight_operand_modes():
+    """"fp16" holds only the fp16 weight, "packed" only the codes and scales (a quarter of the bytes);
+    both agree to fp32 summation order; an unsupported group size is refused for "packed"."""
     from krea2_svdquant_b200.linear import SVDQuantLinear
     from krea2_svdquant_b200.quant import make_synthetic_state
     x, st = make_synthetic_state(300, 512, 384, 32, 64, seed=5, device="cuda")
-    auto = SVDQuantLinear(st, backend="b200")
     packed, fp16 = _module_pair(st)
-    small, large = x[: SVDQuantLinear.PACKED_MAX_TOKENS], x
-    assert torch.equal(auto(small), packed(small))
-    assert torch.equal(auto(large), fp16(large))
-    p = auto.prepare()
-    assert p.w16 is not None and p.codes is not None
+    pp, pf = packed.prepare(), fp16.prepare()
+    assert pp.w16 is None and pp.codes is not None and pf.codes is None and pf.w16 is not None
+    assert pp.codes.numel() * pp.codes.element_size() * 4 == pf.w16.numel() * pf.w16.element_size()
+    packed.output_fp32 = fp16.output_fp32 = True
+    assert O.rel_fro(packed(x).cpu().numpy(), fp16(x).cpu().numpy()) <= TOL_ORDER
+    st.group_size = 16
+    with pytest.raises(ValueError):
+        SVDQuantLinear(st, backend="b200", weight_operand="packed").prepare()
+    with pytest.raises(ValueError):
+        SVDQuantLinear(st, backend="b200", weight_operand="auto")
