@@ -80,8 +80,13 @@ int svdq_selftest_bounded_wait(int limit_us, cudaStream_t stream);
 
 /*
  * Device workspace (bytes) the activation passes need for the low-rank
- * down-projection: fp32 partial sums of K slices, combined in a fixed order
- * by a second launch.  0 when rank + lora_rank == 0 or mid is not requested.
+ * down-projection: 64 KiB of row-band arrival counters, then the fp32 partial
+ * sums of the K slices.  The last K slice of each row band to finish adds the
+ * partials in slice order (deterministic) and writes mid_hl, inside the same
+ * launch.  The workspace must be ZERO-FILLED before its first use and 256-byte
+ * aligned; every launch leaves the counters zero again, so it is zeroed only
+ * once.  One launch at a time per workspace (launches ordered on one stream
+ * are fine).  0 when rank + lora_rank == 0 or mid is not requested.
  */
 size_t svdq_act_quant_workspace_bytes(int M, int K_pad, int rank, int lora_rank);
 
@@ -100,7 +105,8 @@ size_t svdq_act_quant_workspace_bytes(int M, int K_pad, int rank, int lora_rank)
  * fp16 and are reported through svdq_device_error (code 0x4200).  Optional
  * outputs may be NULL: out_packed / out_scales (the
  * reference-format codes), out_a16 (the GEMM operand), out_mid_hl (needs
- * rank + lora_rank > 0 and a workspace of svdq_act_quant_workspace_bytes()).
+ * rank + lora_rank > 0 and a workspace of svdq_act_quant_workspace_bytes(),
+ * zero-filled before its first use as described there).
  * out_packed and out_scales are written together (both NULL or both set).
  *   a_group in {64, 128}; K_in <= K_pad; K_pad % 64 == 0; K_pad % a_group == 0;
  *   K_in % 8 == 0; rank % 8 == 0, lora_rank % 8 == 0, rank + lora_rank <= 256;
@@ -123,7 +129,8 @@ int svdq_act_quant(const void* x, int64_t ldx, const void* smooth,
  * warm-up).  The K-slice scratch is a file-scope device array of
  * svdq_act_quant_noalloc_scratch_bytes() (8 MiB) per device; a call needing
  * more (svdq_act_quant_workspace_bytes() > 8 MiB) returns
- * SVDQ_ERR_UNSUPPORTED.  The scratch address is looked up with
+ * SVDQ_ERR_UNSUPPORTED.  The array starts zero (static storage) and every call
+ * leaves its counter words zero, as the workspace contract above requires.  The scratch address is looked up with
  * cudaGetSymbolAddress on the first call in each CUDA context (the device's
  * primary context or another context the host made current), whatever that
  * call's arguments: if that first call would fall inside a stream capture,

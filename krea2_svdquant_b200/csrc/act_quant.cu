@@ -119,24 +119,28 @@ __device__ __forceinline__ uint64_t div_f2(uint64_t a, uint64_t y, uint64_t nb) 
   const uint64_t r = f2_fma(q0, nb, a);
   return f2_fma(r, y, q0);
 }
-// Elements where the Markstein quotient above may differ from IEEE division, as bits 15 / 31 of
-// the result (other bits are don't-care): x with 0 < |x| < 2^-118 (the residual r loses bits
-// below fp32's normal range), or a result that is inf / NaN or, in bf16, at least 2^126 (the
-// product a * y can overflow).  xv: the bf16x2 input; out: the bf16x2 (or f16x2) quotient.
-// Each 16-bit half is tested with one add: h + c sets bit 15 iff h >= 0x8000 - c, and no half
-// carries into the next (h <= 0x7FFF).
-template <bool F16OUT>
-__device__ __forceinline__ uint32_t outside_fast_division(uint32_t xv, uint32_t out) {
+// Where the Markstein quotient above may differ from IEEE division, as bits 15 / 31 of the result
+// (other bits are don't-care): x with 0 < |x| < 2^-118 (the residual r loses bits below fp32's
+// normal range; tested per element on the bf16x2 input), or a result that is inf / NaN or, in
+// bf16, at least 2^126 (the product a * y can overflow; tested on the fp16 output in W4A16 mode
+// and on each quantization group's |x_hat| maximum in W4A4 mode, whose max keeps NaNs).  Each
+// 16-bit half is tested with one add: h + c sets bit 15 iff h >= 0x8000 - c, and no half carries
+// into the next (h <= 0x7FFF).
+__device__ __forceinline__ uint32_t tiny_x_lanes(uint32_t xv) {
   const uint32_t t = xv & 0x7FFF7FFFu;
   const uint32_t nonzero = t + 0x7FFF7FFFu;       // bit 15: |x| bits >= 0x0001
   const uint32_t not_tiny = t + 0x7B807B80u;      // bit 15: |x| bits >= 0x0480 (2^-118)
-  const uint32_t big = (out & 0x7FFF7FFFu) + (F16OUT ? 0x04000400u : 0x01800180u);  // f16 >= inf; bf16 >= 2^126
-  return (nonzero & ~not_tiny) | big;
+  return nonzero & ~not_tiny;
 }
-// running max of |.| over bf16x2 lanes (the sign bit of the result is meaningless)
+// f16x2: bit 15 / 31 set for inf or NaN; bf16x2: for |v| >= 2^126, inf or NaN
+template <bool F16>
+__device__ __forceinline__ uint32_t big_lanes(uint32_t v) {
+  return (v & 0x7FFF7FFFu) + (F16 ? 0x04000400u : 0x01800180u);
+}
+// running max of |.| over bf16x2 lanes, NaN if either is NaN (the sign bit of the result is meaningless)
 __device__ __forceinline__ uint32_t bf2_maxabs(uint32_t m, uint32_t v) {
   uint32_t d;
-  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(m), "r"(v));
+  asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(m), "r"(v));
   return d;
 }
 
@@ -170,6 +174,10 @@ struct AqArgs {
   uint8_t* packed;        // [M, K_pad/2] or null
   __nv_bfloat16* scales;  // [M, K_pad/G] or null
   float* partial;         // [ksplit, M, r_tot] or null
+  uint32_t* counters;     // [bands * nz] arrival counters of the K slices (zero between launches)
+  __nv_bfloat16* mid_hl;  // [M, R2]
+  const float* lora_col_scale;
+  int R2, ksplit;
   int* err;
 };
 
@@ -359,6 +367,25 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
   };
   int pending = -1;  // chunk whose slot waits for its a16 store to finish reading
 
+  // x_hat of chunk c's fragments with IEEE division (__fdiv_rn), from the x tile in shared memory
+  auto ieee_stage = [&](uint32_t (&frj)[4][4], int c) {
+    const int s = c % STAGES;
+    const float4* tb = rst_p + c * (kBK / 2) + t4;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t xr[4];
+      ldmatrix_x4(xs + s * kXTileBytes + swz128(a_row, 2 * kk + a_chk), xr);
+      const float4 cA = tb[8 * kk], cB = tb[8 * kk + 4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float s0 = i < 2 ? -cA.z : -cB.z, s1 = i < 2 ? -cA.w : -cB.w;
+        const uint64_t q = f2_pack(__fdiv_rn(__uint_as_float(xr[i] << 16), s0),
+                                   __fdiv_rn(__uint_as_float(xr[i] & 0xFFFF0000u), s1));
+        frj[kk][i] = W4A16 ? f2_to_h2(q) : f2_to_bf2(q);
+      }
+    }
+  };
+
 #pragma unroll 1
   for (int c0 = 0; c0 < n_loc && ok; c0 += GS) {
     uint32_t fr[GS][4][4];  // x fragments, then x_hat fragments (bf16x2, or f16x2 in W4A16 mode)
@@ -387,25 +414,12 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
           const uint32_t xv = fr[j][kk][i];
           const uint64_t q = div_f2(bf2_to_f2(xv), i < 2 ? yA : yB, i < 2 ? nA : nB);
           fr[j][kk][i] = W4A16 ? f2_to_h2(q) : f2_to_bf2(q);
-          off_domain |= outside_fast_division<W4A16>(xv, fr[j][kk][i]);
+          off_domain |= tiny_x_lanes(xv);
+          if constexpr (W4A16) off_domain |= big_lanes<true>(fr[j][kk][i]);
         }
       }
-      if (slice_ieee || __any_sync(0xffffffffu, (off_domain & 0x80008000u) != 0)) {
-        // rare: redo the whole stage with IEEE division (the x tile is still in shared memory)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          uint32_t xr[4];
-          ldmatrix_x4(xs + s * kXTileBytes + swz128(a_row, 2 * kk + a_chk), xr);
-          const float4 cA = tb[8 * kk], cB = tb[8 * kk + 4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float s0 = i < 2 ? -cA.z : -cB.z, s1 = i < 2 ? -cA.w : -cB.w;
-            const uint64_t q = f2_pack(__fdiv_rn(__uint_as_float(xr[i] << 16), s0),
-                                       __fdiv_rn(__uint_as_float(xr[i] & 0xFFFF0000u), s1));
-            fr[j][kk][i] = W4A16 ? f2_to_h2(q) : f2_to_bf2(q);
-          }
-        }
-      }
+      if (slice_ieee || __any_sync(0xffffffffu, (off_domain & 0x80008000u) != 0))
+        ieee_stage(fr[j], c);  // rare: the x tile is still in shared memory
       if constexpr (!W4A16) {
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
@@ -434,6 +448,23 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
         uint32_t both = bf2_maxabs(__byte_perm(mx[0], mx[1], 0x5410), __byte_perm(mx[0], mx[1], 0x7632));
         both = bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 1));
         both = bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 2));
+        if (__any_sync(0xffffffffu, (big_lanes<false>(both) & 0x80008000u) != 0) && !slice_ieee) {
+          // rare: a quotient of the group reached 2^126, inf or NaN; redo the group with IEEE division
+#pragma unroll
+          for (int j = 0; j < GS; ++j) ieee_stage(fr[j], c0 + j);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t m = 0;
+#pragma unroll
+            for (int j = 0; j < GS; ++j)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) m = bf2_maxabs(m, bf2_maxabs(fr[j][kk][h], fr[j][kk][h + 2]));
+            mx[h] = m;
+          }
+          both = bf2_maxabs(__byte_perm(mx[0], mx[1], 0x5410), __byte_perm(mx[0], mx[1], 0x7632));
+          both = bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 1));
+          both = bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 2));
+        }
         const float am[2] = {fabsf(__uint_as_float(both << 16)), fabsf(__uint_as_float(both & 0xFFFF0000u))};
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -515,21 +546,57 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
     release(pending % STAGES, pending);
   }
 
-  pdl_trigger();  // the finalize launch may start its prologue
+  pdl_trigger();  // the next kernel may start its prologue (it waits for this grid before reading)
 
-  // ---- fp32 partial of the low-rank projection over this K slice ----
+  // ---- low-rank projection: fp32 partial of this K slice; the last slice of a band adds them ----
   if constexpr (NT > 0) {
-    if (ok && a.partial) {
-      float* part = a.partial + (int64_t)blockIdx.y * a.M * a.r_tot;
+    if (a.partial) {
+      if (ok) {
+        float* part = a.partial + (int64_t)blockIdx.y * a.M * a.r_tot;
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (t < ntl) {
-          const int col = r0 + 8 * t + 2 * t4;
-          if (row_g < a.M)
-            *reinterpret_cast<float2*>(part + (int64_t)row_g * a.r_tot + col) = make_float2(acc[t][0], acc[t][1]);
-          if (row_g8 < a.M)
-            *reinterpret_cast<float2*>(part + (int64_t)row_g8 * a.r_tot + col) = make_float2(acc[t][2], acc[t][3]);
+        for (int t = 0; t < NT; ++t) {
+          if (t < ntl) {
+            const int col = r0 + 8 * t + 2 * t4;
+            if (row_g < a.M)
+              __stcg(reinterpret_cast<float2*>(part + (int64_t)row_g * a.r_tot + col), make_float2(acc[t][0], acc[t][1]));
+            if (row_g8 < a.M)
+              __stcg(reinterpret_cast<float2*>(part + (int64_t)row_g8 * a.r_tot + col), make_float2(acc[t][2], acc[t][3]));
+          }
         }
+      }
+      // every CTA of the band arrives, aborted or not, so the count always completes and resets
+      __threadfence();
+      __syncthreads();
+      int* last = issued + STAGES + 1;
+      uint32_t* counter = a.counters + (blockIdx.z * gridDim.x + blockIdx.x);
+      if (tid == 0) {
+        uint32_t old;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+        *last = old == (uint32_t)(a.ksplit - 1);
+      }
+      __syncthreads();
+      if (*last) {
+        // mid_hl of the band's rows and this CTA's columns: the K-slice partials summed in slice
+        // order (deterministic), LoRA columns scaled, split into bf16 hi + lo
+        __threadfence();
+        const int cols = 8 * ntl;
+        const int rows = min(kBM, a.M - m0);
+        for (int i = tid; i < rows * cols; i += kThreads) {
+          const int rr = i / cols, j = r0 + i % cols;
+          const int64_t row = m0 + rr;
+          float v = 0.f;
+          for (int k = 0; k < a.ksplit; ++k) v += __ldcg(a.partial + ((int64_t)k * a.M + row) * a.r_tot + j);
+          if (j >= a.rank) v *= a.lora_col_scale[j - a.rank];
+          const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+          a.mid_hl[row * a.R2 + j] = hi;
+          a.mid_hl[row * a.R2 + a.r_tot + j] = __float2bfloat16_rn(v - __bfloat162float(hi));
+        }
+        if (blockIdx.z == 0) {  // zero padding columns [2 r_tot, R2)
+          const int pad = a.R2 - 2 * a.r_tot;
+          for (int i = tid; i < rows * pad; i += kThreads)
+            a.mid_hl[(int64_t)(m0 + i / pad) * a.R2 + 2 * a.r_tot + i % pad] = __float2bfloat16_rn(0.f);
+        }
+        if (tid == 0) *counter = 0u;  // every other CTA of the band has arrived: ready for the next launch
       }
     }
   }
@@ -541,31 +608,6 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
     for (int s = 0; s < STAGES; ++s)
       if (issued[s] > 0 && !mbar_wait_drain(full_bar(s), (uint32_t)((issued[s] - 1) & 1), kWaitLimitNs))
         atomicCAS(a.err, 0, 0x4180 + s);
-  }
-}
-
-// mid_hl[m] = [hi(v) | lo(v) | 0], v = (sum of the K-slice partials, in slice order) * column scale
-// (LoRA columns), hi = bf16(v), lo = bf16(v - hi).
-__global__ void mid_finalize_kernel(const float* __restrict__ partial, int ksplit, int M, int rank, int r_tot,
-                                    const float* __restrict__ lora_col_scale, __nv_bfloat16* __restrict__ mid_hl,
-                                    int R2) {
-  pdl_wait();
-  pdl_trigger();
-  const int w = R2 - r_tot;  // work items per row: r_tot (hi+lo pairs) + zero padding
-  const int64_t total = (int64_t)M * w;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int row = (int)(i / w), j = (int)(i % w);
-    __nv_bfloat16* out = mid_hl + (int64_t)row * R2;
-    if (j < r_tot) {
-      float v = 0.f;
-      for (int k = 0; k < ksplit; ++k) v += partial[((int64_t)k * M + row) * r_tot + j];
-      if (j >= rank) v *= lora_col_scale[j - rank];
-      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-      out[j] = hi;
-      out[r_tot + j] = __float2bfloat16_rn(v - __bfloat162float(hi));
-    } else {
-      out[r_tot + j] = __float2bfloat16_rn(0.f);
-    }
   }
 }
 
@@ -640,11 +682,19 @@ Geometry geometry(int M, int K_pad, int r_use, int step) {
   return gm;
 }
 
-// Covers both slice steps, so one size serves every group size and mode.
+// Workspace: kCounterBytes of arrival counters (one per row band and low-rank CTA column; zero
+// between launches), then the fp32 K-slice partials.  Covers both slice steps, so one size serves
+// every group size and mode.
+constexpr size_t kCounterBytes = 64 * 1024;
 size_t workspace_bytes(int M, int K_pad, int r_tot) {
   if (r_tot <= 0 || M <= 0 || K_pad <= 0) return 0;
   const int ksplit = std::max(geometry(M, K_pad, r_tot, 1).ksplit, geometry(M, K_pad, r_tot, 2).ksplit);
-  return sizeof(float) * (size_t)ksplit * (size_t)M * (size_t)r_tot;
+  return kCounterBytes + sizeof(float) * (size_t)ksplit * (size_t)M * (size_t)r_tot;
+}
+// Counters one launch uses (row bands x low-rank CTA columns).
+size_t counters_needed(int M, int K_pad, int r_tot, int step) {
+  const Geometry gm = geometry(M, K_pad, r_tot, step);
+  return (size_t)((M + cta_rows(gm.nt) - 1) / cta_rows(gm.nt)) * gm.nz;
 }
 
 struct LaunchSpec {
@@ -699,25 +749,8 @@ int launch_l(const LaunchSpec& L, cudaStream_t stream) {
 }
 
 int launch(const LaunchSpec& L, cudaStream_t stream) {
-  const int st = L.args.lora_rank > 0 ? launch_l<true>(L, stream) : launch_l<false>(L, stream);
-  if (st || !L.args.partial) return st;
-  const int64_t items = (int64_t)L.args.M * (L.R2 - L.args.r_tot);
-  const int blocks = (int)std::min<int64_t>((items + 255) / 256, (int64_t)num_sms() * 8);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(blocks);
-  cfg.blockDim = dim3(256);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, mid_finalize_kernel, (const float*)L.args.partial, L.gm.ksplit,
-                                           L.args.M, L.args.rank, L.args.r_tot, L.lora_col_scale, L.mid_hl, L.R2);
-  if (e != cudaSuccess) return check_cuda(e, "activation pass finalize");
-  return check_launch("activation pass finalize");
+  return L.args.lora_rank > 0 ? launch_l<true>(L, stream) : launch_l<false>(L, stream);
 }
-
 int validate_common(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank, const void* lora_down,
                     const float* lora_col_scale, int lora_rank, int M, int K_in, int K_pad, void* out_a16,
                     void* out_mid_hl, int R2, void* workspace, size_t ws_bytes, const char* who) {
@@ -742,7 +775,9 @@ int validate_common(const void* x, int64_t ldx, const void* smooth, const void* 
   if (out_mid_hl && r_tot > 0 && M > 0) {
     if (!workspace || ws_bytes < workspace_bytes(M, K_pad, r_tot))
       return bad("workspace missing or smaller than svdq_act_quant_workspace_bytes()");
-    if (reinterpret_cast<uintptr_t>(workspace) & 15u) return bad("workspace must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return bad("workspace must be 256-byte aligned");
+    if (std::max(counters_needed(M, K_pad, r_tot, 1), counters_needed(M, K_pad, r_tot, 2)) * 4 > kCounterBytes)
+      return set_error(SVDQ_ERR_UNSUPPORTED, w + ": M too large for the workspace's row-band counters");
   }
   return SVDQ_OK;
 }
@@ -788,7 +823,12 @@ int build_spec(LaunchSpec& L, const void* x, int64_t ldx, const void* smooth, co
   p.smooth = static_cast<const __nv_bfloat16*>(smooth);
   p.packed = static_cast<uint8_t*>(out_packed);
   p.scales = static_cast<__nv_bfloat16*>(out_scales);
-  p.partial = want_mid ? static_cast<float*>(workspace) : nullptr;
+  p.partial = want_mid ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes) : nullptr;
+  p.counters = want_mid ? static_cast<uint32_t*>(workspace) : nullptr;
+  p.mid_hl = static_cast<__nv_bfloat16*>(out_mid_hl);
+  p.lora_col_scale = lora_col_scale;
+  p.R2 = R2;
+  p.ksplit = L.gm.ksplit;
   p.err = device_error_word();
   if (!p.err) return set_error(SVDQ_ERR_CUDA, "device error word unavailable");
   L.gs = G / kBK;

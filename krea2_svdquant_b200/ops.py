@@ -58,9 +58,30 @@ def _lowrank_args(l2, lora_down):
     return rank, lrank, lowrank_width(rank + lrank)
 
 
+_GEMM_WS_KEEP = 8  # workspaces kept per kind (most recently used (device, stream) pairs)
+_act_ws: "collections.OrderedDict[tuple, Tensor]" = collections.OrderedDict()
+_act_ws_lock = threading.Lock()
+
+
 def _workspace(m: int, k_pad: int, rank: int, lrank: int, dev: torch.device) -> Tensor:
+    """The activation pass's workspace: row-band arrival counters, zero between launches (each launch
+    leaves them zero), then the fp32 K-slice partials.  One per (device, stream), kept and grown
+    (zero-filled) as larger calls need; launches on one stream run in order, so they share it.
+    Inside a CUDA graph capture a fresh zero-filled workspace is made (its zero fill is captured
+    too), so a graph never holds the address of a cached workspace that may be freed later."""
     n = int(_lib.lib().svdq_act_quant_workspace_bytes(m, k_pad, rank, lrank))
-    return torch.empty((max(n, 0),), dtype=torch.uint8, device=dev)
+    if torch.cuda.is_current_stream_capturing():
+        return torch.zeros((max(n, 0),), dtype=torch.uint8, device=dev)
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    with _act_ws_lock:
+        ws = _act_ws.get(key)
+        if ws is None or ws.numel() < n:
+            ws = torch.zeros((max(n, 2 * (0 if ws is None else ws.numel())),), dtype=torch.uint8, device=dev)
+            _act_ws[key] = ws
+        _act_ws.move_to_end(key)
+        while len(_act_ws) > _GEMM_WS_KEEP:
+            _act_ws.popitem(last=False)
+    return ws
 
 
 @torch.library.custom_op("svdq_b200::act_quant", mutates_args=())
@@ -199,7 +220,6 @@ def _(l1, lora_up, r2):
 # --------------------------------------------------------------------------- GEMM
 _gemm_ws: "collections.OrderedDict[tuple, Tensor]" = collections.OrderedDict()
 _gemm_ws_lock = threading.Lock()
-_GEMM_WS_KEEP = 8  # workspaces kept (most recently used (device, stream) pairs)
 
 
 def _gemm_workspace(dev: torch.device) -> Optional[Tensor]:
