@@ -51,8 +51,13 @@ __host__ __device__ constexpr int cta_warps(int nt) { return nt >= 8 ? 8 : 4; }
 __host__ __device__ constexpr int cta_rows(int nt) { return 16 * cta_warps(nt); }
 constexpr int kBK = 64;              // columns per stage: one 128-byte swizzle row of bf16
 constexpr int kTargetCtasPerSm = 4;
-// x / low-rank ring depth: 4, or 3 with twelve low-rank tiles so that three CTAs still fit an SM.
-__host__ __device__ constexpr int ring_stages(int nt) { return nt >= 12 ? 3 : 4; }
+// x / low-rank ring depth and a16 staging tiles per warp (16 rows x 64 columns of fp16 each):
+// four stages and two tiles (a warp writes one while the TMA store of the other reads it) without
+// a low-rank operand; three stages and one tile with one, so that four 64-row or two 128-row CTAs
+// fit an SM and the K split fills one wave.
+__host__ __device__ constexpr int ring_stages(int nt) { return nt == 0 ? 4 : 3; }
+__host__ __device__ constexpr int out_bufs(int nt) { return nt == 0 ? 2 : 1; }
+constexpr uint32_t kOutTileBytes = 16 * 64 * 2;
 // Stages per CTA slice, which bounds the reciprocal table: 16 with eight or more low-rank tiles
 // (their CTAs fit three per SM either way), else 12 (a 16-stage table would push the CTA past a
 // quarter of the SM's shared memory).
@@ -137,6 +142,11 @@ template <bool F16>
 __device__ __forceinline__ uint32_t big_lanes(uint32_t v) {
   return (v & 0x7FFF7FFFu) + (F16 ? 0x04000400u : 0x01800180u);
 }
+__device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 v) {
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  return u;
+}
 // running max of |.| over bf16x2 lanes, NaN if either is NaN (the sign bit of the result is meaningless)
 __device__ __forceinline__ uint32_t bf2_maxabs(uint32_t m, uint32_t v) {
   uint32_t d;
@@ -164,6 +174,8 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t addr, uint32_t v) 
 }
 
 struct AqArgs {
+  const __nv_bfloat16* x;  // [M, K_in], row stride ldx (read directly only by the IEEE-division path)
+  int64_t ldx;
   int M, K_in, K_pad;
   int rank, lora_rank, r_tot;
   int n_stages;      // K_pad / 64
@@ -184,7 +196,8 @@ struct AqArgs {
 template <int STAGES, int NT>
 __host__ __device__ constexpr uint32_t aq_smem_layout_bytes() {
   return 1024 /*align slack*/ + STAGES * x_tile_bytes(NT) + STAGES * NT * kLrTileBytes +
-         max_slice_stages(NT) * 32 * 16 /*reciprocal table*/ + 256 /*barriers, counters*/;
+         cta_warps(NT) * out_bufs(NT) * kOutTileBytes + max_slice_stages(NT) * 32 * 16 /*reciprocal table*/ +
+         256 /*barriers, counters*/;
 }
 
 // GS: stages per quantization group (1: G=64, 2: G=128).  NT: 8-column
@@ -209,8 +222,10 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t xs = base;
+  constexpr int kOB = out_bufs(NT);
   const uint32_t ws = xs + STAGES * kXTileBytes;
-  const uint32_t rst = ws + STAGES * NT * kLrTileBytes;
+  const uint32_t obuf = ws + STAGES * NT * kLrTileBytes;  // 1 KB aligned (x and low-rank tiles are)
+  const uint32_t rst = obuf + kWarps * kOB * kOutTileBytes;
   const uint32_t bars = rst + max_slice_stages(NT) * 32 * 16;
   uint8_t* gbase = smem_raw + (base - smem_u32(smem_raw));
   const float4* rst_p = reinterpret_cast<const float4*>(gbase + (rst - base));
@@ -274,7 +289,13 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
       sv[u][0] = live && col < a.K_in ? __bfloat162float(a.smooth[col]) : 1.f;
       sv[u][1] = live && col + 1 < a.K_in ? __bfloat162float(a.smooth[col + 1]) : 1.f;
     }
-    int odd_smooth = 0;  // a smoothing factor outside the normal range (zero, subnormal, inf, NaN)
+    // A smoothing factor outside the normal range (zero, subnormal, inf, NaN), or in W4A4 mode below
+    // 2^-64, sends the slice through IEEE division: with every |s| >= 2^-64, an x whose Markstein
+    // quotient may be off (|x| < 2^-118) has |x_hat| < 2^-53, far below the smallest group scale
+    // (bf16(1e-8) / 7), so it can neither be a group maximum that sets the scale nor get a nonzero
+    // code, and the codes and scales stay exact without a per-element test.
+    constexpr float kSmoothMin = W4A16 ? 1.17549435e-38f : 5.42101086e-20f;
+    int odd_smooth = 0;
 #pragma unroll
     for (int u = 0; u < kTblIters; ++u) {
       const int i = tid + u * kThreads;
@@ -283,7 +304,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const float m = fabsf(sv[u][h]);
-          odd_smooth |= !(m >= 1.17549435e-38f && m <= 3.40282347e38f);
+          odd_smooth |= !(m >= kSmoothMin && m <= 3.40282347e38f);
         }
       }
     }
@@ -304,7 +325,6 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
   const int wrow = warp * 16;              // first row of this warp within the CTA tile
   const int row_g = m0 + wrow + g;         // global rows held by this lane
   const int row_g8 = row_g + 8;
-  const uint32_t my_rows = (uint32_t)warp * (16 * kBK * 2);  // this warp's 16 rows within an x stage
   const bool write_a16 = a.write_a16 != 0;
   const uint32_t cnt_base = smem_u32(cnt);
   bool ok = true;
@@ -357,7 +377,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
     }
   };
 
-  // lane 0: count this warp's release of stage-slot s (chunk c); the fourth release refills it
+  // lane 0: count this warp's release of stage-slot s (chunk c); the last release refills it
   auto release = [&](int s, int c) {
     const uint32_t old = atom_add_acq_rel(cnt_base + 4u * (uint32_t)s, 1u);
     if ((old & (kWarps - 1)) == kWarps - 1) {
@@ -365,31 +385,55 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
       if (c + STAGES < n_loc) issue(s, c + STAGES);
     }
   };
-  int pending = -1;  // chunk whose slot waits for its a16 store to finish reading
 
-  // x_hat of chunk c's fragments with IEEE division (__fdiv_rn), from the x tile in shared memory
-  auto ieee_stage = [&](uint32_t (&frj)[4][4], int c) {
-    const int s = c % STAGES;
+  // x_hat of chunk c's fragments with IEEE division (__fdiv_rn), x read from global memory in
+  // the fragment layout (the stage may already be refilled); rows >= M and columns >= K_in read
+  // as zero, as the TMA box does.  Rare: see the exact-division note at the top of the file.
+  auto ieee_chunk = [&](uint32_t (&frj)[4][4], int c) {
     const float4* tb = rst_p + c * (kBK / 2) + t4;
+    const int kcol = (st0 + c) * kBK + 2 * t4;
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      uint32_t xr[4];
-      ldmatrix_x4(xs + s * kXTileBytes + swz128(a_row, 2 * kk + a_chk), xr);
       const float4 cA = tb[8 * kk], cB = tb[8 * kk + 4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
+        const int row = (i & 1) ? row_g8 : row_g;
+        const int col = kcol + 16 * kk + (i >= 2 ? 8 : 0);
+        const uint32_t xr = (row < a.M && col < a.K_in)
+                                ? __ldg(reinterpret_cast<const unsigned int*>(a.x + (int64_t)row * a.ldx + col))
+                                : 0u;
         const float s0 = i < 2 ? -cA.z : -cB.z, s1 = i < 2 ? -cA.w : -cB.w;
-        const uint64_t q = f2_pack(__fdiv_rn(__uint_as_float(xr[i] << 16), s0),
-                                   __fdiv_rn(__uint_as_float(xr[i] & 0xFFFF0000u), s1));
+        const uint64_t q = f2_pack(__fdiv_rn(__uint_as_float(xr << 16), s0),
+                                   __fdiv_rn(__uint_as_float(xr & 0xFFFF0000u), s1));
         frj[kk][i] = W4A16 ? f2_to_h2(q) : f2_to_bf2(q);
       }
     }
   };
+  // |x_hat| maxima of rows g (low half) and g + 8 (high half) over the group, reduced over the
+  // row's four lanes (NaN if any element is NaN)
+  auto group_max = [&](const uint32_t (&frg)[GS][4][4]) {
+    uint32_t mx[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t m = bf2_maxabs(frg[0][0][h], frg[0][0][h + 2]);
+#pragma unroll
+      for (int j = 0; j < GS; ++j)
+#pragma unroll
+        for (int kk = (j == 0 ? 1 : 0); kk < 4; ++kk) m = bf2_maxabs(m, bf2_maxabs(frg[j][kk][h], frg[j][kk][h + 2]));
+      mx[h] = m;
+    }
+    uint32_t both = bf2_maxabs(__byte_perm(mx[0], mx[1], 0x5410), __byte_perm(mx[0], mx[1], 0x7632));
+    both = bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 1));
+    return bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 2));
+  };
+
+  const uint32_t ob_base = obuf + (uint32_t)warp * (kOB * kOutTileBytes);  // this warp's a16 staging
+  int n_stored = 0;  // a16 stores this warp has issued (lane 0 commits one bulk group per store)
 
 #pragma unroll 1
   for (int c0 = 0; c0 < n_loc && ok; c0 += GS) {
     uint32_t fr[GS][4][4];  // x fragments, then x_hat fragments (bf16x2, or f16x2 in W4A16 mode)
-    uint32_t mxk[GS][4][2];  // per k16 block: |x_hat| max of rows g and g+8 (bf16x2 lanes)
+    // ---- per chunk: load the x fragments, LoRA MMAs on raw x, x_hat = x / smooth ----
 #pragma unroll
     for (int j = 0; j < GS; ++j) {
       const int c = c0 + j, s = c % STAGES;
@@ -402,7 +446,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
       for (int kk = 0; kk < 4; ++kk) ldmatrix_x4(xs + s * kXTileBytes + swz128(a_row, 2 * kk + a_chk), fr[j][kk]);
       if constexpr (LORA) lowrank_mma(fr[j], s, true);  // LoRA down-projection on raw x
       const float4* tb = rst_p + c * (kBK / 2) + t4;
-      uint32_t off_domain = 0;  // bit 15 / 31 set: some element of this stage needs IEEE division
+      uint32_t off_domain = 0;  // W4A16: bit 15 / 31 set where an element needs IEEE division
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const float4 cA = tb[8 * kk], cB = tb[8 * kk + 4];
@@ -414,136 +458,106 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
           const uint32_t xv = fr[j][kk][i];
           const uint64_t q = div_f2(bf2_to_f2(xv), i < 2 ? yA : yB, i < 2 ? nA : nB);
           fr[j][kk][i] = W4A16 ? f2_to_h2(q) : f2_to_bf2(q);
-          off_domain |= tiny_x_lanes(xv);
-          if constexpr (W4A16) off_domain |= big_lanes<true>(fr[j][kk][i]);
+          if constexpr (W4A16) off_domain |= tiny_x_lanes(xv) | big_lanes<true>(fr[j][kk][i]);
         }
       }
-      if (slice_ieee || __any_sync(0xffffffffu, (off_domain & 0x80008000u) != 0))
-        ieee_stage(fr[j], c);  // rare: the x tile is still in shared memory
-      if constexpr (!W4A16) {
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          mxk[j][kk][0] = bf2_maxabs(fr[j][kk][0], fr[j][kk][2]);
-          mxk[j][kk][1] = bf2_maxabs(fr[j][kk][1], fr[j][kk][3]);
-        }
-      }
+      if (slice_ieee || (W4A16 && __any_sync(0xffffffffu, (off_domain & 0x80008000u) != 0)))
+        ieee_chunk(fr[j], c);  // rare
     }
     if (!ok) break;
+
+    // ---- W4A4: group maxima; a quotient of 2^126 or more (or inf / NaN) redoes the group ----
+    uint32_t both = 0;
+    if constexpr (!W4A16) {
+      both = group_max(fr);
+      if (!slice_ieee && __any_sync(0xffffffffu, (big_lanes<false>(both) & 0x80008000u) != 0)) {
+#pragma unroll
+        for (int j = 0; j < GS; ++j) ieee_chunk(fr[j], c0 + j);
+        both = group_max(fr);
+      }
+    }
+    // ---- l2 MMAs on x_hat, then the group's stages go back to the ring ----
+    if (ntl > 0 && a.rank > 0 && r0 < a.rank) {
+#pragma unroll
+      for (int j = 0; j < GS; ++j) lowrank_mma(fr[j], (c0 + j) % STAGES, false);
+    }
+    __syncwarp();
+    if (lane == 0) {
+#pragma unroll
+      for (int j = 0; j < GS; ++j) release((c0 + j) % STAGES, c0 + j);
+    }
+    if (!emit) continue;
 
     // ---- group scale of rows g and g+8 (W4A4) ----
     uint64_t sc2[2], ys2[2], ns2[2], nms2[2];  // scale, RN(1/scale), -scale, -kMagic * scale
     if constexpr (!W4A16) {
-      if (emit) {
-        uint32_t mx[2];
+      const float am[2] = {fabsf(__uint_as_float(both << 16)), fabsf(__uint_as_float(both & 0xFFFF0000u))};
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t m01 = bf2_maxabs(mxk[0][0][h], mxk[0][1][h]), m23 = bf2_maxabs(mxk[0][2][h], mxk[0][3][h]);
-          if constexpr (GS == 2) {
-            m01 = bf2_maxabs(m01, bf2_maxabs(mxk[GS - 1][0][h], mxk[GS - 1][1][h]));
-            m23 = bf2_maxabs(m23, bf2_maxabs(mxk[GS - 1][2][h], mxk[GS - 1][3][h]));
-          }
-          mx[h] = bf2_maxabs(m01, m23);
-        }
-        // both rows' maxima in one bf16x2 (row g low, row g+8 high), reduced over the 4 lanes of the row
-        uint32_t both = bf2_maxabs(__byte_perm(mx[0], mx[1], 0x5410), __byte_perm(mx[0], mx[1], 0x7632));
-        both = bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 1));
-        both = bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 2));
-        if (__any_sync(0xffffffffu, (big_lanes<false>(both) & 0x80008000u) != 0) && !slice_ieee) {
-          // rare: a quotient of the group reached 2^126, inf or NaN; redo the group with IEEE division
-#pragma unroll
-          for (int j = 0; j < GS; ++j) ieee_stage(fr[j], c0 + j);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint32_t m = 0;
-#pragma unroll
-            for (int j = 0; j < GS; ++j)
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk) m = bf2_maxabs(m, bf2_maxabs(fr[j][kk][h], fr[j][kk][h + 2]));
-            mx[h] = m;
-          }
-          both = bf2_maxabs(__byte_perm(mx[0], mx[1], 0x5410), __byte_perm(mx[0], mx[1], 0x7632));
-          both = bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 1));
-          both = bf2_maxabs(both, __shfl_xor_sync(0xffffffffu, both, 2));
-        }
-        const float am[2] = {fabsf(__uint_as_float(both << 16)), fabsf(__uint_as_float(both & 0xFFFF0000u))};
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float v = fmaxf(am[h], eps);
-          const float q0 = v * y7;
-          const float sc = __bfloat162float(__float2bfloat16_rn(fmaf(fmaf(-q0, 7.0f, v), y7, q0)));
-          const float ys = __frcp_rn(sc);
-          a16_range |= sc > kA16ScaleMax;
-          sc2[h] = f2_pack(sc, sc);
-          ys2[h] = f2_pack(ys, ys);
-          ns2[h] = f2_pack(-sc, -sc);
-          nms2[h] = f2_pack(-kMagic * sc, -kMagic * sc);
-          if constexpr (PACKED) {
-            const int row = h ? row_g8 : row_g;
-            if (t4 == 0 && row < a.M && a.scales)
-              a.scales[(int64_t)row * (a.K_pad / a.G) + (st0 + c0) * kBK / a.G] = __float2bfloat16_rn(sc);
-          }
+      for (int h = 0; h < 2; ++h) {
+        const float v = fmaxf(am[h], eps);
+        const float q0 = v * y7;
+        const float sc = __bfloat162float(__float2bfloat16_rn(fmaf(fmaf(-q0, 7.0f, v), y7, q0)));
+        const float ys = __frcp_rn(sc);
+        a16_range |= sc > kA16ScaleMax;
+        sc2[h] = f2_pack(sc, sc);
+        ys2[h] = f2_pack(ys, ys);
+        ns2[h] = f2_pack(-sc, -sc);
+        nms2[h] = f2_pack(-kMagic * sc, -kMagic * sc);
+        if constexpr (PACKED) {
+          const int row = h ? row_g8 : row_g;
+          if (t4 == 0 && row < a.M && a.scales)
+            a.scales[(int64_t)row * (a.K_pad / a.G) + (st0 + c0) * kBK / a.G] = __float2bfloat16_rn(sc);
         }
       }
     }
 
+    // ---- per chunk: codes, a16 through this warp's staging tile and a TMA store ----
 #pragma unroll
     for (int j = 0; j < GS; ++j) {
-      const int c = c0 + j, s = c % STAGES;
+      const int c = c0 + j;
       const int kcol = (st0 + c) * kBK;
-      const uint32_t my_tile = xs + s * kXTileBytes + my_rows;  // a16 overwrites this warp's x rows
-      const bool store = emit && write_a16;
-      if (emit) {
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          uint32_t o[4];
-          if constexpr (W4A16) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) o[i] = fr[j][kk][i];
-          } else {
-            uint32_t nib[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int h = i & 1;
-              const uint64_t q = div_f2(bf2_to_f2(fr[j][kk][i]), ys2[h], ns2[h]);
-              const uint64_t m = f2_add(q, mag2);                 // low mantissa bits = rint(q)
-              o[i] = f2_to_h2(f2_fma(m, sc2[h], nms2[h]));         // rint(q) * scale, exact in fp16
-              // offset-binary code q + 8 = two's-complement low nibble with its top bit flipped
-              nib[i] = (((uint32_t)m & 0xFu) | (((uint32_t)(m >> 32) & 0xFu) << 4)) ^ 0x88u;
-            }
-            if constexpr (PACKED) {
-              uint8_t* prow_g = a.packed + (int64_t)row_g * (a.K_pad / 2) + (kcol + 16 * kk + 2 * t4) / 2;
-              uint8_t* prow_g8 = prow_g + (int64_t)8 * (a.K_pad / 2);
-              if (row_g < a.M) { prow_g[0] = (uint8_t)nib[0]; prow_g[4] = (uint8_t)nib[2]; }
-              if (row_g8 < a.M) { prow_g8[0] = (uint8_t)nib[1]; prow_g8[4] = (uint8_t)nib[3]; }
-            }
-          }
-          if (store) stmatrix_x4(my_tile + swz128(lane & 15, 2 * kk + (lane >> 4)), o[0], o[1], o[2], o[3]);
-        }
-        if (store) fence_proxy_async_smem();
+      const uint32_t my_tile = ob_base + (uint32_t)(n_stored % kOB) * kOutTileBytes;
+      if (write_a16) {
+        // the store that last used this staging tile must have read it
+        if (lane == 0 && n_stored >= kOB) bulk_wait_read<kOB - 1>();
+        __syncwarp();
       }
-      if (ntl > 0 && a.rank > 0 && r0 < a.rank) lowrank_mma(fr[j], s, false);  // l2 on x_hat
-
-      // one single-lane section per stage: store this stage's a16, then release the
-      // previous stage once its store has read the tile (or this one, without a store)
-      __syncwarp();
-      if (lane == 0) {
-        if (store) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t o[4];
+        if constexpr (W4A16) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) o[i] = fr[j][kk][i];
+        } else {
+          uint32_t nib[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int h = i & 1;
+            const uint64_t q = div_f2(bf2_to_f2(fr[j][kk][i]), ys2[h], ns2[h]);
+            const uint64_t m = f2_add(q, mag2);                 // low mantissa bits = rint(q)
+            o[i] = f2_to_h2(f2_fma(m, sc2[h], nms2[h]));         // rint(q) * scale, exact in fp16
+            // offset-binary code q + 8 = two's-complement low nibble with its top bit flipped
+            nib[i] = (((uint32_t)m & 0xFu) | (((uint32_t)(m >> 32) & 0xFu) << 4)) ^ 0x88u;
+          }
+          if constexpr (PACKED) {
+            uint8_t* prow_g = a.packed + (int64_t)row_g * (a.K_pad / 2) + (kcol + 16 * kk + 2 * t4) / 2;
+            uint8_t* prow_g8 = prow_g + (int64_t)8 * (a.K_pad / 2);
+            if (row_g < a.M) { prow_g[0] = (uint8_t)nib[0]; prow_g[4] = (uint8_t)nib[2]; }
+            if (row_g8 < a.M) { prow_g8[0] = (uint8_t)nib[1]; prow_g8[4] = (uint8_t)nib[3]; }
+          }
+        }
+        if (write_a16) stmatrix_x4(my_tile + swz128(lane & 15, 2 * kk + (lane >> 4)), o[0], o[1], o[2], o[3]);
+      }
+      if (write_a16) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
           if (m0 + wrow < a.M) tma_store_2d(&tm_a16, my_tile, kcol, m0 + wrow);
           bulk_commit();
-          if (pending >= 0) {
-            bulk_wait_read<1>();
-            release(pending % STAGES, pending);
-          }
-        } else {
-          release(s, c);
         }
+        ++n_stored;
       }
-      pending = store ? c : -1;
     }
-  }
-  if (lane == 0 && pending >= 0) {
-    bulk_wait_read<0>();
-    release(pending % STAGES, pending);
   }
 
   pdl_trigger();  // the next kernel may start its prologue (it waits for this grid before reading)
@@ -564,37 +578,61 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
           }
         }
       }
-      // every CTA of the band arrives, aborted or not, so the count always completes and resets
-      __threadfence();
+      // every CTA of the band arrives, aborted or not, so the count always completes and resets.
+      // The CTA barrier orders every thread's partial stores before thread 0's release (the
+      // release is cumulative); thread 0's acquire plus the barrier order the last CTA's reads
+      // after every slice's stores.
       __syncthreads();
       int* last = issued + STAGES + 1;
       uint32_t* counter = a.counters + (blockIdx.z * gridDim.x + blockIdx.x);
       if (tid == 0) {
+        __threadfence();
         uint32_t old;
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
         *last = old == (uint32_t)(a.ksplit - 1);
+        if (*last) __threadfence();
       }
       __syncthreads();
       if (*last) {
         // mid_hl of the band's rows and this CTA's columns: the K-slice partials summed in slice
-        // order (deterministic), LoRA columns scaled, split into bf16 hi + lo
-        __threadfence();
-        const int cols = 8 * ntl;
+        // order (deterministic), LoRA columns scaled, split into bf16 hi + lo.  A thread owns four
+        // adjacent columns of one row and issues the loads of up to 16 slices at once.
+        const int c4 = 2 * ntl;  // four-column groups of this CTA
         const int rows = min(kBM, a.M - m0);
-        for (int i = tid; i < rows * cols; i += kThreads) {
-          const int rr = i / cols, j = r0 + i % cols;
+        const int64_t kstride = (int64_t)a.M * a.r_tot / 4;  // one slice, in float4
+        for (int i = tid; i < rows * c4; i += kThreads) {
+          const int rr = i / c4, j = r0 + 4 * (i - rr * c4);
           const int64_t row = m0 + rr;
-          float v = 0.f;
-          for (int k = 0; k < a.ksplit; ++k) v += __ldcg(a.partial + ((int64_t)k * a.M + row) * a.r_tot + j);
-          if (j >= a.rank) v *= a.lora_col_scale[j - a.rank];
-          const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-          a.mid_hl[row * a.R2 + j] = hi;
-          a.mid_hl[row * a.R2 + a.r_tot + j] = __float2bfloat16_rn(v - __bfloat162float(hi));
+          const float4* src = reinterpret_cast<const float4*>(a.partial + row * a.r_tot + j);
+          float4 t[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u)
+            if (u < a.ksplit) t[u] = __ldcg(src + u * kstride);
+          float4 v = t[0];
+#pragma unroll
+          for (int u = 1; u < 16; ++u)
+            if (u < a.ksplit) { v.x += t[u].x; v.y += t[u].y; v.z += t[u].z; v.w += t[u].w; }
+          for (int k = 16; k < a.ksplit; ++k) {
+            const float4 w = __ldcg(src + k * kstride);
+            v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+          }
+          if (j >= a.rank) {  // LoRA columns (lora_rank is a multiple of 8: all four or none)
+            const float4 cs = *reinterpret_cast<const float4*>(a.lora_col_scale + (j - a.rank));
+            v.x *= cs.x; v.y *= cs.y; v.z *= cs.z; v.w *= cs.w;
+          }
+          const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y), h23 = __floats2bfloat162_rn(v.z, v.w);
+          const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+          const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
+          const __nv_bfloat162 l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
+          __nv_bfloat16* dst = a.mid_hl + row * a.R2 + j;
+          *reinterpret_cast<uint2*>(dst) = make_uint2(bf162_bits(h01), bf162_bits(h23));
+          *reinterpret_cast<uint2*>(dst + a.r_tot) = make_uint2(bf162_bits(l01), bf162_bits(l23));
         }
-        if (blockIdx.z == 0) {  // zero padding columns [2 r_tot, R2)
-          const int pad = a.R2 - 2 * a.r_tot;
-          for (int i = tid; i < rows * pad; i += kThreads)
-            a.mid_hl[(int64_t)(m0 + i / pad) * a.R2 + 2 * a.r_tot + i % pad] = __float2bfloat16_rn(0.f);
+        if (blockIdx.z == 0) {  // zero padding columns [2 r_tot, R2): a multiple of 16 columns
+          const int pad8 = (a.R2 - 2 * a.r_tot) / 8;
+          for (int i = tid; i < rows * pad8; i += kThreads)
+            *reinterpret_cast<uint4*>(a.mid_hl + (int64_t)(m0 + i / pad8) * a.R2 + 2 * a.r_tot + 8 * (i % pad8)) =
+                make_uint4(0u, 0u, 0u, 0u);
         }
         if (tid == 0) *counter = 0u;  // every other CTA of the band has arrived: ready for the next launch
       }
@@ -772,6 +810,9 @@ int validate_common(const void* x, int64_t ldx, const void* smooth, const void* 
     return bad("x, smooth, l2, lora_down must be 16-byte aligned");
   if (K_pad % kBK != 0) return bad("K_pad must be a multiple of 64");
   if (out_a16 && (reinterpret_cast<uintptr_t>(out_a16) & 15u)) return bad("a16 must be 16-byte aligned");
+  if (out_mid_hl && (reinterpret_cast<uintptr_t>(out_mid_hl) & 15u)) return bad("mid_hl must be 16-byte aligned");
+  if (lora_col_scale && (reinterpret_cast<uintptr_t>(lora_col_scale) & 15u))
+    return bad("lora_col_scale must be 16-byte aligned");
   if (out_mid_hl && r_tot > 0 && M > 0) {
     if (!workspace || ws_bytes < workspace_bytes(M, K_pad, r_tot))
       return bad("workspace missing or smaller than svdq_act_quant_workspace_bytes()");
@@ -810,6 +851,8 @@ int build_spec(LaunchSpec& L, const void* x, int64_t ldx, const void* smooth, co
                                    kBK, 16, CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
   AqArgs& p = L.args;
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = ldx;
   p.M = M;
   p.K_in = K_in;
   p.K_pad = K_pad;
