@@ -121,6 +121,23 @@ int svdq_act_quant(const void* x, int64_t ldx, const void* smooth,
                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
+ * svdq_act_quant for the int8-code GEMM (svdq_w4a4_gemm): the same quantization (codes and scales
+ * bit-exact with quantize_symmetric_int4, src/krea2_svdquant/quant/pack.py:6-23), written as
+ *   out_codes8    [M, K_pad] int8: q in [-8, 7] (the unpacked form of pack_int4's codes);
+ *   out_ascales_t [K_pad / a_group, lda_s] fp32: the bf16 group scales, group-major (row g holds
+ *                 the scales of group g for tokens 0..M-1), lda_s >= M;
+ * plus out_mid_hl as svdq_act_quant writes it (same workspace rules).  No a16 is written.
+ *   out_codes8 and out_ascales_t 16-byte aligned; other requirements as svdq_act_quant.
+ */
+int svdq_act_quant_i8(const void* x, int64_t ldx, const void* smooth,
+                      const void* l2, int rank,
+                      const void* lora_down, const float* lora_col_scale, int lora_rank,
+                      int M, int K_in, int K_pad, int a_group,
+                      void* out_codes8, float* out_ascales_t, int64_t lda_s,
+                      void* out_mid_hl, int R2,
+                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
  * svdq_act_quant without a workspace argument: allocates nothing.  No
  * counterpart in the reference (its activation quantization runs in torch /
  * Triton and allocates through the framework).  For callers that cannot
@@ -263,10 +280,12 @@ int svdq_prepare_packed(const void* qweight, const void* scales, int scale_dtype
 
 /*
  * Packed-weight SVDQuant linear GEMM: the same computation as svdq_linear_gemm, with the weight
- * read as the half-byte codes + fp16 group scales of svdq_prepare_packed and converted to fp16
- * in shared memory (exactly, see above) inside the kernel; no fp16 weight is allocated.  Weight
- * rows are the tcgen05 MMA's M dimension and tokens its N (16 to 128 per tile), so small
- * batches run small MMAs and read 4x fewer weight bytes.  When the tiles leave SMs idle, a
+ * read as the half-byte codes + fp16 group scales of svdq_prepare_packed and converted on chip;
+ * no fp16 weight is allocated.  Weight rows are the tcgen05 MMA's M dimension and tokens its N
+ * (16 to 128 per tile), so small batches run small MMAs and read 4x fewer weight bytes.  Up to
+ * 64 tokens the weights enter the MMA as exact fp16 integers q and each group's fp32 partial is
+ * scaled by its weight scale in registers (as svdq_w4a4_gemm, with a16 for the activation);
+ * above that they are converted to q * scale (exact, see above).  When the tiles leave SMs idle, a
  * cluster of 2, 4 or 8 CTAs splits K and sums its fp32 partials through distributed shared
  * memory in a fixed order (deterministic).  Replaces F.linear(x_hat, w_res) + F.linear(mid, l1)
  * + bias of svd.py:158-162 and the in-loop dequantization of kernels/triton/generic_int4.py:19-133.
@@ -278,6 +297,31 @@ int svdq_packed_gemm(const void* a16, const void* codes, const void* scales16, i
                      const void* mid_hl, const void* up_hl, int R2, const void* bias,
                      void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
                      cudaStream_t stream);
+
+/*
+ * W4A4 GEMM on INT4 codes with kind::i8 tensor-core MMAs, for small batches: the weight read as
+ * the half-byte codes + fp16 group scales of svdq_prepare_packed and converted to int8 on chip;
+ * the activation as int8 codes with fp32 group scales (svdq_act_quant_i8).  Each K group's
+ * products are summed exactly in int32 in tensor memory, then rescaled into fp32:
+ *   out[m, n] = sum_g s_w[n, g] * s_a[m, g] * sum_{k in g} q_w[n, k] q_a[m, k]
+ *             + mid_hl[m] . up_hl[n] + bias[n]
+ * which is the reference's W4A4 formula (README.md:64; the residual product of
+ * src/krea2_svdquant/quant/svd.py:158 on quantized activations, low-rank up + bias of
+ * svd.py:159-162) with the int MMAs the reference's Blackwell kernel leaves as a TODO
+ * (src/krea2_svdquant/kernels/gluon/blackwell_fused_svdquant.py:32-35).  Tokens are the MMA's N
+ * dimension (16, 32 or 64 per tile), so the rescale costs a few instructions per output element
+ * and group: meant for batches up to 64 tokens (larger M runs, in tiles of 64 tokens, but slower
+ * than the fp16-operand GEMMs).  Split K over clusters as svdq_packed_gemm (deterministic).
+ *   K_pad % 128 == 0; w_group in {64, 128, 256}, a_group in {64, 128}, both dividing K_pad;
+ *   lda_s % 4 == 0 and lda_s >= M rounded up to 64 (entries past M are read, not used);
+ *   codes8, ascales_t, codes, scales16 16-byte aligned; N % 8 == 0, ldo % 8 == 0;
+ *   R2 % 64 == 0 (may be 0); out_dtype in {SVDQ_BF16, SVDQ_FP32}; bias may be NULL.
+ */
+int svdq_w4a4_gemm(const void* codes8, const float* ascales_t, int64_t lda_s, int a_group,
+                   const void* codes, const void* scales16, int w_group,
+                   const void* mid_hl, const void* up_hl, int R2, const void* bias,
+                   void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
+                   cudaStream_t stream);
 
 /*
  * The launch plan of svdq_packed_gemm for a shape on the current device: out4 = {token tile TN,

@@ -29,6 +29,9 @@ SIGNATURES = {
     "svdq_act_quant": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
                         c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                         c_void_p, ctypes.c_size_t, c_void_p], c_int),
+    "svdq_act_quant_i8": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                           c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_void_p, c_int,
+                           c_void_p, ctypes.c_size_t, c_void_p], c_int),
     "svdq_act_quant_noalloc_scratch_bytes": ([], ctypes.c_size_t),
     "svdq_act_quant_noalloc": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
                                 c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
@@ -58,6 +61,8 @@ SIGNATURES = {
                              c_void_p], c_int),
     "svdq_packed_gemm": ([c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
                           c_int64, c_int, c_int, c_int, c_void_p], c_int),
+    "svdq_w4a4_gemm": ([c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                        c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_void_p], c_int),
     "svdq_packed_gemm_plan": ([c_int, c_int, c_int, ctypes.POINTER(c_int)], c_int),
 }
 

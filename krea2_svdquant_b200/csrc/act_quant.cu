@@ -185,6 +185,9 @@ struct AqArgs {
   const __nv_bfloat16* smooth;
   uint8_t* packed;        // [M, K_pad/2] or null
   __nv_bfloat16* scales;  // [M, K_pad/G] or null
+  int8_t* codes8;         // [M, K_pad] int8 codes q, or null
+  float* ascales_t;       // [K_pad/G, lda_s] fp32 scales, group-major, or null
+  int64_t lda_s;
   float* partial;         // [ksplit, M, r_tot] or null
   uint32_t* counters;     // [bands * nz] arrival counters of the K slices (zero between launches)
   __nv_bfloat16* mid_hl;  // [M, R2]
@@ -505,8 +508,11 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
         nms2[h] = f2_pack(-kMagic * sc, -kMagic * sc);
         if constexpr (PACKED) {
           const int row = h ? row_g8 : row_g;
-          if (t4 == 0 && row < a.M && a.scales)
-            a.scales[(int64_t)row * (a.K_pad / a.G) + (st0 + c0) * kBK / a.G] = __float2bfloat16_rn(sc);
+          if (t4 == 0 && row < a.M) {
+            const int grp = (st0 + c0) * kBK / a.G;
+            if (a.scales) a.scales[(int64_t)row * (a.K_pad / a.G) + grp] = __float2bfloat16_rn(sc);
+            if (a.ascales_t) a.ascales_t[(int64_t)grp * a.lda_s + row] = sc;
+          }
         }
       }
     }
@@ -529,7 +535,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
 #pragma unroll
           for (int i = 0; i < 4; ++i) o[i] = fr[j][kk][i];
         } else {
-          uint32_t nib[4];
+          uint32_t nib[4], c8[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int h = i & 1;
@@ -538,12 +544,27 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
             o[i] = f2_to_h2(f2_fma(m, sc2[h], nms2[h]));         // rint(q) * scale, exact in fp16
             // offset-binary code q + 8 = two's-complement low nibble with its top bit flipped
             nib[i] = (((uint32_t)m & 0xFu) | (((uint32_t)(m >> 32) & 0xFu) << 4)) ^ 0x88u;
+            c8[i] = ((uint32_t)m & 0xFFu) | (((uint32_t)(m >> 32) & 0xFFu) << 8);  // two int8 codes
           }
           if constexpr (PACKED) {
-            uint8_t* prow_g = a.packed + (int64_t)row_g * (a.K_pad / 2) + (kcol + 16 * kk + 2 * t4) / 2;
-            uint8_t* prow_g8 = prow_g + (int64_t)8 * (a.K_pad / 2);
-            if (row_g < a.M) { prow_g[0] = (uint8_t)nib[0]; prow_g[4] = (uint8_t)nib[2]; }
-            if (row_g8 < a.M) { prow_g8[0] = (uint8_t)nib[1]; prow_g8[4] = (uint8_t)nib[3]; }
+            if (a.packed) {
+              uint8_t* prow_g = a.packed + (int64_t)row_g * (a.K_pad / 2) + (kcol + 16 * kk + 2 * t4) / 2;
+              uint8_t* prow_g8 = prow_g + (int64_t)8 * (a.K_pad / 2);
+              if (row_g < a.M) { prow_g[0] = (uint8_t)nib[0]; prow_g[4] = (uint8_t)nib[2]; }
+              if (row_g8 < a.M) { prow_g8[0] = (uint8_t)nib[1]; prow_g8[4] = (uint8_t)nib[3]; }
+            }
+            if (a.codes8) {
+              int8_t* crow_g = a.codes8 + (int64_t)row_g * a.K_pad + kcol + 16 * kk + 2 * t4;
+              int8_t* crow_g8 = crow_g + (int64_t)8 * a.K_pad;
+              if (row_g < a.M) {
+                *reinterpret_cast<uint16_t*>(crow_g) = (uint16_t)c8[0];
+                *reinterpret_cast<uint16_t*>(crow_g + 8) = (uint16_t)c8[2];
+              }
+              if (row_g8 < a.M) {
+                *reinterpret_cast<uint16_t*>(crow_g8) = (uint16_t)c8[1];
+                *reinterpret_cast<uint16_t*>(crow_g8 + 8) = (uint16_t)c8[3];
+              }
+            }
           }
         }
         if (write_a16) stmatrix_x4(my_tile + swz128(lane & 15, 2 * kk + (lane >> 4)), o[0], o[1], o[2], o[3]);
@@ -866,6 +887,9 @@ int build_spec(LaunchSpec& L, const void* x, int64_t ldx, const void* smooth, co
   p.smooth = static_cast<const __nv_bfloat16*>(smooth);
   p.packed = static_cast<uint8_t*>(out_packed);
   p.scales = static_cast<__nv_bfloat16*>(out_scales);
+  p.codes8 = nullptr;
+  p.ascales_t = nullptr;
+  p.lda_s = 0;
   p.partial = want_mid ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes) : nullptr;
   p.counters = want_mid ? static_cast<uint32_t*>(workspace) : nullptr;
   p.mid_hl = static_cast<__nv_bfloat16*>(out_mid_hl);
@@ -927,5 +951,34 @@ extern "C" int svdq_w4a16_prep(const void* x, int64_t ldx, const void* smooth, c
     return st;
   L.w4a16 = true;
   L.packed = false;
+  return launch(L, stream);
+}
+
+extern "C" int svdq_act_quant_i8(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank,
+                                 const void* lora_down, const float* lora_col_scale, int lora_rank, int M, int K_in,
+                                 int K_pad, int a_group, void* out_codes8, float* out_ascales_t, int64_t lda_s,
+                                 void* out_mid_hl, int R2, void* workspace, size_t workspace_bytes,
+                                 cudaStream_t stream) {
+  using namespace svdq;
+  int st = validate_common(x, ldx, smooth, l2, rank, lora_down, lora_col_scale, lora_rank, M, K_in, K_pad, nullptr,
+                           out_mid_hl, R2, workspace, workspace_bytes, "svdq_act_quant_i8");
+  if (st) return st;
+  SVDQ_REQUIRE(a_group == 64 || a_group == 128, "svdq_act_quant_i8: a_group must be 64 or 128");
+  SVDQ_REQUIRE(K_pad % a_group == 0, "svdq_act_quant_i8: K_pad must be a multiple of a_group");
+  SVDQ_REQUIRE(out_codes8 && out_ascales_t, "svdq_act_quant_i8: codes and scales outputs are required");
+  SVDQ_REQUIRE((reinterpret_cast<uintptr_t>(out_codes8) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out_ascales_t) & 15u) == 0,
+               "svdq_act_quant_i8: codes and scales must be 16-byte aligned");
+  SVDQ_REQUIRE(lda_s >= M, "svdq_act_quant_i8: lda_s must be >= M");
+  if (M == 0) return SVDQ_OK;
+  LaunchSpec L;
+  if ((st = build_spec(L, x, ldx, smooth, l2, false, rank, lora_down, lora_col_scale, lora_rank, M, K_in, K_pad,
+                       a_group, nullptr, nullptr, nullptr, out_mid_hl, R2, workspace)))
+    return st;
+  L.args.codes8 = static_cast<int8_t*>(out_codes8);
+  L.args.ascales_t = out_ascales_t;
+  L.args.lda_s = lda_s;
+  L.w4a16 = false;
+  L.packed = true;
   return launch(L, stream);
 }

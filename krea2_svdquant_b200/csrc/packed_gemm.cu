@@ -612,6 +612,15 @@ int launch_pw_tn(int tn, const CUtensorMap& ta, const CUtensorMap& tc, const CUt
 }
 
 }  // namespace
+
+// The small-batch kernel (packed_small.cu): batches of up to kSmallBatchMax tokens.
+constexpr int kSmallBatchMax = 64;
+int packed_small_gemm(const void* act, bool i8, const float* ascales_t, int64_t lda_s, int a_group, const void* codes,
+                      const void* scales16, int w_group, const void* mid_hl, const void* up_hl, int R2,
+                      const void* bias, void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
+                      cudaStream_t stream);
+int packed_small_plan(int M, int N, int K_pad, int* out4);
+
 }  // namespace svdq
 
 extern "C" int svdq_prepare_packed(const void* qweight, const void* scales, int scale_dtype, int N, int K_pad,
@@ -658,6 +667,7 @@ extern "C" int svdq_packed_gemm_plan(int M, int N, int K_pad, int* out4) {
   using namespace svdq;
   SVDQ_REQUIRE(out4, "svdq_packed_gemm_plan: out4 is NULL");
   SVDQ_REQUIRE(M > 0 && N > 0 && K_pad > 0 && K_pad % 64 == 0, "svdq_packed_gemm_plan: bad M/N/K_pad");
+  if (M <= kSmallBatchMax) return packed_small_plan(M, N, K_pad, out4);
   const PwPlan p = plan_packed(M, N, K_pad);
   out4[0] = p.tn;
   out4[1] = p.ks;
@@ -681,6 +691,12 @@ extern "C" int svdq_packed_gemm(const void* a16, const void* codes, const void* 
   SVDQ_REQUIRE(out_dtype == SVDQ_BF16 || out_dtype == SVDQ_FP32, "svdq_packed_gemm: out_dtype must be bf16 or fp32");
   SVDQ_REQUIRE(!bias || (reinterpret_cast<uintptr_t>(bias) & 1u) == 0, "svdq_packed_gemm: bias must be 2-byte aligned");
   if (M == 0) return SVDQ_OK;
+  if (M <= kSmallBatchMax) {
+    SVDQ_REQUIRE((reinterpret_cast<uintptr_t>(a16) & 15u) == 0 && (reinterpret_cast<uintptr_t>(codes) & 15u) == 0,
+                 "svdq_packed_gemm: a16 and codes must be 16-byte aligned");
+    return packed_small_gemm(a16, false, nullptr, 0, 0, codes, scales16, w_group, mid_hl, up_hl, R2, bias, out,
+                             out_dtype, ldo, M, N, K_pad, stream);
+  }
   int* err = device_error_word();
   if (!err) return set_error(SVDQ_ERR_CUDA, "svdq_packed_gemm: device error word unavailable");
   const PwPlan p = plan_packed(M, N, K_pad);

@@ -264,6 +264,16 @@ class SVDQuantLinear(nn.Module):
         up_hl = p.up_hl if include_lora else p.up_hl_base
         if self.backend is BackendKind.B200_W4A16:
             a16, mid = ops.w4a16_prep(x2, p.smooth, p.l2_f16, lora_down, col_scale, p.k_pad)
+        elif p.w16 is None and self._int8_path(x2.shape[0], p):
+            # small batch, packed weight: int8 codes and the kind::i8 GEMM with per-group rescale
+            codes8, ascales, mid = ops.act_quant_i8(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
+                                                    self.act_group_size)
+            lowrank = (mid, up_hl) if mid.numel() else (None, None)
+            y = ops.w4a4_gemm(codes8, ascales, self.act_group_size, p.codes, p.scales16, self.group_size,
+                              *lowrank, p.bias, out_fp32)
+            if self.check_device_errors:
+                _lib.raise_on_device_error(f"SVDQuantLinear {tuple(self.original_shape)}")
+            return y.reshape(*lead, n)
         else:
             a16, mid, _, _ = ops.act_quant(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
                                            self.act_group_size, True, False)
@@ -275,6 +285,13 @@ class SVDQuantLinear(nn.Module):
         if self.check_device_errors:
             _lib.raise_on_device_error(f"SVDQuantLinear {tuple(self.original_shape)}")
         return y.reshape(*lead, n)
+
+    # Batches up to this many tokens take the int8-code GEMM when the weight is packed (W4A4).
+    INT8_PATH_MAX_TOKENS = 64
+
+    def _int8_path(self, m: int, p: PreparedOperands) -> bool:
+        return (0 < m <= self.INT8_PATH_MAX_TOKENS and p.k_pad % 128 == 0 and self.group_size in (64, 128, 256)
+                and self.act_group_size in (64, 128) and p.k_pad % self.act_group_size == 0)
 
     def _forward_base(self, x: torch.Tensor) -> torch.Tensor:
         """SVDQuant base term (residual + low-rank + bias), without LoRA branches."""

@@ -125,6 +125,46 @@ def _(x, smooth, l2, lora_down, lora_col_scale, k_pad, a_group, emit_a16, emit_p
             e((m, k_pad // a_group) if emit_packed else (0,), dtype=torch.bfloat16))
 
 
+def ascales_ld(m: int) -> int:
+    """Row stride of the group-major activation scales of ``act_quant_i8``: M rounded up to 64 (the
+    int8 GEMM reads whole 64-token tiles; entries past M are zero)."""
+    return round_up(max(m, 1), 64)
+
+
+@torch.library.custom_op("svdq_b200::act_quant_i8", mutates_args=())
+def act_quant_i8(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Optional[Tensor],
+                 lora_col_scale: Optional[Tensor], k_pad: int, a_group: int) -> tuple[Tensor, Tensor, Tensor]:
+    """W4A4 activation pass for the int8-code GEMM: the codes of ``quantize_symmetric_int4(x / smooth,
+    a_group)`` as int8 ``[M, K_pad]``, its bf16 scales as fp32 group-major ``[K_pad/a_group,
+    ascales_ld(M)]`` (zero past M), and ``mid_hl [M, R2]``."""
+    _need_cuda("act_quant_i8", x, smooth, l2, lora_down, lora_col_scale)
+    _need(x.dim() == 2 and x.dtype == torch.bfloat16, "act_quant_i8: x must be a 2-D bf16 tensor")
+    _need(x.stride(1) == 1, "act_quant_i8: x must have unit column stride")
+    m, k_in = x.shape
+    rank, lrank, r2 = _lowrank_args(l2, lora_down)
+    dev = x.device
+    codes = torch.empty((m, k_pad), dtype=torch.int8, device=dev)
+    lda = ascales_ld(m)
+    ascales = torch.zeros((k_pad // a_group, lda), dtype=torch.float32, device=dev)
+    mid = torch.empty((m, r2) if r2 else (0,), dtype=torch.bfloat16, device=dev)
+    if m == 0:
+        return codes, ascales, mid
+    ws = _workspace(m, k_pad, rank, lrank, dev) if r2 else None
+    _lib.call("svdq_act_quant_i8", _p(x), x.stride(0), _p(smooth), _p(l2), rank, _p(lora_down),
+              _p(lora_col_scale), lrank, m, k_in, k_pad, a_group, _p(codes), _p(ascales), lda,
+              _p(mid), r2, _p(ws), 0 if ws is None else ws.numel(), _stream(dev))
+    return codes, ascales, mid
+
+
+@act_quant_i8.register_fake
+def _(x, smooth, l2, lora_down, lora_col_scale, k_pad, a_group):
+    m = x.shape[0]
+    _, _, r2 = _lowrank_args(l2, lora_down)
+    return (x.new_empty((m, k_pad), dtype=torch.int8),
+            x.new_empty((k_pad // a_group, ascales_ld(m)), dtype=torch.float32),
+            x.new_empty((m, r2) if r2 else (0,), dtype=torch.bfloat16))
+
+
 @torch.library.custom_op("svdq_b200::w4a16_prep", mutates_args=())
 def w4a16_prep(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Optional[Tensor],
                lora_col_scale: Optional[Tensor], k_pad: int) -> tuple[Tensor, Tensor]:
@@ -337,3 +377,31 @@ def packed_gemm(a16: Tensor, codes: Tensor, scales16: Tensor, w_group: int, mid_
 @packed_gemm.register_fake
 def _(a16, codes, scales16, w_group, mid_hl, up_hl, bias, out_fp32):
     return a16.new_empty((a16.shape[0], codes.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
+
+
+@torch.library.custom_op("svdq_b200::w4a4_gemm", mutates_args=())
+def w4a4_gemm(codes8: Tensor, ascales: Tensor, a_group: int, codes: Tensor, scales16: Tensor, w_group: int,
+              mid_hl: Optional[Tensor], up_hl: Optional[Tensor], bias: Optional[Tensor], out_fp32: bool) -> Tensor:
+    """W4A4 GEMM with kind::i8 tensor-core MMAs on int8 codes (``act_quant_i8``) and the packed weight
+    (``prepare_packed``): per-group int32 partials rescaled by weight and activation scales, plus
+    ``mid_hl @ up_hl^T + bias``.  Meant for batches up to 64 tokens."""
+    _need_cuda("w4a4_gemm", codes8, ascales, codes, scales16, mid_hl, up_hl, bias)
+    _need(codes8.dtype == torch.int8 and codes8.is_contiguous(), "w4a4_gemm: codes8 must be contiguous int8")
+    _need(ascales.dtype == torch.float32 and ascales.is_contiguous(), "w4a4_gemm: ascales must be contiguous fp32")
+    m, k_pad = codes8.shape
+    n = codes.shape[0]
+    _need(codes.shape[1] * 2 == k_pad, "w4a4_gemm: activation / weight K mismatch")
+    r2 = 0 if mid_hl is None or mid_hl.numel() == 0 else mid_hl.shape[1]
+    _need(r2 == 0 or (up_hl is not None and tuple(up_hl.shape) == (n, r2)), "w4a4_gemm: up_hl shape mismatch")
+    out = torch.empty((m, n), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=codes8.device)
+    if m == 0:
+        return out
+    _lib.call("svdq_w4a4_gemm", _p(codes8), _p(ascales), ascales.shape[1], a_group, _p(codes), _p(scales16), w_group,
+              _p(mid_hl) if r2 else None, _p(up_hl) if r2 else None, r2, _p(bias), _p(out),
+              _lib.SVDQ_FP32 if out_fp32 else _lib.SVDQ_BF16, out.stride(0), m, n, k_pad, _stream(codes8.device))
+    return out
+
+
+@w4a4_gemm.register_fake
+def _(codes8, ascales, a_group, codes, scales16, w_group, mid_hl, up_hl, bias, out_fp32):
+    return codes8.new_empty((codes8.shape[0], codes.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
