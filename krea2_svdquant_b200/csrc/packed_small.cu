@@ -40,9 +40,11 @@
 //
 // Roles (16 warps): warp 0 TMA of code boxes and weight scales; warp 1 tensor-memory allocation
 // and the MMA issue; warp 2 TMA of token tiles (and low-rank tiles); warps 4-7 rescale and
-// epilogue; warps 8-15 conversion (two per lane quarter, alternate weight stages).  Every role
-// waits by spinning on mbarrier.test_wait (a suspending try_wait costs a few hundred nanoseconds
-// to wake, which this latency-bound pipeline cannot hide).  Every wait is bounded (error word
+// epilogue; warps 8-15 conversion (two per lane quarter, alternate weight stages).  The
+// single-thread roles wait by spinning on mbarrier.test_wait; the warps poll it with a short
+// nanosleep in between (a suspending try_wait costs a few hundred nanoseconds to wake, which this
+// latency-bound pipeline cannot hide, and a spinning warp takes issue slots from the MMA thread
+// on its SM sub-partition).  Every wait is bounded (error word
 // codes 0x55xx-0x58xx); a wait that runs out raises the CTA's abort flag, every role leaves its
 // loop, and all CTAs still meet at the cluster barriers.
 #include <algorithm>
@@ -58,48 +60,51 @@ constexpr uint32_t SB_BOX_BYTES = SB_ROWS * SB_BOX_K / 2;  // 16 KiB
 constexpr int SB_PS = 6;                     // code-box ring (shared memory)
 constexpr int SB_LS = 2;                     // low-rank A ring
 constexpr uint32_t SB_LR_BYTES = SB_ROWS * 64 * 2;  // up_hl tile: 128 rows x 64 bf16
-constexpr int SB_PB_MAX = 8;                 // partial-sum buffers in tensor memory, most
 constexpr int SB_CONV_WARPS = 8;
 constexpr int SB_THREADS = 32 * (8 + SB_CONV_WARPS);
 constexpr uint32_t SB_TMEM_COLS = 512;
 constexpr uint32_t SB_STAGE_COLS = 32;       // tensor-memory columns of one weight stage (128 B per row)
 constexpr int SB_MAX_SCALES = 8;             // weight scales per row and code box (group 32)
+constexpr int SB_MAX_WCH = 4;                // weight chunks in tensor memory, most
+constexpr int SB_MAX_TB = 16;                // token chunks in shared memory, most
 
-template <int TN>
+// Work is synchronized per chunk: 256 k of the K range (one code box), i.e. 4 weight stages of
+// fp16 or 2 of int8 and their 16 or 8 MMAs, which accumulate into a set of partial buffers (one
+// per K group of the chunk).  One set of waits and commits per chunk keeps the MMA thread's own
+// barrier traffic (each mbarrier operation costs it 100-200 cycles) off the MMA critical path.
+template <int TN, bool I8>
 struct SbLayout {
-  // partial buffers (at least 32 columns each, keeping every MMA destination 32-column aligned)
-  // and weight stages share the 512 tensor-memory columns: 8 x 32 + 8 x 32 (TN 16, 32) or
-  // 4 x 64 + 8 x 32 (TN 64)
-  static constexpr uint32_t kPCols = TN < 32 ? 32 : TN;
-  static constexpr int kPB = TN <= 32 ? 8 : 4;
-  static constexpr int kAStages = (int)((SB_TMEM_COLS - kPB * kPCols) / SB_STAGE_COLS) > 12
-                                      ? 12
-                                      : (int)((SB_TMEM_COLS - kPB * kPCols) / SB_STAGE_COLS);
-  static constexpr uint32_t kB = (uint32_t)TN * 128;                           // token tile bytes
-  static constexpr int kBStages = TN <= 16 ? 16 : TN <= 32 ? 12 : 8;
+  static constexpr int kSK = I8 ? 128 : 64;                  // k per weight stage
+  static constexpr int kSPB = SB_BOX_K / kSK;                // stages per chunk
+  static constexpr uint32_t kPCols = TN < 32 ? 32 : TN;       // columns per partial buffer (32-aligned)
+  static constexpr uint32_t kWChunkCols = kSPB * SB_STAGE_COLS;
+  static constexpr uint32_t kTokSub = (uint32_t)TN * 128;     // one stage of tokens: TN rows x 128 B
+  static constexpr uint32_t kTokChunk = kSPB * kTokSub;
+  static constexpr int kTB = (int)(65536 / kTokChunk) < 2 ? 2 : (int)(65536 / kTokChunk) > SB_MAX_TB ? SB_MAX_TB
+                                                                                          : (int)(65536 / kTokChunk);
   static constexpr uint32_t kOffP = 0;                                         // code ring
   static constexpr uint32_t kOffB = kOffP + SB_PS * SB_BOX_BYTES;
-  static constexpr uint32_t kOffL = kOffB + kBStages * kB;
+  static constexpr uint32_t kOffL = kOffB + kTB * kTokChunk;
   static constexpr uint32_t kOffS = kOffL + SB_LS * SB_LR_BYTES;               // weight-scale ring
   static constexpr uint32_t kSBytes = SB_ROWS * SB_MAX_SCALES * 2;
   static constexpr uint32_t kOffBar = kOffS + SB_PS * kSBytes;
   static constexpr uint32_t kSmem = kOffBar + 1024 + 1024;                     // barriers + alignment slack
-  static_assert(kAStages >= 4, "weight ring");
-  static_assert((uint32_t)SB_ROWS * TN * 4 <= kOffL, "split-K partial fits over the code and token rings");
+  static_assert(kTokSub % 1024 == 0, "token tiles keep 1 KiB alignment for the 128-byte swizzle");
+  static_assert((uint32_t)SB_ROWS * TN * 4 <= kOffB, "split-K partial fits over the code ring");
   static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
 };
 
 struct SbBars {
   uint64_t full_p[SB_PS];   // code box and its weight scales landed (TMA bytes)
-  uint64_t empty_p[SB_PS];  // code box converted (one arrival per converter warp)
+  uint64_t empty_p[SB_PS];  // code box read (one arrival per converter warp)
   uint64_t empty_s[SB_PS];  // weight scales of the box used (one arrival per rescale warp)
-  uint64_t full_b[16];      // token tile (and, for a low-rank stage, its A) landed
-  uint64_t empty_b[16];     // MMAs reading the token slot done (commit)
-  uint64_t conv[12];        // weight stage written to tensor memory (one arrival per lane quarter)
-  uint64_t empty_a[12];     // MMAs reading the weight stage done (commit)
-  uint64_t empty_l[SB_LS];  // MMAs reading the low-rank A slot done (commit)
-  uint64_t pfull[SB_PB_MAX];   // a group's partial complete (commit)
-  uint64_t pempty[SB_PB_MAX];  // partial read by the rescale warps (one arrival per rescale warp)
+  uint64_t full_b[SB_MAX_TB];   // token chunk (and, for a low-rank chunk, its A) landed
+  uint64_t empty_b[SB_MAX_TB];  // MMAs reading the token chunk done (commit)
+  uint64_t conv[SB_MAX_WCH];    // weight chunk written to tensor memory (one arrival per converter warp)
+  uint64_t empty_a[SB_MAX_WCH]; // MMAs reading the weight chunk done (commit)
+  uint64_t empty_l[SB_LS];      // MMAs reading the low-rank A slot done (commit)
+  uint64_t pfull[2];            // a chunk's partial set complete (commit)
+  uint64_t pempty[2];           // partial set read by the rescale warps (one arrival per rescale warp)
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
@@ -190,10 +195,25 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
-// Bounded wait by spinning on test_wait (see the role notes above).
+// Bounded wait for the multi-warp roles: test_wait polls with a short nanosleep between them, so
+// that waiting warps leave the issue slots of their SM sub-partition to the single-thread MMA and
+// TMA roles (a spinning warp takes a share of them; a suspending try_wait is slow to wake).
 __device__ __forceinline__ bool wait_spin(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
                                           int where) {
-  return mbar_spin_wait(bar, parity, abort_flag, err, where);
+  if (mbar_test_parity(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(32);
+    if (mbar_test_parity(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicCAS(err, 0, where);
+        return false;
+      }
+    }
+  }
 }
 
 // Instruction descriptors: D fp32 (kind::f16) or s32 (kind::i8), K-major A and B, M = 128.
@@ -228,10 +248,8 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
     packed_small_kernel(const __grid_constant__ CUtensorMap tm_tok, const __grid_constant__ CUtensorMap tm_codes,
                         const __grid_constant__ CUtensorMap tm_mid, const __grid_constant__ CUtensorMap tm_up,
                         const SbArgs args) {
-  using L = SbLayout<TN>;
-  constexpr int AS = L::kAStages, BS = L::kBStages, PB = L::kPB;
-  constexpr int SK = I8 ? 128 : 64;          // k per weight stage (128 bytes of operand per row)
-  constexpr int SPB = SB_BOX_K / SK;         // stages per code box
+  using L = SbLayout<TN, I8>;
+  constexpr int SK = L::kSK, SPB = L::kSPB, TB = L::kTB;
   constexpr int KSTEP = I8 ? 32 : 16;        // k per MMA
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -254,10 +272,18 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
   const int b0 = (int)((int64_t)crank * n_box / ks), b1 = (int)((int64_t)(crank + 1) * n_box / ks);
   const int k0 = b0 * SB_BOX_K, k1 = min(b1 * SB_BOX_K, args.K_pad);  // this CTA's K range
   const int n_res = (k1 - k0) / SK;                                     // weight stages
-  const int n_lr = crank == ks - 1 ? args.n_lr : 0;
-  const int pg_steps = args.pg_k / KSTEP;                               // MMAs per partial group
-  const int n_pg = (k1 - k0) / args.pg_k;                               // residual partial groups
+  const int n_ch = b1 - b0;                                             // residual chunks
+  const int n_lr = crank == ks - 1 ? args.n_lr : 0;                     // low-rank chunks (one stage each)
+  const int pg_k = args.pg_k;
+  const int lg_steps = __ffs(pg_k / KSTEP) - 1;                         // log2(MMAs per group)
+  const int gpc = SB_BOX_K / pg_k;                                      // groups per full chunk
   const int spg = SB_BOX_K / args.w_group;                              // weight scales per row and box
+  // tensor memory: partial sets, then the weight-chunk ring
+  const uint32_t set_cols = (uint32_t)gpc * L::kPCols;
+  const int psets = 2 * set_cols + 2 * L::kWChunkCols <= SB_TMEM_COLS ? 2 : 1;
+  const int wch_fit = (int)((SB_TMEM_COLS - psets * set_cols) / L::kWChunkCols);
+  const int WCH = wch_fit > SB_MAX_WCH ? SB_MAX_WCH : wch_fit;
+  auto stages_of = [&](int c) { return min(SPB, n_res - c * SPB); };
 
   auto bar = [&](const uint64_t& b) { return smem_u32(&b); };
 
@@ -267,16 +293,16 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
       mbar_init(bar(bars->empty_p[s]), SB_CONV_WARPS);
       mbar_init(bar(bars->empty_s[s]), 4);
     }
-    for (int s = 0; s < BS; ++s) {
+    for (int s = 0; s < TB; ++s) {
       mbar_init(bar(bars->full_b[s]), 1);
       mbar_init(bar(bars->empty_b[s]), 1);
     }
-    for (int s = 0; s < AS; ++s) {
-      mbar_init(bar(bars->conv[s]), 4);
+    for (int s = 0; s < SB_MAX_WCH; ++s) {
+      mbar_init(bar(bars->conv[s]), SB_CONV_WARPS);
       mbar_init(bar(bars->empty_a[s]), 1);
     }
     for (int s = 0; s < SB_LS; ++s) mbar_init(bar(bars->empty_l[s]), 1);
-    for (int s = 0; s < PB; ++s) {
+    for (int s = 0; s < 2; ++s) {
       mbar_init(bar(bars->pfull[s]), 1);
       mbar_init(bar(bars->pempty[s]), 4);
     }
@@ -300,18 +326,17 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t tmem_w = tmem + PB * L::kPCols;  // weight stages after the partial buffers
+  const uint32_t tmem_w = tmem + psets * set_cols;  // weight chunks after the partial sets
   pdl_wait();  // operands may come from the previous kernel on the stream
   pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------ code boxes + their weight scales
-      const int nbx = b1 - b0;
       uint32_t filled = 0, par = 0;
       bool ok = true;
       const uint32_t sbytes = (uint32_t)(SB_ROWS * spg * 2);
-      for (int it = 0; it < nbx && ok; ++it) {
+      for (int it = 0; it < n_ch && ok; ++it) {
         const int s = it % SB_PS;
         const uint32_t ph = (uint32_t)(it / SB_PS) & 1u;
         if (!(ok = mbar_spin_wait(bar(bars->empty_p[s]), ph ^ 1u, abort_flag, args.err, kSbWaitPackedEmpty))) break;
@@ -329,25 +354,26 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
     }
   } else if (warp == 2) {
     if (lane == 0) {
-      // ------------------------------------------------ token tiles (+ low-rank A)
+      // ------------------------------------------------ token chunks (+ low-rank A)
       uint32_t filled = 0, par = 0;
       bool ok = true;
-      const int iters = n_res + n_lr;
-      for (int it = 0; it < iters && ok; ++it) {
-        const int s = it % BS;
-        const uint32_t ph = (uint32_t)(it / BS) & 1u;
+      for (int it = 0; it < n_ch + n_lr && ok; ++it) {
+        const int s = it % TB;
+        const uint32_t ph = (uint32_t)(it / TB) & 1u;
         if (!(ok = mbar_spin_wait(bar(bars->empty_b[s]), ph ^ 1u, abort_flag, args.err, kSbWaitTileEmpty))) break;
         const uint32_t fb = bar(bars->full_b[s]);
-        const uint32_t bdst = b_ring + (uint32_t)s * L::kB;
-        if (it < n_res) {
-          mbar_arrive_expect_tx(fb, L::kB);
-          tma_load_2d(bdst, &tm_tok, fb, k0 + it * SK, m0);
+        const uint32_t bdst = b_ring + (uint32_t)s * L::kTokChunk;
+        if (it < n_ch) {
+          const int st = stages_of(it);
+          mbar_arrive_expect_tx(fb, (uint32_t)st * L::kTokSub);
+          for (int j = 0; j < st; ++j)
+            tma_load_2d(bdst + (uint32_t)j * L::kTokSub, &tm_tok, fb, k0 + (it * SPB + j) * SK, m0);
         } else {
-          const int j = it - n_res, ls = j % SB_LS;
+          const int j = it - n_ch, ls = j % SB_LS;
           const uint32_t lph = (uint32_t)(j / SB_LS) & 1u;
           if (!(ok = mbar_spin_wait(bar(bars->empty_l[ls]), lph ^ 1u, abort_flag, args.err, kSbWaitLowrankEmpty)))
             break;
-          mbar_arrive_expect_tx(fb, L::kB + SB_LR_BYTES);
+          mbar_arrive_expect_tx(fb, L::kTokSub + SB_LR_BYTES);
           tma_load_2d(l_ring + (uint32_t)ls * SB_LR_BYTES, &tm_up, fb, j * 64, n0);
           tma_load_2d(bdst, &tm_mid, fb, j * 64, m0);
         }
@@ -355,62 +381,57 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
         par = (par & ~(1u << s)) | (ph << s);
       }
       if (!ok)
-        for (int s = 0; s < BS; ++s)
+        for (int s = 0; s < TB; ++s)
           if (filled & (1u << s)) mbar_wait_drain(bar(bars->full_b[s]), (par >> s) & 1u, 100000000ull);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ------------------------------------------------ MMA issue
+      // ------------------------------------------------ MMA issue, one chunk per round of waits
       const uint32_t idesc_res = I8 ? idesc_i8(TN) : idesc_f16(0u /*f16*/, TN);
       const uint32_t idesc_lr = idesc_f16(kFmtBF16, TN);
       bool ok = true;
-      int step = 0;  // residual MMA index over the CTA's K range
-      for (int it = 0; it < n_res && ok; ++it) {
-        const int bs = it % BS, as = it % AS;
-        if (!(ok = mbar_spin_wait(bar(bars->full_b[bs]), (uint32_t)(it / BS) & 1u, abort_flag, args.err,
-                                  kSbWaitMmaTile)))
-          break;
-        if (!(ok = mbar_spin_wait(bar(bars->conv[as]), (uint32_t)(it / AS) & 1u, abort_flag, args.err,
-                                  kSbWaitMmaConv)))
-          break;
+      int tb = 0, wc = 0, ps = 0;
+      uint32_t tph = 0, wph = 0, pph = 0;
+      const int step_mask = (1 << lg_steps) - 1;
+      for (int c = 0; c < n_ch + n_lr && ok; ++c) {
+        const bool res = c < n_ch;
+        if (!(ok = mbar_spin_wait(bar(bars->full_b[tb]), tph, abort_flag, args.err, kSbWaitMmaTile))) break;
+        if (res && !(ok = mbar_spin_wait(bar(bars->conv[wc]), wph, abort_flag, args.err, kSbWaitMmaConv))) break;
+        if (!(ok = mbar_spin_wait(bar(bars->pempty[ps]), pph ^ 1u, abort_flag, args.err, kSbWaitMmaPartial))) break;
         tc_fence_after();
-        const uint64_t db = desc_k_sw128(b_ring + (uint32_t)bs * L::kB);
-        const uint32_t ta = tmem_w + (uint32_t)as * SB_STAGE_COLS;
-#pragma unroll 1
-        for (int kk = 0; kk < 4; ++kk, ++step) {
-          const int pg = step / pg_steps, first = step % pg_steps == 0, last = step % pg_steps == pg_steps - 1;
-          const int pb = pg % PB;
-          if (first && !(ok = mbar_spin_wait(bar(bars->pempty[pb]), ((uint32_t)(pg / PB) & 1u) ^ 1u, abort_flag,
-                                             args.err, kSbWaitMmaPartial)))
-            break;
-          const uint32_t d = tmem + (uint32_t)pb * L::kPCols;
-          if constexpr (I8) umma_i8_tmem_a(d, ta + 8u * kk, db + (uint64_t)(2 * kk), idesc_res, first ? 0u : 1u);
-          else umma_f16_1_tmem_a(d, ta + 8u * kk, db + (uint64_t)(2 * kk), idesc_res, first ? 0u : 1u);
-          if (last) umma_commit_1(bar(bars->pfull[pb]));
-        }
-        if (!ok) break;
-        umma_commit_1(bar(bars->empty_a[as]));
-        umma_commit_1(bar(bars->empty_b[bs]));
-      }
-      for (int j = 0; j < n_lr && ok; ++j) {
-        const int it = n_res + j, bs = it % BS, ls = j % SB_LS;
-        const int pg = n_pg + j, pb = pg % PB;
-        if (!(ok = mbar_spin_wait(bar(bars->full_b[bs]), (uint32_t)(it / BS) & 1u, abort_flag, args.err,
-                                  kSbWaitMmaTile)))
-          break;
-        if (!(ok = mbar_spin_wait(bar(bars->pempty[pb]), ((uint32_t)(pg / PB) & 1u) ^ 1u, abort_flag, args.err,
-                                  kSbWaitMmaPartial)))
-          break;
-        tc_fence_after();
-        const uint64_t db = desc_k_sw128(b_ring + (uint32_t)bs * L::kB);
-        const uint64_t da = desc_k_sw128(l_ring + (uint32_t)ls * SB_LR_BYTES);
-        const uint32_t d = tmem + (uint32_t)pb * L::kPCols;
+        const uint32_t dset = tmem + (uint32_t)ps * set_cols;
+        const uint32_t tok = b_ring + (uint32_t)tb * L::kTokChunk;
+        if (res) {
+          const int st = stages_of(c);
+          const uint32_t wbase = tmem_w + (uint32_t)wc * L::kWChunkCols;
+          for (int j = 0; j < st; ++j) {
+            const uint64_t db = desc_k_sw128(tok + (uint32_t)j * L::kTokSub);
+            const uint32_t ta = wbase + (uint32_t)j * SB_STAGE_COLS;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16_1(d, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk), idesc_lr, kk > 0 ? 1u : 0u);
-        umma_commit_1(bar(bars->pfull[pb]));
-        umma_commit_1(bar(bars->empty_l[ls]));
-        umma_commit_1(bar(bars->empty_b[bs]));
+            for (int kk = 0; kk < 4; ++kk) {
+              const int step = j * 4 + kk;
+              const uint32_t d = dset + (uint32_t)(step >> lg_steps) * L::kPCols;
+              const uint32_t acc = (step & step_mask) ? 1u : 0u;
+              if constexpr (I8) umma_i8_tmem_a(d, ta + 8u * kk, db + (uint64_t)(2 * kk), idesc_res, acc);
+              else umma_f16_1_tmem_a(d, ta + 8u * kk, db + (uint64_t)(2 * kk), idesc_res, acc);
+            }
+          }
+          umma_commit_1(bar(bars->pfull[ps]));
+          umma_commit_1(bar(bars->empty_a[wc]));
+          if (++wc == WCH) { wc = 0; wph ^= 1u; }
+        } else {
+          const int ls = (c - n_ch) % SB_LS;
+          const uint64_t db = desc_k_sw128(tok);
+          const uint64_t da = desc_k_sw128(l_ring + (uint32_t)ls * SB_LR_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16_1(dset, da + (uint64_t)(2 * kk), db + (uint64_t)(2 * kk), idesc_lr, kk > 0 ? 1u : 0u);
+          umma_commit_1(bar(bars->pfull[ps]));
+          umma_commit_1(bar(bars->empty_l[ls]));
+        }
+        umma_commit_1(bar(bars->empty_b[tb]));
+        if (++tb == TB) { tb = 0; tph ^= 1u; }
+        if (++ps == psets) { ps = 0; pph ^= 1u; }
       }
       // no MMA may be in flight when the CTA frees tensor memory or exits
       umma_commit_1(bar(bars->mma_done));
@@ -422,51 +443,61 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
     }
   } else if (warp >= 8) {
     // ------------------------------------------------ conversion: codes -> integers in tensor memory
-    // Two warps per lane quarter take alternate weight stages; a thread converts its row's
-    // 128 bytes of operand per stage and stores them with one tcgen05.st.
+    // Two warps per lane quarter split each chunk's stages (alternately); a thread converts its
+    // row's 128 bytes of operand per stage and stores them with one tcgen05.st.  Each warp
+    // arrives once per chunk on the chunk's barriers, stages or not.
     const int q = warp & 3, half = (warp - 8) >> 2;
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const uint32_t r7 = (uint32_t)(row & 7);
+    constexpr int kChunks16 = SK / 32;  // 16-byte code chunks per stage and row
+    constexpr int kMine = SPB / 2;      // stages per chunk of this warp (a full chunk)
     bool ok = true;
-    for (int it = half; it < n_res && ok; it += 2) {
-      const int bx = it / SPB, ps = bx % SB_PS, ls = it % SPB;
-      const int as = it % AS;
-      if (!(ok = __all_sync(0xffffffffu, wait_spin(bar(bars->full_p[ps]), (uint32_t)(bx / SB_PS) & 1u, abort_flag,
+    int wc = 0;
+    uint32_t wph = 0;
+    for (int c = 0; c < n_ch && ok; ++c) {
+      const int ps = c % SB_PS, st = stages_of(c);
+      if (!(ok = __all_sync(0xffffffffu, wait_spin(bar(bars->full_p[ps]), (uint32_t)(c / SB_PS) & 1u, abort_flag,
                                                    args.err, kSbWaitConvPacked))))
         break;
-      // this stage's codes: SK / 2 bytes of the row, 16-byte chunks c (swizzled: c ^ (row % 8))
-      constexpr int kChunks = SK / 32;
-      uint32_t w[4 * kChunks];
+      uint32_t w[kMine][4 * kChunks16];
       const uint32_t rbase = p_ring + (uint32_t)ps * SB_BOX_BYTES + (uint32_t)row * 128u;
 #pragma unroll
-      for (int c = 0; c < kChunks; ++c) {
-        const uint4 v = lds128(rbase + ((((uint32_t)(ls * kChunks + c)) ^ r7) << 4));
-        w[4 * c] = v.x;
-        w[4 * c + 1] = v.y;
-        w[4 * c + 2] = v.z;
-        w[4 * c + 3] = v.w;
-      }
-      uint32_t o[32];
+      for (int i = 0; i < kMine; ++i) {
+        const int j = half + 2 * i;  // stage within the chunk
 #pragma unroll
-      for (int i = 0; i < 4 * kChunks; ++i) {
-        if constexpr (I8) codes_to_i8(w[i], o + 2 * i);
-        else codes_to_f16(w[i], o + 4 * i);
+        for (int cc = 0; cc < kChunks16; ++cc) {
+          const uint4 v = j < st ? lds128(rbase + ((((uint32_t)(j * kChunks16 + cc)) ^ r7) << 4)) : make_uint4(0, 0, 0, 0);
+          w[i][4 * cc] = v.x;
+          w[i][4 * cc + 1] = v.y;
+          w[i][4 * cc + 2] = v.z;
+          w[i][4 * cc + 3] = v.w;
+        }
       }
-      // the warp's last stage of this box: every lane has read its codes
-      if (it + 2 >= (bx + 1) * SPB || it + 2 >= n_res) {
-        __syncwarp();
-        if (lane == 0) arrive_cta(bar(bars->empty_p[ps]));
-      }
-      if (!(ok = __all_sync(0xffffffffu, wait_spin(bar(bars->empty_a[as]), ((uint32_t)(it / AS) & 1u) ^ 1u,
-                                                   abort_flag, args.err, kSbWaitConvEmpty))))
+      __syncwarp();
+      if (lane == 0) arrive_cta(bar(bars->empty_p[ps]));  // every lane has read its codes
+      if (!(ok = __all_sync(0xffffffffu, wait_spin(bar(bars->empty_a[wc]), wph ^ 1u, abort_flag, args.err,
+                                                   kSbWaitConvEmpty))))
         break;
       tc_fence_after();
-      tmem_st32(tmem_w + lane_off + (uint32_t)as * SB_STAGE_COLS, o);
+#pragma unroll
+      for (int i = 0; i < kMine; ++i) {
+        const int j = half + 2 * i;
+        if (j < st) {
+          uint32_t o[32];
+#pragma unroll
+          for (int e = 0; e < 4 * kChunks16; ++e) {
+            if constexpr (I8) codes_to_i8(w[i][e], o + 2 * e);
+            else codes_to_f16(w[i][e], o + 4 * e);
+          }
+          tmem_st32(tmem_w + lane_off + (uint32_t)wc * L::kWChunkCols + (uint32_t)j * SB_STAGE_COLS, o);
+        }
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) arrive_cta(bar(bars->conv[as]));
+      if (lane == 0) arrive_cta(bar(bars->conv[wc]));
+      if (++wc == WCH) { wc = 0; wph ^= 1u; }
     }
   } else if (warp >= 4) {
     // ------------------------------------------------ rescale: partials -> fp32 accumulators
@@ -477,68 +508,98 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
 #pragma unroll
     for (int t = 0; t < TN; ++t) acc[t] = 0.f;
     bool ok = true;
-    const int pg_per_box = SB_BOX_K / args.pg_k;
-    for (int pg = 0; pg < n_pg + n_lr && ok; ++pg) {
-      const bool res = pg < n_pg;
-      const int bx = pg / pg_per_box, ps = bx % SB_PS;
-      if (res && pg % pg_per_box == 0)
-        ok = wait_spin(bar(bars->full_p[ps]), (uint32_t)(bx / SB_PS) & 1u, abort_flag, args.err, kSbWaitScales);
-      const int pb = pg % PB;
-      ok = ok && wait_spin(bar(bars->pfull[pb]), (uint32_t)(pg / PB) & 1u, abort_flag, args.err, kSbWaitRescale);
+    const int n_pg = (k1 - k0) / pg_k;  // residual groups
+    // I8: the activation scales of the next group, loaded one group ahead (global memory latency);
+    // with 64 tokens that would take too many registers, and each group's are loaded in place
+    constexpr bool kPre = I8 && TN <= 32;
+    float4 sa_next[kPre ? TN / 4 : 1];
+    auto sa_ptr = [&](int pg) {
+      return reinterpret_cast<const float4*>(args.ascales_t + (int64_t)((k0 + pg * pg_k) / args.a_group) * args.lda_s +
+                                             m0);
+    };
+    auto load_sa = [&](int pg) {
+      if constexpr (kPre) {
+        if (pg < n_pg) {
+          const float4* src = sa_ptr(pg);
+#pragma unroll
+          for (int t = 0; t < TN / 4; ++t) sa_next[t] = __ldg(src + t);
+        }
+      }
+    };
+    load_sa(0);
+    int ps = 0, pg = 0;
+    uint32_t pph = 0;
+    for (int c = 0; c < n_ch + n_lr && ok; ++c) {
+      const bool res = c < n_ch;
+      const int bps = c % SB_PS;
+      if (res) ok = wait_spin(bar(bars->full_p[bps]), (uint32_t)(c / SB_PS) & 1u, abort_flag, args.err, kSbWaitScales);
+      ok = ok && wait_spin(bar(bars->pfull[ps]), pph, abort_flag, args.err, kSbWaitRescale);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc_fence_after();
-      float sw = 1.f;
-      const float* sa = nullptr;
-      if (res) {
-        const int kg = k0 + pg * args.pg_k;  // first k of the group
-        const uint32_t sidx = (uint32_t)(row * spg + (kg % SB_BOX_K) / args.w_group);
-        sw = __half2float(__ushort_as_half(lds16(s_ring + (uint32_t)ps * L::kSBytes + 2u * sidx)));
-        if constexpr (I8) sa = args.ascales_t + (int64_t)(kg / args.a_group) * args.lda_s + m0;
-        if (pg % pg_per_box == pg_per_box - 1 || pg == n_pg - 1) {
-          __syncwarp();
-          if (lane == 0) arrive_cta(bar(bars->empty_s[ps]));  // done with the box's weight scales
-        }
-      }
-      // the partial in chunks of at most 32 columns (registers), released after the last load
-      constexpr int CH = TN < 32 ? TN : 32;
-      const uint32_t src = tmem + lane_off + (uint32_t)pb * L::kPCols;
+      const int ng = res ? stages_of(c) * SK / pg_k : 1;
+      const uint32_t sset = tmem + lane_off + (uint32_t)ps * set_cols;
+      for (int g = 0; g < ng; ++g, pg += res ? 1 : 0) {
+        float sw = 1.f;
+        float4 sa[kPre ? TN / 4 : 1];
+        const float4* sa_g = nullptr;
+        if (res) {
+          sw = __half2float(__ushort_as_half(
+              lds16(s_ring + (uint32_t)bps * L::kSBytes + 2u * (uint32_t)(row * spg + (g * pg_k) / args.w_group))));
+          if constexpr (kPre) {
 #pragma unroll
-      for (int c = 0; c < TN / CH; ++c) {
-        uint32_t v[CH];
-        if constexpr (CH == 16) {
-          tmem_ld16(src, v);
-          tmem_ld_wait_regs16(v);
-        } else {
-          tmem_ld32(src + 32u * c, v);
-          tmem_ld_wait_regs(v);
-        }
-        if (c == TN / CH - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) arrive_cta(bar(bars->pempty[pb]));  // the MMA may refill the buffer
-        }
-        float* a = acc + c * CH;
-        if (!res) {
-#pragma unroll
-          for (int t = 0; t < CH; ++t) a[t] += __uint_as_float(v[t]);
-        } else if constexpr (I8) {
-#pragma unroll
-          for (int t = 0; t < CH; t += 4) {
-            const float4 s4 = __ldg(reinterpret_cast<const float4*>(sa + c * CH + t));
-            a[t] = fmaf((float)(int)v[t], sw * s4.x, a[t]);
-            a[t + 1] = fmaf((float)(int)v[t + 1], sw * s4.y, a[t + 1]);
-            a[t + 2] = fmaf((float)(int)v[t + 2], sw * s4.z, a[t + 2]);
-            a[t + 3] = fmaf((float)(int)v[t + 3], sw * s4.w, a[t + 3]);
+            for (int t = 0; t < TN / 4; ++t) sa[t] = sa_next[t];
+            load_sa(pg + 1);
+          } else if constexpr (I8) {
+            sa_g = sa_ptr(pg);
           }
-        } else {
+        }
+        // the partial in chunks of at most 32 columns (registers)
+        constexpr int CH = TN < 32 ? TN : 32;
+        const uint32_t src = sset + (uint32_t)g * L::kPCols;
 #pragma unroll
-          for (int t = 0; t < CH; ++t) a[t] = fmaf(__uint_as_float(v[t]), sw, a[t]);
+        for (int cc = 0; cc < TN / CH; ++cc) {
+          uint32_t v[CH];
+          if constexpr (CH == 16) {
+            tmem_ld16(src, v);
+            tmem_ld_wait_regs16(v);
+          } else {
+            tmem_ld32(src + 32u * cc, v);
+            tmem_ld_wait_regs(v);
+          }
+          if (g == ng - 1 && cc == TN / CH - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_cta(bar(bars->pempty[ps]));  // the MMA may refill the set
+          }
+          float* a = acc + cc * CH;
+          if (!res) {
+#pragma unroll
+            for (int t = 0; t < CH; ++t) a[t] += __uint_as_float(v[t]);
+          } else if constexpr (I8) {
+#pragma unroll
+            for (int t = 0; t < CH; t += 4) {
+              float4 s4;
+              if constexpr (kPre) s4 = sa[(cc * CH + t) / 4];
+              else s4 = __ldg(sa_g + (cc * CH + t) / 4);
+              a[t] = fmaf((float)(int)v[t], sw * s4.x, a[t]);
+              a[t + 1] = fmaf((float)(int)v[t + 1], sw * s4.y, a[t + 1]);
+              a[t + 2] = fmaf((float)(int)v[t + 2], sw * s4.z, a[t + 2]);
+              a[t + 3] = fmaf((float)(int)v[t + 3], sw * s4.w, a[t + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < CH; ++t) a[t] = fmaf(__uint_as_float(v[t]), sw, a[t]);
+          }
         }
       }
+      if (res) {
+        __syncwarp();
+        if (lane == 0) arrive_cta(bar(bars->empty_s[bps]));  // done with the box's weight scales
+      }
+      if (++ps == psets) { ps = 0; pph ^= 1u; }
     }
     // ---------------------------------------------- epilogue: out, or this CTA's split-K partial
-    // (every MMA has completed once the last partial was read: the partial stores may reuse the
-    // code ring)
+    // (every MMA has completed once the last partial was read: the partial may reuse the code ring)
     if (ok && !*abort_flag) {
       const int n = n0 + row;
       if (ks > 1) {
@@ -595,13 +656,13 @@ struct SbPlan {
   int tn, ks, units_n, units_m;
 };
 
-int sb_pick_tn(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : 64; }
+int sb_pick_tn(int M, int pg_k) { return M <= 16 ? 16 : (M <= 32 || pg_k < 64) ? 32 : 64; }
 
 // Split factor: among KS in {1, 2, 4, 8} (at least two code boxes per CTA), the fewest waves of
 // CTAs (one per SM), then the fullest last wave; ties go to the smaller KS.
-SbPlan sb_plan(int M, int N, int K_pad) {
+SbPlan sb_plan(int M, int N, int K_pad, int pg_k) {
   SbPlan p;
-  p.tn = sb_pick_tn(M);
+  p.tn = sb_pick_tn(M, pg_k);
   p.units_n = (N + SB_ROWS - 1) / SB_ROWS;
   p.units_m = (M + p.tn - 1) / p.tn;
   const int n_box = (K_pad + SB_BOX_K - 1) / SB_BOX_K;
@@ -627,7 +688,7 @@ template <int TN, bool I8, bool OUT_F32>
 int launch_sb(const CUtensorMap& tt, const CUtensorMap& tc, const CUtensorMap& tmid, const CUtensorMap& tup,
               const SbArgs& a, int grid, cudaStream_t stream) {
   auto kern = packed_small_kernel<TN, I8, OUT_F32>;
-  constexpr uint32_t smem = SbLayout<TN>::kSmem;
+  constexpr uint32_t smem = SbLayout<TN, I8>::kSmem;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "packed small-batch GEMM: shared memory attribute");
   cudaLaunchConfig_t cfg = {};
@@ -669,7 +730,8 @@ int packed_small_gemm(const void* act, bool i8, const float* ascales_t, int64_t 
                       cudaStream_t stream) {
   int* err = device_error_word();
   if (!err) return set_error(SVDQ_ERR_CUDA, "packed small-batch GEMM: device error word unavailable");
-  const SbPlan p = sb_plan(M, N, K_pad);
+  const int pg_k = std::min(w_group, i8 ? a_group : w_group);
+  const SbPlan p = sb_plan(M, N, K_pad, pg_k);
   CUtensorMap tt, tc, tmid, tup;
   int st;
   if ((st = make_tma_2d(&tt, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, K_pad, M,
@@ -701,7 +763,7 @@ int packed_small_gemm(const void* act, bool i8, const float* ascales_t, int64_t 
   a.K_pad = K_pad;
   a.w_group = w_group;
   a.a_group = i8 ? a_group : w_group;
-  a.pg_k = std::min(a.w_group, a.a_group);
+  a.pg_k = pg_k;
   a.n_lr = R2 / 64;
   a.ks = p.ks;
   a.units_n = p.units_n;
@@ -715,7 +777,7 @@ int packed_small_gemm(const void* act, bool i8, const float* ascales_t, int64_t 
 }
 
 int packed_small_plan(int M, int N, int K_pad, int* out4) {
-  const SbPlan p = sb_plan(M, N, K_pad);
+  const SbPlan p = sb_plan(M, N, K_pad, 64);
   out4[0] = p.tn;
   out4[1] = p.ks;
   out4[2] = p.units_n * p.units_m * p.ks;
