@@ -87,7 +87,10 @@ struct SbLayout {
   static constexpr uint32_t kOffL = kOffB + kTB * kTokChunk;
   static constexpr uint32_t kOffS = kOffL + SB_LS * SB_LR_BYTES;               // weight-scale ring
   static constexpr uint32_t kSBytes = SB_ROWS * SB_MAX_SCALES * 2;
-  static constexpr uint32_t kOffBar = kOffS + SB_PS * kSBytes;
+  // I8: activation scales of a chunk (at most 4 groups x TN), staged per rescale warp, double buffered
+  static constexpr uint32_t kSaBuf = 4 * TN * 4;
+  static constexpr uint32_t kOffA = kOffS + SB_PS * kSBytes;
+  static constexpr uint32_t kOffBar = kOffA + (I8 ? 4 * 2 * kSaBuf : 0);
   static constexpr uint32_t kSmem = kOffBar + 1024 + 1024;                     // barriers + alignment slack
   static_assert(kTokSub % 1024 == 0, "token tiles keep 1 KiB alignment for the 128-byte swizzle");
   static_assert((uint32_t)SB_ROWS * TN * 4 <= kOffB, "split-K partial fits over the code ring");
@@ -155,6 +158,12 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
+__device__ __forceinline__ float4 lds128f(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ uint16_t lds16(uint32_t addr) {
   unsigned short v;
   asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
@@ -276,8 +285,10 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
   const int n_lr = crank == ks - 1 ? args.n_lr : 0;                     // low-rank chunks (one stage each)
   const int pg_k = args.pg_k;
   const int lg_steps = __ffs(pg_k / KSTEP) - 1;                         // log2(MMAs per group)
-  const int gpc = SB_BOX_K / pg_k;                                      // groups per full chunk
-  const int spg = SB_BOX_K / args.w_group;                              // weight scales per row and box
+  // group widths are powers of two: shifts, not divisions, on the latency-bound single-warp paths
+  const int lg_pg = __ffs(pg_k) - 1, lg_wg = __ffs(args.w_group) - 1, lg_ag = __ffs(args.a_group) - 1;
+  const int gpc = SB_BOX_K >> lg_pg;                                    // groups per full chunk
+  const int spg = SB_BOX_K >> lg_wg;                                    // weight scales per row and box
   // tensor memory: partial sets, then the weight-chunk ring
   const uint32_t set_cols = (uint32_t)gpc * L::kPCols;
   const int psets = 2 * set_cols + 2 * L::kWChunkCols <= SB_TMEM_COLS ? 2 : 1;
@@ -508,87 +519,103 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
 #pragma unroll
     for (int t = 0; t < TN; ++t) acc[t] = 0.f;
     bool ok = true;
-    const int n_pg = (k1 - k0) / pg_k;  // residual groups
-    // I8: the activation scales of the next group, loaded one group ahead (global memory latency);
-    // with 64 tokens that would take too many registers, and each group's are loaded in place
-    constexpr bool kPre = I8 && TN <= 32;
-    float4 sa_next[kPre ? TN / 4 : 1];
-    auto sa_ptr = [&](int pg) {
-      return reinterpret_cast<const float4*>(args.ascales_t + (int64_t)((k0 + pg * pg_k) / args.a_group) * args.lda_s +
-                                             m0);
-    };
-    auto load_sa = [&](int pg) {
-      if constexpr (kPre) {
-        if (pg < n_pg) {
-          const float4* src = sa_ptr(pg);
+    // I8: a chunk's activation scales ([group][token], fp32) are loaded from global memory one chunk
+    // ahead into registers, then staged in this warp's shared-memory buffer (reads broadcast)
+    constexpr int kSaRegs = I8 ? (4 * TN + 31) / 32 : 1;
+    float sa_pre[kSaRegs];
+    const uint32_t sa_smem = base + L::kOffA + (uint32_t)q * 2u * L::kSaBuf;
+    float* sa_gen = reinterpret_cast<float*>(gbase + L::kOffA + (uint32_t)q * 2u * L::kSaBuf);
+    auto sa_fetch = [&](int c) {  // chunk c's scales -> sa_pre (every lane its elements)
+      if constexpr (I8) {
+        if (c < n_ch) {
+          const int ngc = (stages_of(c) * SK) >> lg_pg, pg0 = c * gpc;
 #pragma unroll
-          for (int t = 0; t < TN / 4; ++t) sa_next[t] = __ldg(src + t);
+          for (int j = 0; j < kSaRegs; ++j) {
+            const int e = lane + 32 * j, g = e / TN, t = e % TN;
+            sa_pre[j] = g < ngc ? __ldg(args.ascales_t + (int64_t)((k0 + ((pg0 + g) << lg_pg)) >> lg_ag) * args.lda_s +
+                                        m0 + t)
+                                : 0.f;
+          }
         }
       }
     };
-    load_sa(0);
-    int ps = 0, pg = 0;
+    auto sa_stage = [&](int c) {  // sa_pre -> buffer (c & 1)
+      if constexpr (I8) {
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < kSaRegs; ++j) {
+          const int e = lane + 32 * j;
+          if (e < 4 * TN) sa_gen[(c & 1) * 4 * TN + e] = sa_pre[j];
+        }
+        __syncwarp();
+      }
+    };
+    sa_fetch(0);
+    sa_stage(0);
+    // partial buffers loaded per batch of groups (about 64 registers), one tcgen05.wait::ld each
+    constexpr int GB = TN <= 16 ? 4 : TN <= 32 ? 2 : 1;
+    int ps = 0;
     uint32_t pph = 0;
     for (int c = 0; c < n_ch + n_lr && ok; ++c) {
       const bool res = c < n_ch;
       const int bps = c % SB_PS;
+      sa_fetch(c + 1);
       if (res) ok = wait_spin(bar(bars->full_p[bps]), (uint32_t)(c / SB_PS) & 1u, abort_flag, args.err, kSbWaitScales);
       ok = ok && wait_spin(bar(bars->pfull[ps]), pph, abort_flag, args.err, kSbWaitRescale);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc_fence_after();
-      const int ng = res ? stages_of(c) * SK / pg_k : 1;
+      const int ng = res ? (stages_of(c) * SK) >> lg_pg : 1;
       const uint32_t sset = tmem + lane_off + (uint32_t)ps * set_cols;
-      for (int g = 0; g < ng; ++g, pg += res ? 1 : 0) {
-        float sw = 1.f;
-        float4 sa[kPre ? TN / 4 : 1];
-        const float4* sa_g = nullptr;
-        if (res) {
-          sw = __half2float(__ushort_as_half(
-              lds16(s_ring + (uint32_t)bps * L::kSBytes + 2u * (uint32_t)(row * spg + (g * pg_k) / args.w_group))));
-          if constexpr (kPre) {
+      // columns in halves of 32 for 64 tokens (registers)
+      constexpr int CW = TN <= 32 ? TN : 32;
+      for (int g0 = 0; g0 < ng; g0 += GB) {
 #pragma unroll
-            for (int t = 0; t < TN / 4; ++t) sa[t] = sa_next[t];
-            load_sa(pg + 1);
-          } else if constexpr (I8) {
-            sa_g = sa_ptr(pg);
-          }
-        }
-        // the partial in chunks of at most 32 columns (registers)
-        constexpr int CH = TN < 32 ? TN : 32;
-        const uint32_t src = sset + (uint32_t)g * L::kPCols;
+        for (int h = 0; h < TN / CW; ++h) {
+          uint32_t v[GB][CW];
 #pragma unroll
-        for (int cc = 0; cc < TN / CH; ++cc) {
-          uint32_t v[CH];
-          if constexpr (CH == 16) {
-            tmem_ld16(src, v);
-            tmem_ld_wait_regs16(v);
-          } else {
-            tmem_ld32(src + 32u * cc, v);
-            tmem_ld_wait_regs(v);
+          for (int b = 0; b < GB; ++b) {
+            if (g0 + b < ng) {
+              const uint32_t src = sset + (uint32_t)(g0 + b) * L::kPCols + (uint32_t)(h * CW);
+              if constexpr (CW == 16) tmem_ld16(src, reinterpret_cast<uint32_t(&)[16]>(v[b][0]));
+              else tmem_ld32(src, reinterpret_cast<uint32_t(&)[32]>(v[b][0]));
+            }
           }
-          if (g == ng - 1 && cc == TN / CH - 1) {
+          tmem_ld_wait();
+#pragma unroll
+          for (int b = 0; b < GB; ++b)
+#pragma unroll
+            for (int t = 0; t < CW; ++t) asm volatile("" : "+r"(v[b][t]));  // no use before the wait
+          if (g0 + GB >= ng && h == TN / CW - 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) arrive_cta(bar(bars->pempty[ps]));  // the MMA may refill the set
           }
-          float* a = acc + cc * CH;
-          if (!res) {
+          float* a = acc + h * CW;
 #pragma unroll
-            for (int t = 0; t < CH; ++t) a[t] += __uint_as_float(v[t]);
-          } else if constexpr (I8) {
+          for (int b = 0; b < GB; ++b) {
+            const int g = g0 + b;
+            if (g >= ng) break;
+            if (!res) {
 #pragma unroll
-            for (int t = 0; t < CH; t += 4) {
-              float4 s4;
-              if constexpr (kPre) s4 = sa[(cc * CH + t) / 4];
-              else s4 = __ldg(sa_g + (cc * CH + t) / 4);
-              a[t] = fmaf((float)(int)v[t], sw * s4.x, a[t]);
-              a[t + 1] = fmaf((float)(int)v[t + 1], sw * s4.y, a[t + 1]);
-              a[t + 2] = fmaf((float)(int)v[t + 2], sw * s4.z, a[t + 2]);
-              a[t + 3] = fmaf((float)(int)v[t + 3], sw * s4.w, a[t + 3]);
+              for (int t = 0; t < CW; ++t) a[t] += __uint_as_float(v[b][t]);
+              continue;
             }
-          } else {
+            const float sw = __half2float(__ushort_as_half(
+                lds16(s_ring + (uint32_t)bps * L::kSBytes + 2u * (uint32_t)(row * spg + ((g << lg_pg) >> lg_wg)))));
+            if constexpr (I8) {
+              const uint32_t sa_row = sa_smem + (uint32_t)(((c & 1) * 4 + g) * TN + h * CW) * 4u;
 #pragma unroll
-            for (int t = 0; t < CH; ++t) a[t] = fmaf(__uint_as_float(v[t]), sw, a[t]);
+              for (int t = 0; t < CW; t += 4) {
+                const float4 s4 = lds128f(sa_row + 4u * t);
+                a[t] = fmaf((float)(int)v[b][t], sw * s4.x, a[t]);
+                a[t + 1] = fmaf((float)(int)v[b][t + 1], sw * s4.y, a[t + 1]);
+                a[t + 2] = fmaf((float)(int)v[b][t + 2], sw * s4.z, a[t + 2]);
+                a[t + 3] = fmaf((float)(int)v[b][t + 3], sw * s4.w, a[t + 3]);
+              }
+            } else {
+#pragma unroll
+              for (int t = 0; t < CW; ++t) a[t] = fmaf(__uint_as_float(v[b][t]), sw, a[t]);
+            }
           }
         }
       }
@@ -596,6 +623,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
         __syncwarp();
         if (lane == 0) arrive_cta(bar(bars->empty_s[bps]));  // done with the box's weight scales
       }
+      sa_stage(c + 1);
       if (++ps == psets) { ps = 0; pph ^= 1u; }
     }
     // ---------------------------------------------- epilogue: out, or this CTA's split-K partial
