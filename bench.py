@@ -370,9 +370,11 @@ def measure_w4a16_lora(dev, flush, iters: int) -> dict:
 
 def measure_small_batch(dev, flush, iters: int) -> dict:
     """The config-2/4 layer (K6144 N16384, rank 32, group 64, bias) at small batches, where the
-    weight bytes bound the GEMM: the packed-weight GEMM (half-byte codes + fp16 scales converted in
-    shared memory) against the fp16-weight GEMM on the same activation operand, each against its
-    roofline max(bytes / HBM peak, 2MNK / bf16 peak).  Kernel times with the L2 flushed."""
+    weight bytes bound the GEMM.  Packed-weight GEMMs (half-byte codes + fp16 scales, no fp16 weight
+    in memory): the int8-code W4A4 GEMM (kind::i8, per-group rescale; batches up to 64 tokens) and
+    the fp16-operand packed GEMM (the W4A16 path) against the fp16-weight GEMM, each against its
+    roofline max(bytes / HBM peak, 2MNK / bf16 peak).  Kernel times with the L2 flushed; the
+    module's whole forward (activation pass + GEMM) of the packed layer as ``linear_us``."""
     import torch
 
     from krea2_svdquant_b200 import ops
@@ -383,33 +385,40 @@ def measure_small_batch(dev, flush, iters: int) -> dict:
     hbm = float(peaks.get("hbm_gbs") or 6650.0) * 1e9
     tc = _bf16_peak() * 1e12
     _, st = make_synthetic_state(256, K, N, RANK, GROUP, seed=9, device=dev)
-    mod = SVDQuantLinear(st, backend="b200", weight_operand="fp16")
-    p = mod.prepare(dev)
-    pk = SVDQuantLinear(st, backend="b200", weight_operand="packed").prepare(dev)
+    p = SVDQuantLinear(st, backend="b200", weight_operand="fp16").prepare(dev)
+    mod_pk = SVDQuantLinear(st, backend="b200", weight_operand="packed")
+    pk = mod_pk.prepare(dev)
     r2 = p.up_hl.shape[1]
     out = {}
     for m in (16, 64, 256):
         x = torch.randn(m, K, device=dev).bfloat16()
         a16, mid, _, _ = ops.act_quant(x, p.smooth, p.l2, None, None, p.k_pad, 64, True, False)
-        t_pk = statistics.median(_device_times(
-            lambda: ops.packed_gemm(a16, pk.codes, pk.scales16, GROUP, mid, p.up_hl, p.bias, False), iters, flush))
-        t_16 = statistics.median(_device_times(
-            lambda: ops.linear_gemm(a16, p.w16, mid, p.up_hl, p.bias, False), iters, flush))
-        t_lin = statistics.median(_device_times(lambda: mod(x), iters, flush))
-        act_out = m * K * 2 + m * N * 2 + m * r2 * 2 + N * r2 * 2 + N * 2  # a16, out, mid_hl, up_hl, bias
-        b_pk = N * K // 2 + N * (K // GROUP) * 2 + act_out
-        b_16 = N * K * 2 + act_out
+        lowrank = m * r2 * 2 + N * r2 * 2 + N * 2 + m * N * 2  # mid_hl, up_hl, bias, out
+        w_pk = N * K // 2 + N * (K // GROUP) * 2
         flops = 2 * m * N * K
-        roof_pk = max(b_pk / hbm, flops / tc)
-        roof_16 = max(b_16 / hbm, flops / tc)
-        out[f"M{m}"] = {
-            "packed_gemm_us": round(t_pk * 1e3, 2), "packed_bytes": b_pk,
-            "packed_bound": "hbm" if b_pk / hbm >= flops / tc else "tensor",
-            "packed_roofline_us": round(roof_pk * 1e6, 2), "packed_frac": round(roof_pk / (t_pk * 1e-3), 3),
-            "packed_achieved_gbs": round(b_pk / (t_pk * 1e-3) / 1e9, 1),
-            "fp16_gemm_us": round(t_16 * 1e3, 2), "fp16_roofline_us": round(roof_16 * 1e6, 2),
-            "fp16_frac": round(roof_16 / (t_16 * 1e-3), 3),
-            "linear_us": round(t_lin * 1e3, 2), "linear_tops": round(flops / (t_lin * 1e-3) / 1e12, 1)}
+        row = {}
+
+        def put(name, t_ms, act_bytes, w_bytes):
+            b = w_bytes + act_bytes + lowrank
+            roof = max(b / hbm, flops / tc)
+            row.update({f"{name}_us": round(t_ms * 1e3, 2), f"{name}_bytes": b,
+                        f"{name}_bound": "hbm" if b / hbm >= flops / tc else "tensor",
+                        f"{name}_roofline_us": round(roof * 1e6, 2), f"{name}_frac": round(roof / (t_ms * 1e-3), 3)})
+
+        if m <= 64:
+            c8, asc, mid8 = ops.act_quant_i8(x, p.smooth, p.l2, None, None, p.k_pad, 64)
+            put("w4a4_i8_gemm", statistics.median(_device_times(
+                lambda: ops.w4a4_gemm(c8, asc, 64, pk.codes, pk.scales16, GROUP, mid8, p.up_hl, p.bias, False),
+                iters, flush)), m * K + asc.numel() * 4, w_pk)
+        put("packed_f16_gemm", statistics.median(_device_times(
+            lambda: ops.packed_gemm(a16, pk.codes, pk.scales16, GROUP, mid, p.up_hl, p.bias, False), iters, flush)),
+            m * K * 2, w_pk)
+        put("fp16_gemm", statistics.median(_device_times(
+            lambda: ops.linear_gemm(a16, p.w16, mid, p.up_hl, p.bias, False), iters, flush)), m * K * 2, N * K * 2)
+        t_lin = statistics.median(_device_times(lambda: mod_pk(x), iters, flush))
+        row.update({"linear_packed_us": round(t_lin * 1e3, 2), "linear_packed_tops": round(flops / (t_lin * 1e-3) / 1e12, 1),
+                    "linear_packed_path": "int8 codes + kind::i8 GEMM" if m <= 64 else "a16 + packed fp16-operand GEMM"})
+        out[f"M{m}"] = row
     return {"config": "K6144 N16384 rank 32 group 64 bias, W4A4, small batches (BASELINE config 4's HBM regime)",
             "hbm_peak_gbs": hbm / 1e9, "per_batch": out,
             "plan_tn_ks_grid_ctas_per_sm": {f"M{m}": _packed_plan(m, N, K) for m in (16, 64, 256)}}

@@ -163,6 +163,11 @@ __device__ __forceinline__ float4 lds128f(uint32_t addr) {
   asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
   return v;
 }
+__device__ __forceinline__ float ldg_f32_volatile(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ uint16_t lds16(uint32_t addr) {
   unsigned short v;
@@ -532,8 +537,9 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < kSaRegs; ++j) {
             const int e = lane + 32 * j, g = e / TN, t = e % TN;
-            sa_pre[j] = g < ngc ? __ldg(args.ascales_t + (int64_t)((k0 + ((pg0 + g) << lg_pg)) >> lg_ag) * args.lda_s +
-                                        m0 + t)
+            // volatile: issued here, a chunk before its use, not sunk next to the use
+            sa_pre[j] = g < ngc ? ldg_f32_volatile(args.ascales_t + (int64_t)((k0 + ((pg0 + g) << lg_pg)) >> lg_ag) *
+                                                                        args.lda_s + m0 + t)
                                 : 0.f;
           }
         }
