@@ -38,9 +38,10 @@
 // groups); after a cluster barrier each CTA adds one slice of rows over all KS partials through
 // distributed shared memory, in rank order (deterministic), adds the bias and stores.
 //
-// Roles (16 warps): warp 0 TMA of code boxes and weight scales; warp 1 tensor-memory allocation
-// and the MMA issue; warp 2 TMA of token tiles (and low-rank tiles); warps 4-7 rescale and
-// epilogue; warps 8-15 conversion (two per lane quarter, alternate weight stages).  The
+// Roles (20 warps): warp 0 TMA of code boxes and weight scales; warp 1 tensor-memory allocation
+// and the MMA issue; warp 2 TMA of token tiles (and low-rank tiles); warps 4-7 and 16-19 rescale
+// and epilogue (two per lane quarter, each half of the tokens); warps 8-15 conversion (two per
+// lane quarter, alternate weight stages).  The
 // single-thread roles wait by spinning on mbarrier.test_wait; the warps poll it with a short
 // nanosleep in between (a suspending try_wait costs a few hundred nanoseconds to wake, which this
 // latency-bound pipeline cannot hide, and a spinning warp takes issue slots from the MMA thread
@@ -61,7 +62,8 @@ constexpr int SB_PS = 6;                     // code-box ring (shared memory)
 constexpr int SB_LS = 2;                     // low-rank A ring
 constexpr uint32_t SB_LR_BYTES = SB_ROWS * 64 * 2;  // up_hl tile: 128 rows x 64 bf16
 constexpr int SB_CONV_WARPS = 8;
-constexpr int SB_THREADS = 32 * (8 + SB_CONV_WARPS);
+constexpr int SB_RESCALE_WARPS = 8;          // two per lane quarter, each half of the tokens
+constexpr int SB_THREADS = 32 * (4 + SB_CONV_WARPS + SB_RESCALE_WARPS);
 constexpr uint32_t SB_TMEM_COLS = 512;
 constexpr uint32_t SB_STAGE_COLS = 32;       // tensor-memory columns of one weight stage (128 B per row)
 constexpr int SB_MAX_SCALES = 8;             // weight scales per row and code box (group 32)
@@ -90,7 +92,7 @@ struct SbLayout {
   // I8: activation scales of a chunk (at most 4 groups x TN), staged per rescale warp, double buffered
   static constexpr uint32_t kSaBuf = 4 * TN * 4;
   static constexpr uint32_t kOffA = kOffS + SB_PS * kSBytes;
-  static constexpr uint32_t kOffBar = kOffA + (I8 ? 4 * 2 * kSaBuf : 0);
+  static constexpr uint32_t kOffBar = kOffA + (I8 ? SB_RESCALE_WARPS * 2 * kSaBuf : 0);
   static constexpr uint32_t kSmem = kOffBar + 1024 + 1024;                     // barriers + alignment slack
   static_assert(kTokSub % 1024 == 0, "token tiles keep 1 KiB alignment for the 128-byte swizzle");
   static_assert((uint32_t)SB_ROWS * TN * 4 <= kOffB, "split-K partial fits over the code ring");
@@ -106,8 +108,8 @@ struct SbBars {
   uint64_t conv[SB_MAX_WCH];    // weight chunk written to tensor memory (one arrival per converter warp)
   uint64_t empty_a[SB_MAX_WCH]; // MMAs reading the weight chunk done (commit)
   uint64_t empty_l[SB_LS];      // MMAs reading the low-rank A slot done (commit)
-  uint64_t pfull[2];            // a chunk's partial set complete (commit)
-  uint64_t pempty[2];           // partial set read by the rescale warps (one arrival per rescale warp)
+  uint64_t pfull[3];            // a chunk's partial set complete (commit)
+  uint64_t pempty[3];           // partial set read by the rescale warps (one arrival per rescale warp)
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
@@ -167,6 +169,12 @@ __device__ __forceinline__ float ldg_f32_volatile(const float* p) {
   float v;
   asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
   return v;
+}
+// 32 lanes x 8 consecutive 32-bit columns: thread i of the warp gets lane (base + i).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ uint16_t lds16(uint32_t addr) {
@@ -296,7 +304,11 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
   const int spg = SB_BOX_K >> lg_wg;                                    // weight scales per row and box
   // tensor memory: partial sets, then the weight-chunk ring
   const uint32_t set_cols = (uint32_t)gpc * L::kPCols;
-  const int psets = 2 * set_cols + 2 * L::kWChunkCols <= SB_TMEM_COLS ? 2 : 1;
+  // as many partial sets (up to 3) as leave room for two weight chunks: the MMAs of chunk c + psets
+  // wait for the rescale of chunk c
+  const int psets = 3 * set_cols + 2 * L::kWChunkCols <= SB_TMEM_COLS   ? 3
+                    : 2 * set_cols + 2 * L::kWChunkCols <= SB_TMEM_COLS ? 2
+                                                                        : 1;
   const int wch_fit = (int)((SB_TMEM_COLS - psets * set_cols) / L::kWChunkCols);
   const int WCH = wch_fit > SB_MAX_WCH ? SB_MAX_WCH : wch_fit;
   auto stages_of = [&](int c) { return min(SPB, n_res - c * SPB); };
@@ -307,7 +319,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
     for (int s = 0; s < SB_PS; ++s) {
       mbar_init(bar(bars->full_p[s]), 1);
       mbar_init(bar(bars->empty_p[s]), SB_CONV_WARPS);
-      mbar_init(bar(bars->empty_s[s]), 4);
+      mbar_init(bar(bars->empty_s[s]), SB_RESCALE_WARPS);
     }
     for (int s = 0; s < TB; ++s) {
       mbar_init(bar(bars->full_b[s]), 1);
@@ -318,9 +330,9 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
       mbar_init(bar(bars->empty_a[s]), 1);
     }
     for (int s = 0; s < SB_LS; ++s) mbar_init(bar(bars->empty_l[s]), 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < 3; ++s) {
       mbar_init(bar(bars->pfull[s]), 1);
-      mbar_init(bar(bars->pempty[s]), 4);
+      mbar_init(bar(bars->pempty[s]), SB_RESCALE_WARPS);
     }
     mbar_init(bar(bars->mma_done), 1);
     bars->abort_flag = 0;
@@ -457,7 +469,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
       }
       if (!ok) *abort_flag = 1;
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 8 && warp < 16) {
     // ------------------------------------------------ conversion: codes -> integers in tensor memory
     // Two warps per lane quarter split each chunk's stages (alternately); a thread converts its
     // row's 128 bytes of operand per stage and stores them with one tcgen05.st.  Each warp
@@ -517,19 +529,22 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------ rescale: partials -> fp32 accumulators
-    const int q = warp & 3;
+    // warps 4-7 take tokens [0, TN/2) and warps 16-19 tokens [TN/2, TN) of the same rows
+    const int q = warp & 3, rh = warp >= 16 ? 1 : 0;
+    constexpr int TH = TN / 2;
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    float acc[TN];
+    float acc[TH];
 #pragma unroll
-    for (int t = 0; t < TN; ++t) acc[t] = 0.f;
+    for (int t = 0; t < TH; ++t) acc[t] = 0.f;
     bool ok = true;
     // I8: a chunk's activation scales ([group][token], fp32) are loaded from global memory one chunk
     // ahead into registers, then staged in this warp's shared-memory buffer (reads broadcast)
     constexpr int kSaRegs = I8 ? (4 * TN + 31) / 32 : 1;
     float sa_pre[kSaRegs];
-    const uint32_t sa_smem = base + L::kOffA + (uint32_t)q * 2u * L::kSaBuf;
-    float* sa_gen = reinterpret_cast<float*>(gbase + L::kOffA + (uint32_t)q * 2u * L::kSaBuf);
+    const int rw = q + 4 * rh;  // rescale warp index
+    const uint32_t sa_smem = base + L::kOffA + (uint32_t)rw * 2u * L::kSaBuf;
+    float* sa_gen = reinterpret_cast<float*>(gbase + L::kOffA + (uint32_t)rw * 2u * L::kSaBuf);
     auto sa_fetch = [&](int c) {  // chunk c's scales -> sa_pre (every lane its elements)
       if constexpr (I8) {
         if (c < n_ch) {
@@ -559,7 +574,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
     sa_fetch(0);
     sa_stage(0);
     // partial buffers loaded per batch of groups (about 64 registers), one tcgen05.wait::ld each
-    constexpr int GB = TN <= 16 ? 4 : TN <= 32 ? 2 : 1;
+    constexpr int GB = TH <= 8 ? 4 : TH <= 16 ? 2 : 1;
     int ps = 0;
     uint32_t pph = 0;
     for (int c = 0; c < n_ch + n_lr && ok; ++c) {
@@ -572,17 +587,17 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
       tc_fence_after();
       const int ng = res ? (stages_of(c) * SK) >> lg_pg : 1;
       const uint32_t sset = tmem + lane_off + (uint32_t)ps * set_cols;
-      // columns in halves of 32 for 64 tokens (registers)
-      constexpr int CW = TN <= 32 ? TN : 32;
+      constexpr int CW = TH;  // this warp's columns: 8, 16 or 32
       for (int g0 = 0; g0 < ng; g0 += GB) {
 #pragma unroll
-        for (int h = 0; h < TN / CW; ++h) {
+        for (int h = 0; h < 1; ++h) {
           uint32_t v[GB][CW];
 #pragma unroll
           for (int b = 0; b < GB; ++b) {
             if (g0 + b < ng) {
-              const uint32_t src = sset + (uint32_t)(g0 + b) * L::kPCols + (uint32_t)(h * CW);
-              if constexpr (CW == 16) tmem_ld16(src, reinterpret_cast<uint32_t(&)[16]>(v[b][0]));
+              const uint32_t src = sset + (uint32_t)(g0 + b) * L::kPCols + (uint32_t)(rh * TH);
+              if constexpr (CW == 8) tmem_ld8(src, reinterpret_cast<uint32_t(&)[8]>(v[b][0]));
+              else if constexpr (CW == 16) tmem_ld16(src, reinterpret_cast<uint32_t(&)[16]>(v[b][0]));
               else tmem_ld32(src, reinterpret_cast<uint32_t(&)[32]>(v[b][0]));
             }
           }
@@ -591,12 +606,12 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
           for (int b = 0; b < GB; ++b)
 #pragma unroll
             for (int t = 0; t < CW; ++t) asm volatile("" : "+r"(v[b][t]));  // no use before the wait
-          if (g0 + GB >= ng && h == TN / CW - 1) {
+          if (g0 + GB >= ng) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) arrive_cta(bar(bars->pempty[ps]));  // the MMA may refill the set
           }
-          float* a = acc + h * CW;
+          float* a = acc;
 #pragma unroll
           for (int b = 0; b < GB; ++b) {
             const int g = g0 + b;
@@ -609,7 +624,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
             const float sw = __half2float(__ushort_as_half(
                 lds16(s_ring + (uint32_t)bps * L::kSBytes + 2u * (uint32_t)(row * spg + ((g << lg_pg) >> lg_wg)))));
             if constexpr (I8) {
-              const uint32_t sa_row = sa_smem + (uint32_t)(((c & 1) * 4 + g) * TN + h * CW) * 4u;
+              const uint32_t sa_row = sa_smem + (uint32_t)(((c & 1) * 4 + g) * TN + rh * TH) * 4u;
 #pragma unroll
               for (int t = 0; t < CW; t += 4) {
                 const float4 s4 = lds128f(sa_row + 4u * t);
@@ -639,12 +654,12 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
       if (ks > 1) {
         float* part = reinterpret_cast<float*>(gbase);  // [TN][128]
 #pragma unroll
-        for (int t = 0; t < TN; ++t) part[t * SB_ROWS + row] = acc[t];
+        for (int t = 0; t < TH; ++t) part[(rh * TH + t) * SB_ROWS + row] = acc[t];
       } else if (n < args.N) {
         const float b = args.bias ? __bfloat162float(args.bias[n]) : 0.f;
 #pragma unroll
-        for (int t = 0; t < TN; ++t) {
-          const int m = m0 + t;
+        for (int t = 0; t < TH; ++t) {
+          const int m = m0 + rh * TH + t;
           if (m < args.M) {
             const float y = acc[t] + b;
             if constexpr (OUT_F32) static_cast<float*>(args.out)[(int64_t)m * args.ldo + n] = y;
