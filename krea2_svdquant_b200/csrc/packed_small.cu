@@ -41,11 +41,10 @@
 // Roles (20 warps): warp 0 TMA of code boxes and weight scales; warp 1 tensor-memory allocation
 // and the MMA issue; warp 2 TMA of token tiles (and low-rank tiles); warps 4-7 and 16-19 rescale
 // and epilogue (two per lane quarter, each half of the tokens); warps 8-15 conversion (two per
-// lane quarter, alternate weight stages).  The
-// single-thread roles wait by spinning on mbarrier.test_wait; the warps poll it with a short
-// nanosleep in between (a suspending try_wait costs a few hundred nanoseconds to wake, which this
-// latency-bound pipeline cannot hide, and a spinning warp takes issue slots from the MMA thread
-// on its SM sub-partition).  Every wait is bounded (error word
+// lane quarter, alternate weight stages).  The MMA thread waits by spinning on
+// mbarrier.test_wait; every other role polls it with a short nanosleep in between (a suspending
+// try_wait costs a few hundred nanoseconds to wake, which this latency-bound pipeline cannot
+// hide, and a spinning warp takes issue slots from the MMA thread).  Every wait is bounded (error word
 // codes 0x55xx-0x58xx); a wait that runs out raises the CTA's abort flag, every role leaves its
 // loop, and all CTAs still meet at the cluster barriers.
 #include <algorithm>
@@ -367,8 +366,8 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
       for (int it = 0; it < n_ch && ok; ++it) {
         const int s = it % SB_PS;
         const uint32_t ph = (uint32_t)(it / SB_PS) & 1u;
-        if (!(ok = mbar_spin_wait(bar(bars->empty_p[s]), ph ^ 1u, abort_flag, args.err, kSbWaitPackedEmpty))) break;
-        if (!(ok = mbar_spin_wait(bar(bars->empty_s[s]), ph ^ 1u, abort_flag, args.err, kSbWaitPackedEmpty))) break;
+        if (!(ok = wait_spin(bar(bars->empty_p[s]), ph ^ 1u, abort_flag, args.err, kSbWaitPackedEmpty))) break;
+        if (!(ok = wait_spin(bar(bars->empty_s[s]), ph ^ 1u, abort_flag, args.err, kSbWaitPackedEmpty))) break;
         mbar_arrive_expect_tx(bar(bars->full_p[s]), SB_BOX_BYTES + sbytes);
         tma_load_2d(p_ring + (uint32_t)s * SB_BOX_BYTES, &tm_codes, bar(bars->full_p[s]), (b0 + it) * (SB_BOX_K / 2), n0);
         bulk_g2s(s_ring + (uint32_t)s * L::kSBytes, args.scales16 + ((int64_t)nb * n_box + b0 + it) * SB_ROWS * spg,
@@ -388,7 +387,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
       for (int it = 0; it < n_ch + n_lr && ok; ++it) {
         const int s = it % TB;
         const uint32_t ph = (uint32_t)(it / TB) & 1u;
-        if (!(ok = mbar_spin_wait(bar(bars->empty_b[s]), ph ^ 1u, abort_flag, args.err, kSbWaitTileEmpty))) break;
+        if (!(ok = wait_spin(bar(bars->empty_b[s]), ph ^ 1u, abort_flag, args.err, kSbWaitTileEmpty))) break;
         const uint32_t fb = bar(bars->full_b[s]);
         const uint32_t bdst = b_ring + (uint32_t)s * L::kTokChunk;
         if (it < n_ch) {
@@ -399,7 +398,7 @@ __global__ void __launch_bounds__(SB_THREADS, 1)
         } else {
           const int j = it - n_ch, ls = j % SB_LS;
           const uint32_t lph = (uint32_t)(j / SB_LS) & 1u;
-          if (!(ok = mbar_spin_wait(bar(bars->empty_l[ls]), lph ^ 1u, abort_flag, args.err, kSbWaitLowrankEmpty)))
+          if (!(ok = wait_spin(bar(bars->empty_l[ls]), lph ^ 1u, abort_flag, args.err, kSbWaitLowrankEmpty)))
             break;
           mbar_arrive_expect_tx(fb, L::kTokSub + SB_LR_BYTES);
           tma_load_2d(l_ring + (uint32_t)ls * SB_LR_BYTES, &tm_up, fb, j * 64, n0);
