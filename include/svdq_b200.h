@@ -80,13 +80,12 @@ int svdq_selftest_bounded_wait(int limit_us, cudaStream_t stream);
 
 /*
  * Device workspace (bytes) the activation passes need for the low-rank
- * down-projection: 64 KiB of row-band arrival counters, then the fp32 partial
- * sums of the K slices.  The last K slice of each row band to finish adds the
- * partials in slice order (deterministic) and writes mid_hl, inside the same
- * launch.  The workspace must be ZERO-FILLED before its first use and 256-byte
- * aligned; every launch leaves the counters zero again, so it is zeroed only
- * once.  One launch at a time per workspace (launches ordered on one stream
- * are fine).  0 when rank + lora_rank == 0 or mid is not requested.
+ * down-projection: the fp32 partial sums of the K slices, which a second
+ * launch of the same call adds in slice order (deterministic) into mid_hl.
+ * 256-byte aligned; needs no clearing (every slice writes all of its partials
+ * before the second launch reads them).  One call at a time per workspace
+ * (calls ordered on one stream are fine).  0 when rank + lora_rank == 0 or mid
+ * is not requested.
  */
 size_t svdq_act_quant_workspace_bytes(int M, int K_pad, int rank, int lora_rank);
 
@@ -146,8 +145,8 @@ int svdq_act_quant_i8(const void* x, int64_t ldx, const void* smooth,
  * warm-up).  The K-slice scratch is a file-scope device array of
  * svdq_act_quant_noalloc_scratch_bytes() (8 MiB) per device; a call needing
  * more (svdq_act_quant_workspace_bytes() > 8 MiB) returns
- * SVDQ_ERR_UNSUPPORTED.  The array starts zero (static storage) and every call
- * leaves its counter words zero, as the workspace contract above requires.  The scratch address is looked up with
+ * SVDQ_ERR_UNSUPPORTED.  The scratch needs no clearing (the workspace contract
+ * above), and each call leaves its partial sums in it.  The scratch address is looked up with
  * cudaGetSymbolAddress on the first call in each CUDA context (the device's
  * primary context or another context the host made current), whatever that
  * call's arguments: if that first call would fall inside a stream capture,

@@ -189,10 +189,6 @@ struct AqArgs {
   float* ascales_t;       // [K_pad/G, lda_s] fp32 scales, group-major, or null
   int64_t lda_s;
   float* partial;         // [ksplit, M, r_tot] or null
-  uint32_t* counters;     // [bands * nz] arrival counters of the K slices (zero between launches)
-  __nv_bfloat16* mid_hl;  // [M, R2]
-  const float* lora_col_scale;
-  int R2, ksplit;
   int* err;
 };
 
@@ -583,79 +579,19 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
 
   pdl_trigger();  // the next kernel may start its prologue (it waits for this grid before reading)
 
-  // ---- low-rank projection: fp32 partial of this K slice; the last slice of a band adds them ----
+  // ---- low-rank projection: fp32 partial of this K slice (a second launch adds the slices) ----
   if constexpr (NT > 0) {
-    if (a.partial) {
-      if (ok) {
-        float* part = a.partial + (int64_t)blockIdx.y * a.M * a.r_tot;
+    if (ok && a.partial) {
+      float* part = a.partial + (int64_t)blockIdx.y * a.M * a.r_tot;
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          if (t < ntl) {
-            const int col = r0 + 8 * t + 2 * t4;
-            if (row_g < a.M)
-              __stcg(reinterpret_cast<float2*>(part + (int64_t)row_g * a.r_tot + col), make_float2(acc[t][0], acc[t][1]));
-            if (row_g8 < a.M)
-              __stcg(reinterpret_cast<float2*>(part + (int64_t)row_g8 * a.r_tot + col), make_float2(acc[t][2], acc[t][3]));
-          }
+      for (int t = 0; t < NT; ++t) {
+        if (t < ntl) {
+          const int col = r0 + 8 * t + 2 * t4;
+          if (row_g < a.M)
+            *reinterpret_cast<float2*>(part + (int64_t)row_g * a.r_tot + col) = make_float2(acc[t][0], acc[t][1]);
+          if (row_g8 < a.M)
+            *reinterpret_cast<float2*>(part + (int64_t)row_g8 * a.r_tot + col) = make_float2(acc[t][2], acc[t][3]);
         }
-      }
-      // every CTA of the band arrives, aborted or not, so the count always completes and resets.
-      // The CTA barrier orders every thread's partial stores before thread 0's release (the
-      // release is cumulative); thread 0's acquire plus the barrier order the last CTA's reads
-      // after every slice's stores.
-      __syncthreads();
-      int* last = issued + STAGES + 1;
-      uint32_t* counter = a.counters + (blockIdx.z * gridDim.x + blockIdx.x);
-      if (tid == 0) {
-        __threadfence();
-        uint32_t old;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
-        *last = old == (uint32_t)(a.ksplit - 1);
-        if (*last) __threadfence();
-      }
-      __syncthreads();
-      if (*last) {
-        // mid_hl of the band's rows and this CTA's columns: the K-slice partials summed in slice
-        // order (deterministic), LoRA columns scaled, split into bf16 hi + lo.  A thread owns four
-        // adjacent columns of one row and issues the loads of up to 16 slices at once.
-        const int c4 = 2 * ntl;  // four-column groups of this CTA
-        const int rows = min(kBM, a.M - m0);
-        const int64_t kstride = (int64_t)a.M * a.r_tot / 4;  // one slice, in float4
-        for (int i = tid; i < rows * c4; i += kThreads) {
-          const int rr = i / c4, j = r0 + 4 * (i - rr * c4);
-          const int64_t row = m0 + rr;
-          const float4* src = reinterpret_cast<const float4*>(a.partial + row * a.r_tot + j);
-          float4 t[16];
-#pragma unroll
-          for (int u = 0; u < 16; ++u)
-            if (u < a.ksplit) t[u] = __ldcg(src + u * kstride);
-          float4 v = t[0];
-#pragma unroll
-          for (int u = 1; u < 16; ++u)
-            if (u < a.ksplit) { v.x += t[u].x; v.y += t[u].y; v.z += t[u].z; v.w += t[u].w; }
-          for (int k = 16; k < a.ksplit; ++k) {
-            const float4 w = __ldcg(src + k * kstride);
-            v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
-          }
-          if (j >= a.rank) {  // LoRA columns (lora_rank is a multiple of 8: all four or none)
-            const float4 cs = *reinterpret_cast<const float4*>(a.lora_col_scale + (j - a.rank));
-            v.x *= cs.x; v.y *= cs.y; v.z *= cs.z; v.w *= cs.w;
-          }
-          const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y), h23 = __floats2bfloat162_rn(v.z, v.w);
-          const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
-          const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
-          const __nv_bfloat162 l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
-          __nv_bfloat16* dst = a.mid_hl + row * a.R2 + j;
-          *reinterpret_cast<uint2*>(dst) = make_uint2(bf162_bits(h01), bf162_bits(h23));
-          *reinterpret_cast<uint2*>(dst + a.r_tot) = make_uint2(bf162_bits(l01), bf162_bits(l23));
-        }
-        if (blockIdx.z == 0) {  // zero padding columns [2 r_tot, R2): a multiple of 16 columns
-          const int pad8 = (a.R2 - 2 * a.r_tot) / 8;
-          for (int i = tid; i < rows * pad8; i += kThreads)
-            *reinterpret_cast<uint4*>(a.mid_hl + (int64_t)(m0 + i / pad8) * a.R2 + 2 * a.r_tot + 8 * (i % pad8)) =
-                make_uint4(0u, 0u, 0u, 0u);
-        }
-        if (tid == 0) *counter = 0u;  // every other CTA of the band has arrived: ready for the next launch
       }
     }
   }
@@ -667,6 +603,54 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
     for (int s = 0; s < STAGES; ++s)
       if (issued[s] > 0 && !mbar_wait_drain(full_bar(s), (uint32_t)((issued[s] - 1) & 1), kWaitLimitNs))
         atomicCAS(a.err, 0, 0x4180 + s);
+  }
+}
+
+// mid_hl[m] = [hi(v) | lo(v) | 0], v = (sum of the K-slice partials, in slice order) * column scale
+// (LoRA columns), hi = bf16(v), lo = bf16(v - hi).  A thread owns four adjacent columns of one row
+// (or eight padding columns) and keeps the loads of all slices in flight.  A separate launch:
+// reducing in the last-arriving CTA of each row band left the work to one CTA per band at the end
+// of the pass, which measured slower (38 -> 50 us at rank 32, 60 -> 103 us at rank 96).
+__global__ void mid_finalize_kernel(const float* __restrict__ partial, int ksplit, int M, int rank, int r_tot,
+                                    const float* __restrict__ lora_col_scale, __nv_bfloat16* __restrict__ mid_hl,
+                                    int R2) {
+  pdl_wait();
+  pdl_trigger();
+  const int c4 = r_tot / 4, p8 = (R2 - 2 * r_tot) / 8;  // value items, padding items per row
+  const int w = c4 + p8;
+  const int64_t total = (int64_t)M * w, kstride = (int64_t)M * r_tot / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / w), e = (int)(i % w);
+    __nv_bfloat16* out = mid_hl + (int64_t)row * R2;
+    if (e < c4) {
+      const int j = 4 * e;
+      const float4* src = reinterpret_cast<const float4*>(partial + (int64_t)row * r_tot + j);
+      float4 v = __ldg(src);
+      int k = 1;
+      for (; k + 4 <= ksplit; k += 4) {
+        float4 t[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) t[u] = __ldg(src + (k + u) * kstride);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) { v.x += t[u].x; v.y += t[u].y; v.z += t[u].z; v.w += t[u].w; }
+      }
+      for (; k < ksplit; ++k) {
+        const float4 t = __ldg(src + k * kstride);
+        v.x += t.x; v.y += t.y; v.z += t.z; v.w += t.w;
+      }
+      if (j >= rank) {  // LoRA columns (lora_rank is a multiple of 8: all four or none)
+        const float4 cs = *reinterpret_cast<const float4*>(lora_col_scale + (j - rank));
+        v.x *= cs.x; v.y *= cs.y; v.z *= cs.z; v.w *= cs.w;
+      }
+      const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y), h23 = __floats2bfloat162_rn(v.z, v.w);
+      const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+      const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
+      const __nv_bfloat162 l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
+      *reinterpret_cast<uint2*>(out + j) = make_uint2(bf162_bits(h01), bf162_bits(h23));
+      *reinterpret_cast<uint2*>(out + r_tot + j) = make_uint2(bf162_bits(l01), bf162_bits(l23));
+    } else {
+      *reinterpret_cast<uint4*>(out + 2 * r_tot + 8 * (e - c4)) = make_uint4(0u, 0u, 0u, 0u);
+    }
   }
 }
 
@@ -741,19 +725,12 @@ Geometry geometry(int M, int K_pad, int r_use, int step) {
   return gm;
 }
 
-// Workspace: kCounterBytes of arrival counters (one per row band and low-rank CTA column; zero
-// between launches), then the fp32 K-slice partials.  Covers both slice steps, so one size serves
-// every group size and mode.
-constexpr size_t kCounterBytes = 64 * 1024;
+// Workspace: the fp32 K-slice partials.  Covers both slice steps, so one size serves every group
+// size and mode.
 size_t workspace_bytes(int M, int K_pad, int r_tot) {
   if (r_tot <= 0 || M <= 0 || K_pad <= 0) return 0;
   const int ksplit = std::max(geometry(M, K_pad, r_tot, 1).ksplit, geometry(M, K_pad, r_tot, 2).ksplit);
-  return kCounterBytes + sizeof(float) * (size_t)ksplit * (size_t)M * (size_t)r_tot;
-}
-// Counters one launch uses (row bands x low-rank CTA columns).
-size_t counters_needed(int M, int K_pad, int r_tot, int step) {
-  const Geometry gm = geometry(M, K_pad, r_tot, step);
-  return (size_t)((M + cta_rows(gm.nt) - 1) / cta_rows(gm.nt)) * gm.nz;
+  return sizeof(float) * (size_t)ksplit * (size_t)M * (size_t)r_tot;
 }
 
 struct LaunchSpec {
@@ -808,7 +785,23 @@ int launch_l(const LaunchSpec& L, cudaStream_t stream) {
 }
 
 int launch(const LaunchSpec& L, cudaStream_t stream) {
-  return L.args.lora_rank > 0 ? launch_l<true>(L, stream) : launch_l<false>(L, stream);
+  const int st = L.args.lora_rank > 0 ? launch_l<true>(L, stream) : launch_l<false>(L, stream);
+  if (st || !L.args.partial) return st;
+  const int64_t items = (int64_t)L.args.M * (L.args.r_tot / 4 + (L.R2 - 2 * L.args.r_tot) / 8);
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, (int64_t)num_sms() * 8));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, mid_finalize_kernel, (const float*)L.args.partial, L.gm.ksplit,
+                                           L.args.M, L.args.rank, L.args.r_tot, L.lora_col_scale, L.mid_hl, L.R2);
+  if (e != cudaSuccess) return check_cuda(e, "activation pass finalize");
+  return check_launch("activation pass finalize");
 }
 int validate_common(const void* x, int64_t ldx, const void* smooth, const void* l2, int rank, const void* lora_down,
                     const float* lora_col_scale, int lora_rank, int M, int K_in, int K_pad, void* out_a16,
@@ -838,8 +831,6 @@ int validate_common(const void* x, int64_t ldx, const void* smooth, const void* 
     if (!workspace || ws_bytes < workspace_bytes(M, K_pad, r_tot))
       return bad("workspace missing or smaller than svdq_act_quant_workspace_bytes()");
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return bad("workspace must be 256-byte aligned");
-    if (std::max(counters_needed(M, K_pad, r_tot, 1), counters_needed(M, K_pad, r_tot, 2)) * 4 > kCounterBytes)
-      return set_error(SVDQ_ERR_UNSUPPORTED, w + ": M too large for the workspace's row-band counters");
   }
   return SVDQ_OK;
 }
@@ -890,12 +881,7 @@ int build_spec(LaunchSpec& L, const void* x, int64_t ldx, const void* smooth, co
   p.codes8 = nullptr;
   p.ascales_t = nullptr;
   p.lda_s = 0;
-  p.partial = want_mid ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes) : nullptr;
-  p.counters = want_mid ? static_cast<uint32_t*>(workspace) : nullptr;
-  p.mid_hl = static_cast<__nv_bfloat16*>(out_mid_hl);
-  p.lora_col_scale = lora_col_scale;
-  p.R2 = R2;
-  p.ksplit = L.gm.ksplit;
+  p.partial = want_mid ? static_cast<float*>(workspace) : nullptr;
   p.err = device_error_word();
   if (!p.err) return set_error(SVDQ_ERR_CUDA, "device error word unavailable");
   L.gs = G / kBK;

@@ -13,11 +13,9 @@
 // stream capture, make one call of any shape before capturing.  The scratch
 // holds kNoAllocScratchBytes; a call that needs more is rejected with
 // SVDQ_ERR_UNSUPPORTED and names the size it needs.
-// The scratch starts zero (static storage).  Its first 64 KiB hold the row-band
-// arrival counters, which must be zero when a call starts: every call leaves them
-// zero again (the last K slice of each band resets its counter).  The partial
-// sums after them need no clearing: every K slice writes all of its partials
-// before the band's last slice reads them.  All calls on one device
+// The scratch holds the K-slice partial sums, which need no clearing: every K
+// slice writes all of its partials before the call's second launch reads them,
+// and each call leaves its own partials behind.  All calls on one device
 // share the one scratch array, so calls that overlap in time (on different
 // streams, or from different host threads) race on it and must be serialized
 // by the caller.

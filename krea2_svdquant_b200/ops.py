@@ -64,11 +64,11 @@ _act_ws_lock = threading.Lock()
 
 
 def _workspace(m: int, k_pad: int, rank: int, lrank: int, dev: torch.device) -> Tensor:
-    """The activation pass's workspace: row-band arrival counters, zero between launches (each launch
-    leaves them zero), then the fp32 K-slice partials.  One per (device, stream), kept and grown
-    (zero-filled) as larger calls need; launches on one stream run in order, so they share it.
-    Inside a CUDA graph capture a fresh zero-filled workspace is made (its zero fill is captured
-    too), so a graph never holds the address of a cached workspace that may be freed later."""
+    """The activation pass's workspace: the fp32 K-slice partials of the low-rank products, which
+    every launch writes in full before its finalize launch adds them (no clearing between calls).
+    One per (device, stream), kept and grown as larger calls need; launches on one stream run in
+    order, so they share it.  Inside a CUDA graph capture a fresh workspace is made, so a graph
+    never holds the address of a cached workspace that may be freed later."""
     n = int(_lib.lib().svdq_act_quant_workspace_bytes(m, k_pad, rank, lrank))
     if torch.cuda.is_current_stream_capturing():
         return torch.zeros((max(n, 0),), dtype=torch.uint8, device=dev)
