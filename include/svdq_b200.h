@@ -53,6 +53,14 @@ enum svdq_status {
 
 enum svdq_dtype { SVDQ_BF16 = 0, SVDQ_FP16 = 1, SVDQ_FP32 = 2 };
 
+/* Epilogue operations of svdq_linear_gemm_epi: y = the linear's output, z = the operand. */
+enum svdq_epilogue {
+  SVDQ_EPI_NONE = 0,
+  SVDQ_EPI_ADD = 1,          /* z + y            residual add                        */
+  SVDQ_EPI_SIGMOID_MUL = 2,  /* z * sigmoid(y)   output gated by this linear         */
+  SVDQ_EPI_SILU_MUL = 3      /* silu(z) * y      gated MLP, z the gate linear's output */
+};
+
 /* One-line description of the last failure on this host thread. */
 const char* svdq_last_error(void);
 /* Library version string ("svdq_b200 <major>.<minor>"). */
@@ -240,6 +248,29 @@ int svdq_linear_gemm_ws(const void* a16, const void* w16,
                         int M, int N, int K_pad,
                         void* workspace, size_t workspace_bytes,
                         cudaStream_t stream);
+
+/*
+ * svdq_linear_gemm_ws whose epilogue also applies one elementwise operation
+ * with an operand z [M, N] (out_dtype, row stride ld_aux): z + y, z * sigmoid(y)
+ * or silu(z) * y, y being the linear's output (enum svdq_epilogue).  With bf16
+ * output, y and the activation are rounded to bf16 before the combining
+ * operation, so the result equals the unfused sequence of bf16 tensor ops
+ * (linear, then sigmoid / silu, then the product or sum).  Replaces the glue
+ * that follows the linears of a transformer block (the gate products and the
+ * residual adds around runtime/linear.py:148-161's forward), saving one
+ * round trip of y through HBM per operation.
+ *   aux: 16-byte aligned, ld_aux >= N, ld_aux % 8 == 0; it may be out itself
+ *   (with ld_aux == ldo): every element is read before the same thread writes
+ *   it.  SVDQ_EPI_NONE ignores aux.  Other arguments as svdq_linear_gemm_ws.
+ */
+int svdq_linear_gemm_epi(const void* a16, const void* w16,
+                         const void* mid_hl, const void* up_hl, int R2,
+                         const void* bias,
+                         int epilogue, const void* aux, int64_t ld_aux,
+                         void* out, int out_dtype, int64_t ldo,
+                         int M, int N, int K_pad,
+                         void* workspace, size_t workspace_bytes,
+                         cudaStream_t stream);
 
 /*
  * The launch plan of svdq_linear_gemm (with_workspace == 0) or

@@ -55,6 +55,9 @@ SIGNATURES = {
     "svdq_linear_gemm_workspace_bytes": ([], ctypes.c_size_t),
     "svdq_linear_gemm_ws": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
                              c_int64, c_int, c_int, c_int, c_void_p, ctypes.c_size_t, c_void_p], c_int),
+    "svdq_linear_gemm_epi": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int64,
+                              c_void_p, c_int, c_int64, c_int, c_int, c_int, c_void_p, ctypes.c_size_t, c_void_p],
+                             c_int),
     "svdq_linear_gemm_schedule": ([c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)], c_int),
     "svdq_linear_gemm_plan": ([c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)], c_int),
     "svdq_prepare_packed": ([c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
@@ -67,6 +70,7 @@ SIGNATURES = {
 }
 
 SVDQ_BF16, SVDQ_FP16, SVDQ_FP32 = 0, 1, 2
+SVDQ_EPI_NONE, SVDQ_EPI_ADD, SVDQ_EPI_SIGMOID_MUL, SVDQ_EPI_SILU_MUL = 0, 1, 2, 3
 STATUS_NAMES = {0: "SVDQ_OK", 1: "SVDQ_ERR_INVALID_ARGUMENT", 2: "SVDQ_ERR_UNSUPPORTED",
                 3: "SVDQ_ERR_CUDA", 4: "SVDQ_ERR_TIMEOUT", 5: "SVDQ_ERR_DEVICE_WAIT"}
 

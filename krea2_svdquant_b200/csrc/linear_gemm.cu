@@ -25,7 +25,8 @@
 //   warp 1      TMEM allocator (both CTAs) and, in the even CTA, MMA issuer
 //               (kind::f16: fp16 for the residual, bf16 for the low-rank term).
 //   warps 4-11  epilogue (both CTAs): two warpgroups, 128 columns each; TMEM ->
-//               registers -> + bias -> bf16/fp32 -> global.
+//               registers -> + bias -> [op with an operand z: z + y, z * sigmoid(y),
+//               silu(z) * y] -> bf16/fp32 -> global.
 // Every mbarrier wait is bounded; a wait that runs out sets a CTA abort flag and
 // the library's device error word, and all roles leave their loops, so both
 // CTAs always reach the closing cluster barrier.
@@ -81,6 +82,9 @@ struct GemmArgs {
   const __nv_bfloat16* bias;
   void* out;
   int64_t ldo;
+  const void* aux;  // epilogue operand z [M, N] in out's dtype (row stride ld_aux), or null
+  int64_t ld_aux;
+  int epi;          // kEpi*: what the epilogue does with y = acc + bias and z
   int M, N;
   int n_k;   // K_pad / 64 residual stages
   int n_lr;  // R2 / 64 low-rank stages
@@ -115,6 +119,38 @@ enum : int {
 };
 
 constexpr uint32_t kFmtF16 = 0;  // kind::f16 format code for fp16
+
+// Epilogue operations: the linear's output y (accumulator + bias) combined with an operand z of
+// the output's shape and dtype, in the order of the elementwise torch ops they replace.  With bf16
+// output every value torch would store (y, the activation) is rounded to bf16 first, so the result
+// is the unfused sequence's.
+enum : int {
+  kEpiNone = 0,
+  kEpiAdd = 1,         // z + y                  (residual add)
+  kEpiSigmoidMul = 2,  // z * sigmoid(y)         (attention output gated by to_gate)
+  kEpiSiluMul = 3,     // silu(z) * y            (gated MLP: z = ff.gate output, y = ff.up)
+};
+
+__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+template <bool F32>
+__device__ __forceinline__ void epi_apply(int op, float (&v)[8], const float (&z)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float y = F32 ? v[e] : bf16r(v[e]);
+    float r;
+    if (op == kEpiAdd) {
+      r = z[e] + y;
+    } else if (op == kEpiSigmoidMul) {
+      const float sg = 1.0f / (1.0f + expf(-y));
+      r = z[e] * (F32 ? sg : bf16r(sg));
+    } else {
+      const float sl = z[e] / (1.0f + expf(-z[e]));
+      r = (F32 ? sl : bf16r(sl)) * y;
+    }
+    v[e] = r;
+  }
+}
 
 __device__ __forceinline__ void advance(int& idx, uint32_t& phase, int n) {
   if (++idx == n) {
@@ -212,6 +248,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     linear_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
                        const __grid_constant__ CUtensorMap tm_mid, const __grid_constant__ CUtensorMap tm_up,
                        const GemmArgs args) {
+  constexpr int kOutBytes = OUT_F32 ? 4 : 2;
+  constexpr int kAuxWords = 32 * kOutBytes / 16;  // 16-byte words of z per 32-column chunk
+  constexpr int kAuxBufs = OUT_F32 ? 1 : 2;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
@@ -375,6 +414,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint4 bias_lane = make_uint4(0u, 0u, 0u, 0u);
       if (args.bias && !contrib && lane < 16 && n0 + col0 + 8 * lane < args.N)
         bias_lane = *reinterpret_cast<const uint4*>(args.bias + n0 + col0 + 8 * lane);
+      // epilogue operand: the lane's row, 32 columns per chunk; bf16 one chunk ahead (the first
+      // one before the accumulator wait), fp32 (twice the registers) at the chunk's start;
+      // streamed with an evict-first hint, it is read once
+      const int grow = m0 + row;
+      const bool use_aux = args.epi != kEpiNone && !contrib;
+      const uint8_t* aux_row = static_cast<const uint8_t*>(args.aux) + (size_t)grow * args.ld_aux * kOutBytes;
+      uint4 ax[kAuxBufs][kAuxWords];
+      auto load_aux = [&](int c, uint4 (&d)[kAuxWords]) {
+#pragma unroll
+        for (int i = 0; i < kAuxWords; ++i) {
+          const int n = n0 + col0 + c * 32 + i * (16 / kOutBytes);
+          d[i] = (grow < args.M && n < args.N) ? __ldcs(reinterpret_cast<const uint4*>(aux_row + (size_t)n * kOutBytes))
+                                               : make_uint4(0u, 0u, 0u, 0u);
+        }
+      };
+      if (use_aux && kAuxBufs == 2) load_aux(0, ax[0]);
       if (!(ok = mbar_wait<true>(tm_full(tb), tb_ph, abort_flag, args.err, kWaitEpiTmemFull))) break;
       tc_fence_after();
       if (n_parts > 0) {
@@ -418,7 +473,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (n_parts > 0)
         for (int g = 0; g < kPartSlots; ++g) issue_group(g);
       const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + col0);
-      const int grow = m0 + row;
       const int64_t rbase = (int64_t)grow * args.ldo;
       uint32_t va[32], vb[32];
       tmem_ld32(taddr, va);
@@ -426,6 +480,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int c = 0; c < EPI_COLS / 32; ++c) {
         uint32_t (&cur)[32] = (c & 1) ? vb : va;
         uint32_t (&nxt)[32] = (c & 1) ? va : vb;
+        if (use_aux && kAuxBufs == 1) load_aux(c, ax[0]);
         tmem_ld_wait_regs(cur);
         if (c + 1 < EPI_COLS / 32) {
           tmem_ld32(taddr + (uint32_t)((c + 1) * 32), nxt);
@@ -435,6 +490,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(mapa_shared(tm_empty(tb), 0));
         }
+        if (use_aux && kAuxBufs == 2 && c + 1 < EPI_COLS / 32) load_aux(c + 1, ax[(c + 1) % kAuxBufs]);
         const int cc = col0 + c * 32;  // tile column of cur[0]
         if (contrib) {
           float4* slot = reinterpret_cast<float4*>(args.partial + (size_t)(2 * pair + (int)rank) * kPartialFloats);
@@ -484,6 +540,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   v[2 * e] += f.x;
                   v[2 * e + 1] += f.y;
                 }
+              }
+              if (use_aux) {
+                float z[8];
+                if constexpr (OUT_F32) {
+                  const uint4 z0 = ax[c % kAuxBufs][2 * (i / 8)], z1 = ax[c % kAuxBufs][2 * (i / 8) + 1];
+                  z[0] = __uint_as_float(z0.x), z[1] = __uint_as_float(z0.y);
+                  z[2] = __uint_as_float(z0.z), z[3] = __uint_as_float(z0.w);
+                  z[4] = __uint_as_float(z1.x), z[5] = __uint_as_float(z1.y);
+                  z[6] = __uint_as_float(z1.z), z[7] = __uint_as_float(z1.w);
+                } else {
+                  const uint4 zw = ax[c % kAuxBufs][i / 8];
+                  const uint32_t zz[4] = {zw.x, zw.y, zw.z, zw.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zz[e]));
+                    z[2 * e] = f.x;
+                    z[2 * e + 1] = f.y;
+                  }
+                }
+                epi_apply<OUT_F32>(args.epi, v, z);
               }
               if constexpr (OUT_F32) {
                 float4* o = reinterpret_cast<float4*>(static_cast<float*>(args.out) + rbase + n);
@@ -608,8 +684,9 @@ Schedule plan_schedule(int tiles, int iters, int max_pairs, bool can_split) {
 }
 
 int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, const void* up_hl, int R2,
-                       const void* bias, void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
-                       void* workspace, size_t workspace_bytes, cudaStream_t stream, const char* who) {
+                       const void* bias, int epilogue, const void* aux, int64_t ld_aux, void* out, int out_dtype,
+                       int64_t ldo, int M, int N, int K_pad, void* workspace, size_t workspace_bytes,
+                       cudaStream_t stream, const char* who) {
   const std::string w(who);
   if (!(a16 && w16 && out)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": null operand pointer");
   if (!(M >= 0 && N > 0 && K_pad > 0)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": bad M/N/K_pad");
@@ -624,6 +701,12 @@ int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, con
     return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": bias must be 16-byte aligned");
   if (reinterpret_cast<uintptr_t>(out) & 15u)
     return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": out must be 16-byte aligned");
+  if (!(epilogue >= kEpiNone && epilogue <= kEpiSiluMul))
+    return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": unknown epilogue operation");
+  if (epilogue != kEpiNone &&
+      !(aux && (reinterpret_cast<uintptr_t>(aux) & 15u) == 0 && ld_aux >= N && ld_aux % 8 == 0))
+    return set_error(SVDQ_ERR_INVALID_ARGUMENT,
+                     w + ": the epilogue operand must be non-null and 16-byte aligned, ld_aux >= N, ld_aux % 8 == 0");
   if (M == 0) return SVDQ_OK;
   int* err = device_error_word();
   if (!err) return set_error(SVDQ_ERR_CUDA, w + ": device error word unavailable");
@@ -652,6 +735,9 @@ int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, con
   a.bias = static_cast<const __nv_bfloat16*>(bias);
   a.out = out;
   a.ldo = ldo;
+  a.aux = epilogue != kEpiNone ? aux : nullptr;
+  a.ld_aux = epilogue != kEpiNone ? ld_aux : 0;
+  a.epi = epilogue;
   a.M = M;
   a.N = N;
   a.n_k = K_pad / 64;
@@ -699,8 +785,8 @@ int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, con
 extern "C" int svdq_linear_gemm(const void* a16, const void* w16, const void* mid_hl, const void* up_hl, int R2,
                                 const void* bias, void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
                                 cudaStream_t stream) {
-  return svdq::launch_linear_gemm(a16, w16, mid_hl, up_hl, R2, bias, out, out_dtype, ldo, M, N, K_pad, nullptr, 0,
-                                  stream, "svdq_linear_gemm");
+  return svdq::launch_linear_gemm(a16, w16, mid_hl, up_hl, R2, bias, svdq::kEpiNone, nullptr, 0, out, out_dtype, ldo,
+                                  M, N, K_pad, nullptr, 0, stream, "svdq_linear_gemm");
 }
 
 extern "C" size_t svdq_linear_gemm_workspace_bytes(void) { return svdq::workspace_bytes_for(svdq::num_sms() / 2); }
@@ -713,8 +799,21 @@ extern "C" int svdq_linear_gemm_ws(const void* a16, const void* w16, const void*
   if (workspace && workspace_bytes < svdq::workspace_bytes_for(svdq::num_sms() / 2))
     return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT,
                            "svdq_linear_gemm_ws: workspace smaller than svdq_linear_gemm_workspace_bytes()");
-  return svdq::launch_linear_gemm(a16, w16, mid_hl, up_hl, R2, bias, out, out_dtype, ldo, M, N, K_pad, workspace,
-                                  workspace_bytes, stream, "svdq_linear_gemm_ws");
+  return svdq::launch_linear_gemm(a16, w16, mid_hl, up_hl, R2, bias, svdq::kEpiNone, nullptr, 0, out, out_dtype, ldo,
+                                  M, N, K_pad, workspace, workspace_bytes, stream, "svdq_linear_gemm_ws");
+}
+
+extern "C" int svdq_linear_gemm_epi(const void* a16, const void* w16, const void* mid_hl, const void* up_hl, int R2,
+                                    const void* bias, int epilogue, const void* aux, int64_t ld_aux, void* out,
+                                    int out_dtype, int64_t ldo, int M, int N, int K_pad, void* workspace,
+                                    size_t workspace_bytes, cudaStream_t stream) {
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_linear_gemm_epi: workspace must be 256-byte aligned");
+  if (workspace && workspace_bytes < svdq::workspace_bytes_for(svdq::num_sms() / 2))
+    return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT,
+                           "svdq_linear_gemm_epi: workspace smaller than svdq_linear_gemm_workspace_bytes()");
+  return svdq::launch_linear_gemm(a16, w16, mid_hl, up_hl, R2, bias, epilogue, aux, ld_aux, out, out_dtype, ldo, M, N,
+                                  K_pad, workspace, workspace_bytes, stream, "svdq_linear_gemm_epi");
 }
 
 extern "C" int svdq_linear_gemm_plan(int tiles, int iters, int max_pairs, int with_workspace, int* out4) {

@@ -243,7 +243,8 @@ class SVDQuantLinear(nn.Module):
         return self._prepared
 
     # ------------------------------------------------------------------ forward
-    def _run(self, x: torch.Tensor, include_lora: bool) -> torch.Tensor:
+    def _run(self, x: torch.Tensor, include_lora: bool,
+             epilogue: tuple[str, torch.Tensor] | None = None) -> torch.Tensor:
         if not x.is_cuda:
             raise ValueError("SVDQuantLinear (b200) needs CUDA activations; this runtime has no CPU path")
         if x.dtype not in (torch.bfloat16, torch.float32):
@@ -273,18 +274,39 @@ class SVDQuantLinear(nn.Module):
                               *lowrank, p.bias, out_fp32)
             if self.check_device_errors:
                 _lib.raise_on_device_error(f"SVDQuantLinear {tuple(self.original_shape)}")
-            return y.reshape(*lead, n)
+            return ops.apply_epilogue(y.reshape(*lead, n), epilogue)
         else:
             a16, mid, _, _ = ops.act_quant(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
                                            self.act_group_size, True, False)
         lowrank = (mid, up_hl) if mid.numel() else (None, None)
-        if p.w16 is None:
+        z = self._fusable_operand(epilogue, x2.shape[0], out_fp32) if p.w16 is not None else None
+        if z is not None:
+            # the combining op runs in the GEMM's epilogue: y never makes a round trip through HBM
+            y = ops.linear_gemm_epi(a16, p.w16, *lowrank, p.bias, out_fp32, ops.EPILOGUES[epilogue[0]], z)
+            epilogue = None
+        elif p.w16 is None:
             y = ops.packed_gemm(a16, p.codes, p.scales16, self.group_size, *lowrank, p.bias, out_fp32)
         else:
             y = ops.linear_gemm(a16, p.w16, *lowrank, p.bias, out_fp32)
         if self.check_device_errors:
             _lib.raise_on_device_error(f"SVDQuantLinear {tuple(self.original_shape)}")
-        return y.reshape(*lead, n)
+        return ops.apply_epilogue(y.reshape(*lead, n), epilogue)
+
+    def _fusable_operand(self, epilogue, m: int, out_fp32: bool) -> torch.Tensor | None:
+        """The epilogue operand as the fused GEMM epilogue takes it ([M, N] rows, output dtype,
+        16-byte aligned rows), or None when the operation has to run unfused."""
+        if epilogue is None:
+            return None
+        op, z = epilogue
+        n = self.original_shape[0]
+        if op not in ops.EPILOGUES or not z.is_cuda or z.numel() != m * n:
+            return None
+        if z.dtype != (torch.float32 if out_fp32 else torch.bfloat16):
+            return None
+        z2 = z.reshape(m, n)
+        if z2.stride(1) != 1 or z2.stride(0) % 8 or z2.data_ptr() % 16:
+            return None
+        return z2
 
     # Batches up to this many tokens take the int8-code GEMM when the weight is packed (W4A4).
     INT8_PATH_MAX_TOKENS = 64
@@ -297,15 +319,21 @@ class SVDQuantLinear(nn.Module):
         """SVDQuant base term (residual + low-rank + bias), without LoRA branches."""
         return self._run(x, include_lora=False)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, epilogue: tuple[str, torch.Tensor] | None = None) -> torch.Tensor:
+        """``y = SVDQuant(x)`` (runtime/linear.py:148-161).  ``epilogue=(op, z)`` also combines y with
+        a tensor z of y's shape: ``"add"`` gives ``z + y``, ``"sigmoid_mul"`` ``z * sigmoid(y)``,
+        ``"silu_mul"`` ``silu(z) * y`` (the glue after a block's linears).  On the fp16-weight
+        GEMM the operation runs in its epilogue; its result equals the unfused torch ops'."""
         if "_forward_base" in self.__dict__:
             # an instance-level override of the base (as the reference's LoRA test does,
             # test_lora_loading.py:60): keep the reference's composition base + adapters
             y = self._forward_base(x)
             for adapter in self.lora_adapters:
                 y = y + adapter(x)
-            return y
-        return self._run(x, include_lora=True)
+            return ops.apply_epilogue(y, epilogue)
+        if epilogue is not None and epilogue[0] not in ops.EPILOGUES:
+            raise ValueError(f"unknown epilogue operation {epilogue[0]!r}; expected one of {sorted(ops.EPILOGUES)}")
+        return self._run(x, include_lora=True, epilogue=epilogue)
 
     def release_prepared(self) -> None:
         """Drop the derived device operands (they are rebuilt on the next forward)."""

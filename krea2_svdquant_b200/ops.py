@@ -313,6 +313,56 @@ def _(a16, w16, mid_hl, up_hl, bias, out_fp32):
     return a16.new_empty((a16.shape[0], w16.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
 
 
+EPILOGUES = {"add": _lib.SVDQ_EPI_ADD, "sigmoid_mul": _lib.SVDQ_EPI_SIGMOID_MUL, "silu_mul": _lib.SVDQ_EPI_SILU_MUL}
+
+
+@torch.library.custom_op("svdq_b200::linear_gemm_epi", mutates_args=())
+def linear_gemm_epi(a16: Tensor, w16: Tensor, mid_hl: Optional[Tensor], up_hl: Optional[Tensor],
+                    bias: Optional[Tensor], out_fp32: bool, epilogue: int, aux: Tensor) -> Tensor:
+    """``linear_gemm`` whose epilogue combines its output y with ``aux`` (z, [M, N] in the output
+    dtype): ``z + y``, ``z * sigmoid(y)`` or ``silu(z) * y`` (``EPILOGUES``)."""
+    _need_cuda("linear_gemm_epi", a16, w16, mid_hl, up_hl, bias, aux)
+    _need(a16.dtype == torch.float16 and w16.dtype == torch.float16, "linear_gemm_epi: a16/w16 must be fp16")
+    m, k_pad = a16.shape
+    n = w16.shape[0]
+    _need(w16.shape[1] == k_pad, "linear_gemm_epi: activation / weight K mismatch")
+    r2 = 0 if mid_hl is None or mid_hl.numel() == 0 else mid_hl.shape[1]
+    _need(r2 == 0 or (up_hl is not None and tuple(up_hl.shape) == (n, r2)), "linear_gemm_epi: up_hl shape mismatch")
+    out_dtype = torch.float32 if out_fp32 else torch.bfloat16
+    _need(aux.dtype == out_dtype and aux.dim() == 2 and tuple(aux.shape) == (m, n) and aux.stride(1) == 1,
+          "linear_gemm_epi: aux must be [M, N] in the output dtype with unit column stride")
+    out = torch.empty((m, n), dtype=out_dtype, device=a16.device)
+    if m == 0:
+        return out
+    ws = _gemm_workspace(a16.device)
+    _lib.call("svdq_linear_gemm_epi", _p(a16), _p(w16), _p(mid_hl) if r2 else None, _p(up_hl) if r2 else None, r2,
+              _p(bias), int(epilogue), _p(aux), aux.stride(0), _p(out),
+              _lib.SVDQ_FP32 if out_fp32 else _lib.SVDQ_BF16, out.stride(0), m, n, k_pad,
+              _p(ws), 0 if ws is None else ws.numel(), _stream(a16.device))
+    return out
+
+
+@linear_gemm_epi.register_fake
+def _(a16, w16, mid_hl, up_hl, bias, out_fp32, epilogue, aux):
+    return a16.new_empty((a16.shape[0], w16.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
+
+
+def apply_epilogue(y: Tensor, epilogue: Optional[tuple[str, Tensor]]) -> Tensor:
+    """The unfused form of an epilogue operation, as torch ops on the linear's output ``y``: the
+    sequence the fused GEMM epilogue reproduces."""
+    if epilogue is None:
+        return y
+    op, z = epilogue
+    z = z.reshape(y.shape)
+    if op == "add":
+        return z + y
+    if op == "sigmoid_mul":
+        return z * torch.sigmoid(y)
+    if op == "silu_mul":
+        return torch.nn.functional.silu(z) * y
+    raise ValueError(f"unknown epilogue operation {op!r}; expected one of {sorted(EPILOGUES)}")
+
+
 # --------------------------------------------------------------------------- packed-weight GEMM
 @torch.library.custom_op("svdq_b200::prepare_packed", mutates_args=())
 def prepare_packed(qweight: Tensor, scales: Tensor, w_group: int) -> tuple[Tensor, Tensor, Tensor]:

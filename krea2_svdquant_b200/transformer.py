@@ -11,7 +11,9 @@
   stand-in: pre-RMSNorm, grouped-query attention (48 query heads, 12 KV heads,
   head dim 128) through ``scaled_dot_product_attention``, a sigmoid gate from
   ``attn.to_gate`` on the attention output, ``attn.to_out.0``, pre-RMSNorm
-  gated MLP ``ff.down(silu(ff.gate(h)) * ff.up(h))``, residual adds.  Timestep
+  gated MLP ``ff.down(silu(ff.gate(h)) * ff.up(h))``, residual adds.  The gate
+  products and the residual adds run in the epilogues of the GEMMs whose
+  outputs they consume (``SVDQuantLinear.forward(x, epilogue=...)``).  Timestep
   modulation and RoPE are left out; every quantized linear has the exact
   shape and module path of the real model (``transformer_blocks.{i}.attn.to_q``
   ...), so the checkpoint, LoRA and offload paths address it unchanged.
@@ -29,6 +31,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from . import ops
 from .config import BackendKind
 from .linear import SVDQuantLinear
 from .load import CONFIG_NAME, TENSORS_NAME, load_svdquant_transformer
@@ -120,14 +123,16 @@ class _Attention(nn.Module):
         self.to_gate = lin("attn.to_gate")
         self.to_out = nn.ModuleList([lin("attn.to_out.0")])
 
-    def forward(self, h: torch.Tensor, b: int, l: int) -> torch.Tensor:
+    def forward(self, h: torch.Tensor, b: int, l: int, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """``to_out(o * sigmoid(to_gate(h)))``, plus ``residual`` when given."""
         c = self.cfg
         q = self.to_q(h).view(b, l, c.heads, c.head_dim).transpose(1, 2)
         k = self.to_k(h).view(b, l, c.kv_heads, c.head_dim).transpose(1, 2)
         v = self.to_v(h).view(b, l, c.kv_heads, c.head_dim).transpose(1, 2)
         o = F.scaled_dot_product_attention(q, k, v, enable_gqa=True)
         o = o.transpose(1, 2).reshape(b * l, c.heads * c.head_dim)
-        return self.to_out[0](o * torch.sigmoid(self.to_gate(h)))
+        gated = _linear(self.to_gate, h, ("sigmoid_mul", o))
+        return _linear(self.to_out[0], gated, None if residual is None else ("add", residual))
 
 
 class _FeedForward(nn.Module):
@@ -137,8 +142,20 @@ class _FeedForward(nn.Module):
         self.up = lin("ff.up")
         self.down = lin("ff.down")
 
-    def forward(self, h: torch.Tensor) -> torch.Tensor:
-        return self.down(F.silu(self.gate(h)) * self.up(h))
+    def forward(self, h: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """``down(silu(gate(h)) * up(h))``, plus ``residual`` when given."""
+        prod = _linear(self.up, h, ("silu_mul", self.gate(h)))
+        return _linear(self.down, prod, None if residual is None else ("add", residual))
+
+
+def _linear(lin: nn.Module, x: torch.Tensor, epilogue: tuple[str, torch.Tensor] | None) -> torch.Tensor:
+    """``lin(x)`` followed by an elementwise operation with a second tensor (``ops.apply_epilogue``):
+    inside the GEMM's epilogue for SVDQuant layers, as separate torch ops for any other module."""
+    if epilogue is None:
+        return lin(x)
+    if isinstance(lin, SVDQuantLinear):
+        return lin(x, epilogue=epilogue)
+    return ops.apply_epilogue(lin(x), epilogue)
 
 
 class Krea2StandInBlock(nn.Module):
@@ -150,9 +167,11 @@ class Krea2StandInBlock(nn.Module):
         self.ff = _FeedForward(lin)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        # x + attn(norm1(x)), then x + ff(norm2(x)); the residual adds (and the gate products
+        # inside attn and ff) run in the epilogues of the linears that produce their operands
         b, l, d = x.shape
-        x = x + self.attn(self.norm1(x).reshape(b * l, d), b, l).view(b, l, d)
-        return x + self.ff(self.norm2(x).reshape(b * l, d)).view(b, l, d)
+        x = self.attn(self.norm1(x).reshape(b * l, d), b, l, residual=x.reshape(b * l, d)).view(b, l, d)
+        return self.ff(self.norm2(x).reshape(b * l, d), residual=x.reshape(b * l, d)).view(b, l, d)
 
 
 class Krea2StandInTransformer(nn.Module):

@@ -132,24 +132,33 @@ def test_fp32_blocks_vs_staged_oracle(backend):
 
 
 def test_forward_linears_in_situ():
+    """Every linear of the bf16 model against the staged oracle on the input it received.  Four of
+    the eight per block fuse the following glue into their GEMM epilogue (gate products, residual
+    adds); for those the oracle's bf16 output goes through the same glue as torch ops."""
+    from krea2_svdquant_b200 import ops
     from krea2_svdquant_b200.linear import SVDQuantLinear
     cfg, model = _small_model()
     seen = []
 
-    def hook(mod, args, out):
-        seen.append((mod, args[0].detach().clone(), out.detach().clone()))
+    def hook(mod, args, kwargs, out):
+        epi = kwargs.get("epilogue")
+        epi = None if epi is None else (epi[0], epi[1].detach().clone())
+        seen.append((mod, args[0].detach().clone(), out.detach().clone(), epi))
 
-    hs = [m.register_forward_hook(hook) for m in model.modules() if isinstance(m, SVDQuantLinear)]
+    hs = [m.register_forward_hook(hook, with_kwargs=True) for m in model.modules() if isinstance(m, SVDQuantLinear)]
     with torch.no_grad():
         model(*_inputs(cfg))
     torch.cuda.synchronize()
     for h in hs:
         h.remove()
     assert len(seen) == 16
-    for mod, x, y in seen:
+    assert sum(epi is not None for *_, epi in seen) == 8
+    for mod, x, y, epi in seen:
         ref, _ = staged_oracle(x.float().cpu().numpy(), state_numpy(mod.state))
-        err = O.rel_fro(y.float().cpu().numpy(), O.bf16_round(ref.astype(np.float32)))
-        assert err <= TOL_LINEAR_BF16, err
+        want = torch.from_numpy(ref.astype(np.float32)).to(y.device).to(y.dtype).reshape(y.shape)
+        want = ops.apply_epilogue(want, epi)
+        err = O.rel_fro(y.float().cpu().numpy(), want.float().cpu().numpy())
+        assert err <= TOL_LINEAR_BF16, (epi and epi[0], err)
 
 
 def test_forward_matches_oracle_linear_model():
