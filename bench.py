@@ -417,7 +417,8 @@ def measure_small_batch(dev, flush, iters: int) -> dict:
             lambda: ops.linear_gemm(a16, p.w16, mid, p.up_hl, p.bias, False), iters, flush)), m * K * 2, N * K * 2)
         t_lin = statistics.median(_device_times(lambda: mod_pk(x), iters, flush))
         row.update({"linear_packed_us": round(t_lin * 1e3, 2), "linear_packed_tops": round(flops / (t_lin * 1e-3) / 1e12, 1),
-                    "linear_packed_path": "int8 codes + kind::i8 GEMM" if m <= 64 else "a16 + packed fp16-operand GEMM"})
+                    "linear_packed_path": ("int8 codes + kind::i8 GEMM" if m <= SVDQuantLinear.INT8_PATH_MAX_TOKENS
+                                           else "a16 + packed fp16-operand GEMM")})
         out[f"M{m}"] = row
     return {"config": "K6144 N16384 rank 32 group 64 bias, W4A4, small batches (BASELINE config 4's HBM regime)",
             "hbm_peak_gbs": hbm / 1e9, "per_batch": out,

@@ -27,8 +27,9 @@
 // fp16 integers in registers and store them with tcgen05.st into a ring of weight stages
 // (128 bytes of K per row each: 64 k of fp16 or 128 k of int8).  Token tiles arrive by TMA in the
 // same 128-byte-row geometry.  Each K group's MMAs accumulate into their own tensor-memory
-// partial buffer (a ring of four to eight); the rescale warps (one per lane quarter, thread =
-// weight row) load it, release it and fold it into TN fp32 accumulators.
+// partial buffer; a chunk's buffers form a set, and up to three sets are in flight.  The rescale
+// warps (two per lane quarter, thread = weight row, each half of the tokens) load a set, release
+// it and fold it into fp32 accumulators.
 //
 // The low-rank term runs as extra groups at the end of the CTA's K range with scale 1: up_hl
 // rows (A, shared memory) times mid_hl tokens (B), kind::f16 with bf16 operands.

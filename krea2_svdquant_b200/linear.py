@@ -309,7 +309,10 @@ class SVDQuantLinear(nn.Module):
         return z2
 
     # Batches up to this many tokens take the int8-code GEMM when the weight is packed (W4A4).
-    INT8_PATH_MAX_TOKENS = 64
+    # Measured on B200 at K6144 N16384 (GEMM only, L2 flushed): int8 codes 33.8 / 34.6 / 41.4 us
+    # at 1 / 16 / 32 tokens against 39.2 / 40.0 / 41.0 us for the packed fp16-operand GEMM; at 48
+    # and 64 tokens the fp16-operand GEMM is faster (49.3 against 55.5 us).
+    INT8_PATH_MAX_TOKENS = 32
 
     def _int8_path(self, m: int, p: PreparedOperands) -> bool:
         return (0 < m <= self.INT8_PATH_MAX_TOKENS and p.k_pad % 128 == 0 and self.group_size in (64, 128, 256)
