@@ -300,6 +300,30 @@ def _device_times(fn, iters: int, flush, warmup: int = 2) -> list[float]:
     return out
 
 
+def _device_times_ab(fns, iters: int, flush, warmup: int = 2) -> list[list[float]]:
+    """Per-call device times (ms) of several variants, alternated call by call (the order rotating
+    each round) so that clock and power-state drift hits every variant alike; L2 flushed before
+    each call."""
+    import torch
+    for _ in range(warmup):
+        for fn in fns:
+            flush()
+            fn()
+    torch.cuda.synchronize()
+    out = [[] for _ in fns]
+    for it in range(iters):
+        for j in range(len(fns)):
+            i = (j + it) % len(fns)
+            flush()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fns[i]()
+            b.record()
+            b.synchronize()
+            out[i].append(a.elapsed_time(b))
+    return out
+
+
 def _gemm_waves(m: int, n: int, k_pad: int, r2: int) -> dict:
     """Wave efficiency of the GEMM's 256x256 pair tiles and whether its last wave is split."""
     import ctypes
@@ -317,19 +341,27 @@ def _gemm_waves(m: int, n: int, k_pad: int, r2: int) -> dict:
 
 def measure_block_linears(dev, flush, iters: int) -> dict:
     """the 8 quantized linears of one Krea2 block at M=4352 (4096 image +
-    256 text tokens), rank 32, group 64, W4A4; time = sum of the 8 module forwards."""
+    256 text tokens), rank 32, group 64, W4A4.  ``tops`` times the block's linears with the
+    attention projections that read the same activations (to_q / to_k / to_v / to_gate) as one
+    grouped launch (``grouped_forward``) and the others alone;
+    ``tops_separate`` runs the same groups' layers one by one (timed alternately with the grouped
+    form, so power-state drift hits both alike); ``per_linear`` times each forward alone."""
     import torch
 
-    from krea2_svdquant_b200.linear import SVDQuantLinear
+    from krea2_svdquant_b200.linear import SVDQuantLinear, grouped_forward
     from krea2_svdquant_b200.quant import random_state
     from krea2_svdquant_b200.transformer import Krea2StandInConfig
 
     m_tok = 4352
     gen = torch.Generator(device=dev).manual_seed(3)
+    shapes = Krea2StandInConfig().linear_shapes()
+    mods, xs = {}, {}
+    for name, (n, k) in shapes.items():
+        mods[name] = SVDQuantLinear(random_state(n, k, 32, 64, device=dev, generator=gen), backend="b200")
+        xs[name] = torch.randn(m_tok, k, device=dev, generator=gen).bfloat16()
     per, total_ops, total_ms = {}, 0, 0.0
-    for name, (n, k) in Krea2StandInConfig().linear_shapes().items():
-        mod = SVDQuantLinear(random_state(n, k, 32, 64, device=dev, generator=gen), backend="b200")
-        x = torch.randn(m_tok, k, device=dev, generator=gen).bfloat16()
+    for name, (n, k) in shapes.items():
+        mod, x = mods[name], xs[name]
         prep = mod.prepare(dev)
         torch.cuda.nvtx.range_push(f"block_linear:{name}")  # lets a profiler capture one layer's launches
         ms = statistics.median(_device_times(lambda: mod(x), iters, flush))
@@ -339,11 +371,35 @@ def measure_block_linears(dev, flush, iters: int) -> dict:
                      **_gemm_waves(m_tok, n, prep.k_pad, 0 if prep.up_hl is None else prep.up_hl.shape[1])}
         total_ops += ops_
         total_ms += ms
-        del mod, x
-    tops = total_ops / (total_ms * 1e-3) / 1e12
+    # ff.gate + ff.up as one launch measured no faster (2176 tiles fill 30 waves either way), so
+    # only the attention projections, whose small to_k / to_v leave ragged waves, are grouped
+    groups = [["attn.to_q", "attn.to_k", "attn.to_v", "attn.to_gate"], ["attn.to_out.0"], ["ff.gate"], ["ff.up"],
+              ["ff.down"]]
+    grouped = {}
+    grouped_ms = sep_ms = 0.0
+    for grp in groups:
+        layers, x = [mods[nm] for nm in grp], xs[grp[0]]
+        sep_fn = lambda: [layer(x) for layer in layers]  # noqa: E731
+        grp_fn = (lambda: grouped_forward(layers, x)) if len(grp) > 1 else sep_fn
+        torch.cuda.nvtx.range_push("block_group:" + "+".join(grp))
+        t_sep, t_grp = _device_times_ab([sep_fn, grp_fn], iters, flush)
+        torch.cuda.nvtx.range_pop()
+        ms_g, ms_s = statistics.median(t_grp), statistics.median(t_sep)
+        ops_ = sum(2 * m_tok * shapes[nm][0] * shapes[nm][1] for nm in grp)
+        grouped["+".join(grp)] = {"us": round(ms_g * 1e3, 1), "tops": round(ops_ / (ms_g * 1e-3) / 1e12, 1),
+                                  "us_separate": round(ms_s * 1e3, 1)}
+        grouped_ms += ms_g
+        sep_ms += ms_s
+    tops = total_ops / (grouped_ms * 1e-3) / 1e12
+    tops_sep = total_ops / (sep_ms * 1e-3) / 1e12
+    del mods, xs
     return {"config": "BASELINE config 3: 8 linears of one Krea2 block, M=4352, rank 32, group 64, W4A4",
-            "ops": total_ops, "ms": round(total_ms, 4), "tops": round(tops, 1),
-            "frac_of_measured_bf16_peak": round(tops / _bf16_peak(), 4), "per_linear": per}
+            "ops": total_ops, "ms": round(grouped_ms, 4), "tops": round(tops, 1),
+            "frac_of_measured_bf16_peak": round(tops / _bf16_peak(), 4),
+            "grouping": ("to_q+to_k+to_v+to_gate as one grouped launch (same input); each group timed "
+                         "alternately with its layers' separate forwards"),
+            "per_group": grouped, "ms_separate": round(sep_ms, 4), "tops_separate": round(tops_sep, 1),
+            "ms_sum_of_linears": round(total_ms, 4), "per_linear": per}
 
 
 def measure_w4a16_lora(dev, flush, iters: int) -> dict:

@@ -273,6 +273,37 @@ int svdq_linear_gemm_epi(const void* a16, const void* w16,
                          cudaStream_t stream);
 
 /*
+ * One GEMM of a grouped launch (svdq_linear_gemm_group): the operands and output of one
+ * svdq_linear_gemm_epi call, with the dimensions the group shares taken out.
+ */
+typedef struct svdq_gemm_problem {
+  const void* a16;     /* [M, K_pad] fp16 */
+  const void* w16;     /* [N, K_pad] fp16 */
+  const void* mid_hl;  /* [M, R2] bf16 (unused when R2 == 0) */
+  const void* up_hl;   /* [N, R2] bf16 (unused when R2 == 0) */
+  const void* bias;    /* [N] bf16, 16-byte aligned, or NULL */
+  int epilogue;        /* enum svdq_epilogue */
+  const void* aux;     /* epilogue operand [M, N] in out_dtype, row stride ld_aux */
+  int64_t ld_aux;
+  void* out;           /* [M, N], row stride ldo (multiple of 8) */
+  int64_t ldo;
+  int N;               /* multiple of 8 */
+} svdq_gemm_problem;
+
+/*
+ * Up to four GEMMs that share M, K_pad and R2 (linears reading the same activations, such as a
+ * transformer block's q / k / v projections) as one persistent launch: their 256x256 tiles are
+ * numbered problem after problem and the CTA pairs walk them as one list, so a small problem
+ * (few tiles) fills the waves of the others instead of leaving a ragged last wave of its own; the
+ * split tail (workspace) applies to the group's last wave.  Each problem computes what
+ * svdq_linear_gemm_epi computes for it.  num_problems in [1, 4]; arguments as
+ * svdq_linear_gemm_epi.
+ */
+int svdq_linear_gemm_group(const svdq_gemm_problem* problems, int num_problems, int R2,
+                           int out_dtype, int M, int K_pad,
+                           void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
  * The launch plan of svdq_linear_gemm (with_workspace == 0) or
  * svdq_linear_gemm_ws (with_workspace != 0) for a shape on the current device:
  * out4 = {CTA pairs, tiles computed whole, K iterations per pair in the split

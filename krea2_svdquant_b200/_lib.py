@@ -19,6 +19,13 @@ c_void_p = ctypes.c_void_p
 c_int = ctypes.c_int
 c_int64 = ctypes.c_int64
 
+class GemmProblem(ctypes.Structure):
+    """``svdq_gemm_problem`` of include/svdq_b200.h: one GEMM of ``svdq_linear_gemm_group``."""
+    _fields_ = [("a16", c_void_p), ("w16", c_void_p), ("mid_hl", c_void_p), ("up_hl", c_void_p),
+                ("bias", c_void_p), ("epilogue", c_int), ("aux", c_void_p), ("ld_aux", c_int64),
+                ("out", c_void_p), ("ldo", c_int64), ("N", c_int)]
+
+
 # name -> (argtypes, restype) for every entry point of include/svdq_b200.h
 SIGNATURES = {
     "svdq_last_error": ([], ctypes.c_char_p),
@@ -58,6 +65,8 @@ SIGNATURES = {
     "svdq_linear_gemm_epi": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int64,
                               c_void_p, c_int, c_int64, c_int, c_int, c_int, c_void_p, ctypes.c_size_t, c_void_p],
                              c_int),
+    "svdq_linear_gemm_group": ([ctypes.POINTER(GemmProblem), c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                ctypes.c_size_t, c_void_p], c_int),
     "svdq_linear_gemm_schedule": ([c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)], c_int),
     "svdq_linear_gemm_plan": ([c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)], c_int),
     "svdq_prepare_packed": ([c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,

@@ -78,17 +78,33 @@ struct Barriers {
 
 constexpr size_t SMEM_BYTES = (size_t)STAGES * AB_BYTES + sizeof(Barriers) + 1024;
 
-struct GemmArgs {
+// One GEMM of a launch.  A grouped launch runs up to kMaxProblems GEMMs that share M, K_pad and
+// R2 (layers reading the same activations) over one persistent grid: their tiles are numbered
+// one after the other, problem by problem.
+constexpr int kMaxProblems = 4;
+struct GemmProblem {
   const __nv_bfloat16* bias;
   void* out;
   int64_t ldo;
   const void* aux;  // epilogue operand z [M, N] in out's dtype (row stride ld_aux), or null
   int64_t ld_aux;
   int epi;          // kEpi*: what the epilogue does with y = acc + bias and z
-  int M, N;
+  int N;
+  int num_n_blocks;
+  int tile_start;   // index of the problem's first tile
+};
+
+struct TmaSet {  // tensor maps of each problem: a16, w16, mid_hl, up_hl
+  CUtensorMap a[kMaxProblems], w[kMaxProblems], mid[kMaxProblems], up[kMaxProblems];
+};
+
+struct GemmArgs {
+  GemmProblem prob[kMaxProblems];
+  int num_problems;
+  int M;
   int n_k;   // K_pad / 64 residual stages
   int n_lr;  // R2 / 64 low-rank stages
-  int num_m_blocks, num_n_blocks;  // pair tiles: 256 rows x 256 columns
+  int num_m_blocks;  // pair tiles: 256 rows x 256 columns
   int iters;       // K iterations of one tile: n_k + n_lr
   int dp_tiles;    // tiles [0, dp_tiles) are computed whole, round-robin over the pairs
   int tail_len;    // K iterations per pair in the split tail
@@ -164,6 +180,35 @@ __device__ __forceinline__ void advance(int& idx, uint32_t& phase, int n) {
 // M4096 N16384 K6144 this reads 570 MB of DRAM against 707 MB for plain column-major order
 // (groups of 4: 989 MB, groups of 12: 633 MB and 2% slower).
 constexpr int kGroupM = 8;
+
+// Problem of global tile t, and t's index within it.  Unrolled over the problems so that every
+// parameter access has a constant offset.
+__device__ __forceinline__ int tile_problem(const GemmArgs& a, int& t) {
+  int p = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxProblems; ++i)
+    if (i < a.num_problems && t >= a.prob[i].tile_start) p = i;
+  int start = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxProblems; ++i)
+    if (i == p) start = a.prob[i].tile_start;
+  t -= start;
+  return p;
+}
+__device__ __forceinline__ GemmProblem get_problem(const GemmArgs& a, int p) {
+  GemmProblem r = a.prob[0];
+#pragma unroll
+  for (int i = 1; i < kMaxProblems; ++i)
+    if (i == p) r = a.prob[i];
+  return r;
+}
+__device__ __forceinline__ const CUtensorMap* pick_map(const CUtensorMap (&m)[kMaxProblems], int p) {
+  const CUtensorMap* r = &m[0];
+#pragma unroll
+  for (int i = 1; i < kMaxProblems; ++i)
+    if (i == p) r = &m[i];
+  return r;
+}
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = kGroupM * num_n;
@@ -245,9 +290,7 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
 
 template <bool OUT_F32>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    linear_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
-                       const __grid_constant__ CUtensorMap tm_mid, const __grid_constant__ CUtensorMap tm_up,
-                       const GemmArgs args) {
+    linear_gemm_kernel(const __grid_constant__ TmaSet maps, const __grid_constant__ GemmArgs args) {
   constexpr int kOutBytes = OUT_F32 ? 4 : 2;
   constexpr int kAuxWords = 32 * kOutBytes / 16;  // 16-byte words of z per 32-column chunk
   constexpr int kAuxBufs = OUT_F32 ? 1 : 2;
@@ -288,11 +331,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    prefetch_tma_desc(&tm_a);
-    prefetch_tma_desc(&tm_w);
-    if (args.n_lr > 0) {
-      prefetch_tma_desc(&tm_mid);
-      prefetch_tma_desc(&tm_up);
+#pragma unroll
+    for (int i = 0; i < kMaxProblems; ++i) {
+      if (i < args.num_problems) {
+        prefetch_tma_desc(&maps.a[i]);
+        prefetch_tma_desc(&maps.w[i]);
+        if (args.n_lr > 0) {
+          prefetch_tma_desc(&maps.mid[i]);
+          prefetch_tma_desc(&maps.up[i]);
+        }
+      }
     }
   }
   if (warp == 1) {
@@ -319,8 +367,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       walk_init(wk, args, pair);
       int t, k0, k1;
       while (ok && walk_next(wk, args, pair, num_pairs, t, k0, k1)) {
+        int tp = t;
+        const int p = tile_problem(args, tp);
+        const GemmProblem P = get_problem(args, p);
+        const CUtensorMap* tm_a = pick_map(maps.a, p);
+        const CUtensorMap* tm_w = pick_map(maps.w, p);
+        const CUtensorMap* tm_mid = pick_map(maps.mid, p);
+        const CUtensorMap* tm_up = pick_map(maps.up, p);
         int mb, nb;
-        tile_coords(t, args.num_m_blocks, args.num_n_blocks, mb, nb);
+        tile_coords(tp, args.num_m_blocks, P.num_n_blocks, mb, nb);
         const int m0 = mb * (2 * BM) + (int)rank * BM;
         const int n0 = nb * BN + (int)rank * BN_HALF;
         for (int s = k0; ok && s < k1; ++s) {
@@ -328,11 +383,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t full_c = mapa_shared(full_bar(stage), 0);
           if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * AB_BYTES);
           if (s < args.n_k) {
-            tma_load_2d_pair(stage_a(stage), &tm_a, full_c, s * 64, m0);
-            tma_load_2d_pair(stage_b(stage), &tm_w, full_c, s * 64, n0);
+            tma_load_2d_pair(stage_a(stage), tm_a, full_c, s * 64, m0);
+            tma_load_2d_pair(stage_b(stage), tm_w, full_c, s * 64, n0);
           } else {
-            tma_load_2d_pair(stage_a(stage), &tm_mid, full_c, (s - args.n_k) * 64, m0);
-            tma_load_2d_pair(stage_b(stage), &tm_up, full_c, (s - args.n_k) * 64, n0);
+            tma_load_2d_pair(stage_a(stage), tm_mid, full_c, (s - args.n_k) * 64, m0);
+            tma_load_2d_pair(stage_b(stage), tm_up, full_c, (s - args.n_k) * 64, n0);
           }
           filled |= 1u << stage;
           par = (par & ~(1u << stage)) | (phase << stage);
@@ -399,8 +454,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     walk_init(wk, args, pair);
     int t, k0, k1;
     while (ok && walk_next(wk, args, pair, num_pairs, t, k0, k1)) {
+      int tp = t;
+      const GemmProblem P = get_problem(args, tile_problem(args, tp));
       int mb, nb;
-      tile_coords(t, args.num_m_blocks, args.num_n_blocks, mb, nb);
+      tile_coords(tp, args.num_m_blocks, P.num_n_blocks, mb, nb);
       const int m0 = mb * (2 * BM) + (int)rank * BM;
       const int n0 = nb * BN;
       const bool contrib = k0 > 0;  // a later piece of a split tile: hand the partial to its owner
@@ -412,20 +469,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // bias of the warpgroup's 128 columns: lane l < 16 holds columns 8l .. 8l+7, loaded
       // before the accumulator wait so its latency hides behind the MMAs
       uint4 bias_lane = make_uint4(0u, 0u, 0u, 0u);
-      if (args.bias && !contrib && lane < 16 && n0 + col0 + 8 * lane < args.N)
-        bias_lane = *reinterpret_cast<const uint4*>(args.bias + n0 + col0 + 8 * lane);
+      if (P.bias && !contrib && lane < 16 && n0 + col0 + 8 * lane < P.N)
+        bias_lane = *reinterpret_cast<const uint4*>(P.bias + n0 + col0 + 8 * lane);
       // epilogue operand: the lane's row, 32 columns per chunk; bf16 one chunk ahead (the first
       // one before the accumulator wait), fp32 (twice the registers) at the chunk's start;
       // streamed with an evict-first hint, it is read once
       const int grow = m0 + row;
-      const bool use_aux = args.epi != kEpiNone && !contrib;
-      const uint8_t* aux_row = static_cast<const uint8_t*>(args.aux) + (size_t)grow * args.ld_aux * kOutBytes;
+      const bool use_aux = P.epi != kEpiNone && !contrib;
+      const uint8_t* aux_row = static_cast<const uint8_t*>(P.aux) + (size_t)grow * P.ld_aux * kOutBytes;
       uint4 ax[kAuxBufs][kAuxWords];
       auto load_aux = [&](int c, uint4 (&d)[kAuxWords]) {
 #pragma unroll
         for (int i = 0; i < kAuxWords; ++i) {
           const int n = n0 + col0 + c * 32 + i * (16 / kOutBytes);
-          d[i] = (grow < args.M && n < args.N) ? __ldcs(reinterpret_cast<const uint4*>(aux_row + (size_t)n * kOutBytes))
+          d[i] = (grow < args.M && n < P.N) ? __ldcs(reinterpret_cast<const uint4*>(aux_row + (size_t)n * kOutBytes))
                                                : make_uint4(0u, 0u, 0u, 0u);
         }
       };
@@ -473,7 +530,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (n_parts > 0)
         for (int g = 0; g < kPartSlots; ++g) issue_group(g);
       const uint32_t taddr = tmem_base + lane_off + (uint32_t)(tb * BN + col0);
-      const int64_t rbase = (int64_t)grow * args.ldo;
+      const int64_t rbase = (int64_t)grow * P.ldo;
       uint32_t va[32], vb[32];
       tmem_ld32(taddr, va);
 #pragma unroll
@@ -528,11 +585,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             const int n = nc + i;
-            if (n < args.N) {
+            if (n < P.N) {
               float v[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(cur[i + e]);
-              if (args.bias) {
+              if (P.bias) {
                 const __nv_bfloat162* bb = reinterpret_cast<const __nv_bfloat162*>(bw[i / 8]);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -559,10 +616,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     z[2 * e + 1] = f.y;
                   }
                 }
-                epi_apply<OUT_F32>(args.epi, v, z);
+                epi_apply<OUT_F32>(P.epi, v, z);
               }
               if constexpr (OUT_F32) {
-                float4* o = reinterpret_cast<float4*>(static_cast<float*>(args.out) + rbase + n);
+                float4* o = reinterpret_cast<float4*>(static_cast<float*>(P.out) + rbase + n);
                 o[0] = make_float4(v[0], v[1], v[2], v[3]);
                 o[1] = make_float4(v[4], v[5], v[6], v[7]);
               } else {
@@ -572,7 +629,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
                   w[e] = *reinterpret_cast<uint32_t*>(&h);
                 }
-                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(args.out) + rbase + n) =
+                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(P.out) + rbase + n) =
                     make_uint4(w[0], w[1], w[2], w[3]);
               }
             }
@@ -683,73 +740,93 @@ Schedule plan_schedule(int tiles, int iters, int max_pairs, bool can_split) {
   return s;
 }
 
-int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, const void* up_hl, int R2,
-                       const void* bias, int epilogue, const void* aux, int64_t ld_aux, void* out, int out_dtype,
-                       int64_t ldo, int M, int N, int K_pad, void* workspace, size_t workspace_bytes,
-                       cudaStream_t stream, const char* who) {
+// Validates a group of GEMMs sharing M, K_pad and R2 and launches them as one persistent grid
+// (a single problem is the plain GEMM).
+int launch_linear_gemm_group(const svdq_gemm_problem* probs, int np, int R2, int out_dtype, int M, int K_pad,
+                             void* workspace, size_t workspace_bytes, cudaStream_t stream, const char* who) {
   const std::string w(who);
-  if (!(a16 && w16 && out)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": null operand pointer");
-  if (!(M >= 0 && N > 0 && K_pad > 0)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": bad M/N/K_pad");
+  if (!probs || np < 1 || np > kMaxProblems)
+    return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": 1 to 4 problems per launch");
+  if (!(M >= 0 && K_pad > 0)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": bad M/K_pad");
   if (K_pad % 64 != 0) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": K_pad must be a multiple of 64");
-  if (!(N % 8 == 0 && ldo >= N && ldo % 8 == 0))
-    return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": N and ldo must be multiples of 8, ldo >= N");
   if (!(R2 >= 0 && R2 % 64 == 0)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": R2 must be a multiple of 64");
-  if (R2 > 0 && !(mid_hl && up_hl)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": mid_hl/up_hl are NULL");
   if (!(out_dtype == SVDQ_BF16 || out_dtype == SVDQ_FP32))
     return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": out_dtype must be bf16 or fp32");
-  if (bias && (reinterpret_cast<uintptr_t>(bias) & 15u))
-    return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": bias must be 16-byte aligned");
-  if (reinterpret_cast<uintptr_t>(out) & 15u)
-    return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": out must be 16-byte aligned");
-  if (!(epilogue >= kEpiNone && epilogue <= kEpiSiluMul))
-    return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": unknown epilogue operation");
-  if (epilogue != kEpiNone &&
-      !(aux && (reinterpret_cast<uintptr_t>(aux) & 15u) == 0 && ld_aux >= N && ld_aux % 8 == 0))
-    return set_error(SVDQ_ERR_INVALID_ARGUMENT,
-                     w + ": the epilogue operand must be non-null and 16-byte aligned, ld_aux >= N, ld_aux % 8 == 0");
+  for (int i = 0; i < np; ++i) {
+    const svdq_gemm_problem& q = probs[i];
+    const std::string wi = np > 1 ? w + " (problem " + std::to_string(i) + ")" : w;
+    if (!(q.a16 && q.w16 && q.out)) return set_error(SVDQ_ERR_INVALID_ARGUMENT, wi + ": null operand pointer");
+    if (!(q.N > 0 && q.N % 8 == 0 && q.ldo >= q.N && q.ldo % 8 == 0))
+      return set_error(SVDQ_ERR_INVALID_ARGUMENT, wi + ": N and ldo must be positive multiples of 8, ldo >= N");
+    if (R2 > 0 && !(q.mid_hl && q.up_hl))
+      return set_error(SVDQ_ERR_INVALID_ARGUMENT, wi + ": mid_hl/up_hl are NULL");
+    if (q.bias && (reinterpret_cast<uintptr_t>(q.bias) & 15u))
+      return set_error(SVDQ_ERR_INVALID_ARGUMENT, wi + ": bias must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(q.out) & 15u)
+      return set_error(SVDQ_ERR_INVALID_ARGUMENT, wi + ": out must be 16-byte aligned");
+    if (!(q.epilogue >= kEpiNone && q.epilogue <= kEpiSiluMul))
+      return set_error(SVDQ_ERR_INVALID_ARGUMENT, wi + ": unknown epilogue operation");
+    if (q.epilogue != kEpiNone &&
+        !(q.aux && (reinterpret_cast<uintptr_t>(q.aux) & 15u) == 0 && q.ld_aux >= q.N && q.ld_aux % 8 == 0))
+      return set_error(SVDQ_ERR_INVALID_ARGUMENT,
+                       wi + ": the epilogue operand must be non-null and 16-byte aligned, ld_aux >= N, ld_aux % 8 == 0");
+  }
   if (M == 0) return SVDQ_OK;
   int* err = device_error_word();
   if (!err) return set_error(SVDQ_ERR_CUDA, w + ": device error word unavailable");
 
-  CUtensorMap tm_a, tm_w, tm_mid, tm_up;
-  int st;
-  if ((st = make_tma_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a16, K_pad, M, (uint64_t)K_pad * 2, 64, BM,
-                        CU_TENSOR_MAP_SWIZZLE_128B)))
-    return st;
-  if ((st = make_tma_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w16, K_pad, N, (uint64_t)K_pad * 2, 64, BN_HALF,
-                        CU_TENSOR_MAP_SWIZZLE_128B)))
-    return st;
-  if (R2 > 0) {
-    if ((st = make_tma_2d(&tm_mid, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, mid_hl, R2, M, (uint64_t)R2 * 2, 64, BM,
+  TmaSet maps;
+  GemmArgs a{};
+  a.num_m_blocks = (M + 2 * BM - 1) / (2 * BM);
+  int tiles = 0;
+  for (int i = 0; i < np; ++i) {
+    const svdq_gemm_problem& q = probs[i];
+    int st;
+    if ((st = make_tma_2d(&maps.a[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, q.a16, K_pad, M, (uint64_t)K_pad * 2, 64, BM,
                           CU_TENSOR_MAP_SWIZZLE_128B)))
       return st;
-    if ((st = make_tma_2d(&tm_up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, up_hl, R2, N, (uint64_t)R2 * 2, 64, BN_HALF,
-                          CU_TENSOR_MAP_SWIZZLE_128B)))
+    if ((st = make_tma_2d(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, q.w16, K_pad, q.N, (uint64_t)K_pad * 2, 64,
+                          BN_HALF, CU_TENSOR_MAP_SWIZZLE_128B)))
       return st;
-  } else {
-    tm_mid = tm_a;
-    tm_up = tm_w;
+    if (R2 > 0) {
+      if ((st = make_tma_2d(&maps.mid[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q.mid_hl, R2, M, (uint64_t)R2 * 2, 64,
+                            BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+      if ((st = make_tma_2d(&maps.up[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q.up_hl, R2, q.N, (uint64_t)R2 * 2, 64,
+                            BN_HALF, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    } else {
+      maps.mid[i] = maps.a[i];
+      maps.up[i] = maps.w[i];
+    }
+    GemmProblem& g = a.prob[i];
+    g.bias = static_cast<const __nv_bfloat16*>(q.bias);
+    g.out = q.out;
+    g.ldo = q.ldo;
+    g.epi = q.epilogue;
+    g.aux = q.epilogue != kEpiNone ? q.aux : nullptr;
+    g.ld_aux = q.epilogue != kEpiNone ? q.ld_aux : 0;
+    g.N = q.N;
+    g.num_n_blocks = (q.N + BN - 1) / BN;
+    g.tile_start = tiles;
+    tiles += a.num_m_blocks * g.num_n_blocks;
   }
-
-  GemmArgs a;
-  a.bias = static_cast<const __nv_bfloat16*>(bias);
-  a.out = out;
-  a.ldo = ldo;
-  a.aux = epilogue != kEpiNone ? aux : nullptr;
-  a.ld_aux = epilogue != kEpiNone ? ld_aux : 0;
-  a.epi = epilogue;
+  for (int i = np; i < kMaxProblems; ++i) {  // never selected (tile_problem stops at num_problems)
+    maps.a[i] = maps.a[0];
+    maps.w[i] = maps.w[0];
+    maps.mid[i] = maps.mid[0];
+    maps.up[i] = maps.up[0];
+    a.prob[i] = a.prob[0];
+  }
+  a.num_problems = np;
   a.M = M;
-  a.N = N;
   a.n_k = K_pad / 64;
   a.n_lr = R2 / 64;
-  a.num_m_blocks = (M + 2 * BM - 1) / (2 * BM);
-  a.num_n_blocks = (N + BN - 1) / BN;
   a.iters = a.n_k + a.n_lr;
   a.err = err;
   auto kern = out_dtype == SVDQ_FP32 ? linear_gemm_kernel<true> : linear_gemm_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
   if (e != cudaSuccess) return check_cuda(e, (w + ": shared memory attribute").c_str());
-  const int tiles = a.num_m_blocks * a.num_n_blocks;
   const int max_pairs = max_resident_pairs(reinterpret_cast<const void*>(kern));
   const bool can_split = workspace != nullptr && workspace_bytes >= workspace_bytes_for(num_sms() / 2) &&
                          (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0;
@@ -775,9 +852,29 @@ int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, con
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  e = cudaLaunchKernelEx(&cfg, kern, tm_a, tm_w, tm_mid, tm_up, a);
+  e = cudaLaunchKernelEx(&cfg, kern, maps, a);
   if (e != cudaSuccess) return check_cuda(e, (w + " launch").c_str());
   return check_launch((w + " launch").c_str());
+}
+
+int launch_linear_gemm(const void* a16, const void* w16, const void* mid_hl, const void* up_hl, int R2,
+                       const void* bias, int epilogue, const void* aux, int64_t ld_aux, void* out, int out_dtype,
+                       int64_t ldo, int M, int N, int K_pad, void* workspace, size_t workspace_bytes,
+                       cudaStream_t stream, const char* who) {
+  svdq_gemm_problem q{};
+  q.a16 = a16;
+  q.w16 = w16;
+  q.mid_hl = mid_hl;
+  q.up_hl = up_hl;
+  q.bias = bias;
+  q.epilogue = epilogue;
+  q.aux = aux;
+  q.ld_aux = ld_aux;
+  q.out = out;
+  q.ldo = ldo;
+  q.N = N;
+  if (N <= 0) return set_error(SVDQ_ERR_INVALID_ARGUMENT, std::string(who) + ": bad M/N/K_pad");
+  return launch_linear_gemm_group(&q, 1, R2, out_dtype, M, K_pad, workspace, workspace_bytes, stream, who);
 }
 
 }  // namespace svdq
@@ -814,6 +911,17 @@ extern "C" int svdq_linear_gemm_epi(const void* a16, const void* w16, const void
                            "svdq_linear_gemm_epi: workspace smaller than svdq_linear_gemm_workspace_bytes()");
   return svdq::launch_linear_gemm(a16, w16, mid_hl, up_hl, R2, bias, epilogue, aux, ld_aux, out, out_dtype, ldo, M, N,
                                   K_pad, workspace, workspace_bytes, stream, "svdq_linear_gemm_epi");
+}
+
+extern "C" int svdq_linear_gemm_group(const svdq_gemm_problem* problems, int num_problems, int R2, int out_dtype,
+                                      int M, int K_pad, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_linear_gemm_group: workspace must be 256-byte aligned");
+  if (workspace && workspace_bytes < svdq::workspace_bytes_for(svdq::num_sms() / 2))
+    return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT,
+                           "svdq_linear_gemm_group: workspace smaller than svdq_linear_gemm_workspace_bytes()");
+  return svdq::launch_linear_gemm_group(problems, num_problems, R2, out_dtype, M, K_pad, workspace, workspace_bytes,
+                                        stream, "svdq_linear_gemm_group");
 }
 
 extern "C" int svdq_linear_gemm_plan(int tiles, int iters, int max_pairs, int with_workspace, int* out4) {

@@ -20,6 +20,7 @@ swallows kernel errors and reruns its simulation, linear.py:133-154).
 from __future__ import annotations
 
 from dataclasses import dataclass
+from typing import Sequence
 
 import torch
 import torch.nn.functional as F
@@ -82,6 +83,12 @@ class PreparedOperands:
     codes: torch.Tensor | None     # [n, k_pad/2] u8 kernel-order codes (weight_operand "packed")
     scales16: torch.Tensor | None  # fp16 group scales in the packed GEMM's tile order (with codes)
     bias: torch.Tensor | None      # [n] bf16
+
+
+def _kernels():
+    """The op implementations for a forward: the plain functions in eager mode (no dispatcher on
+    the host's critical path), the registered custom ops while ``torch.compile`` traces."""
+    return ops if torch.compiler.is_compiling() else ops.eager
 
 
 def _pad_rows(t: torch.Tensor, rows: int) -> torch.Tensor:
@@ -243,51 +250,64 @@ class SVDQuantLinear(nn.Module):
         return self._prepared
 
     # ------------------------------------------------------------------ forward
-    def _run(self, x: torch.Tensor, include_lora: bool,
-             epilogue: tuple[str, torch.Tensor] | None = None) -> torch.Tensor:
+    def _prologue(self, x: torch.Tensor) -> tuple[PreparedOperands, torch.Size, torch.Tensor, bool]:
+        """Checks x and returns (prepared operands, leading shape, x as [M, K_in] bf16 rows the
+        activation pass can read, whether the output is fp32)."""
         if not x.is_cuda:
             raise ValueError("SVDQuantLinear (b200) needs CUDA activations; this runtime has no CPU path")
         if x.dtype not in (torch.bfloat16, torch.float32):
             raise TypeError(f"SVDQuantLinear (b200) takes bf16 or fp32 activations, got {x.dtype}")
-        n, k_orig = self.original_shape
+        k_orig = self.original_shape[1]
         if x.shape[-1] != k_orig:
             raise ValueError(f"expected [..., {k_orig}] activations, got {tuple(x.shape)}")
         p = self.prepare(x.device)
-        lead = x.shape[:-1]
         x2 = x.reshape(-1, k_orig)
         if x2.dtype != torch.bfloat16:
             x2 = x2.to(torch.bfloat16)
         if p.k_in != k_orig or x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
             x2 = _pad_cols(x2, p.k_in).contiguous()
-        out_fp32 = self.output_fp32 or x.dtype == torch.float32
+        return p, x.shape[:-1], x2, self.output_fp32 or x.dtype == torch.float32
+
+    def _a16_operands(self, p: PreparedOperands, x2: torch.Tensor, include_lora: bool):
+        """The activation pass for the fp16-operand GEMMs: (a16, (mid_hl, up_hl) or (None, None))."""
         lora_down = p.lora_down if include_lora else None
         col_scale = p.lora_col_scale if include_lora else None
         up_hl = p.up_hl if include_lora else p.up_hl_base
+        k = _kernels()
         if self.backend is BackendKind.B200_W4A16:
-            a16, mid = ops.w4a16_prep(x2, p.smooth, p.l2_f16, lora_down, col_scale, p.k_pad)
-        elif p.w16 is None and self._int8_path(x2.shape[0], p):
+            a16, mid = k.w4a16_prep(x2, p.smooth, p.l2_f16, lora_down, col_scale, p.k_pad)
+        else:
+            a16, mid, _, _ = k.act_quant(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
+                                         self.act_group_size, True, False)
+        return a16, ((mid, up_hl) if mid.numel() else (None, None))
+
+    def _run(self, x: torch.Tensor, include_lora: bool,
+             epilogue: tuple[str, torch.Tensor] | None = None) -> torch.Tensor:
+        p, lead, x2, out_fp32 = self._prologue(x)
+        n = self.original_shape[0]
+        k = _kernels()
+        if self.backend is not BackendKind.B200_W4A16 and p.w16 is None and self._int8_path(x2.shape[0], p):
             # small batch, packed weight: int8 codes and the kind::i8 GEMM with per-group rescale
-            codes8, ascales, mid = ops.act_quant_i8(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
+            codes8, ascales, mid = k.act_quant_i8(x2, p.smooth, p.l2, p.lora_down if include_lora else None,
+                                                    p.lora_col_scale if include_lora else None, p.k_pad,
                                                     self.act_group_size)
+            up_hl = p.up_hl if include_lora else p.up_hl_base
             lowrank = (mid, up_hl) if mid.numel() else (None, None)
-            y = ops.w4a4_gemm(codes8, ascales, self.act_group_size, p.codes, p.scales16, self.group_size,
+            y = k.w4a4_gemm(codes8, ascales, self.act_group_size, p.codes, p.scales16, self.group_size,
                               *lowrank, p.bias, out_fp32)
             if self.check_device_errors:
                 _lib.raise_on_device_error(f"SVDQuantLinear {tuple(self.original_shape)}")
             return ops.apply_epilogue(y.reshape(*lead, n), epilogue)
-        else:
-            a16, mid, _, _ = ops.act_quant(x2, p.smooth, p.l2, lora_down, col_scale, p.k_pad,
-                                           self.act_group_size, True, False)
-        lowrank = (mid, up_hl) if mid.numel() else (None, None)
+        a16, lowrank = self._a16_operands(p, x2, include_lora)
         z = self._fusable_operand(epilogue, x2.shape[0], out_fp32) if p.w16 is not None else None
         if z is not None:
             # the combining op runs in the GEMM's epilogue: y never makes a round trip through HBM
-            y = ops.linear_gemm_epi(a16, p.w16, *lowrank, p.bias, out_fp32, ops.EPILOGUES[epilogue[0]], z)
+            y = k.linear_gemm_epi(a16, p.w16, *lowrank, p.bias, out_fp32, ops.EPILOGUES[epilogue[0]], z)
             epilogue = None
         elif p.w16 is None:
-            y = ops.packed_gemm(a16, p.codes, p.scales16, self.group_size, *lowrank, p.bias, out_fp32)
+            y = k.packed_gemm(a16, p.codes, p.scales16, self.group_size, *lowrank, p.bias, out_fp32)
         else:
-            y = ops.linear_gemm(a16, p.w16, *lowrank, p.bias, out_fp32)
+            y = k.linear_gemm(a16, p.w16, *lowrank, p.bias, out_fp32)
         if self.check_device_errors:
             _lib.raise_on_device_error(f"SVDQuantLinear {tuple(self.original_shape)}")
         return ops.apply_epilogue(y.reshape(*lead, n), epilogue)
@@ -346,3 +366,53 @@ class SVDQuantLinear(nn.Module):
         n, k = self.original_shape
         return (f"in_features={k}, out_features={n}, rank={self.l1.shape[1]}, group_size={self.group_size}, "
                 f"backend={self.backend.value}, loras={len(self.lora_adapters)}")
+
+
+def grouped_forward(layers: Sequence[nn.Module], x: torch.Tensor) -> list[torch.Tensor]:
+    """``[layer(x) for layer in layers]`` for layers that read the same activations (a block's q / k
+    / v projections, its gated-MLP pair).  When every layer is an ``SVDQuantLinear`` on the
+    fp16-weight GEMM with the same padded K and low-rank width, their GEMMs run as one grouped
+    persistent launch (``svdq_linear_gemm_group``, up to four): a layer with few tiles fills the
+    waves of the others instead of ending in a ragged wave of its own.  Otherwise, and for layers
+    with forward hooks or an overridden ``_forward_base``, the layers run one by one."""
+    layers = list(layers)
+    if not _groupable(layers, x):
+        return [layer(x) for layer in layers]
+    k = _kernels()
+    outs = []
+    for start in range(0, len(layers), 4):
+        chunk = layers[start:start + 4]
+        a16s, w16s, mids, ups, biases = [], [], [], [], []
+        lead, out_fp32 = None, False
+        for layer in chunk:
+            p, lead, x2, out_fp32 = layer._prologue(x)
+            a16, (mid, up) = layer._a16_operands(p, x2, include_lora=True)
+            a16s.append(a16)
+            w16s.append(p.w16)
+            mids.append(mid)
+            ups.append(up)
+            biases.append(p.bias)
+        ys = k.linear_gemm_group(a16s, w16s, mids, ups, biases, out_fp32)
+        if any(layer.check_device_errors for layer in chunk):
+            _lib.raise_on_device_error(f"grouped SVDQuantLinear {[tuple(l.original_shape) for l in chunk]}")
+        outs += [y.reshape(*lead, layer.original_shape[0]) for y, layer in zip(ys, chunk)]
+    return outs
+
+
+def _groupable(layers: list[nn.Module], x: torch.Tensor) -> bool:
+    if len(layers) < 2 or not x.is_cuda or x.dtype not in (torch.bfloat16, torch.float32):
+        return False
+    keys = set()
+    for layer in layers:
+        if not isinstance(layer, SVDQuantLinear) or "_forward_base" in layer.__dict__:
+            return False
+        if layer._forward_hooks or layer._forward_pre_hooks:
+            return False
+        if x.shape[-1] != layer.original_shape[1]:
+            return False
+        p = layer.prepare(x.device)
+        if p.w16 is None:
+            return False
+        r2 = 0 if p.up_hl is None else p.up_hl.shape[1]
+        keys.add((p.k_pad, r2, layer.output_fp32))
+    return len(keys) == 1

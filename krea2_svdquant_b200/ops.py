@@ -10,6 +10,7 @@ from __future__ import annotations
 import collections
 import ctypes
 import threading
+import types
 from typing import Optional
 
 import torch
@@ -23,8 +24,17 @@ def _p(t: Optional[Tensor]):
     return ctypes.c_void_p(t.data_ptr()) if t is not None and t.numel() > 0 else None
 
 
+def _raw_stream(dev: torch.device) -> int:
+    """The current CUDA stream of ``dev`` as a handle (the allocator's fast path, used by every
+    call; ``torch.cuda.current_stream`` builds a Python stream object each time)."""
+    get = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if get is not None:
+        return int(get(dev.index if dev.index is not None else torch.cuda.current_device()))
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
 def _stream(dev: torch.device):
-    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    return ctypes.c_void_p(_raw_stream(dev))
 
 
 def _need_cuda(name: str, *ts: Optional[Tensor]) -> None:
@@ -51,6 +61,19 @@ def lowrank_width(r_tot: int) -> int:
 _DT = {torch.bfloat16: _lib.SVDQ_BF16, torch.float16: _lib.SVDQ_FP16, torch.float32: _lib.SVDQ_FP32}
 
 
+_EAGER: dict = {}
+
+
+def _op(name: str):
+    """Registers the decorated function as the custom op ``svdq_b200::<name>`` and keeps the plain
+    function in ``eager`` as well: the module layer calls it directly outside ``torch.compile``,
+    which saves the dispatcher's 10-20 us per call (host time that a small layer cannot hide)."""
+    def deco(fn):
+        _EAGER[name] = fn
+        return torch.library.custom_op(f"svdq_b200::{name}", fn, mutates_args=())
+    return deco
+
+
 # --------------------------------------------------------------------------- activation passes
 def _lowrank_args(l2, lora_down):
     rank = 0 if l2 is None else l2.shape[0]
@@ -72,7 +95,7 @@ def _workspace(m: int, k_pad: int, rank: int, lrank: int, dev: torch.device) -> 
     n = int(_lib.lib().svdq_act_quant_workspace_bytes(m, k_pad, rank, lrank))
     if torch.cuda.is_current_stream_capturing():
         return torch.zeros((max(n, 0),), dtype=torch.uint8, device=dev)
-    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    key = (dev.index, _raw_stream(dev))
     with _act_ws_lock:
         ws = _act_ws.get(key)
         if ws is None or ws.numel() < n:
@@ -84,7 +107,7 @@ def _workspace(m: int, k_pad: int, rank: int, lrank: int, dev: torch.device) -> 
     return ws
 
 
-@torch.library.custom_op("svdq_b200::act_quant", mutates_args=())
+@_op("act_quant")
 def act_quant(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Optional[Tensor],
               lora_col_scale: Optional[Tensor], k_pad: int, a_group: int, emit_a16: bool,
               emit_packed: bool) -> tuple[Tensor, Tensor, Tensor, Tensor]:
@@ -131,7 +154,7 @@ def ascales_ld(m: int) -> int:
     return round_up(max(m, 1), 64)
 
 
-@torch.library.custom_op("svdq_b200::act_quant_i8", mutates_args=())
+@_op("act_quant_i8")
 def act_quant_i8(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Optional[Tensor],
                  lora_col_scale: Optional[Tensor], k_pad: int, a_group: int) -> tuple[Tensor, Tensor, Tensor]:
     """W4A4 activation pass for the int8-code GEMM: the codes of ``quantize_symmetric_int4(x / smooth,
@@ -165,7 +188,7 @@ def _(x, smooth, l2, lora_down, lora_col_scale, k_pad, a_group):
             x.new_empty((m, r2) if r2 else (0,), dtype=torch.bfloat16))
 
 
-@torch.library.custom_op("svdq_b200::w4a16_prep", mutates_args=())
+@_op("w4a16_prep")
 def w4a16_prep(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Optional[Tensor],
                lora_col_scale: Optional[Tensor], k_pad: int) -> tuple[Tensor, Tensor]:
     """W4A16 activation pass: ``a16 = fp16(x / smooth)`` (fp32 division) and the low-rank
@@ -197,7 +220,7 @@ def _(x, smooth, l2, lora_down, lora_col_scale, k_pad):
 
 
 # --------------------------------------------------------------------------- converter
-@torch.library.custom_op("svdq_b200::quantize_weight", mutates_args=())
+@_op("quantize_weight")
 def quantize_weight(w: Tensor, group: int, scale_dtype: torch.dtype) -> tuple[Tensor, Tensor]:
     """fp32 residual ``w [N, K]`` -> ``(packed [N, K_pad/2] u8, scales [N, K_pad/group])``, bit-exact with
     the reference's ``pack_int4(quantize_symmetric_int4(w, group, dim=1))`` (scales rounded once to
@@ -222,7 +245,7 @@ def _(w, group, scale_dtype):
 
 
 # --------------------------------------------------------------------------- load-time operands
-@torch.library.custom_op("svdq_b200::repack_weight", mutates_args=())
+@_op("repack_weight")
 def repack_weight(qweight: Tensor, scales: Tensor, w_group: int) -> Tensor:
     """Checkpoint INT4 weight -> ``w16 [N, K_pad]`` fp16 = q * scale."""
     _need_cuda("repack_weight", qweight, scales)
@@ -241,7 +264,7 @@ def _(qweight, scales, w_group):
     return qweight.new_empty((qweight.shape[0], qweight.shape[1] * 2), dtype=torch.float16)
 
 
-@torch.library.custom_op("svdq_b200::build_up_hl", mutates_args=())
+@_op("build_up_hl")
 def build_up_hl(l1: Tensor, lora_up: Optional[Tensor], r2: int) -> Tensor:
     """``[up | up | 0]`` with ``up = [l1 | lora_up]`` (bf16) for the fused low-rank MMA."""
     _need_cuda("build_up_hl", l1, lora_up)
@@ -271,7 +294,7 @@ def _gemm_workspace(dev: torch.device) -> Optional[Tensor]:
     keep the workspace's address after this cache had evicted and freed it."""
     if torch.cuda.is_current_stream_capturing():
         return None
-    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    key = (dev.index, _raw_stream(dev))
     with _gemm_ws_lock:
         ws = _gemm_ws.get(key)
         if ws is not None:
@@ -287,7 +310,7 @@ def _gemm_workspace(dev: torch.device) -> Optional[Tensor]:
     return ws
 
 
-@torch.library.custom_op("svdq_b200::linear_gemm", mutates_args=())
+@_op("linear_gemm")
 def linear_gemm(a16: Tensor, w16: Tensor, mid_hl: Optional[Tensor], up_hl: Optional[Tensor],
                 bias: Optional[Tensor], out_fp32: bool) -> Tensor:
     """``a16 @ w16^T + mid_hl @ up_hl^T + bias`` on tcgen05 CTA pairs (fp32 accumulation)."""
@@ -316,7 +339,7 @@ def _(a16, w16, mid_hl, up_hl, bias, out_fp32):
 EPILOGUES = {"add": _lib.SVDQ_EPI_ADD, "sigmoid_mul": _lib.SVDQ_EPI_SIGMOID_MUL, "silu_mul": _lib.SVDQ_EPI_SILU_MUL}
 
 
-@torch.library.custom_op("svdq_b200::linear_gemm_epi", mutates_args=())
+@_op("linear_gemm_epi")
 def linear_gemm_epi(a16: Tensor, w16: Tensor, mid_hl: Optional[Tensor], up_hl: Optional[Tensor],
                     bias: Optional[Tensor], out_fp32: bool, epilogue: int, aux: Tensor) -> Tensor:
     """``linear_gemm`` whose epilogue combines its output y with ``aux`` (z, [M, N] in the output
@@ -347,6 +370,49 @@ def _(a16, w16, mid_hl, up_hl, bias, out_fp32, epilogue, aux):
     return a16.new_empty((a16.shape[0], w16.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
 
 
+@_op("linear_gemm_group")
+def linear_gemm_group(a16: list[Tensor], w16: list[Tensor], mid_hl: list[Optional[Tensor]],
+                      up_hl: list[Optional[Tensor]], bias: list[Optional[Tensor]], out_fp32: bool) -> list[Tensor]:
+    """Up to four ``linear_gemm`` problems sharing M, K_pad and the low-rank width R2 as one
+    persistent launch (``svdq_linear_gemm_group``)."""
+    n_p = len(a16)
+    _need(1 <= n_p <= 4 and len(w16) == n_p and len(mid_hl) == n_p and len(up_hl) == n_p and len(bias) == n_p,
+          "linear_gemm_group: 1 to 4 problems with one entry per list")
+    _need_cuda("linear_gemm_group", *a16, *w16, *mid_hl, *up_hl, *bias)
+    m, k_pad = a16[0].shape
+    r2s = {0 if t is None or t.numel() == 0 else t.shape[1] for t in mid_hl}
+    _need(len(r2s) == 1, "linear_gemm_group: every problem needs the same low-rank width R2")
+    r2 = r2s.pop()
+    dev = a16[0].device
+    probs = (_lib.GemmProblem * n_p)()
+    outs = []
+    for i in range(n_p):
+        a, w = a16[i], w16[i]
+        _need(a.dtype == torch.float16 and w.dtype == torch.float16, "linear_gemm_group: a16/w16 must be fp16")
+        _need(tuple(a.shape) == (m, k_pad) and w.shape[1] == k_pad, "linear_gemm_group: M / K_pad mismatch")
+        n = w.shape[0]
+        _need(r2 == 0 or (up_hl[i] is not None and tuple(up_hl[i].shape) == (n, r2)),
+              "linear_gemm_group: up_hl shape mismatch")
+        out = torch.empty((m, n), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=dev)
+        outs.append(out)
+        probs[i] = _lib.GemmProblem(a.data_ptr(), w.data_ptr(), mid_hl[i].data_ptr() if r2 else None,
+                                    up_hl[i].data_ptr() if r2 else None,
+                                    None if bias[i] is None else bias[i].data_ptr(), 0, None, 0,
+                                    out.data_ptr(), out.stride(0), n)
+    if m == 0:
+        return outs
+    ws = _gemm_workspace(dev)
+    _lib.call("svdq_linear_gemm_group", probs, n_p, r2, _lib.SVDQ_FP32 if out_fp32 else _lib.SVDQ_BF16, m, k_pad,
+              _p(ws), 0 if ws is None else ws.numel(), _stream(dev))
+    return outs
+
+
+@linear_gemm_group.register_fake
+def _(a16, w16, mid_hl, up_hl, bias, out_fp32):
+    dt = torch.float32 if out_fp32 else torch.bfloat16
+    return [a.new_empty((a.shape[0], w.shape[0]), dtype=dt) for a, w in zip(a16, w16)]
+
+
 def apply_epilogue(y: Tensor, epilogue: Optional[tuple[str, Tensor]]) -> Tensor:
     """The unfused form of an epilogue operation, as torch ops on the linear's output ``y``: the
     sequence the fused GEMM epilogue reproduces."""
@@ -364,7 +430,7 @@ def apply_epilogue(y: Tensor, epilogue: Optional[tuple[str, Tensor]]) -> Tensor:
 
 
 # --------------------------------------------------------------------------- packed-weight GEMM
-@torch.library.custom_op("svdq_b200::prepare_packed", mutates_args=())
+@_op("prepare_packed")
 def prepare_packed(qweight: Tensor, scales: Tensor, w_group: int) -> tuple[Tensor, Tensor, Tensor]:
     """Checkpoint INT4 weight -> the packed-weight GEMM's operands: ``codes [N, K_pad/2]`` u8 in the
     kernel's nibble order, ``scales16`` fp16 in the kernel's tile order (``packed_scales_numel``
@@ -402,7 +468,7 @@ def packed_scales_numel(n: int, k_pad: int, w_group: int) -> int:
     return -(-n // 128) * -(-k_pad // 256) * 128 * (256 // w_group)
 
 
-@torch.library.custom_op("svdq_b200::packed_gemm", mutates_args=())
+@_op("packed_gemm")
 def packed_gemm(a16: Tensor, codes: Tensor, scales16: Tensor, w_group: int, mid_hl: Optional[Tensor],
                 up_hl: Optional[Tensor], bias: Optional[Tensor], out_fp32: bool) -> Tensor:
     """``a16 @ (q * s)^T + mid_hl @ up_hl^T + bias`` with the weight read as packed codes and converted
@@ -429,7 +495,7 @@ def _(a16, codes, scales16, w_group, mid_hl, up_hl, bias, out_fp32):
     return a16.new_empty((a16.shape[0], codes.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
 
 
-@torch.library.custom_op("svdq_b200::w4a4_gemm", mutates_args=())
+@_op("w4a4_gemm")
 def w4a4_gemm(codes8: Tensor, ascales: Tensor, a_group: int, codes: Tensor, scales16: Tensor, w_group: int,
               mid_hl: Optional[Tensor], up_hl: Optional[Tensor], bias: Optional[Tensor], out_fp32: bool) -> Tensor:
     """W4A4 GEMM with kind::i8 tensor-core MMAs on int8 codes (``act_quant_i8``) and the packed weight
@@ -455,3 +521,7 @@ def w4a4_gemm(codes8: Tensor, ascales: Tensor, a_group: int, codes: Tensor, scal
 @w4a4_gemm.register_fake
 def _(codes8, ascales, a_group, codes, scales16, w_group, mid_hl, up_hl, bias, out_fp32):
     return codes8.new_empty((codes8.shape[0], codes.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
+
+
+# The plain implementations of the ops above, same names and arguments.
+eager = types.SimpleNamespace(**_EAGER)

@@ -13,7 +13,8 @@
   ``attn.to_gate`` on the attention output, ``attn.to_out.0``, pre-RMSNorm
   gated MLP ``ff.down(silu(ff.gate(h)) * ff.up(h))``, residual adds.  The gate
   products and the residual adds run in the epilogues of the GEMMs whose
-  outputs they consume (``SVDQuantLinear.forward(x, epilogue=...)``).  Timestep
+  outputs they consume (``SVDQuantLinear.forward(x, epilogue=...)``), and the
+  q / k / v projections run as one grouped GEMM launch (``grouped_forward``).  Timestep
   modulation and RoPE are left out; every quantized linear has the exact
   shape and module path of the real model (``transformer_blocks.{i}.attn.to_q``
   ...), so the checkpoint, LoRA and offload paths address it unchanged.
@@ -33,7 +34,7 @@ from torch import nn
 
 from . import ops
 from .config import BackendKind
-from .linear import SVDQuantLinear
+from .linear import SVDQuantLinear, grouped_forward
 from .load import CONFIG_NAME, TENSORS_NAME, load_svdquant_transformer
 from .lora import load_svdquant_lora_adapters
 from .quant import random_state
@@ -126,9 +127,11 @@ class _Attention(nn.Module):
     def forward(self, h: torch.Tensor, b: int, l: int, residual: torch.Tensor | None = None) -> torch.Tensor:
         """``to_out(o * sigmoid(to_gate(h)))``, plus ``residual`` when given."""
         c = self.cfg
-        q = self.to_q(h).view(b, l, c.heads, c.head_dim).transpose(1, 2)
-        k = self.to_k(h).view(b, l, c.kv_heads, c.head_dim).transpose(1, 2)
-        v = self.to_v(h).view(b, l, c.kv_heads, c.head_dim).transpose(1, 2)
+        # q / k / v read the same h: one grouped GEMM launch when they are SVDQuant layers
+        q, k, v = grouped_forward([self.to_q, self.to_k, self.to_v], h)
+        q = q.view(b, l, c.heads, c.head_dim).transpose(1, 2)
+        k = k.view(b, l, c.kv_heads, c.head_dim).transpose(1, 2)
+        v = v.view(b, l, c.kv_heads, c.head_dim).transpose(1, 2)
         o = F.scaled_dot_product_attention(q, k, v, enable_gqa=True)
         o = o.transpose(1, 2).reshape(b * l, c.heads * c.head_dim)
         gated = _linear(self.to_gate, h, ("sigmoid_mul", o))

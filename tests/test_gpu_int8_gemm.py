@@ -75,9 +75,13 @@ def test_act_quant_i8_edges():
 
 
 def _module_pair(st):
+    """The packed layer routes every batch the int8-code GEMM takes (up to 64 tokens) to it; the
+    module's default threshold (INT8_PATH_MAX_TOKENS) is lower, where the fp16-operand packed GEMM
+    is faster."""
     from krea2_svdquant_b200.linear import SVDQuantLinear
-    return (SVDQuantLinear(st, backend="b200", weight_operand="packed"),
-            SVDQuantLinear(st, backend="b200", weight_operand="fp16"))
+    packed = SVDQuantLinear(st, backend="b200", weight_operand="packed")
+    packed.INT8_PATH_MAX_TOKENS = 64
+    return packed, SVDQuantLinear(st, backend="b200", weight_operand="fp16")
 
 
 @pytest.mark.parametrize("m,k,n,r,grp,bias", [
