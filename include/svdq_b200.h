@@ -87,6 +87,15 @@ int svdq_device_error(int* code, int clear);
 int svdq_selftest_bounded_wait(int limit_us, cudaStream_t stream);
 
 /*
+ * Diagnostic for the GEMM epilogue's activations: out[i] = bf16(sigmoid(in[i])) for
+ * SVDQ_EPI_SIGMOID_MUL or bf16(silu(in[i])) for SVDQ_EPI_SILU_MUL, computed by the device code
+ * svdq_linear_gemm_epi uses for bf16 output (fast instructions with an exact fallback near bf16
+ * rounding midpoints).  in / out: n bf16 values.  Lets a test compare it with torch.sigmoid /
+ * torch.nn.functional.silu over every bf16 input.
+ */
+int svdq_selftest_epilogue_act(int epilogue, const void* in, void* out, int n, cudaStream_t stream);
+
+/*
  * Device workspace (bytes) the activation passes need for the low-rank
  * down-projection: the fp32 partial sums of the K slices, which a second
  * launch of the same call adds in slice order (deterministic) into mid_hl.
@@ -296,8 +305,8 @@ typedef struct svdq_gemm_problem {
  * numbered problem after problem and the CTA pairs walk them as one list, so a small problem
  * (few tiles) fills the waves of the others instead of leaving a ragged last wave of its own; the
  * split tail (workspace) applies to the group's last wave.  Each problem computes what
- * svdq_linear_gemm_epi computes for it.  num_problems in [1, 4]; arguments as
- * svdq_linear_gemm_epi.
+ * svdq_linear_gemm_epi computes for it.  num_problems in [1, 4]; every problem takes the same
+ * epilogue operation (the kernel is compiled per operation); arguments as svdq_linear_gemm_epi.
  */
 int svdq_linear_gemm_group(const svdq_gemm_problem* problems, int num_problems, int R2,
                            int out_dtype, int M, int K_pad,

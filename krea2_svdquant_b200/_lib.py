@@ -32,6 +32,7 @@ SIGNATURES = {
     "svdq_version": ([], ctypes.c_char_p),
     "svdq_device_error": ([ctypes.POINTER(c_int), c_int], c_int),
     "svdq_selftest_bounded_wait": ([c_int, c_void_p], c_int),
+    "svdq_selftest_epilogue_act": ([c_int, c_void_p, c_void_p, c_int, c_void_p], c_int),
     "svdq_act_quant_workspace_bytes": ([c_int, c_int, c_int, c_int], ctypes.c_size_t),
     "svdq_act_quant": ([c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
                         c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int,

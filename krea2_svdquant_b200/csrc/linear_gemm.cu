@@ -86,9 +86,9 @@ struct GemmProblem {
   const __nv_bfloat16* bias;
   void* out;
   int64_t ldo;
-  const void* aux;  // epilogue operand z [M, N] in out's dtype (row stride ld_aux), or null
+  const void* aux;  // epilogue operand z [M, N] in out's dtype (row stride ld_aux); the operation is
+                    // the kernel's EPI template parameter, shared by the problems of a launch
   int64_t ld_aux;
-  int epi;          // kEpi*: what the epilogue does with y = acc + bias and z
   int N;
   int num_n_blocks;
   int tile_start;   // index of the problem's first tile
@@ -149,22 +149,49 @@ enum : int {
 
 __device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
-template <bool F32>
-__device__ __forceinline__ void epi_apply(int op, float (&v)[8], const float (&z)[8]) {
+// sigmoid(v) or silu(v) in fp32 as torch evaluates them (expf, IEEE division).
+template <int EPI>
+__device__ __noinline__ float act_exact(float v) {
+  return EPI == kEpiSigmoidMul ? 1.0f / (1.0f + expf(-v)) : v / (1.0f + expf(-v));
+}
+// The same rounded to bf16, from the approximate exponential and division instructions.  For
+// |v| <= 64 they differ from the exact fp32 value by at most ~85 ulp (__expf: 2 + 1.173|v| ulp,
+// __fdividef: 2 ulp, plus the roundings), so a result whose low 16 bits lie more than 256 ulp
+// from the bf16 rounding midpoint 0x8000 rounds to the same bf16 as the exact value; the others,
+// and |v| > 64 or NaN, take the exact path (out of line: 128 inlined copies per tile would overflow
+// the instruction cache and stall the MMA-issuing thread).  tests/test_gpu_epilogue.py checks all
+// 65536 bf16 inputs against torch.
+template <int EPI>
+__device__ __forceinline__ float act_bf16(float v) {
+  if (fabsf(v) <= 64.0f) {
+    const float r = __fdividef(1.0f, 1.0f + __expf(-v));
+    const float s = EPI == kEpiSigmoidMul ? r : v * r;
+    if ((__float_as_uint(s) & 0xFFFFu) - 0x7F00u > 0x200u) return bf16r(s);
+  }
+  return bf16r(act_exact<EPI>(v));
+}
+
+// The operation on 8 outputs (the kernel is instantiated per operation, so a launch without one
+// carries no epilogue-operand code).  fp32 output evaluates the activation exactly, out of line.
+template <bool F32, int EPI>
+__device__ __noinline__ void epi_act8_f32(float (&v)[8], const float (&z)[8]) {
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const float y = F32 ? v[e] : bf16r(v[e]);
-    float r;
-    if (op == kEpiAdd) {
-      r = z[e] + y;
-    } else if (op == kEpiSigmoidMul) {
-      const float sg = 1.0f / (1.0f + expf(-y));
-      r = z[e] * (F32 ? sg : bf16r(sg));
-    } else {
-      const float sl = z[e] / (1.0f + expf(-z[e]));
-      r = (F32 ? sl : bf16r(sl)) * y;
+  for (int e = 0; e < 8; ++e)
+    v[e] = EPI == kEpiSigmoidMul ? z[e] * act_exact<EPI>(v[e]) : act_exact<EPI>(z[e]) * v[e];
+}
+template <bool F32, int EPI>
+__device__ __forceinline__ void epi_apply(float (&v)[8], const float (&z)[8]) {
+  if constexpr (EPI == kEpiAdd) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = z[e] + (F32 ? v[e] : bf16r(v[e]));
+  } else if constexpr (F32) {
+    epi_act8_f32<F32, EPI>(v, z);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float y = bf16r(v[e]);
+      v[e] = EPI == kEpiSigmoidMul ? z[e] * act_bf16<EPI>(y) : act_bf16<EPI>(z[e]) * y;
     }
-    v[e] = r;
   }
 }
 
@@ -288,7 +315,7 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
   return v;
 }
 
-template <bool OUT_F32>
+template <bool OUT_F32, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     linear_gemm_kernel(const __grid_constant__ TmaSet maps, const __grid_constant__ GemmArgs args) {
   constexpr int kOutBytes = OUT_F32 ? 4 : 2;
@@ -475,9 +502,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // one before the accumulator wait), fp32 (twice the registers) at the chunk's start;
       // streamed with an evict-first hint, it is read once
       const int grow = m0 + row;
-      const bool use_aux = P.epi != kEpiNone && !contrib;
+      const bool use_aux = EPI != kEpiNone && !contrib;
       const uint8_t* aux_row = static_cast<const uint8_t*>(P.aux) + (size_t)grow * P.ld_aux * kOutBytes;
-      uint4 ax[kAuxBufs][kAuxWords];
+      uint4 ax[EPI != kEpiNone ? kAuxBufs : 1][kAuxWords];
       auto load_aux = [&](int c, uint4 (&d)[kAuxWords]) {
 #pragma unroll
         for (int i = 0; i < kAuxWords; ++i) {
@@ -598,7 +625,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   v[2 * e + 1] += f.y;
                 }
               }
-              if (use_aux) {
+              if constexpr (EPI != kEpiNone) {
+               if (use_aux) {
                 float z[8];
                 if constexpr (OUT_F32) {
                   const uint4 z0 = ax[c % kAuxBufs][2 * (i / 8)], z1 = ax[c % kAuxBufs][2 * (i / 8) + 1];
@@ -616,7 +644,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     z[2 * e + 1] = f.y;
                   }
                 }
-                epi_apply<OUT_F32>(P.epi, v, z);
+                epi_apply<OUT_F32, EPI>(v, z);
+               }
               }
               if constexpr (OUT_F32) {
                 float4* o = reinterpret_cast<float4*>(static_cast<float*>(P.out) + rbase + n);
@@ -803,7 +832,6 @@ int launch_linear_gemm_group(const svdq_gemm_problem* probs, int np, int R2, int
     g.bias = static_cast<const __nv_bfloat16*>(q.bias);
     g.out = q.out;
     g.ldo = q.ldo;
-    g.epi = q.epilogue;
     g.aux = q.epilogue != kEpiNone ? q.aux : nullptr;
     g.ld_aux = q.epilogue != kEpiNone ? q.ld_aux : 0;
     g.N = q.N;
@@ -824,7 +852,17 @@ int launch_linear_gemm_group(const svdq_gemm_problem* probs, int np, int R2, int
   a.n_lr = R2 / 64;
   a.iters = a.n_k + a.n_lr;
   a.err = err;
-  auto kern = out_dtype == SVDQ_FP32 ? linear_gemm_kernel<true> : linear_gemm_kernel<false>;
+  const int epi = probs[0].epilogue;
+  for (int i = 1; i < np; ++i)
+    if (probs[i].epilogue != epi)
+      return set_error(SVDQ_ERR_INVALID_ARGUMENT, w + ": every problem of a group takes the same epilogue operation");
+  using Kern = void (*)(const TmaSet, const GemmArgs);
+  static const Kern kerns[2][4] = {
+      {linear_gemm_kernel<false, kEpiNone>, linear_gemm_kernel<false, kEpiAdd>,
+       linear_gemm_kernel<false, kEpiSigmoidMul>, linear_gemm_kernel<false, kEpiSiluMul>},
+      {linear_gemm_kernel<true, kEpiNone>, linear_gemm_kernel<true, kEpiAdd>,
+       linear_gemm_kernel<true, kEpiSigmoidMul>, linear_gemm_kernel<true, kEpiSiluMul>}};
+  const Kern kern = kerns[out_dtype == SVDQ_FP32 ? 1 : 0][epi];
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
   if (e != cudaSuccess) return check_cuda(e, (w + ": shared memory attribute").c_str());
   const int max_pairs = max_resident_pairs(reinterpret_cast<const void*>(kern));
@@ -940,7 +978,7 @@ extern "C" int svdq_linear_gemm_schedule(int M, int N, int K_pad, int R2, int wi
   if (!out4) return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_linear_gemm_schedule: out4 is NULL");
   if (!(M >= 0 && N > 0 && K_pad > 0 && K_pad % 64 == 0 && R2 >= 0 && R2 % 64 == 0))
     return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_linear_gemm_schedule: bad M/N/K_pad/R2");
-  auto kern = svdq::linear_gemm_kernel<false>;
+  auto kern = svdq::linear_gemm_kernel<false, svdq::kEpiNone>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)svdq::SMEM_BYTES);
   if (e != cudaSuccess) return svdq::check_cuda(e, "svdq_linear_gemm_schedule: shared memory attribute");
   const int tiles = ((M + 2 * svdq::BM - 1) / (2 * svdq::BM)) * ((N + svdq::BN - 1) / svdq::BN);
@@ -952,4 +990,28 @@ extern "C" int svdq_linear_gemm_schedule(int M, int N, int K_pad, int R2, int wi
   out4[2] = sc.tail_len;
   out4[3] = sc.tail_total;
   return SVDQ_OK;
+}
+
+namespace svdq {
+namespace {
+template <int EPI>
+__global__ void epilogue_act_selftest_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __float2bfloat16_rn(act_bf16<EPI>(__bfloat162float(in[i])));
+}
+}  // namespace
+}  // namespace svdq
+
+extern "C" int svdq_selftest_epilogue_act(int epilogue, const void* in, void* out, int n, cudaStream_t stream) {
+  if (!(epilogue == svdq::kEpiSigmoidMul || epilogue == svdq::kEpiSiluMul) || !in || !out || n < 0)
+    return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_selftest_epilogue_act: bad arguments");
+  if (n == 0) return SVDQ_OK;
+  const dim3 grid((n + 255) / 256), block(256);
+  const auto* x = static_cast<const __nv_bfloat16*>(in);
+  auto* y = static_cast<__nv_bfloat16*>(out);
+  if (epilogue == svdq::kEpiSigmoidMul)
+    svdq::epilogue_act_selftest_kernel<svdq::kEpiSigmoidMul><<<grid, block, 0, stream>>>(x, y, n);
+  else
+    svdq::epilogue_act_selftest_kernel<svdq::kEpiSiluMul><<<grid, block, 0, stream>>>(x, y, n);
+  return svdq::check_launch("svdq_selftest_epilogue_act");
 }

@@ -78,6 +78,25 @@ def test_epilogue_matches_unfused(op, shape, out_fp32):
     assert _rel(fused, ref) <= (1e-5 if out_fp32 else TOL_FP64)
 
 
+@pytest.mark.parametrize("op", ["sigmoid_mul", "silu_mul"])
+def test_epilogue_activation_every_bf16(op):
+    """The bf16-output activation (fast exponential and division, exact fallback near rounding
+    midpoints) against torch's own sigmoid / silu on every one of the 65536 bf16 bit patterns."""
+    from krea2_svdquant_b200 import _lib
+    bits = torch.arange(65536, dtype=torch.int32, device="cuda").to(torch.int16)
+    x = bits.view(torch.bfloat16)
+    out = torch.empty_like(x)
+    code = _lib.SVDQ_EPI_SIGMOID_MUL if op == "sigmoid_mul" else _lib.SVDQ_EPI_SILU_MUL
+    st = _lib.lib().svdq_selftest_epilogue_act(code, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                               65536, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == 0, _lib.lib().svdq_last_error().decode()
+    want = torch.sigmoid(x) if op == "sigmoid_mul" else torch.nn.functional.silu(x)
+    nan = torch.isnan(want)
+    assert torch.equal(torch.isnan(out), nan)
+    diff = (out.view(torch.int16) != want.view(torch.int16)) & ~nan
+    assert int(diff.sum()) == 0, x[diff][:8].float().tolist()
+
+
 def test_epilogue_in_place():
     """The operand may be the output buffer itself (each element is read before it is written).
     Both launches run without a workspace (unsplit), so only the aliasing differs."""

@@ -118,10 +118,17 @@ def test_group_rejects_bad_arguments():
         ops.linear_gemm_group(a16, w16, mid, up, bias, False)  # five problems
     with pytest.raises(ValueError):
         ops.linear_gemm_group(a16[:2], w16[:2], [mid[0], None], up[:2], bias[:2], False)  # R2 differs
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     probs = (_lib.GemmProblem * 5)()
-    st = _lib.lib().svdq_linear_gemm_group(probs, 5, 64, _lib.SVDQ_BF16, 256, 256, None, 0,
-                                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-    assert st == 1
+    assert _lib.lib().svdq_linear_gemm_group(probs, 5, 64, _lib.SVDQ_BF16, 256, 256, None, 0, stream) == 1
+    # the epilogue operation is per launch: a group mixing operations is rejected
+    outs = [torch.empty(256, 256, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    z = torch.zeros(256, 256, device="cuda", dtype=torch.bfloat16)
+    probs = (_lib.GemmProblem * 2)()
+    for i, epi in enumerate((_lib.SVDQ_EPI_ADD, _lib.SVDQ_EPI_SILU_MUL)):
+        probs[i] = _lib.GemmProblem(a16[i].data_ptr(), w16[i].data_ptr(), mid[i].data_ptr(), up[i].data_ptr(),
+                                    bias[i].data_ptr(), epi, z.data_ptr(), 256, outs[i].data_ptr(), 256, 256)
+    assert _lib.lib().svdq_linear_gemm_group(probs, 2, 64, _lib.SVDQ_BF16, 256, 256, None, 0, stream) == 1
     torch.cuda.synchronize()
 
 
