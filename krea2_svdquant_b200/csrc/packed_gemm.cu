@@ -9,7 +9,8 @@
 // over a dequantized weight.
 //
 // Orientation (swap AB): the weight rows are the MMA's M (128 TMEM lanes per CTA) and the tokens
-// its N (TN columns, 16 to 128), so 16 tokens cost a 128x16 MMA instead of most of a 128x256 tile.
+// its N (TN columns, 16 to 256), so 16 tokens cost a 128x16 MMA instead of most of a 128x256 tile,
+// and up to 256 tokens share one conversion of each weight tile.
 // The accumulator lands in TMEM as [weight row][token] and leaves transposed.
 //
 // Tensor memory holds the accumulator (columns [0, TN)) and a ring of converted weight stages
@@ -35,16 +36,21 @@
 // one slice of rows over all KS partials through distributed shared memory, in rank order (a
 // fixed order: results are deterministic), adds the bias and stores.
 //
-// The converters are software-pipelined: a group's TMEM stores drain while the next group
-// converts, and are published (tcgen05.wait::st, then the stage barriers) after it.
+// The converters convert a group into registers while the MMAs still hold its TMEM slots, store it
+// once they are free and publish it right away (tcgen05.wait::st, then the group's barrier).
+// Publishing only after converting the next group (to hide the store drain) put a conversion on
+// the MMAs' critical path: measured at 256 tokens, the MMA thread then idled 0.3-0.5 us per group.
 //
 // Roles (20 warps): warp 0 TMA of packed codes (4-deep ring of 128 rows x 256 k groups, 128-byte
 // swizzle so the converters' shared loads are free of bank conflicts); warp 2 TMA of
 // the token tiles (a16, or mid_hl with up_hl for the low-rank stages); warp 1 TMEM allocation and
 // the MMA issue; warps 4-19 conversion (four warps per TMEM lane quarter); warps 4-7 the epilogue.
 // The single-thread roles (TMA producers, MMA issue) wait by spinning on mbarrier.test_wait; the 16
-// converter warps and the epilogue wait with try_wait, which suspends them, so that waiting
-// converters do not take issue slots and shared-memory bandwidth from the MMA thread on their SMSP.
+// converter warps and the epilogue poll test_wait with a short nanosleep in between, so that waiting
+// converters take few issue slots from the MMA thread on their SMSP (a suspending try_wait takes
+// 0.13-0.36 us to return even on a completed phase, twice per code group on the converters' chain).
+// The converters publish a code group's four TMEM stages as soon as they are stored, and the MMAs
+// release them, with one barrier per group.
 // Every wait is bounded (error word codes 0x51xx-0x54xx); a wait that runs out raises the CTA's
 // abort flag and every role leaves its loop, so all CTAs still meet at the cluster barriers.
 #include <algorithm>
@@ -74,7 +80,7 @@ struct PwLayout {
   static constexpr uint32_t kAccCols = TN < 32 ? 32 : TN;                     // accumulator columns
   static constexpr int kAStages = std::min<int>(12, (PW_TMEM_COLS - kAccCols) / PW_STAGE_COLS) / PW_SUB * PW_SUB;
   static constexpr uint32_t kB = (uint32_t)TN * PW_KB * 2;                    // token tile bytes per stage
-  static constexpr int kBStages = kB <= 2048 ? 16 : kB <= 4096 ? 12 : 6;
+  static constexpr int kBStages = kB <= 2048 ? 16 : kB <= 4096 ? 12 : kB <= 16384 ? 6 : 3;
   static constexpr uint32_t kOffL = 0;                                        // low-rank A ring
   static constexpr uint32_t kOffB = kOffL + PW_LSTAGES * PW_A_BYTES;
   static constexpr uint32_t kOffP = kOffB + kBStages * kB;
@@ -310,16 +316,23 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
         if (!(ok = mbar_spin_wait(bar(bars->full_b[bs]), bph, abort_flag, args.err, kPwWaitMmaTile))) break;
         const uint64_t db = desc_k_sw128(b_ring + (uint32_t)bs * L::kB);
         if (it < n_res) {
+          // a code group's stages are published together and released together, on the barriers
+          // of the group's last TMEM slot (one wait and one commit per group, not per stage)
           const int as = it % AS;
-          if (!(ok = mbar_spin_wait(bar(bars->conv[as]), (uint32_t)(it / AS) & 1u, abort_flag, args.err, kPwWaitMmaConv)))
-            break;
-          tc_fence_after();
+          const int gi = it / PW_SUB;
+          const int gslot = (gi * PW_SUB + PW_SUB - 1) % AS;
+          if (it % PW_SUB == 0) {
+            if (!(ok = mbar_spin_wait(bar(bars->conv[gslot]), (uint32_t)(gi / (AS / PW_SUB)) & 1u, abort_flag,
+                                      args.err, kPwWaitMmaConv)))
+              break;
+            tc_fence_after();
+          }
           const uint32_t ta = tmem + L::kAccCols + (uint32_t)as * PW_STAGE_COLS;
 #pragma unroll
           for (int kk = 0; kk < PW_KB / 16; ++kk)
             umma_f16_1_tmem_a(tmem, ta + (uint32_t)(kk * 8), db + (uint64_t)(kk * 2), idesc_res,
                               (it > 0 || kk > 0) ? 1u : 0u);
-          umma_commit_1(bar(bars->empty_a[as]));
+          if (it % PW_SUB == PW_SUB - 1 || it == n_res - 1) umma_commit_1(bar(bars->empty_a[gslot]));
         } else {
           const int ls = (it - n_res) % PW_LSTAGES;
           tc_fence_after();
@@ -353,13 +366,12 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
     const uint32_t r7 = (uint32_t)(row & 7);
     const int spg = args.spg, gshift = spg == 8 ? 5 : spg == 4 ? 6 : spg == 2 ? 7 : 8;  // log2(G)
     bool ok = true;
-    int prev_nsub = 0;  // stages of the previous group whose TMEM stores are not yet published
     for (int gi = 0; gi < n_groups && ok; ++gi) {
       const int ps = gi % PW_PSTAGES;
       const int it0 = gi * PW_SUB;                 // first stage of the group (CTA-relative)
       const int nsub = min(PW_SUB, n_res - it0);
-      ok = mbar_wait(bar(bars->full_p[ps]), (uint32_t)(gi / PW_PSTAGES) & 1u, abort_flag, args.err,
-                          kPwWaitConvPacked);
+      ok = wait_spin(bar(bars->full_p[ps]), (uint32_t)(gi / PW_PSTAGES) & 1u, abort_flag, args.err,
+                     kPwWaitConvPacked);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;  // the lanes of a warp leave together
       const uint32_t srow = s_ring + (uint32_t)ps * PW_S_BYTES + (uint32_t)(row * spg) * 2u;
       const uint32_t prow = p_ring + (uint32_t)ps * PW_P_BYTES + code_row + 8u * (uint32_t)(part & 1);
@@ -383,41 +395,29 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive_cta(bar(bars->empty_p[ps]));  // every lane has consumed its codes
-      // the previous group's TMEM stores drained while this group converted: publish them
-      if (gi > 0) {
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0)
-          for (int j = 0; j < prev_nsub; ++j) mbar_arrive_cta(bar(bars->conv[(it0 - PW_SUB + j) % AS]));
-      }
+      // this group's TMEM slots are free once the MMAs of the group that used them last are done
+      ok = wait_spin(bar(bars->empty_a[(it0 + PW_SUB - 1) % AS]), ((uint32_t)(gi / (AS / PW_SUB)) & 1u) ^ 1u,
+                     abort_flag, args.err, kPwWaitConvEmpty);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      tc_fence_after();
 #pragma unroll
-      for (int j = 0; j < PW_SUB; ++j) {
-        if (j < nsub) {
-          const int it = it0 + j, as = it % AS;
-          ok = mbar_wait(bar(bars->empty_a[as]), ((uint32_t)(it / AS) & 1u) ^ 1u, abort_flag, args.err,
-                              kPwWaitConvEmpty);
-          if (!(ok = __all_sync(0xffffffffu, ok))) break;
-          tc_fence_after();
-          tmem_st8(tmem + lane_off + L::kAccCols + (uint32_t)as * PW_STAGE_COLS + 8u * (uint32_t)part, v[j]);
-        }
-      }
-      if (!ok) break;
-      prev_nsub = nsub;
-    }
-    if (ok && n_groups > 0) {
+      for (int j = 0; j < PW_SUB; ++j)
+        if (j < nsub)
+          tmem_st8(tmem + lane_off + L::kAccCols + (uint32_t)((it0 + j) % AS) * PW_STAGE_COLS + 8u * (uint32_t)part,
+                   v[j]);
+      // publish the group at once (one arrival per warp on the barrier of its last TMEM slot): the
+      // MMAs wait for nothing but the stores, whose drain is short next to converting a group
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0)
-        for (int j = 0; j < prev_nsub; ++j) mbar_arrive_cta(bar(bars->conv[((n_groups - 1) * PW_SUB + j) % AS]));
+      if (lane == 0) mbar_arrive_cta(bar(bars->conv[(it0 + PW_SUB - 1) % AS]));
     }
     if (warp < 8) {
       // ---------------------------------------------- epilogue: TMEM -> registers -> out or partial
       const int erow = q * 32 + lane;
       const int n = n0 + erow;
       const uint32_t taddr = tmem + lane_off;
-      const bool done = mbar_wait(bar(bars->mma_done), 0, abort_flag, args.err, kPwWaitEpilogue) && !*abort_flag;
+      const bool done = wait_spin(bar(bars->mma_done), 0, abort_flag, args.err, kPwWaitEpilogue) && !*abort_flag;
       if (__all_sync(0xffffffffu, done)) {
         tc_fence_after();
         float bias_v = 0.f;
@@ -535,14 +535,17 @@ struct PwPlan {
   int tn, ks, units_n, units_m;
 };
 
-int pick_tn(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+// 256-token tiles put a 256-token batch into one wave of CTAs that each convert their weight
+// tile once (128-token tiles: two waves, each converting every weight tile again).
+int pick_tn(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256; }
 
 uint32_t pw_smem(int tn) {
   switch (tn) {
     case 16: return PwLayout<16>::kSmem;
     case 32: return PwLayout<32>::kSmem;
     case 64: return PwLayout<64>::kSmem;
-    default: return PwLayout<128>::kSmem;
+    case 128: return PwLayout<128>::kSmem;
+    default: return PwLayout<256>::kSmem;
   }
 }
 
@@ -607,7 +610,8 @@ int launch_pw_tn(int tn, const CUtensorMap& ta, const CUtensorMap& tc, const CUt
     case 16: return launch_pw<16, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
     case 32: return launch_pw<32, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
     case 64: return launch_pw<64, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
-    default: return launch_pw<128, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
+    case 128: return launch_pw<128, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
+    default: return launch_pw<256, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
   }
 }
 

@@ -217,27 +217,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
-// Bounded wait for the multi-warp roles: test_wait polls with a short nanosleep between them, so
-// that waiting warps leave the issue slots of their SM sub-partition to the single-thread MMA and
-// TMA roles (a spinning warp takes a share of them; a suspending try_wait is slow to wake).
-__device__ __forceinline__ bool wait_spin(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
-                                          int where) {
-  if (mbar_test_parity(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    __nanosleep(32);
-    if (mbar_test_parity(bar, parity)) return true;
-    if ((i & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        atomicCAS(err, 0, where);
-        return false;
-      }
-    }
-  }
-}
-
 // Instruction descriptors: D fp32 (kind::f16) or s32 (kind::i8), K-major A and B, M = 128.
 __host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_fmt, int n) { return make_idesc(ab_fmt, ab_fmt, SB_ROWS, n); }
 __host__ __device__ constexpr uint32_t idesc_i8(int n) {

@@ -179,6 +179,27 @@ __device__ __forceinline__ bool mbar_spin_wait(uint32_t bar, uint32_t parity, vo
   }
 }
 
+// Bounded wait for the multi-warp roles: test_wait polls with a short nanosleep between them, so
+// that waiting warps leave the issue slots of their SM sub-partition to the single-thread MMA and
+// TMA roles (a spinning warp takes a share of them; a suspending try_wait is slow to wake).
+__device__ __forceinline__ bool wait_spin(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int where) {
+  if (mbar_test_parity(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(32);
+    if (mbar_test_parity(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicCAS(err, 0, where);
+        return false;
+      }
+    }
+  }
+}
+
 // Bounded wait that ignores the abort flag: used while draining in-flight
 // copies or MMAs after an abort.  Returns false if the limit ran out.
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity,

@@ -87,8 +87,10 @@ def _module_pair(st, backend="b200"):
     (16, 6144, 1536, 32, 64, True),     # to_k shape at 16 tokens: split K over clusters
     (37, 640, 520, 16, 64, False),      # ragged M and N (520 = 4 x 128 + 8)
     (64, 2048, 6144, 32, 128, True),    # group 128
-    (200, 1024, 768, 64, 64, True),     # two token tiles
+    (200, 1024, 768, 64, 64, True),     # one 256-token tile, ragged M
     (256, 1024, 2048, 32, 64, True),    # BASELINE config 1 shape
+    (600, 1024, 768, 32, 64, True),     # three 256-token tiles, the last one ragged
+    (300, 2048, 512, 32, 64, True),     # 256-token tiles split over K in clusters
 ])
 def test_packed_w4a4_vs_staged_oracle(m, k, n, r, grp, bias):
     from krea2_svdquant_b200.quant import make_synthetic_state
