@@ -428,7 +428,8 @@ def measure_small_batch(dev, flush, iters: int) -> dict:
     """The config-2/4 layer (K6144 N16384, rank 32, group 64, bias) at small batches, where the
     weight bytes bound the GEMM.  Packed-weight GEMMs (half-byte codes + fp16 scales, no fp16 weight
     in memory): the int8-code W4A4 GEMM (kind::i8, per-group rescale; batches up to 64 tokens) and
-    the fp16-operand packed GEMM (the W4A16 path) against the fp16-weight GEMM, each against its
+    the fp16-operand packed GEMM (the W4A16 path) against the fp16-weight GEMMs (CTA-pair tiles, and
+    the small-batch one with weight rows as the MMA's M), each against its
     roofline max(bytes / HBM peak, 2MNK / bf16 peak).  Kernel times with the L2 flushed; the
     module's whole forward (activation pass + GEMM) of the packed layer as ``linear_us``."""
     import torch
@@ -471,6 +472,8 @@ def measure_small_batch(dev, flush, iters: int) -> dict:
             m * K * 2, w_pk)
         put("fp16_gemm", statistics.median(_device_times(
             lambda: ops.linear_gemm(a16, p.w16, mid, p.up_hl, p.bias, False), iters, flush)), m * K * 2, N * K * 2)
+        put("fp16_small_gemm", statistics.median(_device_times(
+            lambda: ops.linear_gemm_small(a16, p.w16, mid, p.up_hl, p.bias, False), iters, flush)), m * K * 2, N * K * 2)
         t_lin = statistics.median(_device_times(lambda: mod_pk(x), iters, flush))
         row.update({"linear_packed_us": round(t_lin * 1e3, 2), "linear_packed_tops": round(flops / (t_lin * 1e-3) / 1e12, 1),
                     "linear_packed_path": ("int8 codes + kind::i8 GEMM" if m <= SVDQuantLinear.INT8_PATH_MAX_TOKENS

@@ -233,6 +233,24 @@ int svdq_linear_gemm(const void* a16, const void* w16,
                      cudaStream_t stream);
 
 /*
+ * svdq_linear_gemm for small batches, swap-AB: the weight rows are the tcgen05 MMA's M (128 per
+ * CTA) and the tokens its N (16 to 256 per tile), so a 16-token batch runs 128x16 MMAs instead
+ * of 256x256 tiles that are mostly padding, and the layer is bound by the bytes of w16 rather
+ * than by MMAs.  Same computation, operands and output as svdq_linear_gemm; the fp32 summation
+ * order differs (split K over clusters of 2-8 CTAs when the tiles would leave SMs idle, summed in
+ * a fixed order, so results are deterministic).  The slot of the reference's small-batch Triton
+ * path (kernels/triton/generic_int4.py:19-133).
+ *   a16 and w16 16-byte aligned; K_pad % 64 == 0, N % 8 == 0, ldo % 8 == 0, R2 % 64 == 0;
+ *   out_dtype in {SVDQ_BF16, SVDQ_FP32}; bias may be NULL.  Any M; meant for M <= 256.
+ */
+int svdq_linear_gemm_small(const void* a16, const void* w16,
+                           const void* mid_hl, const void* up_hl, int R2,
+                           const void* bias,
+                           void* out, int out_dtype, int64_t ldo,
+                           int M, int N, int K_pad,
+                           cudaStream_t stream);
+
+/*
  * Bytes of the split-tail workspace of svdq_linear_gemm_ws on the current
  * device (sync words plus one fp32 256x128 partial tile per CTA of a full grid).
  */

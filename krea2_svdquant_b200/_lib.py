@@ -66,6 +66,8 @@ SIGNATURES = {
     "svdq_linear_gemm_epi": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int64,
                               c_void_p, c_int, c_int64, c_int, c_int, c_int, c_void_p, ctypes.c_size_t, c_void_p],
                              c_int),
+    "svdq_linear_gemm_small": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int64,
+                                c_int, c_int, c_int, c_void_p], c_int),
     "svdq_linear_gemm_group": ([ctypes.POINTER(GemmProblem), c_int, c_int, c_int, c_int, c_int, c_void_p,
                                 ctypes.c_size_t, c_void_p], c_int),
     "svdq_linear_gemm_schedule": ([c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)], c_int),

@@ -75,7 +75,10 @@ constexpr uint32_t PW_TMEM_COLS = 512;
 constexpr uint32_t PW_STAGE_COLS = PW_KB / 2;         // TMEM columns of one converted stage
 static_assert(PW_CONV_WARPS * 32 * 8 * PW_SUB == (int)PW_P_BYTES, "four 8-byte pieces of codes per converter thread");
 
-template <int TN>
+// W16: the weight arrives as fp16 tiles (the load-time q * s operand) by TMA into a shared-memory
+// ring and the MMA reads A from there; no conversion.  Otherwise packed codes are converted into a
+// TMEM ring.
+template <int TN, bool W16 = false>
 struct PwLayout {
   static constexpr uint32_t kAccCols = TN < 32 ? 32 : TN;                     // accumulator columns
   static constexpr int kAStages = std::min<int>(12, (PW_TMEM_COLS - kAccCols) / PW_STAGE_COLS) / PW_SUB * PW_SUB;
@@ -84,8 +87,9 @@ struct PwLayout {
   static constexpr uint32_t kOffL = 0;                                        // low-rank A ring
   static constexpr uint32_t kOffB = kOffL + PW_LSTAGES * PW_A_BYTES;
   static constexpr uint32_t kOffP = kOffB + kBStages * kB;
-  static constexpr uint32_t kOffS = kOffP + PW_PSTAGES * PW_P_BYTES;         // group-scale ring
-  static constexpr uint32_t kOffBar = kOffS + PW_PSTAGES * PW_S_BYTES;
+  static constexpr int kWStages = W16 ? (TN >= 128 ? 6 : 8) : 0;             // fp16 weight ring (W16)
+  static constexpr uint32_t kOffS = kOffP + (W16 ? kWStages : PW_PSTAGES) * PW_P_BYTES;  // group-scale ring
+  static constexpr uint32_t kOffBar = kOffS + (W16 ? 0 : PW_PSTAGES * PW_S_BYTES);
   static constexpr uint32_t kSmem = kOffBar + 1024 + 1024;                   // barriers + alignment slack
   static_assert(kB % 1024 == 0, "token tiles keep 1 KiB alignment for the 128-byte swizzle");
   static_assert(kAStages >= 2 * PW_SUB, "the TMEM weight ring holds at least two code groups (one converting, one draining)");
@@ -179,13 +183,13 @@ __device__ __forceinline__ void convert_word(uint32_t w, uint32_t s_lo, uint32_t
   o[3] = h2_mul(h2_sub((w8 & 0x00F000F0u) | kExp, kOffHi), s_hi);
 }
 
-template <int TN, bool OUT_F32>
+template <int TN, bool OUT_F32, bool W16 = false>
 __global__ void __launch_bounds__(PW_THREADS, 1)
     packed_gemm_kernel(const __grid_constant__ CUtensorMap tm_a16, const __grid_constant__ CUtensorMap tm_codes,
                        const __grid_constant__ CUtensorMap tm_mid, const __grid_constant__ CUtensorMap tm_up,
                        const PwArgs args) {
-  using L = PwLayout<TN>;
-  constexpr int AS = L::kAStages, BS = L::kBStages;
+  using L = PwLayout<TN, W16>;
+  constexpr int AS = L::kAStages, BS = L::kBStages, WS = L::kWStages > 0 ? L::kWStages : 1;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -221,7 +225,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
       mbar_init(bar(bars->empty_b[s]), 1);
     }
     for (int s = 0; s < AS; ++s) {
-      mbar_init(bar(bars->conv[s]), PW_CONV_WARPS);
+      mbar_init(bar(bars->conv[s]), W16 ? 1 : PW_CONV_WARPS);  // W16: the weight ring's TMA bytes
       mbar_init(bar(bars->empty_a[s]), 1);
     }
     for (int s = 0; s < PW_LSTAGES; ++s) mbar_init(bar(bars->empty_l[s]), 1);
@@ -248,7 +252,26 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
   pdl_wait();  // operands may come from the previous kernel on the stream
   pdl_trigger();
 
-  if (warp == 0) {
+  if (warp == 0 && W16) {
+    if (lane == 0) {
+      // ------------------------------------------------ fp16 weight tiles: 128 rows x 64 k per stage
+      // (tm_codes maps the fp16 weight here; conv / empty_a are the ring's full / empty barriers)
+      uint32_t filled = 0, par = 0;
+      bool ok = true;
+      for (int it = 0; it < n_res && ok; ++it) {
+        const int ws = it % WS;
+        const uint32_t ph = (uint32_t)(it / WS) & 1u;
+        if (!(ok = mbar_spin_wait(bar(bars->empty_a[ws]), ph ^ 1u, abort_flag, args.err, kPwWaitPackedEmpty))) break;
+        mbar_arrive_expect_tx(bar(bars->conv[ws]), PW_P_BYTES);
+        tma_load_2d(p_ring + (uint32_t)ws * PW_P_BYTES, &tm_codes, bar(bars->conv[ws]), (kb0 + it) * PW_KB, n0);
+        filled |= 1u << ws;
+        par = (par & ~(1u << ws)) | (ph << ws);
+      }
+      if (!ok)
+        for (int ws = 0; ws < WS; ++ws)
+          if (filled & (1u << ws)) mbar_wait_drain(bar(bars->conv[ws]), (par >> ws) & 1u, 100000000ull);
+    }
+  } else if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------ packed codes: one 128-row x 256-k group per box
       uint32_t filled = 0, par = 0;
@@ -310,7 +333,19 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
         const uint32_t bph = (uint32_t)(it / BS) & 1u;
         if (!(ok = mbar_spin_wait(bar(bars->full_b[bs]), bph, abort_flag, args.err, kPwWaitMmaTile))) break;
         const uint64_t db = desc_k_sw128(b_ring + (uint32_t)bs * L::kB);
-        if (it < n_res) {
+        if (W16 && it < n_res) {
+          // fp16 weight stage from the shared-memory ring
+          const int ws = it % WS;
+          if (!(ok = mbar_spin_wait(bar(bars->conv[ws]), (uint32_t)(it / WS) & 1u, abort_flag, args.err,
+                                    kPwWaitMmaConv)))
+            break;
+          tc_fence_after();
+          const uint64_t da = desc_k_sw128(p_ring + (uint32_t)ws * PW_P_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < PW_KB / 16; ++kk)
+            umma_f16_1(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc_res, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_1(bar(bars->empty_a[ws]));
+        } else if (it < n_res) {
           // a code group's stages are published together and released together, on the barriers
           // of the group's last TMEM slot (one wait and one commit per group, not per stage)
           const int as = it % AS;
@@ -361,7 +396,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
     const uint32_t r7 = (uint32_t)(row & 7);
     const int spg = args.spg, gshift = spg == 8 ? 5 : spg == 4 ? 6 : spg == 2 ? 7 : 8;  // log2(G)
     bool ok = true;
-    for (int gi = 0; gi < n_groups && ok; ++gi) {
+    for (int gi = 0; gi < (W16 ? 0 : n_groups) && ok; ++gi) {  // W16: nothing to convert
       const int ps = gi % PW_PSTAGES;
       const int it0 = gi * PW_SUB;                 // first stage of the group (CTA-relative)
       const int nsub = min(PW_SUB, n_res - it0);
@@ -572,11 +607,11 @@ PwPlan plan_packed(int M, int N, int K_pad) {
   return p;
 }
 
-template <int TN, bool OUT_F32>
+template <int TN, bool OUT_F32, bool W16 = false>
 int launch_pw(const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMap& tmid, const CUtensorMap& tup,
               const PwArgs& a, int grid, cudaStream_t stream) {
-  auto kern = packed_gemm_kernel<TN, OUT_F32>;
-  constexpr uint32_t smem = PwLayout<TN>::kSmem;
+  auto kern = packed_gemm_kernel<TN, OUT_F32, W16>;
+  constexpr uint32_t smem = PwLayout<TN, W16>::kSmem;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "svdq_packed_gemm: shared memory attribute");
   cudaLaunchConfig_t cfg = {};
@@ -598,15 +633,15 @@ int launch_pw(const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMap& t
   return check_launch("svdq_packed_gemm launch");
 }
 
-template <bool OUT_F32>
+template <bool OUT_F32, bool W16 = false>
 int launch_pw_tn(int tn, const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMap& tmid, const CUtensorMap& tup,
                  const PwArgs& a, int grid, cudaStream_t stream) {
   switch (tn) {
-    case 16: return launch_pw<16, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
-    case 32: return launch_pw<32, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
-    case 64: return launch_pw<64, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
-    case 128: return launch_pw<128, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
-    default: return launch_pw<256, OUT_F32>(ta, tc, tmid, tup, a, grid, stream);
+    case 16: return launch_pw<16, OUT_F32, W16>(ta, tc, tmid, tup, a, grid, stream);
+    case 32: return launch_pw<32, OUT_F32, W16>(ta, tc, tmid, tup, a, grid, stream);
+    case 64: return launch_pw<64, OUT_F32, W16>(ta, tc, tmid, tup, a, grid, stream);
+    case 128: return launch_pw<128, OUT_F32, W16>(ta, tc, tmid, tup, a, grid, stream);
+    default: return launch_pw<256, OUT_F32, W16>(ta, tc, tmid, tup, a, grid, stream);
   }
 }
 
@@ -734,4 +769,59 @@ extern "C" int svdq_packed_gemm(const void* a16, const void* codes, const void* 
   const int grid = p.units_n * p.units_m * p.ks;
   return out_dtype == SVDQ_FP32 ? launch_pw_tn<true>(p.tn, ta, tc, tmid, tup, a, grid, stream)
                                 : launch_pw_tn<false>(p.tn, ta, tc, tmid, tup, a, grid, stream);
+}
+
+extern "C" int svdq_linear_gemm_small(const void* a16, const void* w16, const void* mid_hl, const void* up_hl, int R2,
+                                      const void* bias, void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
+                                      cudaStream_t stream) {
+  using namespace svdq;
+  SVDQ_REQUIRE(a16 && w16 && out, "svdq_linear_gemm_small: null operand pointer");
+  SVDQ_REQUIRE(M >= 0 && N > 0 && K_pad > 0 && K_pad % 64 == 0, "svdq_linear_gemm_small: bad M/N/K_pad");
+  SVDQ_REQUIRE((reinterpret_cast<uintptr_t>(a16) & 15u) == 0 && (reinterpret_cast<uintptr_t>(w16) & 15u) == 0,
+               "svdq_linear_gemm_small: a16 and w16 must be 16-byte aligned");
+  SVDQ_REQUIRE(N % 8 == 0 && ldo >= N && ldo % 8 == 0, "svdq_linear_gemm_small: N and ldo must be multiples of 8, ldo >= N");
+  SVDQ_REQUIRE(R2 >= 0 && R2 % 64 == 0, "svdq_linear_gemm_small: R2 must be a multiple of 64");
+  SVDQ_REQUIRE(R2 == 0 || (mid_hl && up_hl), "svdq_linear_gemm_small: mid_hl/up_hl are NULL");
+  SVDQ_REQUIRE(out_dtype == SVDQ_BF16 || out_dtype == SVDQ_FP32,
+               "svdq_linear_gemm_small: out_dtype must be bf16 or fp32");
+  SVDQ_REQUIRE(!bias || (reinterpret_cast<uintptr_t>(bias) & 1u) == 0, "svdq_linear_gemm_small: bias must be 2-byte aligned");
+  if (M == 0) return SVDQ_OK;
+  int* err = device_error_word();
+  if (!err) return set_error(SVDQ_ERR_CUDA, "svdq_linear_gemm_small: device error word unavailable");
+  const PwPlan p = plan_packed(M, N, K_pad);
+  CUtensorMap ta, tw, tmid, tup;
+  int st;
+  if ((st = make_tma_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a16, K_pad, M, (uint64_t)K_pad * 2, PW_KB, p.tn,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if ((st = make_tma_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w16, K_pad, N, (uint64_t)K_pad * 2, PW_KB, PW_ROWS,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if (R2 > 0) {
+    if ((st = make_tma_2d(&tmid, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, mid_hl, R2, M, (uint64_t)R2 * 2, PW_KB, p.tn,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+    if ((st = make_tma_2d(&tup, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, up_hl, R2, N, (uint64_t)R2 * 2, PW_KB, PW_ROWS,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+  } else {
+    tmid = ta;
+    tup = ta;
+  }
+  PwArgs a;
+  a.scales16 = nullptr;  // the fp16 weight already holds q * s
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.out = out;
+  a.ldo = ldo;
+  a.M = M;
+  a.N = N;
+  a.n_k = K_pad / PW_KB;
+  a.n_lr = R2 / PW_KB;
+  a.spg = 1;
+  a.ks = p.ks;
+  a.units_n = p.units_n;
+  a.err = err;
+  const int grid = p.units_n * p.units_m * p.ks;
+  return out_dtype == SVDQ_FP32 ? launch_pw_tn<true, true>(p.tn, ta, tw, tmid, tup, a, grid, stream)
+                                : launch_pw_tn<false, true>(p.tn, ta, tw, tmid, tup, a, grid, stream);
 }

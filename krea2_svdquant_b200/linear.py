@@ -306,6 +306,8 @@ class SVDQuantLinear(nn.Module):
             epilogue = None
         elif p.w16 is None:
             y = k.packed_gemm(a16, p.codes, p.scales16, self.group_size, *lowrank, p.bias, out_fp32)
+        elif self._small_gemm(x2.shape[0]):
+            y = k.linear_gemm_small(a16, p.w16, *lowrank, p.bias, out_fp32)
         else:
             y = k.linear_gemm(a16, p.w16, *lowrank, p.bias, out_fp32)
         if self.check_device_errors:
@@ -315,8 +317,8 @@ class SVDQuantLinear(nn.Module):
     def _fusable_operand(self, epilogue, m: int, out_fp32: bool) -> torch.Tensor | None:
         """The epilogue operand as the fused GEMM epilogue takes it ([M, N] rows, output dtype,
         16-byte aligned rows), or None when the operation has to run unfused."""
-        if epilogue is None:
-            return None
+        if epilogue is None or self._small_gemm(m):
+            return None  # small batches take the small GEMM, which has no epilogue operations
         op, z = epilogue
         n = self.original_shape[0]
         if op not in ops.EPILOGUES or not z.is_cuda or z.numel() != m * n:
@@ -327,6 +329,17 @@ class SVDQuantLinear(nn.Module):
         if z2.stride(1) != 1 or z2.stride(0) % 8 or z2.data_ptr() % 16:
             return None
         return z2
+
+    # Small batches take the small-batch fp16-weight GEMM (weight rows as the MMA's M, tokens as its
+    # N) instead of the CTA-pair GEMM's 256x256 tiles, where it measured faster on B200 (K6144, L2
+    # flushed): always up to 64 tokens (N16384: 45 against 47-57 us; N6144: 29-31 against 35-39;
+    # N1536: 16 against 31), up to 128 tokens for N <= 8192 and up to 384 for N <= 2048 (N1536 at
+    # 384 tokens: 27 against 35 us).
+    SMALL_GEMM_MAX_TOKENS = 384
+
+    def _small_gemm(self, m: int) -> bool:
+        n = self.original_shape[0]
+        return m <= 64 or (m <= 128 and n <= 8192) or (m <= self.SMALL_GEMM_MAX_TOKENS and n <= 2048)
 
     # Batches up to this many tokens take the int8-code GEMM when the weight is packed (W4A4).
     # Measured on B200 at K6144 N16384 (GEMM only, L2 flushed): int8 codes 33.8 / 34.6 / 41.4 us
@@ -420,7 +433,10 @@ def _groupable(layers: list[nn.Module], x: torch.Tensor) -> bool:
         return False
     if not all(isinstance(layer, SVDQuantLinear) for layer in layers):
         return False
-    row_blocks = -(-(x.numel() // max(1, x.shape[-1])) // 256)
+    m = x.numel() // max(1, x.shape[-1])
+    if any(layer._small_gemm(m) for layer in layers):
+        return False  # those layers take the small-batch GEMM
+    row_blocks = -(-m // 256)
     fewest_tiles = min(row_blocks * -(-layer.original_shape[0] // 256) for layer in layers)
     if fewest_tiles >= GROUP_MAX_WAVES * _pairs_per_device(x.device):
         return False

@@ -336,6 +336,32 @@ def _(a16, w16, mid_hl, up_hl, bias, out_fp32):
     return a16.new_empty((a16.shape[0], w16.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
 
 
+@_op("linear_gemm_small")
+def linear_gemm_small(a16: Tensor, w16: Tensor, mid_hl: Optional[Tensor], up_hl: Optional[Tensor],
+                      bias: Optional[Tensor], out_fp32: bool) -> Tensor:
+    """``linear_gemm`` for small batches (``svdq_linear_gemm_small``: weight rows as the MMA's M,
+    tokens as its N, bound by the bytes of w16)."""
+    _need_cuda("linear_gemm_small", a16, w16, mid_hl, up_hl, bias)
+    _need(a16.dtype == torch.float16 and w16.dtype == torch.float16, "linear_gemm_small: a16/w16 must be fp16")
+    m, k_pad = a16.shape
+    n = w16.shape[0]
+    _need(w16.shape[1] == k_pad, "linear_gemm_small: activation / weight K mismatch")
+    r2 = 0 if mid_hl is None or mid_hl.numel() == 0 else mid_hl.shape[1]
+    _need(r2 == 0 or (up_hl is not None and tuple(up_hl.shape) == (n, r2)), "linear_gemm_small: up_hl shape mismatch")
+    out = torch.empty((m, n), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=a16.device)
+    if m == 0:
+        return out
+    _lib.call("svdq_linear_gemm_small", _p(a16), _p(w16), _p(mid_hl) if r2 else None, _p(up_hl) if r2 else None, r2,
+              _p(bias), _p(out), _lib.SVDQ_FP32 if out_fp32 else _lib.SVDQ_BF16, out.stride(0), m, n, k_pad,
+              _stream(a16.device))
+    return out
+
+
+@linear_gemm_small.register_fake
+def _(a16, w16, mid_hl, up_hl, bias, out_fp32):
+    return a16.new_empty((a16.shape[0], w16.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
+
+
 EPILOGUES = {"add": _lib.SVDQ_EPI_ADD, "sigmoid_mul": _lib.SVDQ_EPI_SIGMOID_MUL, "silu_mul": _lib.SVDQ_EPI_SILU_MUL}
 
 
