@@ -45,6 +45,9 @@ def _rel(a, b):
 SHAPES = [
     # M, N, K_pad, R2, bias
     (1, 2048, 1024, 64, True),      # one token
+    (16, 2048, 2048, 128, True),    # two low-rank stages
+    (16, 1024, 1024, 192, True),    # three low-rank stages (rank 32 + LoRA 64)
+    (32, 512, 1024, 0, True),       # no low-rank term, 32-token tile
     (16, 1536, 6144, 64, True),     # to_k shape: 12 weight tiles, split K over clusters
     (37, 1000, 640, 64, False),     # ragged M and N, no bias
     (64, 16384, 6144, 64, True),    # the config-2 layer at 64 tokens
