@@ -83,11 +83,18 @@ struct PwLayout {
   static constexpr uint32_t kAccCols = TN < 32 ? 32 : TN;                     // accumulator columns
   static constexpr int kAStages = std::min<int>(12, (PW_TMEM_COLS - kAccCols) / PW_STAGE_COLS) / PW_SUB * PW_SUB;
   static constexpr uint32_t kB = (uint32_t)TN * PW_KB * 2;                    // token tile bytes per stage
-  static constexpr int kBStages = kB <= 2048 ? 16 : kB <= 4096 ? 12 : kB <= 16384 ? 6 : 3;
+  // W16 with up to 64 tokens: two CTAs per SM (8 warps, the accumulator's TMEM columns only, about
+  // 106 KB of shared memory), so each SM streams the weight through two TMA rings
+  static constexpr bool kTwoPerSm = W16 && TN <= 64;
+  static constexpr int kBStages = kTwoPerSm ? (kB <= 2048 ? 8 : kB <= 4096 ? 4 : 3)
+                                            : kB <= 2048 ? 16 : kB <= 4096 ? 12 : kB <= 16384 ? 6 : 3;
   static constexpr uint32_t kOffL = 0;                                        // low-rank A ring
   static constexpr uint32_t kOffB = kOffL + PW_LSTAGES * PW_A_BYTES;
   static constexpr uint32_t kOffP = kOffB + kBStages * kB;
-  static constexpr int kWStages = W16 ? (TN >= 128 ? 6 : 8) : 0;             // fp16 weight ring (W16)
+  static constexpr int kWStages = !W16 ? 0 : kTwoPerSm ? 3 : 6;             // fp16 weight ring (W16)
+  static constexpr int kThreads = kTwoPerSm ? 256 : PW_THREADS;             // W16: no converter warps
+  static constexpr uint32_t kTmemCols = !W16 ? PW_TMEM_COLS : kAccCols <= 32 ? 32 : kAccCols <= 64 ? 64
+                                        : kAccCols <= 128 ? 128 : 256;
   static constexpr uint32_t kOffS = kOffP + (W16 ? kWStages : PW_PSTAGES) * PW_P_BYTES;  // group-scale ring
   static constexpr uint32_t kOffBar = kOffS + (W16 ? 0 : PW_PSTAGES * PW_S_BYTES);
   static constexpr uint32_t kSmem = kOffBar + 1024 + 1024;                   // barriers + alignment slack
@@ -184,7 +191,7 @@ __device__ __forceinline__ void convert_word(uint32_t w, uint32_t s_lo, uint32_t
 }
 
 template <int TN, bool OUT_F32, bool W16 = false>
-__global__ void __launch_bounds__(PW_THREADS, 1)
+__global__ void __launch_bounds__(PwLayout<TN, W16>::kThreads, PwLayout<TN, W16>::kTwoPerSm ? 2 : 1)
     packed_gemm_kernel(const __grid_constant__ CUtensorMap tm_a16, const __grid_constant__ CUtensorMap tm_codes,
                        const __grid_constant__ CUtensorMap tm_mid, const __grid_constant__ CUtensorMap tm_up,
                        const PwArgs args) {
@@ -242,7 +249,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc_1(smem_u32(&bars->tmem_base), PW_TMEM_COLS);
+    tmem_alloc_1(smem_u32(&bars->tmem_base), L::kTmemCols);
     tmem_relinquish_1();
   }
   tc_fence_before();
@@ -484,7 +491,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
     cluster_sync();  // every CTA's partial is in its shared memory
     const int rows = PW_ROWS / ks;
     const uint32_t part_local = base;
-    for (int o = threadIdx.x; o < rows * TN; o += PW_THREADS) {
+    for (int o = threadIdx.x; o < rows * TN; o += L::kThreads) {
       const int rl = o % rows, col = o / rows;
       const int row = crank * rows + rl;
       const int n = n0 + row, m = m0 + col;
@@ -505,7 +512,7 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
   }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_1(tmem, PW_TMEM_COLS);
+    tmem_dealloc_1(tmem, L::kTmemCols);
   }
 }
 
@@ -559,7 +566,8 @@ __global__ void prepare_scales_kernel(const T* __restrict__ in, __half* __restri
   if (__syncthreads_or(bad) && threadIdx.x == 0 && inexact) atomicExch(inexact, 1);
 }
 
-int pw_ctas_per_sm(uint32_t) { return 1; }
+// CTAs of one launch resident per SM: two for the fp16-weight mode with up to 64 tokens per tile.
+int pw_ctas_per_sm(int tn, bool w16) { return w16 && tn <= 64 ? 2 : 1; }
 
 struct PwPlan {
   int tn, ks, units_n, units_m;
@@ -569,27 +577,17 @@ struct PwPlan {
 // tile once (128-token tiles: two waves, each converting every weight tile again).
 int pick_tn(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256; }
 
-uint32_t pw_smem(int tn) {
-  switch (tn) {
-    case 16: return PwLayout<16>::kSmem;
-    case 32: return PwLayout<32>::kSmem;
-    case 64: return PwLayout<64>::kSmem;
-    case 128: return PwLayout<128>::kSmem;
-    default: return PwLayout<256>::kSmem;
-  }
-}
-
 // Split factor: among KS in {1, 2, 4, 8} (at least two code groups per CTA), the fewest waves of
 // CTAs, then the fullest last wave; ties go to the smaller KS.  Each CTA has a fixed cost (set-up,
 // pipeline fill, epilogue, cluster reduction), so an extra wave costs more than idle SMs.
-PwPlan plan_packed(int M, int N, int K_pad) {
+PwPlan plan_packed(int M, int N, int K_pad, bool w16 = false) {
   PwPlan p;
   p.tn = pick_tn(M);
   p.units_n = (N + PW_ROWS - 1) / PW_ROWS;
   p.units_m = (M + p.tn - 1) / p.tn;
   const int n_k = K_pad / PW_KB;
   const long long units = (long long)p.units_n * p.units_m;
-  const long long slots = (long long)num_sms() * pw_ctas_per_sm(pw_smem(p.tn));
+  const long long slots = (long long)num_sms() * pw_ctas_per_sm(p.tn, w16);
   p.ks = 1;
   double best = -1.0;
   long long best_waves = 1ll << 40;
@@ -616,7 +614,7 @@ int launch_pw(const CUtensorMap& ta, const CUtensorMap& tc, const CUtensorMap& t
   if (e != cudaSuccess) return check_cuda(e, "svdq_packed_gemm: shared memory attribute");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(PW_THREADS, 1, 1);
+  cfg.blockDim = dim3(PwLayout<TN, W16>::kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -706,7 +704,7 @@ extern "C" int svdq_packed_gemm_plan(int M, int N, int K_pad, int* out4) {
   out4[0] = p.tn;
   out4[1] = p.ks;
   out4[2] = p.units_n * p.units_m * p.ks;
-  out4[3] = pw_ctas_per_sm(pw_smem(p.tn));
+  out4[3] = pw_ctas_per_sm(p.tn, false);
   return SVDQ_OK;
 }
 
@@ -788,7 +786,7 @@ extern "C" int svdq_linear_gemm_small(const void* a16, const void* w16, const vo
   if (M == 0) return SVDQ_OK;
   int* err = device_error_word();
   if (!err) return set_error(SVDQ_ERR_CUDA, "svdq_linear_gemm_small: device error word unavailable");
-  const PwPlan p = plan_packed(M, N, K_pad);
+  const PwPlan p = plan_packed(M, N, K_pad, true);
   CUtensorMap ta, tw, tmid, tup;
   int st;
   if ((st = make_tma_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a16, K_pad, M, (uint64_t)K_pad * 2, PW_KB, p.tn,
