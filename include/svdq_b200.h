@@ -141,7 +141,8 @@ int svdq_act_quant(const void* x, int64_t ldx, const void* smooth,
  * bit-exact with quantize_symmetric_int4, src/krea2_svdquant/quant/pack.py:6-23), written as
  *   out_codes8    [M, K_pad] int8: q in [-8, 7] (the unpacked form of pack_int4's codes);
  *   out_ascales_t [K_pad / a_group, lda_s] fp32: the bf16 group scales, group-major (row g holds
- *                 the scales of group g for tokens 0..M-1), lda_s >= M;
+ *                 the scales of group g for tokens 0..M-1; tokens M..round_up(M, 64)-1 below
+ *                 lda_s are written as zero), lda_s >= M;
  * plus out_mid_hl as svdq_act_quant writes it (same workspace rules).  No a16 is written.
  *   out_codes8 and out_ascales_t 16-byte aligned; other requirements as svdq_act_quant.
  */

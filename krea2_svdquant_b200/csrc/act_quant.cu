@@ -504,10 +504,14 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), min_ctas(NT))
         nms2[h] = f2_pack(-kMagic * sc, -kMagic * sc);
         if constexpr (PACKED) {
           const int row = h ? row_g8 : row_g;
-          if (t4 == 0 && row < a.M) {
+          if (t4 == 0) {
             const int grp = (st0 + c0) * kBK / a.G;
-            if (a.scales) a.scales[(int64_t)row * (a.K_pad / a.G) + grp] = __float2bfloat16_rn(sc);
-            if (a.ascales_t) a.ascales_t[(int64_t)grp * a.lda_s + row] = sc;
+            if (row < a.M) {
+              if (a.scales) a.scales[(int64_t)row * (a.K_pad / a.G) + grp] = __float2bfloat16_rn(sc);
+              if (a.ascales_t) a.ascales_t[(int64_t)grp * a.lda_s + row] = sc;
+            } else if (a.ascales_t && row < a.lda_s) {
+              a.ascales_t[(int64_t)grp * a.lda_s + row] = 0.0f;  // the padding rows of the last band read as zero
+            }
           }
         }
       }

@@ -168,7 +168,7 @@ def act_quant_i8(x: Tensor, smooth: Tensor, l2: Optional[Tensor], lora_down: Opt
     dev = x.device
     codes = torch.empty((m, k_pad), dtype=torch.int8, device=dev)
     lda = ascales_ld(m)
-    ascales = torch.zeros((k_pad // a_group, lda), dtype=torch.float32, device=dev)
+    ascales = torch.empty((k_pad // a_group, lda), dtype=torch.float32, device=dev)  # the kernel zeroes rows >= M
     mid = torch.empty((m, r2) if r2 else (0,), dtype=torch.bfloat16, device=dev)
     if m == 0:
         return codes, ascales, mid
