@@ -147,30 +147,37 @@ enum : int {
   kEpiSiluMul = 3,     // silu(z) * y            (gated MLP: z = ff.gate output, y = ff.up)
 };
 
-__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+// Two values rounded to bf16 and widened back, through the packed two-value conversion and
+// integer shifts.  The XU pipe also issues the activations' ex2 and reciprocal; with the
+// single-value conversion and its way back instead, ncu counted XU instructions at 14.7% of peak
+// against 9.0% in the sigmoid epilogue, and that launch ran 8 us longer (M 4352, N 6144, K 6144).
+__device__ __forceinline__ float2 bf16r2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(&h);
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
 
 // sigmoid(v) or silu(v) in fp32 as torch evaluates them (expf, IEEE division).
 template <int EPI>
-__device__ __noinline__ float act_exact(float v) {
+__device__ __forceinline__ float act_exact(float v) {
   return EPI == kEpiSigmoidMul ? 1.0f / (1.0f + expf(-v)) : v / (1.0f + expf(-v));
 }
-// The same rounded to bf16, from the approximate exponential and division instructions.  For
-// |v| <= 64 they differ from the exact fp32 value by at most ~85 ulp (__expf: 2 + 1.173|v| ulp,
-// __fdividef: 2 ulp, plus the roundings), so a result whose low 16 bits lie more than 256 ulp
-// from the bf16 rounding midpoint 0x8000 rounds to the same bf16 as the exact value; the others,
-// and |v| > 64 or NaN, take the exact path (out of line: 128 inlined copies per tile would overflow
-// the instruction cache and stall the MMA-issuing thread).  tests/test_gpu_epilogue.py checks all
-// 65536 bf16 inputs against torch.
-template <int EPI>
-__device__ __forceinline__ float act_bf16(float v) {
-  if (fabsf(v) <= 64.0f) {
-    const float r = __fdividef(1.0f, 1.0f + __expf(-v));
-    const float s = EPI == kEpiSigmoidMul ? r : v * r;
-    if ((__float_as_uint(s) & 0xFFFFu) - 0x7F00u > 0x200u) return bf16r(s);
-  }
-  return bf16r(act_exact<EPI>(v));
+// e^x for |x| <= 64, to a few ulp: Cody-Waite style range reduction to base 2 (J.-M. Muller,
+// "Elementary Functions", ch. 11), with the product x * log2(e) formed exactly as hi + lo by an FMA
+// against log2(e) split into a float and its float remainder.  2^hi comes from the ex2.approx
+// instruction and 2^lo as 1 + lo * ln 2: |lo| < 2^-17, so the dropped quadratic term is below
+// 2^-35 relative.  The plain ex2.approx(x * log2 e) loses up to |x| / 2 ulp to the rounding of that
+// product, which epi_act8_fast below would have to cover with a far wider fallback window.
+__device__ __forceinline__ float exp_split(float x) {
+  constexpr float kLog2e = 1.44269502162933349609375f;  // float(log2 e)
+  constexpr float kLog2eLo = 1.925963033500011e-08f;    // log2 e - kLog2e
+  constexpr float kLn2 = 0.693147182464599609375f;
+  const float hi = x * kLog2e;
+  const float lo = fmaf(x, kLog2e, -hi) + x * kLog2eLo;
+  float p;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(hi));
+  return fmaf(p, lo * kLn2, p);
 }
-
 // The operation on 8 outputs (the kernel is instantiated per operation, so a launch without one
 // carries no epilogue-operand code).  fp32 output evaluates the activation exactly, out of line.
 template <bool F32, int EPI>
@@ -183,16 +190,86 @@ template <bool F32, int EPI>
 __device__ __forceinline__ void epi_apply(float (&v)[8], const float (&z)[8]) {
   if constexpr (EPI == kEpiAdd) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = z[e] + (F32 ? v[e] : bf16r(v[e]));
-  } else if constexpr (F32) {
-    epi_act8_f32<F32, EPI>(v, z);
-  } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float y = bf16r(v[e]);
-      v[e] = EPI == kEpiSigmoidMul ? z[e] * act_bf16<EPI>(y) : act_bf16<EPI>(z[e]) * y;
+    for (int e = 0; e < 8; e += 2) {
+      const float2 y = F32 ? make_float2(v[e], v[e + 1]) : bf16r2(v[e], v[e + 1]);
+      v[e] = z[e] + y.x;
+      v[e + 1] = z[e + 1] + y.y;
     }
+  } else {
+    static_assert(F32, "bf16 activations go through epi_act8_bf16");
+    epi_act8_f32<F32, EPI>(v, z);
   }
+}
+// bf16 output of an activation epilogue on 8 outputs y (accumulator + bias) and their operand
+// words zw: the 8 results packed, and a flag set if any of them needs the exact path.
+// The activation comes from exp_split and the approximate reciprocal.  For |v| <= 64 that fp32
+// value differs from the exact path's by at most ~17 ulp (ex2.approx and the reciprocal 2^-22
+// relative each, four roundings, and the exact path's own expf error), so one whose low 16 bits
+// lie more than 32 ulp from the bf16 rounding midpoint 0x8000 rounds to the same bf16 value; the
+// others (about 0.1% of inputs), and |v| > 64 or NaN, are flagged.  tests/test_gpu_epilogue.py
+// checks all 65536 bf16 inputs against torch.
+// Out of line, with every value in registers (no stack frame): a thread's 128 columns per tile
+// share one copy of the code, and the exact path is a separate call that ~1% of calls make.  The
+// same function inlined (16 copies per thread) made the sigmoid and SiLU launches 4-6% slower
+// (M 4352, K 6144, N 6144 and 16384, alternated in one process).
+struct Act8 {
+  uint4 w;        // 8 packed bf16 results
+  uint32_t slow;  // nonzero: some result needs the exact path
+};
+template <int EPI>
+__device__ __noinline__ Act8 epi_act8_fast(float4 ya, float4 yb, uint4 zw) {
+  const float y[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
+  const uint32_t zz[4] = {zw.x, zw.y, zw.z, zw.w};
+  uint32_t w[4], slow = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 zf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zz[e]));
+    const float2 yv = bf16r2(y[2 * e], y[2 * e + 1]);
+    const float v[2] = {EPI == kEpiSigmoidMul ? yv.x : zf.x, EPI == kEpiSigmoidMul ? yv.y : zf.y};
+    float sv[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float r = __fdividef(1.0f, 1.0f + exp_split(-v[h]));
+      sv[h] = EPI == kEpiSigmoidMul ? r : v[h] * r;
+      slow |= (uint32_t)(!(fabsf(v[h]) <= 64.0f) || (__float_as_uint(sv[h]) & 0xFFFFu) - 0x7FE0u <= 0x40u);
+    }
+    const float2 a = bf16r2(sv[0], sv[1]);
+    const float o0 = EPI == kEpiSigmoidMul ? zf.x * a.x : a.x * yv.x;
+    const float o1 = EPI == kEpiSigmoidMul ? zf.y * a.y : a.y * yv.y;
+    __nv_bfloat162 hh = __floats2bfloat162_rn(o0, o1);
+    w[e] = *reinterpret_cast<uint32_t*>(&hh);
+  }
+  return Act8{make_uint4(w[0], w[1], w[2], w[3]), slow};
+}
+// The same from the exact activation, for the calls epi_act8_fast flagged (on its unflagged
+// outputs both give the same bf16, so all eight are recomputed).
+template <int EPI>
+__device__ __noinline__ uint4 epi_act8_exact(float4 ya, float4 yb, uint4 zw) {
+  const float y[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
+  const uint32_t zz[4] = {zw.x, zw.y, zw.z, zw.w};
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 zf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zz[e]));
+    const float2 yv = bf16r2(y[2 * e], y[2 * e + 1]);
+    const float2 a = EPI == kEpiSigmoidMul ? bf16r2(act_exact<EPI>(yv.x), act_exact<EPI>(yv.y))
+                                           : bf16r2(act_exact<EPI>(zf.x), act_exact<EPI>(zf.y));
+    const float o0 = EPI == kEpiSigmoidMul ? zf.x * a.x : a.x * yv.x;
+    const float o1 = EPI == kEpiSigmoidMul ? zf.y * a.y : a.y * yv.y;
+    __nv_bfloat162 hh = __floats2bfloat162_rn(o0, o1);
+    w[e] = *reinterpret_cast<uint32_t*>(&hh);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <int EPI>
+__device__ __forceinline__ uint4 epi_act8_bf16(float4 ya, float4 yb, uint4 zw) {
+  const Act8 r = epi_act8_fast<EPI>(ya, yb, zw);
+  return r.slow ? epi_act8_exact<EPI>(ya, yb, zw) : r.w;
+}
+template <int EPI>
+__device__ __forceinline__ uint2 epi_act4_bf16(float4 ya, uint2 zw) {
+  const uint4 r = epi_act8_bf16<EPI>(ya, make_float4(0.f, 0.f, 0.f, 0.f), make_uint4(zw.x, zw.y, 0u, 0u));
+  return make_uint2(r.x, r.y);
 }
 
 __device__ __forceinline__ void advance(int& idx, uint32_t& phase, int n) {
@@ -625,7 +702,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   v[2 * e + 1] += f.y;
                 }
               }
-              if constexpr (EPI != kEpiNone) {
+              if constexpr (!OUT_F32 && (EPI == kEpiSigmoidMul || EPI == kEpiSiluMul)) {
+                if (use_aux) {
+                  *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(P.out) + rbase + n) =
+                      epi_act8_bf16<EPI>(make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]),
+                                         ax[c % kAuxBufs][i / 8]);
+                  continue;
+                }
+              } else if constexpr (EPI != kEpiNone) {
                if (use_aux) {
                 float z[8];
                 if constexpr (OUT_F32) {
@@ -994,10 +1078,28 @@ extern "C" int svdq_linear_gemm_schedule(int M, int N, int K_pad, int R2, int wi
 
 namespace svdq {
 namespace {
+// The epilogue's activation code on a vector: sigmoid(x) as 1 * sigmoid(x), silu(x) as silu(x) * 1,
+// four values per thread as the GEMM epilogue calls it.
 template <int EPI>
 __global__ void epilogue_act_selftest_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, int n) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) out[i] = __float2bfloat16_rn(act_bf16<EPI>(__bfloat162float(in[i])));
+  const int i0 = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (i0 >= n) return;
+  __nv_bfloat16 x[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) x[k] = i0 + k < n ? in[i0 + k] : __float2bfloat16_rn(0.0f);
+  const __nv_bfloat162 p0 = __halves2bfloat162(x[0], x[1]), p1 = __halves2bfloat162(x[2], x[3]);
+  const uint2 xw = make_uint2(*reinterpret_cast<const uint32_t*>(&p0), *reinterpret_cast<const uint32_t*>(&p1));
+  const uint2 ones = make_uint2(0x3F803F80u, 0x3F803F80u);  // bf16 1.0 twice
+  const uint2 r = EPI == kEpiSigmoidMul
+                      ? epi_act4_bf16<EPI>(make_float4(__bfloat162float(x[0]), __bfloat162float(x[1]),
+                                                       __bfloat162float(x[2]), __bfloat162float(x[3])), ones)
+                      : epi_act4_bf16<EPI>(make_float4(1.0f, 1.0f, 1.0f, 1.0f), xw);
+  const __nv_bfloat162 q0 = *reinterpret_cast<const __nv_bfloat162*>(&r.x);
+  const __nv_bfloat162 q1 = *reinterpret_cast<const __nv_bfloat162*>(&r.y);
+  const __nv_bfloat16 o[4] = {q0.x, q0.y, q1.x, q1.y};
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    if (i0 + k < n) out[i0 + k] = o[k];
 }
 }  // namespace
 }  // namespace svdq
@@ -1006,7 +1108,7 @@ extern "C" int svdq_selftest_epilogue_act(int epilogue, const void* in, void* ou
   if (!(epilogue == svdq::kEpiSigmoidMul || epilogue == svdq::kEpiSiluMul) || !in || !out || n < 0)
     return svdq::set_error(SVDQ_ERR_INVALID_ARGUMENT, "svdq_selftest_epilogue_act: bad arguments");
   if (n == 0) return SVDQ_OK;
-  const dim3 grid((n + 255) / 256), block(256);
+  const dim3 grid((n + 1023) / 1024), block(256);
   const auto* x = static_cast<const __nv_bfloat16*>(in);
   auto* y = static_cast<__nv_bfloat16*>(out);
   if (epilogue == svdq::kEpiSigmoidMul)
