@@ -424,6 +424,46 @@ def measure_w4a16_lora(dev, flush, iters: int) -> dict:
             "lowrank_lora_ops": lowrank}
 
 
+def measure_epilogues(dev, flush, iters: int) -> dict:
+    """The GEMM's epilogue operations at the block's shapes (M 4352 = 4096 + 256 tokens, K 6144,
+    rank 32 as hi/lo R2 64, bf16 output): plain, ``z + y``, ``z * sigmoid(y)`` and ``silu(z) * y``
+    at N 6144 (to_gate / to_out.0) and N 16384 (ff.up), alternated call by call.  Each fused
+    result is first checked bit for bit against the plain GEMM's output combined by torch ops."""
+    import torch
+    import torch.nn.functional as F
+
+    from krea2_svdquant_b200 import ops
+
+    m, k, r2 = 4352, K, 2 * RANK
+    out = {"config": "GEMM epilogue operations, M4352 K6144 rank 32 (R2 64), bf16 output, fp16 operands",
+           "per_n": {}}
+    for n in (6144, 16384):
+        g = torch.Generator(device=dev).manual_seed(n)
+        a16 = (torch.randn(m, k, device=dev, generator=g) * 0.5).half()
+        w16 = (torch.randn(n, k, device=dev, generator=g) * 0.02).half()
+        mid = (torch.randn(m, r2, device=dev, generator=g) * 0.5).bfloat16()
+        up = (torch.randn(n, r2, device=dev, generator=g) * 0.05).bfloat16()
+        b = (torch.randn(n, device=dev, generator=g) * 0.1).bfloat16()
+        z = torch.randn(m, n, device=dev, generator=g).bfloat16()
+        y = ops.eager.linear_gemm(a16, w16, mid, up, b, False)
+        want = {"add": z + y, "sigmoid_mul": z * torch.sigmoid(y), "silu_mul": F.silu(z) * y}
+        names, fns = ["plain"], [lambda: ops.eager.linear_gemm(a16, w16, mid, up, b, False)]
+        for nm, code in ops.EPILOGUES.items():
+            got = ops.eager.linear_gemm_epi(a16, w16, mid, up, b, False, code, z)
+            if not torch.equal(got, want[nm]):
+                raise RuntimeError(f"epilogue {nm} at N{n} differs from the unfused torch ops")
+            names.append(nm)
+            fns.append(lambda code=code: ops.eager.linear_gemm_epi(a16, w16, mid, up, b, False, code, z))
+        del y, want, got
+        ts = _device_times_ab(fns, iters, flush)
+        us = {nm: round(statistics.median(t) * 1e3, 1) for nm, t in zip(names, ts)}
+        us["overhead_us"] = {nm: round(us[nm] - us["plain"], 1) for nm in ops.EPILOGUES}
+        out["per_n"][f"N{n}"] = us
+        del a16, w16, mid, up, b, z
+    out["bit_exact_vs_unfused"] = True
+    return out
+
+
 def measure_small_batch(dev, flush, iters: int) -> dict:
     """The config-2/4 layer (K6144 N16384, rank 32, group 64, bias) at small batches, where the
     weight bytes bound the GEMM.  Packed-weight GEMMs (half-byte codes + fp16 scales, no fp16 weight
@@ -615,6 +655,27 @@ def run_small_batch_only(args) -> None:
     print(json.dumps({"metric": "small-batch SVDQuantLinear K6144 N16384", "small_batch": res}), flush=True)
 
 
+def run_epilogues_only(args) -> None:
+    """--only-epilogues: the GEMM epilogue-operation measurement alone on one GPU (one JSON line)."""
+    import torch
+
+    from krea2_svdquant_b200 import _lib
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    flush_w = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(32 * 1024 * 1024, dtype=torch.int64, device=dev)
+
+    def flush_l2():
+        flush_w.zero_()
+        return flush_r.sum()
+
+    res = measure_epilogues(dev, flush_l2, max(args.warmup, 20))
+    if _lib.device_error():
+        raise RuntimeError("device-side error during the epilogue measurement")
+    print(json.dumps({"metric": "GEMM epilogue operations M4352 K6144", "epilogues": res}), flush=True)
+
+
 def run_block_linears_only(args) -> None:
     """--only-block-linears: the config-3 measurement alone on one GPU (one JSON line)."""
     import torch
@@ -758,6 +819,7 @@ def run_ours(args) -> None:
         extra["block_linears"] = measure_block_linears(dev, flush_l2, 10)
         extra["w4a16_lora"] = measure_w4a16_lora(dev, flush_l2, 10)
         extra["small_batch"] = measure_small_batch(dev, flush_l2, 20)
+        extra["epilogues"] = measure_epilogues(dev, flush_l2, 20)
         torch.cuda.empty_cache()
         extra["forward28"] = measure_forward28(world, rank, dev, args)
         if world == 1 and not args.offload:
@@ -858,6 +920,8 @@ def main() -> None:
                     help="run only the config-3 block-linears measurement (one GPU)")
     ap.add_argument("--only-small-batch", action="store_true",
                     help="run only the small-batch (M 16/64/256) packed-weight measurement (one GPU)")
+    ap.add_argument("--only-epilogues", action="store_true",
+                    help="run only the GEMM epilogue-operation measurement (one GPU)")
     ap.add_argument("--graph", action="store_true",
                     help="replay the resident 28-block forward from a CUDA graph (host launch cost is not on the "
                          "critical path at these sizes, so eager launches are the default)")
@@ -875,6 +939,8 @@ def main() -> None:
         run_block_linears_only(args)
     elif args.only_small_batch:
         run_small_batch_only(args)
+    elif args.only_epilogues:
+        run_epilogues_only(args)
     else:
         run_ours(args)
 
