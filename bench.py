@@ -467,7 +467,8 @@ def measure_epilogues(dev, flush, iters: int) -> dict:
 def measure_small_batch(dev, flush, iters: int) -> dict:
     """The config-2/4 layer (K6144 N16384, rank 32, group 64, bias) at small batches, where the
     weight bytes bound the GEMM.  Packed-weight GEMMs (half-byte codes + fp16 scales, no fp16 weight
-    in memory): the int8-code W4A4 GEMM (kind::i8, per-group rescale; batches up to 64 tokens) and
+    in memory): the int8-code W4A4 GEMMs (kind::i8 with per-group rescale, batches up to 64 tokens;
+    the narrow one on register-resident mma.sync fragments, up to 32 tokens) and
     the fp16-operand packed GEMM (the W4A16 path) against the fp16-weight GEMMs (CTA-pair tiles, and
     the small-batch one with weight rows as the MMA's M), each against its
     roofline max(bytes / HBM peak, 2MNK / bf16 peak).  Kernel times with the L2 flushed; the
@@ -487,7 +488,7 @@ def measure_small_batch(dev, flush, iters: int) -> dict:
     pk = mod_pk.prepare(dev)
     r2 = p.up_hl.shape[1]
     out = {}
-    for m in (16, 64, 256):
+    for m in (16, 32, 64, 256):
         x = torch.randn(m, K, device=dev).bfloat16()
         a16, mid, _, _ = ops.act_quant(x, p.smooth, p.l2, None, None, p.k_pad, 64, True, False)
         lowrank = m * r2 * 2 + N * r2 * 2 + N * 2 + m * N * 2  # mid_hl, up_hl, bias, out
@@ -507,6 +508,10 @@ def measure_small_batch(dev, flush, iters: int) -> dict:
             put("w4a4_i8_gemm", statistics.median(_device_times(
                 lambda: ops.w4a4_gemm(c8, asc, 64, pk.codes, pk.scales16, GROUP, mid8, p.up_hl, p.bias, False),
                 iters, flush)), m * K + asc.numel() * 4, w_pk)
+            if ops.w4a4_narrow_ok(m, N, K, 64, GROUP):
+                put("w4a4_narrow_gemm", statistics.median(_device_times(
+                    lambda: ops.w4a4_gemm_narrow(c8, asc, 64, pk.codes, pk.scales16, GROUP, mid8, p.up_hl, p.bias,
+                                                 False), iters, flush)), m * K + asc.numel() * 4, w_pk)
         put("packed_f16_gemm", statistics.median(_device_times(
             lambda: ops.packed_gemm(a16, pk.codes, pk.scales16, GROUP, mid, p.up_hl, p.bias, False), iters, flush)),
             m * K * 2, w_pk)
@@ -516,12 +521,14 @@ def measure_small_batch(dev, flush, iters: int) -> dict:
             lambda: ops.linear_gemm_small(a16, p.w16, mid, p.up_hl, p.bias, False), iters, flush)), m * K * 2, N * K * 2)
         t_lin = statistics.median(_device_times(lambda: mod_pk(x), iters, flush))
         row.update({"linear_packed_us": round(t_lin * 1e3, 2), "linear_packed_tops": round(flops / (t_lin * 1e-3) / 1e12, 1),
-                    "linear_packed_path": ("int8 codes + kind::i8 GEMM" if m <= SVDQuantLinear.INT8_PATH_MAX_TOKENS
+                    "linear_packed_path": (("int8 codes + narrow mma.sync GEMM" if ops.w4a4_narrow_ok(m, N, K, 64, GROUP)
+                                            else "int8 codes + kind::i8 GEMM")
+                                           if m <= SVDQuantLinear.INT8_PATH_MAX_TOKENS
                                            else "a16 + packed fp16-operand GEMM")})
         out[f"M{m}"] = row
     return {"config": "K6144 N16384 rank 32 group 64 bias, W4A4, small batches (BASELINE config 4's HBM regime)",
             "hbm_peak_gbs": hbm / 1e9, "per_batch": out,
-            "plan_tn_ks_grid_ctas_per_sm": {f"M{m}": _packed_plan(m, N, K) for m in (16, 64, 256)}}
+            "plan_tn_ks_grid_ctas_per_sm": {f"M{m}": _packed_plan(m, N, K) for m in (16, 32, 64, 256)}}
 
 
 def _packed_plan(m: int, n: int, k: int) -> list[int]:

@@ -413,6 +413,27 @@ int svdq_w4a4_gemm(const void* codes8, const float* ascales_t, int64_t lda_s, in
                    cudaStream_t stream);
 
 /*
+ * svdq_w4a4_gemm for narrow batches (up to 16 tokens), with the products on mma.sync int8 fragments
+ * in registers instead of tcgen05 and tensor memory: each warp streams the codes of 16 weight rows
+ * by bulk asynchronous copies into a shared-memory ring of its own, turns each 32-bit word into the
+ * u8 operand of one k-step with two mask operations, and rescales each K group's int32 result in
+ * registers.  K is split over a cluster of two CTAs, whose fp32 partials are added through
+ * distributed shared memory in a fixed order (deterministic).  The tcgen05 kernel spends these
+ * batches converting codes into shared memory and reading each group's result back out of tensor
+ * memory.  Same arguments, operand
+ * layouts and result as svdq_w4a4_gemm (the fp32 sums in another order); also requires
+ *   M <= 16, N % 128 == 0, K_pad % 512 == 0, a_group == w_group == 64, lda_s >= M;
+ *   codes8, codes and scales16 16-byte aligned, ascales_t 4-byte aligned;
+ *   R2 % 16 == 0 (may be 0), mid_hl / up_hl / bias 4-byte aligned; ldo even, out aligned to two
+ *   elements.
+ */
+int svdq_w4a4_gemm_narrow(const void* codes8, const float* ascales_t, int64_t lda_s, int a_group,
+                          const void* codes, const void* scales16, int w_group,
+                          const void* mid_hl, const void* up_hl, int R2, const void* bias,
+                          void* out, int out_dtype, int64_t ldo, int M, int N, int K_pad,
+                          cudaStream_t stream);
+
+/*
  * The launch plan of svdq_packed_gemm for a shape on the current device: out4 = {token tile TN,
  * CTAs per cluster along K, CTAs in the grid, CTAs per SM}.  Host only apart from device
  * attribute queries.

@@ -79,6 +79,8 @@ SIGNATURES = {
     "svdq_w4a4_gemm": ([c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
                         c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_void_p], c_int),
     "svdq_packed_gemm_plan": ([c_int, c_int, c_int, ctypes.POINTER(c_int)], c_int),
+    "svdq_w4a4_gemm_narrow": ([c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
+                               c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_void_p], c_int),
 }
 
 SVDQ_BF16, SVDQ_FP16, SVDQ_FP32 = 0, 1, 2

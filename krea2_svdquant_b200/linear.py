@@ -287,14 +287,17 @@ class SVDQuantLinear(nn.Module):
         n = self.original_shape[0]
         k = _kernels()
         if self.backend is not BackendKind.B200_W4A16 and p.w16 is None and self._int8_path(x2.shape[0], p):
-            # small batch, packed weight: int8 codes and the kind::i8 GEMM with per-group rescale
+            # small batch, packed weight: int8 codes and a GEMM with per-group rescale (up to 32
+            # tokens on register-resident mma.sync fragments, else tcgen05 kind::i8)
             codes8, ascales, mid = k.act_quant_i8(x2, p.smooth, p.l2, p.lora_down if include_lora else None,
                                                     p.lora_col_scale if include_lora else None, p.k_pad,
                                                     self.act_group_size)
             up_hl = p.up_hl if include_lora else p.up_hl_base
             lowrank = (mid, up_hl) if mid.numel() else (None, None)
-            y = k.w4a4_gemm(codes8, ascales, self.act_group_size, p.codes, p.scales16, self.group_size,
-                              *lowrank, p.bias, out_fp32)
+            narrow = ops.w4a4_narrow_ok(x2.shape[0], p.codes.shape[0], p.k_pad, self.act_group_size, self.group_size)
+            gemm = k.w4a4_gemm_narrow if narrow else k.w4a4_gemm
+            y = gemm(codes8, ascales, self.act_group_size, p.codes, p.scales16, self.group_size, *lowrank, p.bias,
+                     out_fp32)
             if self.check_device_errors:
                 _lib.raise_on_device_error(f"SVDQuantLinear {tuple(self.original_shape)}")
             return ops.apply_epilogue(y.reshape(*lead, n), epilogue)

@@ -549,5 +549,38 @@ def _(codes8, ascales, a_group, codes, scales16, w_group, mid_hl, up_hl, bias, o
     return codes8.new_empty((codes8.shape[0], codes.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
 
 
+def w4a4_narrow_ok(m: int, n: int, k_pad: int, a_group: int, w_group: int) -> bool:
+    """Whether ``w4a4_gemm_narrow`` takes this shape (``svdq_w4a4_gemm_narrow``'s requirements)."""
+    return 0 < m <= 16 and n % 128 == 0 and k_pad % 512 == 0 and a_group == 64 and w_group == 64
+
+
+@_op("w4a4_gemm_narrow")
+def w4a4_gemm_narrow(codes8: Tensor, ascales: Tensor, a_group: int, codes: Tensor, scales16: Tensor, w_group: int,
+                     mid_hl: Optional[Tensor], up_hl: Optional[Tensor], bias: Optional[Tensor],
+                     out_fp32: bool) -> Tensor:
+    """``w4a4_gemm`` for up to 16 tokens on mma.sync int8 fragments in registers, K split over a CTA
+    pair; same operands and result, the fp32 sums in another order."""
+    _need_cuda("w4a4_gemm_narrow", codes8, ascales, codes, scales16, mid_hl, up_hl, bias)
+    _need(codes8.dtype == torch.int8 and codes8.is_contiguous(), "w4a4_gemm_narrow: codes8 must be contiguous int8")
+    _need(ascales.dtype == torch.float32 and ascales.is_contiguous(), "w4a4_gemm_narrow: ascales must be contiguous fp32")
+    m, k_pad = codes8.shape
+    n = codes.shape[0]
+    _need(codes.shape[1] * 2 == k_pad, "w4a4_gemm_narrow: activation / weight K mismatch")
+    r2 = 0 if mid_hl is None or mid_hl.numel() == 0 else mid_hl.shape[1]
+    _need(r2 == 0 or (up_hl is not None and tuple(up_hl.shape) == (n, r2)), "w4a4_gemm_narrow: up_hl shape mismatch")
+    out = torch.empty((m, n), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=codes8.device)
+    if m == 0:
+        return out
+    _lib.call("svdq_w4a4_gemm_narrow", _p(codes8), _p(ascales), ascales.shape[1], a_group, _p(codes), _p(scales16),
+              w_group, _p(mid_hl) if r2 else None, _p(up_hl) if r2 else None, r2, _p(bias), _p(out),
+              _lib.SVDQ_FP32 if out_fp32 else _lib.SVDQ_BF16, out.stride(0), m, n, k_pad, _stream(codes8.device))
+    return out
+
+
+@w4a4_gemm_narrow.register_fake
+def _(codes8, ascales, a_group, codes, scales16, w_group, mid_hl, up_hl, bias, out_fp32):
+    return codes8.new_empty((codes8.shape[0], codes.shape[0]), dtype=torch.float32 if out_fp32 else torch.bfloat16)
+
+
 # The plain implementations of the ops above, same names and arguments.
 eager = types.SimpleNamespace(**_EAGER)
