@@ -53,3 +53,19 @@ def test_grouped_forward_falls_back_to_module_calls():
     x = torch.randn(2, 4)
     ya, yb = grouped_forward([a, b], x)
     assert torch.equal(ya, a(x)) and torch.equal(yb, b(x))
+
+
+def test_narrow_int8_gemm_region():
+    """Packed W4A4 batches of up to 16 tokens take the register-fragment GEMM when its layout
+    requirements hold (N % 128, K_pad % 512, groups of 64); the rest of the int8 path keeps the
+    tcgen05 int8-code GEMM."""
+    from krea2_svdquant_b200 import ops
+    assert all(ops.w4a4_narrow_ok(m, 16384, 6144, 64, 64) for m in (1, 8, 16))
+    assert not any(ops.w4a4_narrow_ok(m, 16384, 6144, 64, 64) for m in (0, 17, 32))
+    assert not ops.w4a4_narrow_ok(16, 1000, 6144, 64, 64)    # N not a multiple of 128
+    assert not ops.w4a4_narrow_ok(16, 1536, 1024 + 256, 64, 64)  # K_pad not a multiple of 512
+    assert not ops.w4a4_narrow_ok(16, 1536, 6144, 128, 64)   # activation group 128
+    assert not ops.w4a4_narrow_ok(16, 1536, 6144, 64, 128)   # weight group 128
+    lin = _layer(1536, k=6144, weight_operand="packed")
+    p = types.SimpleNamespace(k_pad=6144)
+    assert lin._int8_path(16, p) and lin._int8_path(17, p)   # both sizes stay on int8 codes
