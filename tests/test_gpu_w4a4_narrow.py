@@ -113,3 +113,15 @@ def test_narrow_rejects_bad_arguments():
     with pytest.raises(_lib.SVDQError):
         ops.w4a4_gemm_narrow(c2, a2, 64, p2.codes, p2.scales16, 64, m2, p2.up_hl_base, p2.bias, True)
     torch.cuda.synchronize()
+
+
+def test_narrow_without_lowrank():
+    """R2 = 0 (no low-rank term): the residual product plus bias alone, fp32 and bf16 output."""
+    from krea2_svdquant_b200 import ops
+    x, _, mod = _packed_layer(11, 2048, 768, 32, seed=77)
+    p = mod.prepare()
+    codes8, ascales, _ = ops.act_quant_i8(x, p.smooth, p.l2, None, None, p.k_pad, 64)
+    for out_fp32 in (True, False):
+        ref = ops.w4a4_gemm(codes8, ascales, 64, p.codes, p.scales16, 64, None, None, p.bias, out_fp32)
+        got = ops.w4a4_gemm_narrow(codes8, ascales, 64, p.codes, p.scales16, 64, None, None, p.bias, out_fp32)
+        assert _rel(got, ref) <= (TOL_ORDER if out_fp32 else TOL_BF16)
