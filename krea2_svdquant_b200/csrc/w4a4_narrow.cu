@@ -1,7 +1,7 @@
-// Narrow-batch W4A4 GEMM (sm_100a): up to 32 tokens against the packed INT4 weight, with the
+// Narrow-batch W4A4 GEMM (sm_100a): up to 16 tokens against the packed INT4 weight, with the
 // products on mma.sync int8 fragments held in registers.
 //
-// At 16-32 tokens the layer's arithmetic is a few GFLOP against 50 MB of weight codes (K 6144,
+// At 16 tokens the layer's arithmetic is a few GFLOP against 50 MB of weight codes (K 6144,
 // N 16384): the time is the weight stream.  The tcgen05 int8-code kernel (packed_small.cu) spends
 // it on the CUDA-core side: it converts the codes into shared memory for the MMA and reads each
 // K group's int32 result back out of tensor memory to rescale it.  Here operands and results stay
@@ -157,11 +157,12 @@ __device__ __forceinline__ void stage_store(NarrowStage<MT>& sm, int buf, const 
 }
 
 // A cluster of two CTAs per 64 weight rows, each over half of the K chunks; warp w owns rows
-// [16 w, 16 w + 16) of the CTA's rows as n8 tiles j = 0, 1.  The second CTA hands its fp32 partial to the
-// first through distributed shared memory, which adds it (a fixed order: deterministic) and writes
-// the output.  Four CTAs per SM: 16 warps hide the latency of the MMA-rescale chains, which eight
-// (one CTA of 128 rows over all of K: 32.8 us at 16 tokens, K 6144, N 16384) left visible, and
-// 64-row CTAs spread N 16384 over all SMs (128-row pairs kept 20 idle: 30.7 us).  MT 16-token tiles (M <= 16 * MT; launched with MT = 1).
+// [16 w, 16 w + 16) of the CTA's rows as n8 tiles j = 0, 1.  The second CTA hands its fp32
+// partial to the first through distributed shared memory, which adds it (a fixed order:
+// deterministic) and writes the output.  Four CTAs share an SM.  At 16 tokens (K 6144, N 16384)
+// one 128-row CTA over all of K took 32.8 us, the K split over a pair 30.7 us, and 64-row CTAs
+// (all SMs busy) also 30.7 us; the TMA ring then gave 29.1 us.  MT 16-token tiles
+// (M <= 16 * MT); launched with MT = 1.
 template <int MT, bool OUT_F32>
 __global__ void __launch_bounds__(kNwThreads, 4)
     w4a4_narrow_kernel(const __grid_constant__ CUtensorMap tm_w, const NarrowArgs a) {

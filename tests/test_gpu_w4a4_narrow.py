@@ -1,9 +1,10 @@
 """Narrow-batch W4A4 GEMM (``svdq_w4a4_gemm_narrow``: mma.sync int8 fragments in registers, K split
 over a CTA pair, up to 16 tokens) against the tcgen05 int8-code GEMM (``svdq_w4a4_gemm``) on the
 same operands (the same exact int32 group sums, fp32 sums in another order) and, through the
-module, against the staged W4A4 oracle (README.md:64).  Shapes cover one token, a full 16-token tile, ragged M, an odd number of
-512-wide K chunks (the pair's halves differ) and a single chunk (the second CTA has none), K 16384,
-LoRA columns in the low-rank term, and no bias."""
+module, against the staged W4A4 oracle (README.md:64).  Shapes cover one token, a full 16-token
+tile, ragged M, an odd number of 512-wide K chunks (the pair's halves differ) and a single chunk
+(the second CTA has none), K 16384, LoRA columns in the low-rank term, no bias, and no low-rank
+term."""
 from __future__ import annotations
 
 import numpy as np
