@@ -87,7 +87,8 @@ def test_warmup_below_three_is_rejected():
     assert r.returncode != 0 and "--warmup" in r.stderr
 
 
-@pytest.mark.parametrize("flag", ["--only-block-linears", "--only-forward", "--no-extra", "--graph"])
+@pytest.mark.parametrize("flag", ["--only-block-linears", "--only-forward", "--only-small-batch",
+                                  "--only-epilogues", "--offload", "--no-extra", "--graph"])
 def test_documented_flags_exist(flag):
     r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--help"],
                        capture_output=True, text=True, timeout=300, cwd=ROOT)
